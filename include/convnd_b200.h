@@ -1,0 +1,177 @@
+/*
+ * convnd_b200.h — C ABI of the B200 (sm_100a) N-dimensional dense convolution library.
+ *
+ * The library replaces the reference's native CUDA backend of torch-convnd 0.5.0
+ * (src/torch_convnd/csrc/convnd.cpp, convnd_cuda.cu, convnd_mixed.cpp). The reference
+ * exposes the path only as two PyTorch dispatcher operators,
+ *
+ *   torch_convnd::conv_nd(Tensor input, Tensor weight, Tensor? bias, int[] stride,
+ *                         int[] padding, int[] dilation, int groups, int workspace_bytes)
+ *   torch_convnd::conv_nd_backward(Tensor grad_output, Tensor input, Tensor weight,
+ *                         int[] stride, int[] padding, int[] dilation, int groups,
+ *                         int workspace_bytes, bool[3] output_mask)
+ *
+ * (schemas: src/torch_convnd/_operators.py:47-56; C++ kernels: convnd.cpp:305-415).
+ * This header carries the same contract through plain pointers and sizes, so that any
+ * host (the bundled PyTorch shim, ctypes, cgo, JNI) can drive the kernels. No torch types
+ * appear here. All tensors are dense, contiguous, channels-first ([N, C, d0, d1, ...]) in
+ * device memory, exactly as the reference's operators see them after `.contiguous()`.
+ *
+ * Error convention: every entry point returns CND_OK (0) or a negative status; the
+ * message of the last failure on the calling thread is returned by cnd_last_error().
+ * Validation failures use the reference's own TORCH_CHECK texts (convnd.cpp:19-100).
+ */
+#ifndef CONVND_B200_H
+#define CONVND_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(_WIN32)
+#define CND_API __declspec(dllexport)
+#else
+#define CND_API __attribute__((visibility("default")))
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* PyTorch tensors have at most 64 dimensions: batch, channels and 62 spatial axes
+ * (reference: csrc/convnd.h:10-11, kMaxSpatialDims). */
+#define CND_MAX_RANK 62
+
+/* Status codes. */
+#define CND_OK 0
+#define CND_ERR_INVALID (-1)     /* bad geometry / arguments (reference TORCH_CHECK texts) */
+#define CND_ERR_UNSUPPORTED (-2) /* dtype or layout that the library does not implement  */
+#define CND_ERR_CUDA (-3)        /* a CUDA runtime/driver call failed                     */
+#define CND_ERR_WORKSPACE (-4)   /* caller-provided workspace is smaller than required    */
+#define CND_ERR_TIMEOUT (-5)     /* a bounded in-kernel wait expired (see cnd_device_status) */
+
+/* Element types (the reference accepts float16, bfloat16, float32, float64:
+ * convnd.cpp:40-42). */
+typedef enum cnd_dtype {
+  CND_F16 = 0,
+  CND_BF16 = 1,
+  CND_F32 = 2,
+  CND_F64 = 3
+} cnd_dtype;
+
+/* How float32 problems use the tensor cores.
+ *   CND_FP32_3XTF32: each fp32 operand is split into a TF32 "big" part and a TF32
+ *                    remainder; three kind::tf32 MMAs recover ~fp32 accuracy (default).
+ *   CND_FP32_TF32:   one kind::tf32 MMA per product (what cuBLAS does under
+ *                    allow_tf32=True in the reference's bmm calls, convnd.cpp:334).
+ *   CND_FP32_SIMT:   exact fp32 CUDA-core path (no tensor cores). */
+typedef enum cnd_fp32_mode {
+  CND_FP32_3XTF32 = 0,
+  CND_FP32_TF32 = 1,
+  CND_FP32_SIMT = 2
+} cnd_fp32_mode;
+
+/* Convolution problem. Mirrors the reference's `Geometry` record (csrc/convnd.h:13-27)
+ * plus batch size and dtype. Filled and validated by cnd_problem_init. */
+typedef struct cnd_problem {
+  int32_t rank;           /* spatial rank, 1..62 */
+  int32_t dtype;          /* cnd_dtype */
+  int32_t fp32_mode;      /* cnd_fp32_mode, only read for CND_F32 */
+  int32_t reserved;
+  int64_t batch;
+  int64_t channels;        /* input channels (all groups) */
+  int64_t output_channels; /* output channels (all groups) */
+  int64_t groups;
+  int64_t input_volume;
+  int64_t output_volume;
+  int64_t kernel_volume;
+  int64_t input[CND_MAX_RANK];
+  int64_t output[CND_MAX_RANK];
+  int64_t kernel[CND_MAX_RANK];
+  int64_t stride[CND_MAX_RANK];
+  int64_t padding[CND_MAX_RANK];
+  int64_t dilation[CND_MAX_RANK];
+} cnd_problem;
+
+/* Validate a geometry and derive output extents and volumes.
+ * Replaces make_geometry (reference csrc/convnd.cpp:33-87): same checks, same order, same
+ * messages ("groups must be positive", "kernel exceeds padded input", "... overflows
+ * int64", ...). `input_shape` is [N, C, d0..], `weight_shape` is [Cout, C/groups, k0..];
+ * both have rank+2 entries. */
+CND_API int cnd_problem_init(cnd_problem* problem, int32_t rank, const int64_t* input_shape,
+                     const int64_t* weight_shape, const int64_t* stride,
+                     const int64_t* padding, const int64_t* dilation, int64_t groups,
+                     int32_t dtype);
+
+/* The reference's patch-budget rule (tile_size, csrc/convnd.cpp:89-100): fails with
+ * "workspace_bytes is too small for one output position; requires at least <n>" when the
+ * budget cannot hold one output position's patch column. The B200 kernels never
+ * materialise patches, so the budget is only validated to keep the operator contract. */
+CND_API int cnd_check_workspace_budget(const cnd_problem* problem, int64_t element_size,
+                               int64_t workspace_bytes);
+
+/* Device scratch bytes that cnd_forward / cnd_backward need for `problem`
+ * (channels-last operand copies, packed weights, split-K partials). */
+CND_API size_t cnd_forward_workspace_size(const cnd_problem* problem);
+CND_API size_t cnd_backward_workspace_size(const cnd_problem* problem, const int32_t output_mask[3]);
+
+/* Forward: y = conv(x, w) + b. Replaces torch_convnd::conv_nd's CUDA kernel
+ * (reference csrc/convnd.cpp:305-343). x: [N, C, in...], w: [Cout, C/g, k...],
+ * b: [Cout] or NULL, y: [N, Cout, out...]; all of `problem->dtype`, contiguous.
+ * `stream` is a cudaStream_t (NULL = legacy default stream). */
+CND_API int cnd_forward(const cnd_problem* problem, const void* x, const void* w, const void* b,
+                void* y, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Backward: fills the gradients selected by output_mask = {dx, dw, db}.
+ * Replaces torch_convnd::conv_nd_backward's CUDA kernel (reference
+ * csrc/convnd.cpp:345-415 for fp32/fp64 and csrc/convnd_mixed.cpp:11-59 for fp16/bf16).
+ * dx has x's shape, dw has w's shape, db has Cout entries, all of `problem->dtype`.
+ * Low-precision gradients accumulate in fp32 and are rounded once, as the reference's
+ * mixed backward does. Pointers whose mask entry is 0 may be NULL. */
+CND_API int cnd_backward(const cnd_problem* problem, const void* dy, const void* x, const void* w,
+                 void* dx, void* dw, void* db, const int32_t output_mask[3],
+                 void* workspace, size_t workspace_bytes, void* stream);
+
+/* Which kernel family cnd_forward / cnd_backward would use for `problem`:
+ * bit 0 = forward on tcgen05, bit 1 = dgrad on tcgen05, bit 2 = wgrad on tcgen05.
+ * A clear bit means the generic CUDA-core kernels run that pass. */
+CND_API int cnd_fast_path_mask(const cnd_problem* problem);
+
+/* Reads and clears the library's device error word (set by a bounded wait that expired
+ * inside a kernel). Returns CND_OK, or CND_ERR_TIMEOUT with the failing site in the
+ * message. Synchronises `stream`. */
+CND_API int cnd_device_status(void* stream);
+
+/* Number of kernels the library launched on this thread since the last reset. */
+CND_API int64_t cnd_launch_count(int32_t reset);
+
+/* Process-wide default for how float32 problems use the tensor cores (cnd_fp32_mode);
+ * cnd_problem_init copies it into each problem. Returns the previous value. */
+CND_API int cnd_set_default_fp32_mode(int32_t mode);
+
+/* Test support for the bounded-wait failure path: launches one small forward kernel
+ * whose producer never issues a load, so the MMA thread's wait expires after
+ * `timeout_ms`; the kernel then returns normally with the device error word set.
+ * Returns CND_ERR_TIMEOUT when that path works (no fault, no hang), another status
+ * otherwise. Allocates and frees its own small buffers. */
+CND_API int cnd_debug_stall_test(int32_t timeout_ms, void* stream);
+
+/* Benchmark support. While enabled, every pass the library launches is bracketed by a
+ * pair of CUDA events recorded on its launching stream. cnd_collect_kernel_timings
+ * synchronises those events, writes up to `capacity` (kind, milliseconds) records and
+ * clears the list; it returns the number written. Kinds: 1 forward pass (tcgen05),
+ * 2 dgrad pass (tcgen05), 3 wgrad pass (tcgen05), 4 activation pack, 5 weight pack,
+ * 6 reductions, 7 generic CUDA-core kernel. */
+CND_API int cnd_set_kernel_timing(int32_t enable);
+CND_API int cnd_collect_kernel_timings(int32_t* kinds, float* milliseconds, int32_t capacity);
+
+/* Message of the last failure on the calling thread ("" if none). */
+CND_API const char* cnd_last_error(void);
+
+/* Library version string. */
+CND_API const char* cnd_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CONVND_B200_H */

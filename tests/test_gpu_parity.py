@@ -1,0 +1,289 @@
+"""GPU parity of the B200 kernels against the reference's outputs and the fp64 oracle.
+
+Every comparison calls the product path (torch_convnd on CUDA: the native shim and the
+C-ABI library) and checks it against (a) golden fixtures made by running the reference
+itself in float64, and (b) the float64 CPU oracle on further seeded geometries. The
+tolerances are the rules in tests/tolerances.py.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import pytest
+import torch
+
+import torch_convnd
+from oracle import convnd_oracle as oracle
+from tolerances import assert_matches
+from torch_convnd import _native, conv_nd
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN_CASES = [
+    "c1", "c2r", "c3r", "c4r", "c5l1r", "c5l2r", "c5l3r", "tiled4d", "full5d", "full6d",
+    "strided_bf16",
+]
+
+
+def _run(x, w, b, dy, stride, padding, dilation, groups, mask=(True, True, True)):
+    """Forward through conv_nd and backward through autograd, on the current device."""
+    x = x.detach().clone().requires_grad_(mask[0])
+    w = w.detach().clone().requires_grad_(mask[1])
+    b = None if b is None else b.detach().clone().requires_grad_(mask[2])
+    y = conv_nd(x, w, b, stride, padding, dilation, groups, backend="native")
+    inputs = [t for t in (x, w, b) if t is not None and t.requires_grad]
+    grads = torch.autograd.grad(y, inputs, dy) if inputs else ()
+    it = iter(grads)
+    dx = next(it) if mask[0] else None
+    dw = next(it) if mask[1] else None
+    db = next(it) if (b is not None and mask[2]) else None
+    return y, dx, dw, db
+
+
+@pytest.mark.parametrize("name", GOLDEN_CASES)
+def test_golden_case(name, golden):
+    record = golden(name)
+    c = record["config"]
+    dtype = record["x"].dtype
+    cuda = lambda t: None if t is None else t.cuda()
+    y, dx, dw, db = _run(cuda(record["x"]), cuda(record["weight"]), cuda(record["bias"]),
+                         cuda(record["grad"]), c["stride"], c["padding"], c["dilation"],
+                         c["groups"])
+    torch.cuda.synchronize()
+    torch_convnd.device_status()
+    assert y.dtype == dtype
+    assert_matches(y, record["y"], dtype, f"{name} y")
+    assert_matches(dx, record["dx"], dtype, f"{name} dx")
+    assert_matches(dw, record["dw"], dtype, f"{name} dw")
+    if record["db"] is not None:
+        assert_matches(db, record["db"], dtype, f"{name} db")
+
+
+def _problem_mask(x, w, stride, padding, dilation, groups):
+    """cnd_fast_path_mask for a geometry (bit 0 fwd, bit 1 dgrad, bit 2 wgrad)."""
+    library = _native.core()
+
+    class Problem(ctypes.Structure):
+        _fields_ = [("rank", ctypes.c_int32), ("dtype", ctypes.c_int32),
+                    ("fp32_mode", ctypes.c_int32), ("reserved", ctypes.c_int32)] + [
+            (n, ctypes.c_int64) for n in ("batch", "channels", "output_channels", "groups",
+                                          "input_volume", "output_volume", "kernel_volume")] + [
+            (n, ctypes.c_int64 * 62)
+            for n in ("input", "output", "kernel", "stride", "padding", "dilation")]
+
+    codes = {torch.float16: 0, torch.bfloat16: 1, torch.float32: 2, torch.float64: 3}
+    arr = lambda v: (ctypes.c_int64 * len(v))(*v)
+    problem = Problem()
+    rank = x.ndim - 2
+    assert library.cnd_problem_init(ctypes.byref(problem), rank, arr(list(x.shape)),
+                                    arr(list(w.shape)), arr(stride), arr(padding), arr(dilation),
+                                    ctypes.c_int64(groups), codes[x.dtype]) == 0
+    return library.cnd_fast_path_mask(ctypes.byref(problem))
+
+
+@pytest.mark.parametrize(
+    ("name", "expected"),
+    [("c2r", 7), ("c3r", 7), ("c4r", 7), ("c5l1r", 5), ("c5l2r", 7), ("c5l3r", 7), ("c1", 7)],
+)
+def test_configs_run_on_tensor_cores(name, expected, golden):
+    """The BASELINE configurations take the tcgen05 path for every pass they need
+    (c5's first layer is strided: its dgrad is never requested in training)."""
+    record = golden(name)
+    c = record["config"]
+    mask = _problem_mask(record["x"], record["weight"], c["stride"], c["padding"], c["dilation"],
+                         c["groups"])
+    assert mask & expected == expected
+
+
+def _sweep():
+    cases = []
+    # (rank, batch, cin, cout, spatial, kernel, stride, padding, dilation, groups)
+    cases.append((4, 2, 32, 64, (6, 5, 7, 9), (3, 3, 3, 3), (1,) * 4, (1,) * 4, (1,) * 4, 1))
+    cases.append((4, 3, 16, 16, (5, 6, 4, 11), (3, 1, 2, 3), (1,) * 4, (1, 0, 1, 1), (1,) * 4, 1))
+    cases.append((4, 2, 64, 48, (4, 4, 5, 6), (2, 2, 2, 2), (1,) * 4, (0, 1, 1, 0), (1, 1, 2, 1), 1))
+    cases.append((4, 2, 20, 24, (5, 5, 5, 5), (3, 3, 3, 3), (1,) * 4, (1,) * 4, (1,) * 4, 2))
+    cases.append((4, 2, 16, 32, (9, 8, 8, 10), (3, 3, 3, 3), (2,) * 4, (1,) * 4, (1,) * 4, 1))
+    cases.append((5, 1, 16, 32, (5, 4, 6, 5, 7), (3,) * 5, (1,) * 5, (1,) * 5, (1,) * 5, 1))
+    cases.append((6, 1, 8, 16, (3, 4, 3, 4, 5, 4), (3,) * 6, (1,) * 6, (1,) * 6, (1,) * 6, 1))
+    cases.append((3, 2, 128, 32, (6, 7, 9), (3, 3, 3), (1,) * 3, (1,) * 3, (1,) * 3, 1))
+    cases.append((2, 2, 32, 16, (13, 17), (3, 5), (1, 1), (1, 2), (1, 1), 1))
+    cases.append((1, 2, 16, 16, (40,), (5,), (1,), (2,), (1,), 1))
+    cases.append((7, 1, 16, 16, (3, 2, 3, 2, 3, 2, 4), (2,) * 7, (1,) * 7, (1,) * 7, (1,) * 7, 1))
+    cases.append((4, 2, 8, 8, (4, 4, 4, 4), (3,) * 4, (1,) * 4, (3, 0, 2, 1), (1, 1, 1, 1), 1))
+    return cases
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32, torch.float16])
+@pytest.mark.parametrize("case", _sweep(), ids=lambda c: f"r{c[0]}_{c[2]}x{c[3]}_g{c[9]}")
+def test_geometry_sweep_against_oracle(case, dtype):
+    rank, batch, cin, cout, spatial, kernel, stride, padding, dilation, groups = case
+    generator = torch.Generator().manual_seed(hash(case) % (2**31))
+    x = torch.randn((batch, cin, *spatial), generator=generator).to(dtype)
+    w = (torch.randn((cout, cin // groups, *kernel), generator=generator) * 0.1).to(dtype)
+    b = torch.randn(cout, generator=generator).to(dtype)
+    y_ref = oracle.forward(x, w, b, stride, padding, dilation, groups)
+    dy = torch.randn(y_ref.shape, generator=generator).to(dtype)
+    dx_ref, dw_ref, db_ref = oracle.backward(dy, x, w, stride, padding, dilation, groups)
+    y, dx, dw, db = _run(x.cuda(), w.cuda(), b.cuda(), dy.cuda(), stride, padding, dilation,
+                         groups)
+    torch.cuda.synchronize()
+    torch_convnd.device_status()
+    assert_matches(y, y_ref, dtype, "y")
+    assert_matches(dx, dx_ref, dtype, "dx")
+    assert_matches(dw, dw_ref, dtype, "dw")
+    assert_matches(db, db_ref, dtype, "db")
+
+
+@pytest.mark.parametrize("rank", [4, 5, 6, 7, 8])
+def test_float64_ranks_match_tap_reference(rank):
+    """Reference tests/test_convnd.py:98-116 on the generic CUDA-core kernels."""
+    generator = torch.Generator().manual_seed(44 + rank)
+    x = torch.randn((1, 4, *((3,) * rank)), generator=generator, dtype=torch.float64)
+    w = torch.randn((4, 2, *((2,) * rank)), generator=generator, dtype=torch.float64)
+    b = torch.randn(4, generator=generator, dtype=torch.float64)
+    stride = (2,) + (1,) * (rank - 1)
+    padding = (0, 1) + (0,) * (rank - 2)
+    dilation = (1,) * rank
+    y_ref = oracle.tap_reference(x, w, b, stride, padding, dilation, 2)
+    dy = torch.randn(y_ref.shape, generator=generator, dtype=torch.float64)
+    refs = oracle.backward(dy, x, w, stride, padding, dilation, 2)
+    y, dx, dw, db = _run(x.cuda(), w.cuda(), b.cuda(), dy.cuda(), stride, padding, dilation, 2)
+    assert_matches(y, y_ref, torch.float64, "y")
+    for got, ref in zip((dx, dw, db), refs, strict=True):
+        assert_matches(got, ref, torch.float64, "grad")
+
+
+def test_gradcheck_and_gradgradcheck_float64():
+    """Reference tests/test_convnd.py:144-156 and :303-309."""
+    x = torch.randn(1, 2, 2, 2, 2, 3, device="cuda", dtype=torch.float64, requires_grad=True)
+    w = torch.randn(2, 2, 2, 1, 2, 2, device="cuda", dtype=torch.float64, requires_grad=True)
+    b = torch.randn(2, device="cuda", dtype=torch.float64, requires_grad=True)
+    assert torch.autograd.gradcheck(
+        lambda x, w, b: conv_nd(x, w, b, padding=(1, 0, 0, 1), stride=(1, 1, 1, 2)),
+        (x, w, b), fast_mode=True)
+    x2 = torch.randn(1, 1, 2, 2, 2, 2, device="cuda", dtype=torch.float64, requires_grad=True)
+    w2 = torch.randn(1, 1, 2, 1, 1, 1, device="cuda", dtype=torch.float64, requires_grad=True)
+    assert torch.autograd.gradgradcheck(lambda x, w: conv_nd(x, w), (x2, w2), fast_mode=True)
+
+
+def test_large_integer_metadata_known_answer():
+    """Reference tests/test_convnd.py:347-356: huge stride/padding give the bias."""
+    x = torch.randn(1, 2, 1, 2, 2, 2, device="cuda", dtype=torch.float64, requires_grad=True)
+    w = torch.randn(3, 2, 1, 1, 1, 1, device="cuda", dtype=torch.float64, requires_grad=True)
+    b = torch.randn(3, device="cuda", dtype=torch.float64, requires_grad=True)
+    y = conv_nd(x, w, b, padding=(2**34, 0, 0, 0), stride=(2**35, 1, 1, 1))
+    torch.testing.assert_close(y, b.reshape(1, 3, 1, 1, 1, 1).expand(1, 3, 2, 2, 2, 2))
+    gx, gw, gb = torch.autograd.grad(y.sum(), (x, w, b))
+    assert torch.count_nonzero(gx) == 0 and torch.count_nonzero(gw) == 0
+    torch.testing.assert_close(gb, torch.full_like(gb, 16.0))
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_deterministic_on_a_side_stream(dtype):
+    """Bitwise-repeatable gradients on a non-default stream (reference
+    tests/test_convnd.py:235-257); the B200 kernels use no atomics."""
+    generator = torch.Generator().manual_seed(7)
+    x = torch.randn(2, 16, 6, 5, 6, 7, generator=generator).to(dtype).cuda()
+    w = (torch.randn(32, 16, 3, 3, 3, 3, generator=generator) * 0.1).to(dtype).cuda()
+    stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(stream):
+        results = []
+        for _ in range(2):
+            xi = x.clone().requires_grad_()
+            wi = w.clone().requires_grad_()
+            out = conv_nd(xi, wi, padding=1)
+            results.append((out, *torch.autograd.grad(out.float().square().sum(), (xi, wi))))
+    stream.synchronize()
+    for first, second in zip(*results, strict=True):
+        assert torch.equal(first, second)
+    expected = oracle.forward(x.cpu(), w.cpu(), None, (1,) * 4, (1,) * 4, (1,) * 4, 1)
+    assert_matches(results[0][0], expected, dtype, "side-stream y")
+
+
+def test_empty_batch():
+    """Reference tests/test_convnd.py:191-201."""
+    layer = torch_convnd.Conv4d(2, 4, 2, device="cuda")
+    x = torch.empty(0, 2, 3, 3, 3, 3, device="cuda", requires_grad=True)
+    y = layer(x)
+    assert y.shape == (0, 4, 2, 2, 2, 2)
+    y.sum().backward()
+    assert x.grad.shape == x.shape
+    assert torch.count_nonzero(layer.weight.grad) == 0
+    assert torch.count_nonzero(layer.bias.grad) == 0
+
+
+def test_autocast_casts_to_bf16():
+    generator = torch.Generator().manual_seed(3)
+    x = torch.randn(2, 16, 5, 5, 5, 5, generator=generator)
+    w = torch.randn(32, 16, 3, 3, 3, 3, generator=generator) * 0.1
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        y = conv_nd(x.cuda(), w.cuda(), padding=1)
+    assert y.dtype == torch.bfloat16
+    expected = oracle.forward(x.bfloat16(), w.bfloat16(), None, (1,) * 4, (1,) * 4, (1,) * 4, 1)
+    assert_matches(y, expected, torch.bfloat16, "autocast y")
+
+
+def test_opcheck_on_cuda():
+    x = torch.randn(1, 2, 3, 3, 3, 3, device="cuda", requires_grad=True)
+    w = torch.randn(4, 2, 2, 2, 2, 2, device="cuda", requires_grad=True)
+    b = torch.randn(4, device="cuda", requires_grad=True)
+    results = torch.library.opcheck(torch.ops.torch_convnd.conv_nd.default,
+                                    (x, w, b, [1] * 4, [0] * 4, [1] * 4, 1, 65536))
+    assert all(value == "SUCCESS" for value in results.values())
+
+
+def test_module_trains_and_round_trips():
+    torch.manual_seed(901)
+    layer = torch_convnd.Conv4d(16, 32, 3, padding=1, device="cuda", dtype=torch.bfloat16)
+    x = torch.randn(2, 16, 4, 4, 4, 4, device="cuda", dtype=torch.bfloat16)
+    optimizer = torch.optim.SGD(layer.parameters(), lr=0.01)
+    before = layer.weight.detach().clone()
+    layer(x).float().square().mean().backward()
+    optimizer.step()
+    assert not torch.equal(layer.weight, before)
+    restored = torch_convnd.ConvNd(16, 32, 3, dimensions=4, padding=1, device="cuda",
+                                   dtype=torch.bfloat16)
+    restored.load_state_dict(layer.state_dict())
+    torch.testing.assert_close(restored(x), layer(x))
+
+
+def test_fp32_precision_modes():
+    generator = torch.Generator().manual_seed(11)
+    x = torch.randn(1, 8, 4, 4, 4, 4, 4, 4, generator=generator)
+    w = torch.randn(16, 8, 3, 3, 3, 3, 3, 3, generator=generator) * (1 / 5832**0.5)
+    expected = oracle.forward(x, w, None, (1,) * 6, (1,) * 6, (1,) * 6, 1)
+    errors = {}
+    try:
+        for mode in ("3xtf32", "tf32", "ieee"):
+            torch_convnd.set_fp32_precision(mode)
+            y = conv_nd(x.cuda(), w.cuda(), padding=1)
+            errors[mode] = float((y.double().cpu() - expected).abs().max())
+    finally:
+        torch_convnd.set_fp32_precision("3xtf32")
+    assert errors["3xtf32"] < 1e-5 and errors["ieee"] < 1e-5
+    assert errors["tf32"] < 5e-3
+
+
+def test_native_kernels_are_launched():
+    torch_convnd.launch_count(reset=True)
+    x = torch.randn(2, 32, 4, 4, 4, 8, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(64, 32, 3, 3, 3, 3, device="cuda", dtype=torch.bfloat16)
+    conv_nd(x, w, padding=1)
+    assert torch_convnd.launch_count() >= 3  # pack x, pack w, tcgen05 pass
+
+
+def test_bounded_wait_reports_timeout_and_context_survives():
+    """A producer that never issues a load makes the MMA thread's bounded wait expire:
+    the kernel returns, the host reads CND_ERR_TIMEOUT, and the context keeps working."""
+    library = _native.core()
+    status = library.cnd_debug_stall_test(50, None)
+    assert status == -5, library.cnd_last_error()
+    assert b"bounded wait expired" in library.cnd_last_error()
+    x = torch.randn(1, 16, 4, 4, 4, 8, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(16, 16, 1, 1, 1, 1, device="cuda", dtype=torch.bfloat16)
+    y = conv_nd(x, w)
+    expected = oracle.forward(x.cpu(), w.cpu(), None, (1,) * 4, (0,) * 4, (1,) * 4, 1)
+    assert_matches(y, expected, torch.bfloat16, "after-timeout y")
+    torch_convnd.device_status()

@@ -1,0 +1,109 @@
+"""Fake (meta) kernels and derivative formulas of the torch_convnd operators.
+
+Registered from Python like the reference's ``_autograd.py`` (fake kernels :8-26,
+autograd :29-46, double backward :49-90): the forward saves (input, weight) and its
+backward calls ``conv_nd_backward`` with ``output_mask = [needs dx, needs dW, has bias
+and needs db]``, so frozen inputs cost no work (a c5-style first layer whose input is
+data runs forward + wgrad only).
+"""
+
+from __future__ import annotations
+
+import torch
+
+
+def _output_extent(size, kernel, step, pad, dil):
+    return (size + 2 * pad - dil * (kernel - 1) - 1) // step + 1
+
+
+def _fake_forward(input, weight, bias, stride, padding, dilation, groups, workspace_bytes):
+    shape = [input.shape[0], weight.shape[0]]
+    for size, kernel, step, pad, dil in zip(
+        input.shape[2:], weight.shape[2:], stride, padding, dilation, strict=True
+    ):
+        shape.append(_output_extent(size, kernel, step, pad, dil))
+    return input.new_empty(shape)
+
+
+def _fake_backward(
+    grad_output, input, weight, stride, padding, dilation, groups, workspace_bytes, output_mask
+):
+    contiguous = torch.contiguous_format
+    grad_input = torch.empty_like(input, memory_format=contiguous) if output_mask[0] else None
+    grad_weight = torch.empty_like(weight, memory_format=contiguous) if output_mask[1] else None
+    grad_bias = input.new_empty(weight.shape[0]) if output_mask[2] else None
+    return grad_input, grad_weight, grad_bias
+
+
+def _setup_context(ctx, inputs, output):
+    input, weight, bias, *geometry = inputs
+    ctx.save_for_backward(input, weight)
+    ctx.geometry = geometry
+    ctx.has_bias = bias is not None
+
+
+def _backward(ctx, grad_output):
+    input, weight = ctx.saved_tensors
+    needs = ctx.needs_input_grad
+    mask = [needs[0], needs[1], ctx.has_bias and needs[2]]
+    grads = torch.ops.torch_convnd.conv_nd_backward.default(
+        grad_output, input, weight, *ctx.geometry, mask
+    )
+    return (*grads, None, None, None, None, None)
+
+
+def _setup_backward_context(ctx, inputs, output):
+    grad_output, input, weight, *rest = inputs
+    ctx.save_for_backward(grad_output, input, weight)
+    ctx.geometry = rest[:-1]  # stride, padding, dilation, groups, workspace_bytes
+
+
+def _backward_backward(ctx, gg_input, gg_weight, gg_bias):
+    """Derivatives of (dx, dW, db) = conv_nd_backward(dy, x, W).
+
+    dx is bilinear in (dy, W), dW in (dy, x) and db linear in dy, so every term is one
+    more forward or backward convolution with the same geometry.
+    """
+    grad_output, input, weight = ctx.saved_tensors
+    geometry = ctx.geometry
+    needs = ctx.needs_input_grad
+    d_grad_output = d_input = d_weight = None
+    terms = []
+    with torch.autocast(device_type=input.device.type, enabled=False):
+        if gg_input is not None:
+            if needs[0]:
+                terms.append(
+                    torch.ops.torch_convnd.conv_nd.default(gg_input, weight, None, *geometry)
+                )
+            if needs[2]:
+                d_weight = torch.ops.torch_convnd.conv_nd_backward.default(
+                    grad_output, gg_input, weight, *geometry, [False, True, False]
+                )[1]
+        if gg_weight is not None:
+            if needs[0]:
+                terms.append(
+                    torch.ops.torch_convnd.conv_nd.default(input, gg_weight, None, *geometry)
+                )
+            if needs[1]:
+                d_input = torch.ops.torch_convnd.conv_nd_backward.default(
+                    grad_output, input, gg_weight, *geometry, [True, False, False]
+                )[0]
+        if gg_bias is not None and needs[0]:
+            shape = (1, -1) + (1,) * (input.ndim - 2)
+            terms.append(gg_bias.reshape(shape).expand_as(grad_output))
+    for term in terms:
+        d_grad_output = term if d_grad_output is None else d_grad_output + term
+    return d_grad_output, d_input, d_weight, None, None, None, None, None, None
+
+
+def register_training() -> None:
+    torch.library.register_fake("torch_convnd::conv_nd")(_fake_forward)
+    torch.library.register_fake("torch_convnd::conv_nd_backward")(_fake_backward)
+    torch.library.register_autograd(
+        "torch_convnd::conv_nd", _backward, setup_context=_setup_context
+    )
+    torch.library.register_autograd(
+        "torch_convnd::conv_nd_backward",
+        _backward_backward,
+        setup_context=_setup_backward_context,
+    )

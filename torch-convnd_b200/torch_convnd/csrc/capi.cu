@@ -1,0 +1,639 @@
+// C-ABI entry points: plan a convolution, lay out the workspace, and run the passes.
+//
+// cnd_forward replaces torch_convnd::conv_nd's CUDA kernel (reference
+// src/torch_convnd/csrc/convnd.cpp:305-343): pack x to channels-last, pack W, one
+// tcgen05 implicit-GEMM launch whose epilogue adds the bias and writes channels-first y.
+// cnd_backward replaces conv_nd_backward (convnd.cpp:345-415, convnd_mixed.cpp:11-59):
+// one pack of dy (which also yields the bias-gradient partials), dgrad as a forward
+// pass over dy with flipped/transposed weights (stride 1), and wgrad as a split-K
+// tcgen05 pass followed by an ordered reduction. Anything outside the tensor-core path
+// runs on the generic CUDA-core kernels. There is no CPU path.
+#include <cuda_runtime.h>
+
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <vector>
+
+#include "generic.cuh"
+#include "internal.h"
+#include "pack.cuh"
+#include "tc_conv.cuh"
+
+namespace cnd {
+
+__device__ unsigned int g_error_word;
+
+namespace {
+
+thread_local int64_t g_launches = 0;
+
+uint64_t wait_timeout_ns() {
+  static uint64_t value = 0;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    uint64_t ms = 2000;
+    if (const char* env = std::getenv("CND_WAIT_TIMEOUT_MS")) {
+      const long long parsed = std::atoll(env);
+      if (parsed > 0) ms = static_cast<uint64_t>(parsed);
+    }
+    value = ms * 1000000ull;
+  });
+  return value;
+}
+
+}  // namespace
+
+void count_launch(int n) { g_launches += n; }
+
+unsigned int* device_error_word() {
+  static std::mutex mutex;
+  static unsigned int* words[128] = {};
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= 128) return nullptr;
+  std::lock_guard<std::mutex> lock(mutex);
+  if (words[device] == nullptr) {
+    void* address = nullptr;
+    if (cudaGetSymbolAddress(&address, g_error_word) == cudaSuccess) {
+      words[device] = static_cast<unsigned int*>(address);
+    }
+  }
+  return words[device];
+}
+
+namespace {
+
+// ---- optional per-pass CUDA-event timing (benchmark support) ----
+std::mutex g_timing_mutex;
+bool g_timing = false;
+struct TimingRecord {
+  int kind;
+  cudaEvent_t start, stop;
+};
+std::vector<TimingRecord> g_timings;
+
+// Brackets one pass with events on its stream when timing is enabled.
+class TimedPass {
+ public:
+  TimedPass(int kind, cudaStream_t stream) : stream_(stream) {
+    std::lock_guard<std::mutex> lock(g_timing_mutex);
+    if (!g_timing) return;
+    record_.kind = kind;
+    if (cudaEventCreate(&record_.start) != cudaSuccess) return;
+    if (cudaEventCreate(&record_.stop) != cudaSuccess) {
+      cudaEventDestroy(record_.start);
+      return;
+    }
+    active_ = true;
+    cudaEventRecord(record_.start, stream_);
+  }
+  ~TimedPass() {
+    if (!active_) return;
+    cudaEventRecord(record_.stop, stream_);
+    std::lock_guard<std::mutex> lock(g_timing_mutex);
+    g_timings.push_back(record_);
+  }
+
+ private:
+  cudaStream_t stream_;
+  TimingRecord record_{};
+  bool active_ = false;
+};
+
+constexpr size_t kAlign = 1024;
+
+size_t align_up(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
+
+int operand_type(int dtype) {
+  if (dtype == CND_BF16) return kOpBF16;
+  if (dtype == CND_F16) return kOpF16;
+  return kOpF32;
+}
+
+int element_bytes(int dtype) {
+  if (dtype == CND_F64) return 8;
+  if (dtype == CND_F32) return 4;
+  return 2;
+}
+
+// Channel count of a packed channels-last operand: rows of 32, 64 or 128 bytes (one
+// swizzle atom), or a multiple of 128 bytes.
+int64_t pad_channels(int op, int64_t c, int64_t minimum) {
+  if (c < minimum) c = minimum;
+  const int64_t unit = op == kOpF32 ? 8 : 16;  // 32 bytes
+  if (c <= unit) return unit;
+  if (c <= 2 * unit) return 2 * unit;
+  if (c <= 4 * unit) return 4 * unit;
+  return (c + 4 * unit - 1) / (4 * unit) * (4 * unit);
+}
+
+int64_t round16(int64_t v) { return (v + 15) / 16 * 16; }
+
+struct Region {
+  size_t offset = 0, bytes = 0;
+};
+
+struct Plan {
+  bool tensor_cores = false;  // dtype allows the tcgen05 path at all
+  int op = 0;
+  int split3 = 0;
+  int pack_mode = 0;
+  int parts = 1;
+  int64_t cin_g = 0, cout_g = 0;
+  int64_t x_pad = 0, dy_pad = 0;
+  bool fast_fwd = false, fast_dgrad = false, fast_wgrad = false;
+  ConvPass fwd{}, dgrad{};
+  WgradPass wgrad{};
+  // workspace
+  Region x_cl, x_cl_small, w_fwd, w_fwd_small, dy_cl, dy_cl_small, w_dg, w_dg_small, partial,
+      bias_partial;
+  size_t total = 0;
+};
+
+void fill_spatial(const cnd_problem& p, int64_t* in, int64_t* out, int64_t* k, int64_t* s,
+                  int64_t* d, int64_t* pad) {
+  for (int a = 0; a < p.rank; ++a) {
+    in[a] = p.input[a];
+    out[a] = p.output[a];
+    k[a] = p.kernel[a];
+    s[a] = p.stride[a];
+    d[a] = p.dilation[a];
+    pad[a] = p.padding[a];
+  }
+}
+
+Region take(size_t* cursor, size_t bytes) {
+  Region r;
+  r.offset = *cursor;
+  r.bytes = bytes;
+  *cursor = align_up(*cursor + bytes);
+  return r;
+}
+
+// Decides the kernel family of every pass and the workspace layout.
+// `forward` selects the forward plan; otherwise `mask` selects the backward passes.
+void make_plan(const cnd_problem& p, bool forward, const int32_t* mask, Plan* plan) {
+  *plan = Plan();
+  plan->cin_g = p.channels / p.groups;
+  plan->cout_g = p.output_channels / p.groups;
+  const bool low = p.dtype == CND_BF16 || p.dtype == CND_F16;
+  const bool f32 = p.dtype == CND_F32 && p.fp32_mode != CND_FP32_SIMT;
+  plan->tensor_cores = (low || f32) && p.rank <= kMaxFastRank && p.batch > 0;
+  if (!plan->tensor_cores) return;
+  plan->op = operand_type(p.dtype);
+  plan->split3 = (p.dtype == CND_F32 && p.fp32_mode == CND_FP32_3XTF32) ? 1 : 0;
+  plan->pack_mode = p.dtype == CND_F32 ? (plan->split3 ? 1 : 2) : 0;
+  plan->parts = plan->split3 ? 2 : 1;
+  const size_t es = element_bytes(p.dtype);
+  plan->x_pad = pad_channels(plan->op, plan->cin_g, 1);
+  plan->dy_pad = pad_channels(plan->op, plan->cout_g, 16);
+  const int64_t taps = p.kernel_volume;
+  size_t cursor = 0;
+
+  if (forward) {
+    ConvPass& f = plan->fwd;
+    f.rank = p.rank;
+    f.batch = p.batch;
+    f.groups = p.groups;
+    fill_spatial(p, f.in, f.out, f.k, f.s, f.d, f.p);
+    f.c_pad = static_cast<int>(plan->x_pad);
+    f.n_real = static_cast<int>(plan->cout_g);
+    f.n_pad = static_cast<int>(round16(plan->cout_g));
+    f.op = plan->op;
+    f.split3 = plan->split3;
+    f.out_dtype = p.dtype;
+    plan->fast_fwd = plan->cout_g <= 256 && conv_pass_supported(f);
+    if (plan->fast_fwd) {
+      const size_t act = static_cast<size_t>(p.batch * p.groups * p.input_volume) * f.c_pad * es;
+      const size_t wts = static_cast<size_t>(p.groups * taps * f.n_pad * f.c_pad) * es;
+      plan->x_cl = take(&cursor, act);
+      if (plan->split3) plan->x_cl_small = take(&cursor, act);
+      plan->w_fwd = take(&cursor, wts);
+      if (plan->split3) plan->w_fwd_small = take(&cursor, wts);
+    }
+    plan->total = cursor;
+    return;
+  }
+
+  // ---- backward ----
+  bool strided = false, wide_pad = false;
+  for (int a = 0; a < p.rank; ++a) {
+    if (p.stride[a] != 1) strided = true;
+    if (p.padding[a] > p.dilation[a] * (p.kernel[a] - 1)) wide_pad = true;
+  }
+  if (mask[0]) {
+    ConvPass& dg = plan->dgrad;
+    dg.rank = p.rank;
+    dg.batch = p.batch;
+    dg.groups = p.groups;
+    for (int a = 0; a < p.rank; ++a) {
+      dg.in[a] = p.output[a];
+      dg.out[a] = p.input[a];
+      dg.k[a] = p.kernel[a];
+      dg.s[a] = 1;
+      dg.d[a] = p.dilation[a];
+      dg.p[a] = p.dilation[a] * (p.kernel[a] - 1) - p.padding[a];
+    }
+    dg.c_pad = static_cast<int>(plan->dy_pad);
+    dg.n_real = static_cast<int>(plan->cin_g);
+    dg.n_pad = static_cast<int>(round16(plan->cin_g));
+    dg.op = plan->op;
+    dg.split3 = plan->split3;
+    dg.out_dtype = p.dtype;
+    plan->fast_dgrad = !strided && !wide_pad && plan->cin_g <= 256 && conv_pass_supported(dg);
+  }
+  if (mask[1]) {
+    WgradPass& wg = plan->wgrad;
+    wg.rank = p.rank;
+    wg.batch = p.batch;
+    wg.groups = p.groups;
+    fill_spatial(p, wg.in, wg.out, wg.k, wg.s, wg.d, wg.p);
+    wg.c_pad = static_cast<int>(plan->x_pad);
+    wg.cin_real = static_cast<int>(plan->cin_g);
+    wg.n_pad = static_cast<int>(plan->dy_pad);
+    wg.n_real = static_cast<int>(plan->cout_g);
+    wg.op = plan->op;
+    wg.split3 = plan->split3;
+    plan->fast_wgrad = plan->cout_g <= 256 && wgrad_pass_supported(wg);
+    if (plan->fast_wgrad) wg.splits = plan_wgrad_splits(wg, 0);
+    if (wg.splits <= 0) plan->fast_wgrad = false;
+  }
+  const bool need_dy = plan->fast_dgrad || plan->fast_wgrad;
+  if (need_dy) {
+    const size_t bytes =
+        static_cast<size_t>(p.batch * p.groups * p.output_volume) * plan->dy_pad * es;
+    plan->dy_cl = take(&cursor, bytes);
+    if (plan->split3) plan->dy_cl_small = take(&cursor, bytes);
+    if (mask[2]) {
+      const size_t blocks = static_cast<size_t>(pack_blocks(p.output_volume));
+      plan->bias_partial = take(&cursor, static_cast<size_t>(p.batch * p.groups) * blocks *
+                                             plan->cout_g * sizeof(float));
+    }
+  }
+  if (plan->fast_dgrad) {
+    const size_t bytes =
+        static_cast<size_t>(p.groups * taps * plan->dgrad.n_pad * plan->dgrad.c_pad) * es;
+    plan->w_dg = take(&cursor, bytes);
+    if (plan->split3) plan->w_dg_small = take(&cursor, bytes);
+  }
+  if (plan->fast_wgrad) {
+    const size_t act = static_cast<size_t>(p.batch * p.groups * p.input_volume) * plan->x_pad * es;
+    plan->x_cl = take(&cursor, act);
+    if (plan->split3) plan->x_cl_small = take(&cursor, act);
+    plan->partial = take(&cursor, static_cast<size_t>(plan->wgrad.splits) * p.groups * taps *
+                                      plan->cin_g * plan->cout_g * sizeof(float));
+  }
+  plan->total = cursor;
+}
+
+void* at(void* base, const Region& r) {
+  return r.bytes == 0 ? nullptr : static_cast<char*>(base) + r.offset;
+}
+
+int check_cuda(const char* what) {
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(CND_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  return CND_OK;
+}
+
+}  // namespace
+}  // namespace cnd
+
+extern "C" {
+
+size_t cnd_forward_workspace_size(const cnd_problem* problem) {
+  if (problem == nullptr) return 0;
+  cnd::Plan plan;
+  cnd::make_plan(*problem, true, nullptr, &plan);
+  return plan.total;
+}
+
+size_t cnd_backward_workspace_size(const cnd_problem* problem, const int32_t output_mask[3]) {
+  if (problem == nullptr || output_mask == nullptr) return 0;
+  cnd::Plan plan;
+  cnd::make_plan(*problem, false, output_mask, &plan);
+  return plan.total;
+}
+
+int cnd_fast_path_mask(const cnd_problem* problem) {
+  if (problem == nullptr) return 0;
+  cnd::Plan fwd, bwd;
+  const int32_t all[3] = {1, 1, 1};
+  cnd::make_plan(*problem, true, nullptr, &fwd);
+  cnd::make_plan(*problem, false, all, &bwd);
+  return (fwd.fast_fwd ? 1 : 0) | (bwd.fast_dgrad ? 2 : 0) | (bwd.fast_wgrad ? 4 : 0);
+}
+
+int cnd_forward(const cnd_problem* problem, const void* x, const void* w, const void* b,
+                void* y, void* workspace, size_t workspace_bytes, void* stream_handle) {
+  using namespace cnd;
+  clear_error();
+  if (problem == nullptr || x == nullptr || w == nullptr || y == nullptr) {
+    return fail(CND_ERR_INVALID, "cnd_forward: null argument");
+  }
+  const cnd_problem& p = *problem;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_handle);
+  if (p.batch == 0) return CND_OK;
+  Plan plan;
+  make_plan(p, true, nullptr, &plan);
+  if (!plan.fast_fwd) {
+    GenericCall call{GenericCall::kForward, problem, x, w, b, y};
+    TimedPass timed(7, stream);
+    return run_generic(call, stream);
+  }
+  if (workspace_bytes < plan.total || (plan.total > 0 && workspace == nullptr)) {
+    return fail(CND_ERR_WORKSPACE, "cnd_forward: workspace of %zu bytes is smaller than %zu",
+                workspace_bytes, plan.total);
+  }
+  PackActArgs pa{};
+  pa.src = x;
+  pa.dst = at(workspace, plan.x_cl);
+  pa.dst_small = at(workspace, plan.x_cl_small);
+  pa.batch = p.batch;
+  pa.groups = p.groups;
+  pa.spatial = p.input_volume;
+  pa.cg = static_cast<int>(plan.cin_g);
+  pa.c_pad = static_cast<int>(plan.x_pad);
+  pa.dtype = p.dtype;
+  pa.mode = plan.pack_mode;
+  pa.chan_partial = nullptr;
+  int rc;
+  {
+    TimedPass timed(4, stream);
+    rc = pack_activations(pa, stream);
+  }
+  if (rc != CND_OK) return rc;
+  PackWeightArgs pw{};
+  pw.w = w;
+  pw.dst = at(workspace, plan.w_fwd);
+  pw.dst_small = at(workspace, plan.w_fwd_small);
+  pw.groups = static_cast<int>(p.groups);
+  pw.cout_g = static_cast<int>(plan.cout_g);
+  pw.cin_g = static_cast<int>(plan.cin_g);
+  pw.taps = static_cast<int>(p.kernel_volume);
+  pw.n_pad = plan.fwd.n_pad;
+  pw.c_pad = plan.fwd.c_pad;
+  pw.dtype = p.dtype;
+  pw.mode = plan.pack_mode;
+  pw.dgrad = 0;
+  {
+    TimedPass timed(5, stream);
+    rc = pack_weights(pw, stream);
+  }
+  if (rc != CND_OK) return rc;
+  ConvPass pass = plan.fwd;
+  pass.act = pa.dst;
+  pass.act_small = pa.dst_small;
+  pass.wt = pw.dst;
+  pass.wt_small = pw.dst_small;
+  pass.dst = y;
+  pass.bias = b;
+  TimedPass timed(1, stream);
+  return launch_conv_pass(pass, stream, wait_timeout_ns(), 0);
+}
+
+int cnd_backward(const cnd_problem* problem, const void* dy, const void* x, const void* w,
+                 void* dx, void* dw, void* db, const int32_t output_mask[3], void* workspace,
+                 size_t workspace_bytes, void* stream_handle) {
+  using namespace cnd;
+  clear_error();
+  if (problem == nullptr || output_mask == nullptr || dy == nullptr || x == nullptr ||
+      w == nullptr) {
+    return fail(CND_ERR_INVALID, "cnd_backward: null argument");
+  }
+  if ((output_mask[0] && dx == nullptr) || (output_mask[1] && dw == nullptr) ||
+      (output_mask[2] && db == nullptr)) {
+    return fail(CND_ERR_INVALID, "cnd_backward: missing gradient buffer");
+  }
+  const cnd_problem& p = *problem;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_handle);
+  const size_t es = element_bytes(p.dtype);
+  if (p.batch == 0) {
+    // Empty batch: zero parameter gradients (reference convnd.cpp:386-393).
+    if (output_mask[1]) {
+      cudaMemsetAsync(dw, 0,
+                      static_cast<size_t>(p.output_channels * (p.channels / p.groups) *
+                                          p.kernel_volume) *
+                          es,
+                      stream);
+    }
+    if (output_mask[2]) cudaMemsetAsync(db, 0, static_cast<size_t>(p.output_channels) * es, stream);
+    return check_cuda("cnd_backward (empty batch)");
+  }
+  Plan plan;
+  make_plan(p, false, output_mask, &plan);
+  if (workspace_bytes < plan.total || (plan.total > 0 && workspace == nullptr)) {
+    return fail(CND_ERR_WORKSPACE, "cnd_backward: workspace of %zu bytes is smaller than %zu",
+                workspace_bytes, plan.total);
+  }
+  int rc = CND_OK;
+  const bool packed_dy = plan.fast_dgrad || plan.fast_wgrad;
+  const int blocks = static_cast<int>(pack_blocks(p.output_volume));
+  if (packed_dy) {
+    PackActArgs pa{};
+    pa.src = dy;
+    pa.dst = at(workspace, plan.dy_cl);
+    pa.dst_small = at(workspace, plan.dy_cl_small);
+    pa.batch = p.batch;
+    pa.groups = p.groups;
+    pa.spatial = p.output_volume;
+    pa.cg = static_cast<int>(plan.cout_g);
+    pa.c_pad = static_cast<int>(plan.dy_pad);
+    pa.dtype = p.dtype;
+    pa.mode = plan.pack_mode;
+    pa.chan_partial = output_mask[2] ? static_cast<float*>(at(workspace, plan.bias_partial)) : nullptr;
+    TimedPass timed(4, stream);
+    rc = pack_activations(pa, stream);
+    if (rc != CND_OK) return rc;
+  }
+  // ---- weight gradient ----
+  if (output_mask[1]) {
+    if (plan.fast_wgrad) {
+      PackActArgs pa{};
+      pa.src = x;
+      pa.dst = at(workspace, plan.x_cl);
+      pa.dst_small = at(workspace, plan.x_cl_small);
+      pa.batch = p.batch;
+      pa.groups = p.groups;
+      pa.spatial = p.input_volume;
+      pa.cg = static_cast<int>(plan.cin_g);
+      pa.c_pad = static_cast<int>(plan.x_pad);
+      pa.dtype = p.dtype;
+      pa.mode = plan.pack_mode;
+      {
+        TimedPass timed(4, stream);
+        rc = pack_activations(pa, stream);
+      }
+      if (rc != CND_OK) return rc;
+      WgradPass wg = plan.wgrad;
+      wg.act = pa.dst;
+      wg.act_small = pa.dst_small;
+      wg.grad = at(workspace, plan.dy_cl);
+      wg.grad_small = at(workspace, plan.dy_cl_small);
+      wg.partial = static_cast<float*>(at(workspace, plan.partial));
+      {
+        TimedPass timed(3, stream);
+        rc = launch_wgrad_pass(wg, stream, wait_timeout_ns());
+      }
+      if (rc != CND_OK) return rc;
+      TimedPass timed(6, stream);
+      rc = reduce_wgrad(wg.partial, wg.splits, static_cast<int>(p.groups),
+                        static_cast<int>(p.kernel_volume), static_cast<int>(plan.cin_g),
+                        static_cast<int>(plan.cout_g), dw, p.dtype, stream);
+      if (rc != CND_OK) return rc;
+    } else {
+      GenericCall call{GenericCall::kWgrad, problem, dy, x, nullptr, dw};
+      TimedPass timed(7, stream);
+      rc = run_generic(call, stream);
+      if (rc != CND_OK) return rc;
+    }
+  }
+  // ---- input gradient ----
+  if (output_mask[0]) {
+    if (plan.fast_dgrad) {
+      PackWeightArgs pw{};
+      pw.w = w;
+      pw.dst = at(workspace, plan.w_dg);
+      pw.dst_small = at(workspace, plan.w_dg_small);
+      pw.groups = static_cast<int>(p.groups);
+      pw.cout_g = static_cast<int>(plan.cout_g);
+      pw.cin_g = static_cast<int>(plan.cin_g);
+      pw.taps = static_cast<int>(p.kernel_volume);
+      pw.n_pad = plan.dgrad.n_pad;
+      pw.c_pad = plan.dgrad.c_pad;
+      pw.dtype = p.dtype;
+      pw.mode = plan.pack_mode;
+      pw.dgrad = 1;
+      {
+        TimedPass timed(5, stream);
+        rc = pack_weights(pw, stream);
+      }
+      if (rc != CND_OK) return rc;
+      ConvPass pass = plan.dgrad;
+      pass.act = at(workspace, plan.dy_cl);
+      pass.act_small = at(workspace, plan.dy_cl_small);
+      pass.wt = pw.dst;
+      pass.wt_small = pw.dst_small;
+      pass.dst = dx;
+      pass.bias = nullptr;
+      TimedPass timed(2, stream);
+      rc = launch_conv_pass(pass, stream, wait_timeout_ns(), 0);
+      if (rc != CND_OK) return rc;
+    } else {
+      GenericCall call{GenericCall::kDgrad, problem, dy, w, nullptr, dx};
+      TimedPass timed(7, stream);
+      rc = run_generic(call, stream);
+      if (rc != CND_OK) return rc;
+    }
+  }
+  // ---- bias gradient ----
+  if (output_mask[2]) {
+    TimedPass timed(packed_dy ? 6 : 7, stream);
+    if (packed_dy) {
+      rc = reduce_bias(static_cast<const float*>(at(workspace, plan.bias_partial)), p.batch,
+                       static_cast<int>(p.groups), blocks, static_cast<int>(plan.cout_g), db,
+                       p.dtype, stream);
+    } else {
+      GenericCall call{GenericCall::kBias, problem, dy, nullptr, nullptr, db};
+      rc = run_generic(call, stream);
+    }
+    if (rc != CND_OK) return rc;
+  }
+  return CND_OK;
+}
+
+int cnd_device_status(void* stream_handle) {
+  using namespace cnd;
+  clear_error();
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_handle);
+  cudaError_t e = cudaStreamSynchronize(stream);
+  if (e != cudaSuccess) return fail(CND_ERR_CUDA, "cudaStreamSynchronize: %s", cudaGetErrorString(e));
+  unsigned int* word = device_error_word();
+  if (word == nullptr) return fail(CND_ERR_CUDA, "device error word unavailable");
+  unsigned int value = 0;
+  e = cudaMemcpy(&value, word, sizeof(value), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return fail(CND_ERR_CUDA, "reading the device error word: %s", cudaGetErrorString(e));
+  if (value != 0) {
+    cudaMemset(word, 0, sizeof(value));
+    return fail(CND_ERR_TIMEOUT,
+                "a bounded wait expired inside a convolution kernel (site 0x%x); results of "
+                "that launch are invalid",
+                value);
+  }
+  return CND_OK;
+}
+
+int cnd_set_kernel_timing(int32_t enable) {
+  std::lock_guard<std::mutex> lock(cnd::g_timing_mutex);
+  const int previous = cnd::g_timing ? 1 : 0;
+  cnd::g_timing = enable != 0;
+  return previous;
+}
+
+int cnd_collect_kernel_timings(int32_t* kinds, float* milliseconds, int32_t capacity) {
+  std::vector<cnd::TimingRecord> records;
+  {
+    std::lock_guard<std::mutex> lock(cnd::g_timing_mutex);
+    records.swap(cnd::g_timings);
+  }
+  int written = 0;
+  for (const auto& r : records) {
+    float ms = -1.0f;
+    if (cudaEventSynchronize(r.stop) == cudaSuccess) cudaEventElapsedTime(&ms, r.start, r.stop);
+    if (written < capacity && kinds != nullptr && milliseconds != nullptr) {
+      kinds[written] = r.kind;
+      milliseconds[written] = ms;
+      ++written;
+    }
+    cudaEventDestroy(r.start);
+    cudaEventDestroy(r.stop);
+  }
+  return written;
+}
+
+int64_t cnd_launch_count(int32_t reset) {
+  const int64_t value = cnd::g_launches;
+  if (reset) cnd::g_launches = 0;
+  return value;
+}
+
+int cnd_debug_stall_test(int32_t timeout_ms, void* stream_handle) {
+  using namespace cnd;
+  clear_error();
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_handle);
+  // A 1x16x8x8 bf16 forward whose producer never issues a load: the MMA thread's bounded
+  // wait on the first stage expires and the kernel returns with the error word set.
+  ConvPass pass{};
+  pass.rank = 2;
+  pass.batch = 1;
+  pass.groups = 1;
+  pass.in[0] = pass.out[0] = 8;
+  pass.in[1] = pass.out[1] = 16;
+  pass.k[0] = pass.k[1] = 1;
+  pass.s[0] = pass.s[1] = 1;
+  pass.d[0] = pass.d[1] = 1;
+  pass.p[0] = pass.p[1] = 0;
+  pass.c_pad = 16;
+  pass.n_real = 16;
+  pass.n_pad = 16;
+  pass.op = kOpBF16;
+  pass.out_dtype = CND_BF16;
+  void* buffer = nullptr;
+  const size_t act = 8 * 16 * 16 * 2, wts = 16 * 16 * 2, out = 16 * 8 * 16 * 2;
+  if (cudaMalloc(&buffer, 3 * 4096 + act + wts + out) != cudaSuccess) {
+    return fail(CND_ERR_CUDA, "cnd_debug_stall_test: allocation failed");
+  }
+  char* base = static_cast<char*>(buffer);
+  cudaMemsetAsync(buffer, 0, 3 * 4096 + act + wts + out, stream);
+  pass.act = base;
+  pass.wt = base + align_up(act);
+  pass.dst = base + align_up(act) + align_up(wts);
+  int rc = launch_conv_pass(pass, stream,
+                            static_cast<uint64_t>(timeout_ms > 0 ? timeout_ms : 50) * 1000000ull, 1);
+  if (rc == CND_OK) rc = cnd_device_status(stream);
+  cudaStreamSynchronize(stream);
+  cudaFree(buffer);
+  return rc;
+}
+
+}  // extern "C"

@@ -1,0 +1,334 @@
+// Layout kernels around the tcgen05 passes (HBM-bound transposes and small reductions).
+//
+// pack_act: channels-first [N][G*Cg][S] -> channels-last [N][G][S][C_pad] (zero-padded
+//   channels), optionally split into TF32 big/small parts for 3xTF32, optionally
+//   producing per-block channel sums (the bias gradient of the reference's
+//   flat_grad.sum({0,3}), convnd.cpp:388-390, fused into the pass that reads dy anyway).
+// pack_weight: [Cout][Cg][taps] -> [G][taps][n_pad][c_pad] for the forward B operand, or
+//   the flipped/transposed dgrad operand [G][taps'][Cin_g pad][Cout_g pad].
+// wgrad_reduce / bias_reduce: ordered (deterministic) sums of fp32 partials.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include "internal.h"
+#include "pack.cuh"
+
+namespace cnd {
+
+namespace {
+
+template <typename T>
+__device__ __forceinline__ float to_float(T v);
+template <>
+__device__ __forceinline__ float to_float<float>(float v) {
+  return v;
+}
+template <>
+__device__ __forceinline__ float to_float<__nv_bfloat16>(__nv_bfloat16 v) {
+  return __bfloat162float(v);
+}
+template <>
+__device__ __forceinline__ float to_float<__half>(__half v) {
+  return __half2float(v);
+}
+
+// Round-to-nearest conversion of fp32 to TF32 (result kept in fp32 storage).
+__device__ __forceinline__ float tf32_round(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+
+template <typename T>
+__device__ __forceinline__ T from_float(float v);
+template <>
+__device__ __forceinline__ float from_float<float>(float v) {
+  return v;
+}
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_float<__nv_bfloat16>(float v) {
+  return __float2bfloat16_rn(v);
+}
+template <>
+__device__ __forceinline__ __half from_float<__half>(float v) {
+  return __float2half_rn(v);
+}
+
+constexpr int kPackPositions = 64;
+
+// One block: 64 positions x all channels of one (n, g). Loads coalesced along positions,
+// stores coalesced along channels.
+template <typename T, int kMode>
+__global__ void __launch_bounds__(256) pack_act_kernel(const T* __restrict__ src,
+                                                       T* __restrict__ dst,
+                                                       T* __restrict__ dst_small, int64_t S,
+                                                       int Cg, int c_pad, int G,
+                                                       float* __restrict__ chan_partial) {
+  extern __shared__ float tile[];  // [c_pad][kPackPositions + 1]
+  const int64_t s0 = static_cast<int64_t>(blockIdx.x) * kPackPositions;
+  const int g = blockIdx.y;
+  const int64_t n = blockIdx.z;
+  const int width = kPackPositions + 1;
+  const T* in = src + (n * G + g) * static_cast<int64_t>(Cg) * S;
+  for (int i = threadIdx.x; i < c_pad * kPackPositions; i += blockDim.x) {
+    const int c = i / kPackPositions;
+    const int s = i - c * kPackPositions;
+    float v = 0.0f;
+    if (c < Cg && s0 + s < S) v = to_float(in[static_cast<int64_t>(c) * S + s0 + s]);
+    tile[c * width + s] = v;
+  }
+  __syncthreads();
+  T* out = dst + ((n * G + g) * S + s0) * c_pad;
+  T* out_small = kMode == 1 ? dst_small + ((n * G + g) * S + s0) * c_pad : nullptr;
+  const int count = static_cast<int>(S - s0 < kPackPositions ? S - s0 : kPackPositions);
+  for (int i = threadIdx.x; i < count * c_pad; i += blockDim.x) {
+    const int s = i / c_pad;
+    const int c = i - s * c_pad;
+    const float v = tile[c * width + s];
+    if constexpr (kMode == 1) {
+      const float big = tf32_round(v);
+      out[i] = from_float<T>(big);
+      out_small[i] = from_float<T>(tf32_round(v - big));
+    } else if constexpr (kMode == 2) {
+      out[i] = from_float<T>(tf32_round(v));
+    } else {
+      out[i] = from_float<T>(v);
+    }
+  }
+  if (chan_partial != nullptr) {
+    // Per-channel sum of this block's positions, in position order.
+    for (int c = threadIdx.x; c < Cg; c += blockDim.x) {
+      float sum = 0.0f;
+      for (int s = 0; s < count; ++s) sum += tile[c * width + s];
+      chan_partial[((n * G + g) * gridDim.x + blockIdx.x) * Cg + c] = sum;
+    }
+  }
+}
+
+template <typename T, int kMode>
+__global__ void pack_weight_kernel(const T* __restrict__ w, T* __restrict__ dst,
+                                   T* __restrict__ dst_small, int G, int cout_g, int cin_g,
+                                   int taps, int n_pad, int c_pad, int dgrad) {
+  const int64_t total = static_cast<int64_t>(G) * taps * n_pad * c_pad;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    int64_t r = i;
+    const int c = static_cast<int>(r % c_pad);
+    r /= c_pad;
+    const int nn = static_cast<int>(r % n_pad);
+    r /= n_pad;
+    const int t = static_cast<int>(r % taps);
+    const int g = static_cast<int>(r / taps);
+    float v = 0.0f;
+    if (!dgrad) {
+      // forward operand: B[n = output channel][k = input channel] of tap t
+      if (nn < cout_g && c < cin_g) {
+        v = to_float(w[((static_cast<int64_t>(g) * cout_g + nn) * cin_g + c) * taps + t]);
+      }
+    } else {
+      // dgrad operand: B[n = input channel][k = output channel] of the flipped tap
+      if (nn < cin_g && c < cout_g) {
+        v = to_float(
+            w[((static_cast<int64_t>(g) * cout_g + c) * cin_g + nn) * taps + (taps - 1 - t)]);
+      }
+    }
+    if constexpr (kMode == 1) {
+      const float big = tf32_round(v);
+      dst[i] = from_float<T>(big);
+      dst_small[i] = from_float<T>(tf32_round(v - big));
+    } else if constexpr (kMode == 2) {
+      dst[i] = from_float<T>(tf32_round(v));
+    } else {
+      dst[i] = from_float<T>(v);
+    }
+  }
+}
+
+template <typename T>
+__global__ void wgrad_reduce_kernel(const float* __restrict__ partial, int splits, int G,
+                                    int taps, int cin_g, int cout_g, T* __restrict__ dw) {
+  const int64_t total = static_cast<int64_t>(G) * cout_g * cin_g * taps;
+  const int64_t per_split = total;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    // dw index i = ((g*cout_g + co)*cin_g + ci)*taps + t
+    int64_t r = i;
+    const int t = static_cast<int>(r % taps);
+    r /= taps;
+    const int ci = static_cast<int>(r % cin_g);
+    r /= cin_g;
+    const int co = static_cast<int>(r % cout_g);
+    const int g = static_cast<int>(r / cout_g);
+    const int64_t p = ((static_cast<int64_t>(g) * taps + t) * cin_g + ci) * cout_g + co;
+    float sum = 0.0f;
+    for (int s = 0; s < splits; ++s) sum += partial[s * per_split + p];
+    dw[i] = from_float<T>(sum);
+  }
+}
+
+template <typename T>
+__global__ void bias_reduce_kernel(const float* __restrict__ partial, int64_t rows, int G,
+                                   int blocks, int cg, T* __restrict__ db) {
+  // partial layout [N][G][blocks][cg]; db[g*cg + c] = sum over n, blocks (in order).
+  const int64_t total = static_cast<int64_t>(G) * cg;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int g = static_cast<int>(i / cg);
+    const int c = static_cast<int>(i % cg);
+    float sum = 0.0f;
+    for (int64_t n = 0; n < rows; ++n) {
+      const float* p = partial + ((n * G + g) * blocks) * static_cast<int64_t>(cg) + c;
+      float part = 0.0f;
+      for (int b = 0; b < blocks; ++b) part += p[static_cast<int64_t>(b) * cg];
+      sum += part;
+    }
+    db[i] = from_float<T>(sum);
+  }
+}
+
+int grid_for(int64_t total, int threads) {
+  int64_t blocks = (total + threads - 1) / threads;
+  if (blocks > 148 * 32) blocks = 148 * 32;
+  if (blocks < 1) blocks = 1;
+  return static_cast<int>(blocks);
+}
+
+template <typename T>
+int pack_act_typed(const PackActArgs& a, cudaStream_t stream) {
+  const int64_t blocks = (a.spatial + kPackPositions - 1) / kPackPositions;
+  if (blocks > 0x7FFFFFFF || a.groups > 65535 || a.batch > 65535) {
+    return fail(CND_ERR_UNSUPPORTED, "pack_act: grid too large");
+  }
+  const dim3 grid(static_cast<unsigned>(blocks), static_cast<unsigned>(a.groups),
+                  static_cast<unsigned>(a.batch));
+  const size_t smem = static_cast<size_t>(a.c_pad) * (kPackPositions + 1) * sizeof(float);
+  if (smem > 200 * 1024) return fail(CND_ERR_UNSUPPORTED, "pack_act: too many channels");
+  const T* src = static_cast<const T*>(a.src);
+  T* dst = static_cast<T*>(a.dst);
+  T* dst_small = static_cast<T*>(a.dst_small);
+  if (a.mode == 1) {
+    auto k = pack_act_kernel<T, 1>;
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    k<<<grid, 256, smem, stream>>>(src, dst, dst_small, a.spatial, a.cg, a.c_pad,
+                                   static_cast<int>(a.groups), a.chan_partial);
+  } else if (a.mode == 2) {
+    auto k = pack_act_kernel<T, 2>;
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    k<<<grid, 256, smem, stream>>>(src, dst, dst_small, a.spatial, a.cg, a.c_pad,
+                                   static_cast<int>(a.groups), a.chan_partial);
+  } else {
+    auto k = pack_act_kernel<T, 0>;
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    k<<<grid, 256, smem, stream>>>(src, dst, dst_small, a.spatial, a.cg, a.c_pad,
+                                   static_cast<int>(a.groups), a.chan_partial);
+  }
+  count_launch();
+  return CND_OK;
+}
+
+template <typename T>
+int pack_weight_typed(const PackWeightArgs& a, cudaStream_t stream) {
+  const int64_t total = a.groups * a.taps * a.n_pad * a.c_pad;
+  const int blocks = grid_for(total, 256);
+  const T* w = static_cast<const T*>(a.w);
+  T* dst = static_cast<T*>(a.dst);
+  T* dst_small = static_cast<T*>(a.dst_small);
+  if (a.mode == 1) {
+    pack_weight_kernel<T, 1><<<blocks, 256, 0, stream>>>(w, dst, dst_small, a.groups, a.cout_g,
+                                                          a.cin_g, a.taps, a.n_pad, a.c_pad,
+                                                          a.dgrad);
+  } else if (a.mode == 2) {
+    pack_weight_kernel<T, 2><<<blocks, 256, 0, stream>>>(w, dst, dst_small, a.groups, a.cout_g,
+                                                          a.cin_g, a.taps, a.n_pad, a.c_pad,
+                                                          a.dgrad);
+  } else {
+    pack_weight_kernel<T, 0><<<blocks, 256, 0, stream>>>(w, dst, dst_small, a.groups, a.cout_g,
+                                                          a.cin_g, a.taps, a.n_pad, a.c_pad,
+                                                          a.dgrad);
+  }
+  count_launch();
+  return CND_OK;
+}
+
+}  // namespace
+
+int pack_activations(const PackActArgs& args, cudaStream_t stream) {
+  int rc;
+  if (args.dtype == CND_BF16) {
+    rc = pack_act_typed<__nv_bfloat16>(args, stream);
+  } else if (args.dtype == CND_F16) {
+    rc = pack_act_typed<__half>(args, stream);
+  } else if (args.dtype == CND_F32) {
+    rc = pack_act_typed<float>(args, stream);
+  } else {
+    return fail(CND_ERR_UNSUPPORTED, "pack_activations: unsupported dtype");
+  }
+  if (rc != CND_OK) return rc;
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(CND_ERR_CUDA, "pack_act launch: %s", cudaGetErrorString(e));
+  return CND_OK;
+}
+
+int pack_weights(const PackWeightArgs& args, cudaStream_t stream) {
+  int rc;
+  if (args.dtype == CND_BF16) {
+    rc = pack_weight_typed<__nv_bfloat16>(args, stream);
+  } else if (args.dtype == CND_F16) {
+    rc = pack_weight_typed<__half>(args, stream);
+  } else if (args.dtype == CND_F32) {
+    rc = pack_weight_typed<float>(args, stream);
+  } else {
+    return fail(CND_ERR_UNSUPPORTED, "pack_weights: unsupported dtype");
+  }
+  if (rc != CND_OK) return rc;
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    return fail(CND_ERR_CUDA, "pack_weight launch: %s", cudaGetErrorString(e));
+  }
+  return CND_OK;
+}
+
+int reduce_wgrad(const float* partial, int splits, int groups, int taps, int cin_g, int cout_g,
+                 void* dw, int dtype, cudaStream_t stream) {
+  const int64_t total = static_cast<int64_t>(groups) * cout_g * cin_g * taps;
+  const int blocks = grid_for(total, 256);
+  if (dtype == CND_BF16) {
+    wgrad_reduce_kernel<<<blocks, 256, 0, stream>>>(partial, splits, groups, taps, cin_g, cout_g,
+                                                    static_cast<__nv_bfloat16*>(dw));
+  } else if (dtype == CND_F16) {
+    wgrad_reduce_kernel<<<blocks, 256, 0, stream>>>(partial, splits, groups, taps, cin_g, cout_g,
+                                                    static_cast<__half*>(dw));
+  } else {
+    wgrad_reduce_kernel<<<blocks, 256, 0, stream>>>(partial, splits, groups, taps, cin_g, cout_g,
+                                                    static_cast<float*>(dw));
+  }
+  count_launch();
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(CND_ERR_CUDA, "wgrad_reduce: %s", cudaGetErrorString(e));
+  return CND_OK;
+}
+
+int reduce_bias(const float* partial, int64_t batch, int groups, int blocks, int cg, void* db,
+                int dtype, cudaStream_t stream) {
+  const int64_t total = static_cast<int64_t>(groups) * cg;
+  const int grid = grid_for(total, 128);
+  if (dtype == CND_BF16) {
+    bias_reduce_kernel<<<grid, 128, 0, stream>>>(partial, batch, groups, blocks, cg,
+                                                 static_cast<__nv_bfloat16*>(db));
+  } else if (dtype == CND_F16) {
+    bias_reduce_kernel<<<grid, 128, 0, stream>>>(partial, batch, groups, blocks, cg,
+                                                 static_cast<__half*>(db));
+  } else {
+    bias_reduce_kernel<<<grid, 128, 0, stream>>>(partial, batch, groups, blocks, cg,
+                                                 static_cast<float*>(db));
+  }
+  count_launch();
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(CND_ERR_CUDA, "bias_reduce: %s", cudaGetErrorString(e));
+  return CND_OK;
+}
+
+int64_t pack_blocks(int64_t spatial) { return (spatial + kPackPositions - 1) / kPackPositions; }
+
+}  // namespace cnd

@@ -1,0 +1,35 @@
+// Host interface of the layout kernels in pack.cu.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace cnd {
+
+// mode: 0 = copy, 1 = 3xTF32 split into big + small, 2 = round to TF32.
+struct PackActArgs {
+  const void* src;      // channels-first [batch][groups*cg][spatial]
+  void* dst;            // channels-last [batch][groups][spatial][c_pad]
+  void* dst_small;      // second part for mode 1
+  int64_t batch, groups, spatial;
+  int cg, c_pad, dtype, mode;
+  float* chan_partial;  // optional [batch][groups][pack_blocks(spatial)][cg]
+};
+
+struct PackWeightArgs {
+  const void* w;        // [groups*cout_g][cin_g][taps]
+  void* dst;            // [groups][taps][n_pad][c_pad]
+  void* dst_small;
+  int groups, cout_g, cin_g, taps, n_pad, c_pad, dtype, mode, dgrad;
+};
+
+int pack_activations(const PackActArgs& args, cudaStream_t stream);
+int pack_weights(const PackWeightArgs& args, cudaStream_t stream);
+int reduce_wgrad(const float* partial, int splits, int groups, int taps, int cin_g, int cout_g,
+                 void* dw, int dtype, cudaStream_t stream);
+int reduce_bias(const float* partial, int64_t batch, int groups, int blocks, int cg, void* db,
+                int dtype, cudaStream_t stream);
+int64_t pack_blocks(int64_t spatial);
+
+}  // namespace cnd

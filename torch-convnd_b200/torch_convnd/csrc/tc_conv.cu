@@ -1,0 +1,1113 @@
+// tcgen05 implicit-GEMM convolution kernels for sm_100a.
+//
+// Replaces the reference's patch pipeline (unfold_cuda -> cuBLAS bmm -> fold_cuda,
+// src/torch_convnd/csrc/convnd_cuda.cu:173-213 and convnd.cpp:305-415): no patch
+// matrix is materialised. For every tap of the kernel, TMA loads a dense box of
+// channels-last activations (out-of-bounds elements read as zero, which is the
+// reference's implicit zero padding, convnd.h:57-76) straight into shared memory in the
+// swizzled K-major (forward/dgrad) or MN-major (wgrad) layout that tcgen05.mma reads;
+// fp32 accumulators live in tensor memory.
+//
+// Warp roles (192 threads): warp 0 = TMA producer (one thread) and TMEM owner,
+// warp 1 = MMA issuer (one thread), warps 2-5 = epilogue (TMEM lanes 32*(warp%4)...).
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cstring>
+#include <mutex>
+
+#include "ptx.cuh"
+#include "tc_conv.cuh"
+
+namespace cnd {
+
+namespace {
+
+constexpr int kThreads = 192;
+constexpr uint32_t kSiteProducer = 0x101, kSiteMma = 0x102, kSiteEpilogue = 0x103,
+                   kSiteDrain = 0x104;
+constexpr uint32_t kSiteWProducer = 0x201, kSiteWMma = 0x202, kSiteWEpilogue = 0x203;
+
+// Per-box bookkeeping, decoded once per tile.
+struct BoxInfo {
+  int32_t valid;
+  int32_t n;
+  int32_t q[3];
+  int32_t ib[3];                 // input coordinate of the box origin, tap 0
+  int32_t ib_o[kMaxOuter];       // input coordinate along each outer axis, tap 0
+  int64_t in_ng_base;            // merged input index of (n, g, outer origin 0)
+  int64_t out_merged;            // merged output index (n, g, outer output position)
+  int64_t outer_lin;             // linear outer output position (without n)
+};
+
+struct ConvKernelParams {
+  BoxGeom g;
+  int n_real, n_pad, cblocks, cblk_elems, ksteps, row_bytes, layout, stages, debug_stall;
+  uint32_t a_box_bytes, a_bytes, b_bytes, a_small_off, b_off, b_small_off, stage_bytes,
+      tx_bytes, idesc, tmem_cols;
+  void* out;
+  const void* bias;
+  int out_dtype;
+  int64_t out_channels_total;
+  int64_t out_volume;
+  unsigned int* err;
+  uint64_t timeout_ns;
+};
+
+struct WgradKernelParams {
+  BoxGeom g;
+  int c_pad, cin_real, n_pad, n_real, tpm, mt_per_cta, mt_total, splits, kc_rows, ksteps;
+  int a_row_bytes, a_layout, b_row_bytes, b_layout, b_blocks, b_blk_elems, a_stages;
+  uint32_t a_tile_bytes, a_part_bytes, a_slot_bytes, b_part_bytes, b_slot_bytes, a_tx, b_tx,
+      idesc, tmem_cols, a_base_off, bar_off;
+  int64_t ptiles;
+  float* partial;
+  unsigned int* err;
+  uint64_t timeout_ns;
+};
+
+__device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
+  const uintptr_t v = reinterpret_cast<uintptr_t>(p);
+  return reinterpret_cast<uint8_t*>((v + 1023) & ~static_cast<uintptr_t>(1023));
+}
+
+// Decodes box `bt` of group `grp` (boxes enumerate q[2] fastest, then q[1], q[0], then
+// the outer output positions, then the batch).
+__device__ void decode_box(const BoxGeom& g, int64_t bt, int grp, BoxInfo& info) {
+  info.valid = bt < g.boxes_per_group ? 1 : 0;
+  if (!info.valid) bt = 0;
+  int64_t rest = bt;
+  info.q[2] = static_cast<int32_t>(rest % g.nbox[2]);
+  rest /= g.nbox[2];
+  info.q[1] = static_cast<int32_t>(rest % g.nbox[1]);
+  rest /= g.nbox[1];
+  info.q[0] = static_cast<int32_t>(rest % g.nbox[0]);
+  rest /= g.nbox[0];
+  // rest = n * out_outer_vol + outer_lin
+  const int64_t outer_lin = rest % g.out_outer_vol;
+  const int64_t n = rest / g.out_outer_vol;
+  info.n = static_cast<int32_t>(n);
+  info.outer_lin = outer_lin;
+  int64_t o = outer_lin;
+  for (int a = g.n_outer - 1; a >= 0; --a) {
+    const int64_t coord = o % g.out_o[a];
+    o /= g.out_o[a];
+    info.ib_o[a] = static_cast<int32_t>(coord * g.s_o[a] - g.p_o[a]);
+  }
+  for (int a = 0; a < 3; ++a) {
+    info.ib[a] = info.q[a] * g.b[a] * g.s[a] - g.p[a];
+  }
+  info.in_ng_base = (n * g.groups + grp) * g.in_merged_per_ng;
+  info.out_merged = (n * g.groups + grp) * g.out_outer_vol + outer_lin;
+}
+
+// Merged input coordinate of a box for the outer taps t_o, or -1 when any outer axis
+// falls into the zero padding (TMA then fills the whole box with zeros).
+__device__ __forceinline__ int32_t merged_input(const BoxGeom& g, const BoxInfo& info,
+                                                const int* t_o) {
+  if (!info.valid) return -1;
+  int64_t m = info.in_ng_base;
+  for (int a = 0; a < g.n_outer; ++a) {
+    const int c = info.ib_o[a] + t_o[a] * g.d_o[a];
+    if (c < 0 || c >= g.in_o[a]) return -1;
+    m += static_cast<int64_t>(c) * g.in_o_stride[a];
+  }
+  return static_cast<int32_t>(m);
+}
+
+// Advances a row-major tap odometer (outer axes, then the three box axes).
+__device__ __forceinline__ void next_tap(const BoxGeom& g, int* t_o, int* t) {
+  if (++t[2] < g.k[2]) return;
+  t[2] = 0;
+  if (++t[1] < g.k[1]) return;
+  t[1] = 0;
+  if (++t[0] < g.k[0]) return;
+  t[0] = 0;
+  for (int a = g.n_outer - 1; a >= 0; --a) {
+    if (++t_o[a] < g.k_o[a]) return;
+    t_o[a] = 0;
+  }
+}
+
+__device__ __forceinline__ void set_tap(const BoxGeom& g, int tap, int* t_o, int* t) {
+  t[2] = tap % g.k[2];
+  tap /= g.k[2];
+  t[1] = tap % g.k[1];
+  tap /= g.k[1];
+  t[0] = tap % g.k[0];
+  tap /= g.k[0];
+  for (int a = g.n_outer - 1; a >= 0; --a) {
+    t_o[a] = tap % g.k_o[a];
+    tap /= g.k_o[a];
+  }
+}
+
+__device__ __forceinline__ void store_value(void* out, int64_t index, float value, int dtype) {
+  if (dtype == CND_BF16) {
+    static_cast<__nv_bfloat16*>(out)[index] = __float2bfloat16_rn(value);
+  } else if (dtype == CND_F16) {
+    static_cast<__half*>(out)[index] = __float2half_rn(value);
+  } else {
+    static_cast<float*>(out)[index] = value;
+  }
+}
+
+__device__ __forceinline__ float load_value(const void* in, int64_t index, int dtype) {
+  if (dtype == CND_BF16) return __bfloat162float(static_cast<const __nv_bfloat16*>(in)[index]);
+  if (dtype == CND_F16) return __half2float(static_cast<const __half*>(in)[index]);
+  return static_cast<const float*>(in)[index];
+}
+
+template <bool kTF32>
+__device__ __forceinline__ void mma(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc,
+                                    uint32_t acc) {
+  if constexpr (kTF32) {
+    dev::mma_tf32(d, a, b, idesc, acc);
+  } else {
+    dev::mma_f16(d, a, b, idesc, acc);
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// Forward / dgrad pass kernel. One CTA = one 128-row tile of output positions (nb boxes)
+// of one group, all n_pad output channels.
+template <bool kTF32, bool kSplit>
+__global__ void __launch_bounds__(kThreads, 1)
+    conv_pass_kernel(const __grid_constant__ CUtensorMap act_map,
+                     const __grid_constant__ CUtensorMap act_small_map,
+                     const __grid_constant__ CUtensorMap wt_map,
+                     const __grid_constant__ CUtensorMap wt_small_map,
+                     const __grid_constant__ ConvKernelParams P) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  uint8_t* stage_base = smem;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + P.stages * P.stage_bytes);
+  uint64_t* empty = full + P.stages;
+  uint64_t* acc_bar = empty + P.stages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_bar + 1);
+  volatile uint32_t* progress = tmem_slot + 1;
+  BoxInfo* boxes = reinterpret_cast<BoxInfo*>(tmem_slot + 4);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int grp = blockIdx.y;
+  const int64_t tile = blockIdx.x;
+  const BoxGeom& g = P.g;
+  const dev::ErrorWord err{P.err};
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < P.stages; ++s) {
+      dev::mbar_init(&full[s], 1);
+      dev::mbar_init(&empty[s], 1);
+    }
+    dev::mbar_init(acc_bar, 1);
+    *progress = 0;
+    dev::fence_barrier_init();
+  }
+  if (warp == 0) dev::tmem_alloc(tmem_slot, P.tmem_cols);
+  if (threadIdx.x >= 64 && threadIdx.x < 64 + g.nb) {
+    const int j = threadIdx.x - 64;
+    decode_box(g, tile * g.nb + j, grp, boxes[j]);
+  }
+  dev::tc_fence_before();
+  __syncthreads();
+  dev::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int nkb = g.taps * P.cblocks;
+
+  if (warp == 0 && lane == 0) {
+    // ---------------- TMA producer ----------------
+    dev::prefetch_tensormap(&act_map);
+    dev::prefetch_tensormap(&wt_map);
+    int t_o[kMaxOuter] = {0, 0, 0, 0, 0, 0};
+    int t[3] = {0, 0, 0};
+    int stage = 0;
+    uint32_t phase = 0;
+    int issued = 0;
+    bool ok = P.debug_stall == 0;
+    for (int tap = 0; tap < g.taps && ok; ++tap) {
+      int32_t mc[kMaxBoxes];
+      for (int j = 0; j < g.nb; ++j) mc[j] = merged_input(g, boxes[j], t_o);
+      const int32_t w_row = grp * g.taps + tap;
+      for (int cb = 0; cb < P.cblocks; ++cb) {
+        if (!dev::mbar_wait(&empty[stage], phase ^ 1u, err, kSiteProducer, P.timeout_ns)) {
+          ok = false;
+          break;
+        }
+        uint8_t* sb = stage_base + stage * P.stage_bytes;
+        dev::mbar_arrive_expect_tx(&full[stage], P.tx_bytes);
+        const int32_t c0 = cb * P.cblk_elems;
+        for (int j = 0; j < g.nb; ++j) {
+          const int32_t x2 = boxes[j].ib[2] + t[2] * g.d[2];
+          const int32_t x1 = boxes[j].ib[1] + t[1] * g.d[1];
+          const int32_t x0 = boxes[j].ib[0] + t[0] * g.d[0];
+          dev::tma_load_5d(sb + j * P.a_box_bytes, &act_map, &full[stage], c0, x2, x1, x0,
+                           mc[j]);
+          if constexpr (kSplit) {
+            dev::tma_load_5d(sb + P.a_small_off + j * P.a_box_bytes, &act_small_map,
+                             &full[stage], c0, x2, x1, x0, mc[j]);
+          }
+        }
+        dev::tma_load_3d(sb + P.b_off, &wt_map, &full[stage], c0, 0, w_row);
+        if constexpr (kSplit) {
+          dev::tma_load_3d(sb + P.b_small_off, &wt_small_map, &full[stage], c0, 0, w_row);
+        }
+        ++issued;
+        if (++stage == P.stages) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      next_tap(g, t_o, t);
+    }
+    if (!ok && issued > 0) {
+      // Let loads already in flight land before the CTA's shared memory goes away.
+      const int pending = issued < P.stages ? issued : P.stages;
+      for (int i = 1; i <= pending; ++i) {
+        const int kb = issued - i;
+        dev::mbar_wait(&full[kb % P.stages], static_cast<uint32_t>((kb / P.stages) & 1), err,
+                       kSiteDrain, P.timeout_ns / 8 + 1);
+      }
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ---------------- MMA issuer ----------------
+    int stage = 0;
+    uint32_t phase = 0;
+    const uint32_t sbo = 8u * static_cast<uint32_t>(P.row_bytes);
+    for (int kb = 0; kb < nkb; ++kb) {
+      if (!dev::mbar_wait(&full[stage], phase, err, kSiteMma, P.timeout_ns)) break;
+      dev::tc_fence_after();
+      const uint32_t sb = dev::smem_u32(stage_base + stage * P.stage_bytes);
+      for (int kk = 0; kk < P.ksteps; ++kk) {
+        const uint32_t koff = static_cast<uint32_t>(kk) * 32u;
+        const uint64_t ad = dev::make_smem_desc(sb + koff, 16, sbo, P.layout);
+        const uint64_t bd = dev::make_smem_desc(sb + P.b_off + koff, 16, sbo, P.layout);
+        const uint32_t acc = (kb | kk) != 0 ? 1u : 0u;
+        if constexpr (kSplit) {
+          const uint64_t ads = dev::make_smem_desc(sb + P.a_small_off + koff, 16, sbo, P.layout);
+          const uint64_t bds = dev::make_smem_desc(sb + P.b_small_off + koff, 16, sbo, P.layout);
+          mma<true>(tmem, ads, bd, P.idesc, acc);
+          mma<true>(tmem, ad, bds, P.idesc, 1u);
+          mma<true>(tmem, ad, bd, P.idesc, 1u);
+        } else {
+          mma<kTF32>(tmem, ad, bd, P.idesc, acc);
+        }
+      }
+      dev::mma_commit(&empty[stage]);
+      *progress = static_cast<uint32_t>(kb + 1);
+      if (++stage == P.stages) {
+        stage = 0;
+        phase ^= 1u;
+      }
+    }
+    dev::mma_commit(acc_bar);
+  } else if (warp >= 2) {
+    // ---------------- epilogue ----------------
+    dev::mbar_wait_progress(acc_bar, 0, progress, err, kSiteEpilogue, P.timeout_ns);
+    dev::tc_fence_after();
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const int j = row / g.box_rows;
+    const int local = row - j * g.box_rows;
+    const int i2 = local % g.b[2];
+    const int i1 = (local / g.b[2]) % g.b[1];
+    const int i0 = local / (g.b[2] * g.b[1]);
+    const BoxInfo& B = boxes[j];
+    const int o0 = B.q[0] * g.b[0] + i0;
+    const int o1 = B.q[1] * g.b[1] + i1;
+    const int o2 = B.q[2] * g.b[2] + i2;
+    const bool valid = B.valid && o0 < g.out[0] && o1 < g.out[1] && o2 < g.out[2];
+    const int64_t sp = B.outer_lin * g.out_box_vol +
+                       (static_cast<int64_t>(o0) * g.out[1] + o1) * g.out[2] + o2;
+    const int64_t base =
+        (static_cast<int64_t>(B.n) * P.out_channels_total + static_cast<int64_t>(grp) * P.n_real) *
+            P.out_volume +
+        sp;
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+    for (int c = 0; c < P.n_pad / 16; ++c) {
+      uint32_t v[16];
+      dev::tmem_load16(lane_addr + static_cast<uint32_t>(c * 16), v);
+      dev::tmem_load_wait();
+      if (valid) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int co = c * 16 + i;
+          if (co < P.n_real) {
+            float value = __uint_as_float(v[i]);
+            if (P.bias != nullptr) {
+              value += load_value(P.bias, static_cast<int64_t>(grp) * P.n_real + co, P.out_dtype);
+            }
+            store_value(P.out, base + static_cast<int64_t>(co) * P.out_volume, value,
+                        P.out_dtype);
+          }
+        }
+      }
+    }
+  }
+  dev::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    dev::tc_fence_after();
+    dev::tmem_dealloc(tmem, P.tmem_cols);
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// Weight-gradient kernel. Grid (split, tap chunk, group). Each CTA accumulates
+// mt_per_cta tiles of 128 (tap, channel) rows x n_pad output channels in TMEM over its
+// range of position tiles, then writes one fp32 partial.
+template <bool kTF32, bool kSplit>
+__global__ void __launch_bounds__(kThreads, 1)
+    wgrad_kernel(const __grid_constant__ CUtensorMap act_map,
+                 const __grid_constant__ CUtensorMap act_small_map,
+                 const __grid_constant__ CUtensorMap grad_map,
+                 const __grid_constant__ CUtensorMap grad_small_map,
+                 const __grid_constant__ WgradKernelParams P) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  uint8_t* b_base = smem;                       // 2 dy slots
+  uint8_t* a_base = smem + P.a_base_off;        // a_stages A slots
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + P.bar_off);
+  uint64_t* b_full = bars;
+  uint64_t* b_empty = bars + 2;
+  uint64_t* a_full = bars + 4;
+  uint64_t* a_empty = a_full + P.a_stages;
+  uint64_t* acc_bar = a_empty + P.a_stages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_bar + 1);
+  volatile uint32_t* progress = tmem_slot + 1;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int split = blockIdx.x;
+  const int chunk = blockIdx.y;
+  const int grp = blockIdx.z;
+  const BoxGeom& g = P.g;
+  const dev::ErrorWord err{P.err};
+  const int64_t p_begin = P.ptiles * split / P.splits;
+  const int64_t p_end = P.ptiles * (split + 1) / P.splits;
+  const int mt_first = chunk * P.mt_per_cta;
+  const int mt_count = min(P.mt_per_cta, P.mt_total - mt_first);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < 2; ++s) {
+      dev::mbar_init(&b_full[s], 1);
+      dev::mbar_init(&b_empty[s], 1);
+    }
+    for (int s = 0; s < P.a_stages; ++s) {
+      dev::mbar_init(&a_full[s], 1);
+      dev::mbar_init(&a_empty[s], 1);
+    }
+    dev::mbar_init(acc_bar, 1);
+    *progress = 0;
+    dev::fence_barrier_init();
+  }
+  if (warp == 0) dev::tmem_alloc(tmem_slot, P.tmem_cols);
+  dev::tc_fence_before();
+  __syncthreads();
+  dev::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // ---------------- TMA producer ----------------
+    dev::prefetch_tensormap(&act_map);
+    dev::prefetch_tensormap(&grad_map);
+    int a_stage = 0, b_slot = 0;
+    uint32_t a_phase = 0, b_phase = 0;
+    bool ok = true;
+    BoxInfo boxes[kMaxBoxes];
+    for (int64_t pt = p_begin; pt < p_end && ok; ++pt) {
+      for (int j = 0; j < g.nb; ++j) decode_box(g, pt * g.nb + j, grp, boxes[j]);
+      // Output-gradient tile (B operand), shared by every tap tile of this CTA.
+      if (!dev::mbar_wait(&b_empty[b_slot], b_phase ^ 1u, err, kSiteWProducer, P.timeout_ns)) {
+        ok = false;
+        break;
+      }
+      uint8_t* bs = b_base + b_slot * P.b_slot_bytes;
+      dev::mbar_arrive_expect_tx(&b_full[b_slot], P.b_tx);
+      for (int j = 0; j < g.nb; ++j) {
+        const int32_t mo = boxes[j].valid ? static_cast<int32_t>(boxes[j].out_merged) : -1;
+        for (int blk = 0; blk < P.b_blocks; ++blk) {
+          uint8_t* dst = bs + blk * (P.kc_rows * 128) + j * g.box_rows * P.b_row_bytes;
+          const int32_t c0 = blk * P.b_blk_elems;
+          const int32_t y2 = boxes[j].q[2] * g.b[2];
+          const int32_t y1 = boxes[j].q[1] * g.b[1];
+          const int32_t y0 = boxes[j].q[0] * g.b[0];
+          dev::tma_load_5d(dst, &grad_map, &b_full[b_slot], c0, y2, y1, y0, mo);
+          if constexpr (kSplit) {
+            dev::tma_load_5d(dst + P.b_part_bytes, &grad_small_map, &b_full[b_slot], c0, y2, y1,
+                             y0, mo);
+          }
+        }
+      }
+      if (++b_slot == 2) {
+        b_slot = 0;
+        b_phase ^= 1u;
+      }
+      // Activation tiles: tpm taps per M tile.
+      int t_o[kMaxOuter] = {0, 0, 0, 0, 0, 0};
+      int t[3] = {0, 0, 0};
+      int tap = mt_first * P.tpm;
+      if (tap < g.taps) set_tap(g, tap, t_o, t);
+      for (int mt = 0; mt < mt_count && ok; ++mt) {
+        if (!dev::mbar_wait(&a_empty[a_stage], a_phase ^ 1u, err, kSiteWProducer,
+                            P.timeout_ns)) {
+          ok = false;
+          break;
+        }
+        uint8_t* as = a_base + a_stage * P.a_slot_bytes;
+        dev::mbar_arrive_expect_tx(&a_full[a_stage], P.a_tx);
+        for (int jt = 0; jt < P.tpm; ++jt, ++tap) {
+          const bool real_tap = tap < g.taps;
+          for (int j = 0; j < g.nb; ++j) {
+            const int32_t mc = real_tap ? merged_input(g, boxes[j], t_o) : -1;
+            const int32_t x2 = boxes[j].ib[2] + t[2] * g.d[2];
+            const int32_t x1 = boxes[j].ib[1] + t[1] * g.d[1];
+            const int32_t x0 = boxes[j].ib[0] + t[0] * g.d[0];
+            uint8_t* dst = as + jt * P.a_tile_bytes + j * g.box_rows * P.a_row_bytes;
+            dev::tma_load_5d(dst, &act_map, &a_full[a_stage], 0, x2, x1, x0, mc);
+            if constexpr (kSplit) {
+              dev::tma_load_5d(dst + P.a_part_bytes, &act_small_map, &a_full[a_stage], 0, x2, x1,
+                               x0, mc);
+            }
+          }
+          if (real_tap) next_tap(g, t_o, t);
+        }
+        if (++a_stage == P.a_stages) {
+          a_stage = 0;
+          a_phase ^= 1u;
+        }
+      }
+    }
+    (void)ok;
+  } else if (warp == 1 && lane == 0) {
+    // ---------------- MMA issuer ----------------
+    int a_stage = 0, b_slot = 0;
+    uint32_t a_phase = 0, b_phase = 0;
+    const uint32_t k_rows = kTF32 ? 8u : 16u;
+    const uint32_t a_sbo = 8u * P.a_row_bytes;
+    const uint32_t b_sbo = 8u * P.b_row_bytes;
+    const uint32_t b_lbo = static_cast<uint32_t>(P.kc_rows) * 128u;
+    bool ok = true;
+    for (int64_t pt = p_begin; pt < p_end && ok; ++pt) {
+      if (!dev::mbar_wait(&b_full[b_slot], b_phase, err, kSiteWMma, P.timeout_ns)) break;
+      const uint32_t bs = dev::smem_u32(b_base + b_slot * P.b_slot_bytes);
+      for (int mt = 0; mt < mt_count; ++mt) {
+        if (!dev::mbar_wait(&a_full[a_stage], a_phase, err, kSiteWMma, P.timeout_ns)) {
+          ok = false;
+          break;
+        }
+        dev::tc_fence_after();
+        const uint32_t as = dev::smem_u32(a_base + a_stage * P.a_slot_bytes);
+        const uint32_t d = tmem + static_cast<uint32_t>(mt * P.n_pad);
+        for (int ks = 0; ks < P.ksteps; ++ks) {
+          const uint32_t aoff = static_cast<uint32_t>(ks) * k_rows * P.a_row_bytes;
+          const uint32_t boff = static_cast<uint32_t>(ks) * k_rows * P.b_row_bytes;
+          const uint64_t ad = dev::make_smem_desc(as + aoff, P.a_tile_bytes, a_sbo, P.a_layout);
+          const uint64_t bd = dev::make_smem_desc(bs + boff, b_lbo, b_sbo, P.b_layout);
+          const uint32_t acc = (pt != p_begin || ks != 0) ? 1u : 0u;
+          if constexpr (kSplit) {
+            const uint64_t ads =
+                dev::make_smem_desc(as + P.a_part_bytes + aoff, P.a_tile_bytes, a_sbo, P.a_layout);
+            const uint64_t bds =
+                dev::make_smem_desc(bs + P.b_part_bytes + boff, b_lbo, b_sbo, P.b_layout);
+            mma<true>(d, ads, bd, P.idesc, acc);
+            mma<true>(d, ad, bds, P.idesc, 1u);
+            mma<true>(d, ad, bd, P.idesc, 1u);
+          } else {
+            mma<kTF32>(d, ad, bd, P.idesc, acc);
+          }
+        }
+        dev::mma_commit(&a_empty[a_stage]);
+        if (++a_stage == P.a_stages) {
+          a_stage = 0;
+          a_phase ^= 1u;
+        }
+      }
+      dev::mma_commit(&b_empty[b_slot]);
+      *progress = static_cast<uint32_t>(pt - p_begin + 1);
+      if (++b_slot == 2) {
+        b_slot = 0;
+        b_phase ^= 1u;
+      }
+    }
+    dev::mma_commit(acc_bar);
+  } else if (warp >= 2) {
+    // ---------------- epilogue: TMEM -> fp32 partial ----------------
+    dev::mbar_wait_progress(acc_bar, 0, progress, err, kSiteWEpilogue, P.timeout_ns);
+    dev::tc_fence_after();
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const int jt = row / P.c_pad;
+    const int ci = row - jt * P.c_pad;
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+    const bool empty_range = p_begin >= p_end;
+    for (int mt = 0; mt < mt_count; ++mt) {
+      const int tap = (mt_first + mt) * P.tpm + jt;
+      const bool valid = tap < g.taps && ci < P.cin_real;
+      float* dst = P.partial +
+                   ((((static_cast<int64_t>(split) * g.groups + grp) * g.taps + tap) *
+                         P.cin_real +
+                     ci) *
+                    P.n_real);
+      for (int c = 0; c < P.n_pad / 16; ++c) {
+        uint32_t v[16];
+        dev::tmem_load16(lane_addr + static_cast<uint32_t>(mt * P.n_pad + c * 16), v);
+        dev::tmem_load_wait();
+        if (valid) {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int co = c * 16 + i;
+            if (co < P.n_real) dst[co] = empty_range ? 0.0f : __uint_as_float(v[i]);
+          }
+        }
+      }
+    }
+  }
+  dev::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    dev::tc_fence_after();
+    dev::tmem_dealloc(tmem, P.tmem_cols);
+  }
+}
+
+// =======================================================================================
+// Host side
+// =======================================================================================
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult status;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &status) ==
+            cudaSuccess &&
+        status == cudaDriverEntryPointSuccess) {
+      encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }
+  });
+  return encode;
+}
+
+CUtensorMapDataType map_type(int op) {
+  if (op == kOpBF16) return CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  if (op == kOpF16) return CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  return CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+}
+
+CUtensorMapSwizzle map_swizzle(int row_bytes) {
+  if (row_bytes == 32) return CU_TENSOR_MAP_SWIZZLE_32B;
+  if (row_bytes == 64) return CU_TENSOR_MAP_SWIZZLE_64B;
+  return CU_TENSOR_MAP_SWIZZLE_128B;
+}
+
+// tcgen05 shared-memory descriptor layout code for a swizzle width in bytes.
+uint32_t desc_layout(int row_bytes) {
+  if (row_bytes == 32) return 6;
+  if (row_bytes == 64) return 4;
+  return 2;
+}
+
+int element_size(int op) { return op == kOpF32 ? 4 : 2; }
+
+// Encodes a 5-D map over a packed channels-last activation tensor
+// [merged][e0][e1][e2][channels] with a box of (cblk, b2*s2, b1*s1, b0*s0, 1) and
+// element strides (1, s2, s1, s0, 1).
+int encode_act_map(CUtensorMap* map, const void* base, int op, int64_t channels,
+                   const int64_t ext[3], int64_t merged, int cblk, const int box[3],
+                   const int stride[3]) {
+  auto encode = tensor_map_encoder();
+  if (encode == nullptr) return fail(CND_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  const int64_t es = element_size(op);
+  cuuint64_t dims[5] = {static_cast<cuuint64_t>(channels), static_cast<cuuint64_t>(ext[2]),
+                        static_cast<cuuint64_t>(ext[1]), static_cast<cuuint64_t>(ext[0]),
+                        static_cast<cuuint64_t>(merged)};
+  cuuint64_t strides[4] = {static_cast<cuuint64_t>(channels * es),
+                           static_cast<cuuint64_t>(channels * ext[2] * es),
+                           static_cast<cuuint64_t>(channels * ext[2] * ext[1] * es),
+                           static_cast<cuuint64_t>(channels * ext[2] * ext[1] * ext[0] * es)};
+  cuuint32_t boxd[5] = {static_cast<cuuint32_t>(cblk),
+                        static_cast<cuuint32_t>(box[2] * stride[2]),
+                        static_cast<cuuint32_t>(box[1] * stride[1]),
+                        static_cast<cuuint32_t>(box[0] * stride[0]), 1};
+  cuuint32_t estr[5] = {1, static_cast<cuuint32_t>(stride[2]), static_cast<cuuint32_t>(stride[1]),
+                        static_cast<cuuint32_t>(stride[0]), 1};
+  const CUresult r = encode(map, map_type(op), 5, const_cast<void*>(base), dims, strides, boxd,
+                            estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                            map_swizzle(static_cast<int>(cblk * es)),
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    return fail(CND_ERR_CUDA, "cuTensorMapEncodeTiled (activations) failed with code %d",
+                static_cast<int>(r));
+  }
+  return CND_OK;
+}
+
+// 3-D map over packed weights [rows][n_pad][c_pad], box (cblk, n_pad, 1).
+int encode_weight_map(CUtensorMap* map, const void* base, int op, int64_t c_pad, int64_t n_pad,
+                      int64_t rows, int cblk) {
+  auto encode = tensor_map_encoder();
+  if (encode == nullptr) return fail(CND_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  const int64_t es = element_size(op);
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(c_pad), static_cast<cuuint64_t>(n_pad),
+                        static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(c_pad * es),
+                           static_cast<cuuint64_t>(c_pad * n_pad * es)};
+  cuuint32_t boxd[3] = {static_cast<cuuint32_t>(cblk), static_cast<cuuint32_t>(n_pad), 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = encode(map, map_type(op), 3, const_cast<void*>(base), dims, strides, boxd,
+                            estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                            map_swizzle(static_cast<int>(cblk * es)),
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    return fail(CND_ERR_CUDA, "cuTensorMapEncodeTiled (weights) failed with code %d",
+                static_cast<int>(r));
+  }
+  return CND_OK;
+}
+
+// Chooses the box shape (outer->inner) and boxes per tile for `rows` positions per tile.
+bool plan_boxes(const int out[3], const int stride[3], int rows, int* nb_out, int b_out[3]) {
+  double best = 1e30;
+  bool found = false;
+  for (int nb = 1; nb <= kMaxBoxes; nb *= 2) {
+    const int per_box = rows / nb;
+    if (per_box < 8 || per_box % 8 != 0) break;
+    for (int b2 = 1; b2 <= per_box; ++b2) {
+      if (per_box % b2 != 0 || b2 * stride[2] > 256) continue;
+      for (int b1 = 1; b1 <= per_box / b2; ++b1) {
+        if ((per_box / b2) % b1 != 0 || b1 * stride[1] > 256) continue;
+        const int b0 = per_box / b2 / b1;
+        if (b0 * stride[0] > 256) continue;
+        const int b[3] = {b0, b1, b2};
+        double padded = 1.0, real = 1.0;
+        for (int a = 0; a < 3; ++a) {
+          padded *= static_cast<double>((out[a] + b[a] - 1) / b[a]) * b[a];
+          real *= out[a];
+        }
+        // Waste first; then fewer boxes; then a longer innermost run.
+        const double score = padded / real + 0.01 * nb - 0.0001 * b2 - 0.00001 * b1;
+        if (score < best) {
+          best = score;
+          found = true;
+          *nb_out = nb;
+          b_out[0] = b0;
+          b_out[1] = b1;
+          b_out[2] = b2;
+        }
+      }
+    }
+  }
+  return found;
+}
+
+// Splits the spatial axes of a pass into outer axes and three box axes and fills the
+// BoxGeom; `rows` is the number of positions per tile.
+bool build_geom(int rank, int64_t batch, int64_t groups, const int64_t* in, const int64_t* out,
+                const int64_t* k, const int64_t* s, const int64_t* d, const int64_t* p, int rows,
+                BoxGeom* g) {
+  std::memset(g, 0, sizeof(*g));
+  if (rank < 1 || rank > kMaxFastRank) return false;
+  const int n_outer = rank > 3 ? rank - 3 : 0;
+  const int lead = 3 - (rank - n_outer);  // unit box axes prepended for ranks < 3
+  g->n_outer = n_outer;
+  const int64_t limit = (int64_t{1} << 31) - 1;
+  for (int a = 0; a < 3; ++a) {
+    const int src = a - lead + n_outer;
+    if (a < lead) {
+      g->out[a] = g->in[a] = g->k[a] = g->s[a] = g->d[a] = 1;
+      g->p[a] = 0;
+      continue;
+    }
+    if (in[src] > limit || out[src] > limit || k[src] > 4096 || s[src] > 8 || d[src] > 65536 ||
+        p[src] > 65536) {
+      return false;
+    }
+    g->out[a] = static_cast<int>(out[src]);
+    g->in[a] = static_cast<int>(in[src]);
+    g->k[a] = static_cast<int>(k[src]);
+    g->s[a] = static_cast<int>(s[src]);
+    g->d[a] = static_cast<int>(d[src]);
+    g->p[a] = static_cast<int>(p[src]);
+  }
+  int64_t in_vol = 1, out_vol = 1, taps = 1;
+  for (int a = n_outer - 1; a >= 0; --a) {
+    if (in[a] > limit || out[a] > limit || k[a] > 4096 || s[a] > limit || d[a] > 65536 ||
+        p[a] > 65536) {
+      return false;
+    }
+    g->out_o[a] = static_cast<int>(out[a]);
+    g->in_o[a] = static_cast<int>(in[a]);
+    g->k_o[a] = static_cast<int>(k[a]);
+    g->s_o[a] = static_cast<int>(s[a]);
+    g->d_o[a] = static_cast<int>(d[a]);
+    g->p_o[a] = static_cast<int>(p[a]);
+    g->in_o_stride[a] = in_vol;
+    g->out_o_stride[a] = out_vol;
+    in_vol *= in[a];
+    out_vol *= out[a];
+  }
+  for (int a = 0; a < rank; ++a) taps *= k[a];
+  if (taps > limit) return false;
+  g->taps = static_cast<int>(taps);
+  g->batch = batch;
+  g->groups = groups;
+  g->in_merged_per_ng = in_vol;
+  g->out_outer_vol = out_vol;
+  g->outer_count = batch * out_vol;
+  g->out_box_vol = static_cast<int64_t>(g->out[0]) * g->out[1] * g->out[2];
+  // Merged TMA coordinates are int32.
+  if (batch * groups * in_vol > limit || batch * groups * out_vol > limit) return false;
+  int nb = 0, b[3] = {0, 0, 0};
+  if (!plan_boxes(g->out, g->s, rows, &nb, b)) return false;
+  g->nb = nb;
+  g->box_rows = rows / nb;
+  for (int a = 0; a < 3; ++a) {
+    g->b[a] = b[a];
+    g->nbox[a] = (g->out[a] + b[a] - 1) / b[a];
+  }
+  g->boxes_per_group =
+      g->outer_count * static_cast<int64_t>(g->nbox[0]) * g->nbox[1] * g->nbox[2];
+  return true;
+}
+
+uint32_t make_idesc(int op, int m, int n, bool a_mn, bool b_mn) {
+  uint32_t desc = 0;
+  desc |= 1u << 4;  // accumulator format F32
+  const uint32_t fmt = op == kOpBF16 ? 1u : (op == kOpF16 ? 0u : 2u);
+  desc |= fmt << 7;
+  desc |= fmt << 10;
+  if (a_mn) desc |= 1u << 15;
+  if (b_mn) desc |= 1u << 16;
+  desc |= static_cast<uint32_t>(n >> 3) << 17;
+  desc |= static_cast<uint32_t>(m >> 4) << 24;
+  return desc;
+}
+
+uint32_t tmem_columns(int needed) {
+  uint32_t cols = 32;
+  while (cols < static_cast<uint32_t>(needed)) cols <<= 1;
+  return cols;
+}
+
+uint32_t round_up(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
+
+int sm_count() {
+  static int count = 0;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, dev);
+    if (count <= 0) count = 148;
+  });
+  return count;
+}
+
+// Bytes of one channel-block row for c_pad channels (the swizzle width), or 0 when the
+// padded channel count is not one of the supported shapes.
+int channel_block_bytes(int op, int c_pad) {
+  const int row = c_pad * element_size(op);
+  if (row == 32 || row == 64 || row == 128) return row;
+  if (row > 128 && row % 128 == 0) return 128;
+  return 0;
+}
+
+}  // namespace
+
+bool conv_pass_supported(const ConvPass& pass) {
+  if (pass.rank < 1 || pass.rank > kMaxFastRank) return false;
+  if (pass.n_pad < 16 || pass.n_pad > 256 || pass.n_pad % 16 != 0) return false;
+  if (channel_block_bytes(pass.op, pass.c_pad) == 0) return false;
+  BoxGeom g;
+  return build_geom(pass.rank, pass.batch, pass.groups, pass.in, pass.out, pass.k, pass.s,
+                    pass.d, pass.p, kTileRows, &g);
+}
+
+int launch_conv_pass(const ConvPass& pass, cudaStream_t stream, uint64_t timeout_ns,
+                     int debug_stall) {
+  ConvKernelParams P;
+  std::memset(&P, 0, sizeof(P));
+  if (!build_geom(pass.rank, pass.batch, pass.groups, pass.in, pass.out, pass.k, pass.s, pass.d,
+                  pass.p, kTileRows, &P.g)) {
+    return fail(CND_ERR_UNSUPPORTED, "geometry outside the tcgen05 path");
+  }
+  const int es = element_size(pass.op);
+  const int row_bytes = channel_block_bytes(pass.op, pass.c_pad);
+  if (row_bytes == 0) return fail(CND_ERR_UNSUPPORTED, "channel count outside the tcgen05 path");
+  const bool tf32 = pass.op == kOpF32;
+  const bool split = tf32 && pass.split3;
+  P.n_real = pass.n_real;
+  P.n_pad = pass.n_pad;
+  P.row_bytes = row_bytes;
+  P.cblk_elems = row_bytes / es;
+  P.cblocks = pass.c_pad / P.cblk_elems;
+  P.ksteps = row_bytes / 32;
+  P.layout = desc_layout(row_bytes);
+  P.debug_stall = debug_stall;
+  P.a_box_bytes = static_cast<uint32_t>(P.g.box_rows * row_bytes);
+  P.a_bytes = P.a_box_bytes * P.g.nb;
+  P.b_bytes = static_cast<uint32_t>(pass.n_pad * row_bytes);
+  const int parts = split ? 2 : 1;
+  P.a_small_off = round_up(P.a_bytes, 1024);
+  P.b_off = round_up(P.a_bytes, 1024) * parts;
+  P.b_small_off = P.b_off + round_up(P.b_bytes, 1024);
+  P.stage_bytes = P.b_off + round_up(P.b_bytes, 1024) * parts;
+  P.tx_bytes = (P.a_bytes + P.b_bytes) * parts;
+  // Two CTAs per SM when the pipeline is at least four stages deep.
+  const uint32_t budget = 100 * 1024;
+  int stages = static_cast<int>(budget / P.stage_bytes);
+  if (stages > 8) stages = 8;
+  if (stages < 4) {
+    stages = static_cast<int>((200 * 1024) / P.stage_bytes);
+    if (stages > 4) stages = 4;
+  }
+  if (stages < 2) return fail(CND_ERR_UNSUPPORTED, "tile does not fit in shared memory");
+  P.stages = stages;
+  P.idesc = make_idesc(pass.op, 128, pass.n_pad, false, false);
+  P.tmem_cols = tmem_columns(pass.n_pad);
+  P.out = pass.dst;
+  P.bias = pass.bias;
+  P.out_dtype = pass.out_dtype;
+  P.out_channels_total = static_cast<int64_t>(pass.groups) * pass.n_real;
+  P.out_volume = 1;
+  for (int a = 0; a < pass.rank; ++a) P.out_volume *= pass.out[a];
+  P.err = device_error_word();
+  P.timeout_ns = timeout_ns;
+
+  const int64_t mtiles = (P.g.boxes_per_group + P.g.nb - 1) / P.g.nb;
+  if (mtiles > 0x7FFFFFFF || pass.groups > 65535) {
+    return fail(CND_ERR_UNSUPPORTED, "grid too large for the tcgen05 path");
+  }
+  if (mtiles == 0) return CND_OK;
+
+  // Packed activation extents: the three box axes and the merged outer dimension.
+  int64_t ext[3];
+  const int n_outer = P.g.n_outer;
+  for (int a = 0; a < 3; ++a) ext[a] = P.g.in[a];
+  const int64_t merged = pass.batch * pass.groups * P.g.in_merged_per_ng;
+  const int box[3] = {P.g.b[0], P.g.b[1], P.g.b[2]};
+  const int strd[3] = {P.g.s[0], P.g.s[1], P.g.s[2]};
+  (void)n_outer;
+  alignas(64) CUtensorMap maps[4];
+  std::memset(maps, 0, sizeof(maps));
+  int rc = encode_act_map(&maps[0], pass.act, pass.op, pass.c_pad, ext, merged, P.cblk_elems, box,
+                          strd);
+  if (rc != CND_OK) return rc;
+  rc = encode_weight_map(&maps[2], pass.wt, pass.op, pass.c_pad, pass.n_pad,
+                         pass.groups * P.g.taps, P.cblk_elems);
+  if (rc != CND_OK) return rc;
+  if (split) {
+    rc = encode_act_map(&maps[1], pass.act_small, pass.op, pass.c_pad, ext, merged, P.cblk_elems,
+                        box, strd);
+    if (rc != CND_OK) return rc;
+    rc = encode_weight_map(&maps[3], pass.wt_small, pass.op, pass.c_pad, pass.n_pad,
+                           pass.groups * P.g.taps, P.cblk_elems);
+    if (rc != CND_OK) return rc;
+  } else {
+    maps[1] = maps[0];
+    maps[3] = maps[2];
+  }
+  const size_t smem = static_cast<size_t>(P.stages) * P.stage_bytes + 1024 +
+                      (2 * P.stages + 1) * 8 + 16 + sizeof(BoxInfo) * kMaxBoxes + 64;
+  const dim3 grid(static_cast<unsigned>(mtiles), static_cast<unsigned>(pass.groups));
+  cudaError_t e;
+  if (split) {
+    auto kernel = conv_pass_kernel<true, true>;
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         static_cast<int>(smem));
+    kernel<<<grid, kThreads, smem, stream>>>(maps[0], maps[1], maps[2], maps[3], P);
+  } else if (tf32) {
+    auto kernel = conv_pass_kernel<true, false>;
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         static_cast<int>(smem));
+    kernel<<<grid, kThreads, smem, stream>>>(maps[0], maps[1], maps[2], maps[3], P);
+  } else {
+    auto kernel = conv_pass_kernel<false, false>;
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         static_cast<int>(smem));
+    kernel<<<grid, kThreads, smem, stream>>>(maps[0], maps[1], maps[2], maps[3], P);
+  }
+  e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    return fail(CND_ERR_CUDA, "conv_pass_kernel launch failed: %s", cudaGetErrorString(e));
+  }
+  count_launch();
+  return CND_OK;
+}
+
+namespace {
+
+struct WgradPlan {
+  WgradKernelParams P;
+  size_t smem;
+  int chunks;
+};
+
+bool plan_wgrad(const WgradPass& pass, int splits_hint, WgradPlan* plan) {
+  WgradKernelParams& P = plan->P;
+  std::memset(&P, 0, sizeof(P));
+  const int es = element_size(pass.op);
+  const bool tf32 = pass.op == kOpF32;
+  const bool split = tf32 && pass.split3;
+  const int parts = split ? 2 : 1;
+  const int a_row = pass.c_pad * es;
+  if (!(a_row == 32 || a_row == 64 || a_row == 128)) return false;
+  if (pass.n_pad < 16 || pass.n_pad > 256 || pass.n_pad % 16 != 0) return false;
+  const int b_row_full = pass.n_pad * es;
+  int b_row = 0;
+  if (b_row_full == 32 || b_row_full == 64 || b_row_full == 128) {
+    b_row = b_row_full;
+  } else if (b_row_full % 128 == 0) {
+    b_row = 128;
+  } else {
+    return false;
+  }
+  P.c_pad = pass.c_pad;
+  P.cin_real = pass.cin_real;
+  P.n_pad = pass.n_pad;
+  P.n_real = pass.n_real;
+  P.tpm = 128 / pass.c_pad;
+  P.a_row_bytes = a_row;
+  P.a_layout = static_cast<int>(desc_layout(a_row));
+  P.b_row_bytes = b_row;
+  P.b_layout = static_cast<int>(desc_layout(b_row));
+  P.b_blocks = b_row_full / b_row;
+  P.b_blk_elems = b_row / es;
+  // Position rows per K chunk: 128, or 64 when the 128-row slots do not fit twice.
+  int kc = 128;
+  for (;;) {
+    const uint32_t a_tile = static_cast<uint32_t>(kc * a_row);
+    const uint32_t a_slot = round_up(a_tile * P.tpm, 1024) * parts;
+    const uint32_t b_slot = round_up(static_cast<uint32_t>(kc * b_row_full), 1024) * parts;
+    if (2 * a_slot + 2 * b_slot <= 200 * 1024 || kc == 64) break;
+    kc = 64;
+  }
+  P.kc_rows = kc;
+  P.ksteps = kc / (tf32 ? 8 : 16);
+  if (!build_geom(pass.rank, pass.batch, pass.groups, pass.in, pass.out, pass.k, pass.s, pass.d,
+                  pass.p, kc, &P.g)) {
+    return false;
+  }
+  P.a_tile_bytes = static_cast<uint32_t>(kc * a_row);
+  P.a_part_bytes = round_up(P.a_tile_bytes * P.tpm, 1024);
+  P.a_slot_bytes = P.a_part_bytes * parts;
+  P.b_part_bytes = round_up(static_cast<uint32_t>(kc * b_row_full), 1024);
+  P.b_slot_bytes = P.b_part_bytes * parts;
+  P.a_tx = P.a_tile_bytes * P.tpm * parts;
+  P.b_tx = static_cast<uint32_t>(kc * b_row_full) * parts;
+  int stages = static_cast<int>((208 * 1024 - 2 * P.b_slot_bytes) / P.a_slot_bytes);
+  if (stages > 6) stages = 6;
+  if (stages < 2) return false;
+  P.a_stages = stages;
+  P.a_base_off = 2 * P.b_slot_bytes;
+  P.bar_off = P.a_base_off + stages * P.a_slot_bytes;
+  P.mt_total = (P.g.taps + P.tpm - 1) / P.tpm;
+  P.mt_per_cta = 512 / pass.n_pad;
+  if (P.mt_per_cta > P.mt_total) P.mt_per_cta = P.mt_total;
+  plan->chunks = (P.mt_total + P.mt_per_cta - 1) / P.mt_per_cta;
+  P.tmem_cols = tmem_columns(P.mt_per_cta * pass.n_pad);
+  P.idesc = make_idesc(pass.op, 128, pass.n_pad, true, true);
+  P.ptiles = (P.g.boxes_per_group + P.g.nb - 1) / P.g.nb;
+  int splits = splits_hint;
+  if (splits <= 0) {
+    const int64_t ctas_per_split = static_cast<int64_t>(plan->chunks) * pass.groups;
+    int64_t s = (sm_count() + ctas_per_split - 1) / ctas_per_split;
+    if (s > P.ptiles) s = P.ptiles;
+    if (s < 1) s = 1;
+    splits = static_cast<int>(s);
+  }
+  P.splits = splits;
+  plan->smem = P.bar_off + (4 + 2 * stages + 1) * 8 + 16 + 1024;
+  return true;
+}
+
+}  // namespace
+
+bool wgrad_pass_supported(const WgradPass& pass) {
+  WgradPlan plan;
+  return pass.rank >= 1 && pass.rank <= kMaxFastRank && plan_wgrad(pass, 1, &plan);
+}
+
+int plan_wgrad_splits(const WgradPass& pass, int sm) {
+  (void)sm;
+  WgradPlan plan;
+  if (!plan_wgrad(pass, 0, &plan)) return 0;
+  return plan.P.splits;
+}
+
+int launch_wgrad_pass(const WgradPass& pass, cudaStream_t stream, uint64_t timeout_ns) {
+  WgradPlan plan;
+  if (!plan_wgrad(pass, pass.splits, &plan)) {
+    return fail(CND_ERR_UNSUPPORTED, "weight-gradient geometry outside the tcgen05 path");
+  }
+  WgradKernelParams& P = plan.P;
+  P.partial = pass.partial;
+  P.err = device_error_word();
+  P.timeout_ns = timeout_ns;
+  if (plan.chunks > 65535 || pass.groups > 65535) {
+    return fail(CND_ERR_UNSUPPORTED, "grid too large for the tcgen05 path");
+  }
+  int64_t ext_in[3], ext_out[3];
+  for (int a = 0; a < 3; ++a) {
+    ext_in[a] = P.g.in[a];
+    ext_out[a] = P.g.out[a];
+  }
+  const int64_t merged_in = pass.batch * pass.groups * P.g.in_merged_per_ng;
+  const int64_t merged_out = pass.batch * pass.groups * P.g.out_outer_vol;
+  const int box[3] = {P.g.b[0], P.g.b[1], P.g.b[2]};
+  const int strd[3] = {P.g.s[0], P.g.s[1], P.g.s[2]};
+  const int ones[3] = {1, 1, 1};
+  const bool split = pass.op == kOpF32 && pass.split3;
+  alignas(64) CUtensorMap maps[4];
+  std::memset(maps, 0, sizeof(maps));
+  int rc = encode_act_map(&maps[0], pass.act, pass.op, pass.c_pad, ext_in, merged_in, pass.c_pad,
+                          box, strd);
+  if (rc != CND_OK) return rc;
+  rc = encode_act_map(&maps[2], pass.grad, pass.op, pass.n_pad, ext_out, merged_out,
+                      P.b_blk_elems, box, ones);
+  if (rc != CND_OK) return rc;
+  if (split) {
+    rc = encode_act_map(&maps[1], pass.act_small, pass.op, pass.c_pad, ext_in, merged_in,
+                        pass.c_pad, box, strd);
+    if (rc != CND_OK) return rc;
+    rc = encode_act_map(&maps[3], pass.grad_small, pass.op, pass.n_pad, ext_out, merged_out,
+                        P.b_blk_elems, box, ones);
+    if (rc != CND_OK) return rc;
+  } else {
+    maps[1] = maps[0];
+    maps[3] = maps[2];
+  }
+  const dim3 grid(static_cast<unsigned>(P.splits), static_cast<unsigned>(plan.chunks),
+                  static_cast<unsigned>(pass.groups));
+  const bool tf32 = pass.op == kOpF32;
+  if (split) {
+    auto kernel = wgrad_kernel<true, true>;
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         static_cast<int>(plan.smem));
+    kernel<<<grid, kThreads, plan.smem, stream>>>(maps[0], maps[1], maps[2], maps[3], P);
+  } else if (tf32) {
+    auto kernel = wgrad_kernel<true, false>;
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         static_cast<int>(plan.smem));
+    kernel<<<grid, kThreads, plan.smem, stream>>>(maps[0], maps[1], maps[2], maps[3], P);
+  } else {
+    auto kernel = wgrad_kernel<false, false>;
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         static_cast<int>(plan.smem));
+    kernel<<<grid, kThreads, plan.smem, stream>>>(maps[0], maps[1], maps[2], maps[3], P);
+  }
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    return fail(CND_ERR_CUDA, "wgrad_kernel launch failed: %s", cudaGetErrorString(e));
+  }
+  count_launch();
+  return CND_OK;
+}
+
+}  // namespace cnd
