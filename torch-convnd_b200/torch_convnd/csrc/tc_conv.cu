@@ -208,7 +208,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     *progress = 0;
     dev::fence_barrier_init();
   }
-  if (warp == 0) dev::tmem_alloc(tmem_slot, P.tmem_cols);
+  if (warp == 0) {
+    __syncwarp();
+    dev::tmem_alloc(tmem_slot, P.tmem_cols);
+  }
   if (threadIdx.x >= 64 && threadIdx.x < 64 + g.nb) {
     const int j = threadIdx.x - 64;
     decode_box(g, tile * g.nb + j, grp, boxes[j]);
@@ -330,6 +333,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
     for (int c = 0; c < P.n_pad / 16; ++c) {
       uint32_t v[16];
+      __syncwarp();
       dev::tmem_load16(lane_addr + static_cast<uint32_t>(c * 16), v);
       dev::tmem_load_wait();
       if (valid) {
@@ -405,7 +409,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     *progress = 0;
     dev::fence_barrier_init();
   }
-  if (warp == 0) dev::tmem_alloc(tmem_slot, P.tmem_cols);
+  if (warp == 0) {
+    __syncwarp();
+    dev::tmem_alloc(tmem_slot, P.tmem_cols);
+  }
   dev::tc_fence_before();
   __syncthreads();
   dev::tc_fence_after();
@@ -555,6 +562,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     P.n_real);
       for (int c = 0; c < P.n_pad / 16; ++c) {
         uint32_t v[16];
+        __syncwarp();
         dev::tmem_load16(lane_addr + static_cast<uint32_t>(mt * P.n_pad + c * 16), v);
         dev::tmem_load_wait();
         if (valid) {
