@@ -141,7 +141,7 @@ CND_API int cnd_fast_path_mask(const cnd_problem* problem);
  * message. Synchronises `stream`. */
 CND_API int cnd_device_status(void* stream);
 
-/* Number of kernels the library launched on this thread since the last reset. */
+/* Number of kernels the library launched (all threads) since the last reset. */
 CND_API int64_t cnd_launch_count(int32_t reset);
 
 /* Process-wide default for how float32 problems use the tensor cores (cnd_fp32_mode);

@@ -98,7 +98,7 @@ def set_fp32_precision(mode: str) -> str:
 
 
 def launch_count(reset: bool = False) -> int:
-    """Kernels the library launched on this thread (since the last reset)."""
+    """Kernels the library launched, from any thread, since the last reset."""
     return int(core().cnd_launch_count(1 if reset else 0))
 
 

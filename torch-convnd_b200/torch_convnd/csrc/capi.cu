@@ -10,6 +10,7 @@
 // runs on the generic CUDA-core kernels. There is no CPU path.
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
@@ -26,7 +27,7 @@ __device__ unsigned int g_error_word;
 
 namespace {
 
-thread_local int64_t g_launches = 0;
+std::atomic<int64_t> g_launches{0};
 
 uint64_t wait_timeout_ns() {
   static uint64_t value = 0;
@@ -44,7 +45,7 @@ uint64_t wait_timeout_ns() {
 
 }  // namespace
 
-void count_launch(int n) { g_launches += n; }
+void count_launch(int n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
 
 unsigned int* device_error_word() {
   static std::mutex mutex;
@@ -592,9 +593,7 @@ int cnd_collect_kernel_timings(int32_t* kinds, float* milliseconds, int32_t capa
 }
 
 int64_t cnd_launch_count(int32_t reset) {
-  const int64_t value = cnd::g_launches;
-  if (reset) cnd::g_launches = 0;
-  return value;
+  return reset ? cnd::g_launches.exchange(0) : cnd::g_launches.load();
 }
 
 int cnd_debug_stall_test(int32_t timeout_ms, void* stream_handle) {
