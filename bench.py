@@ -330,8 +330,8 @@ def run_b200(args):
     torch_convnd.device_status()
     barrier()
     props = torch.cuda.get_device_properties(device)
-    bus = getattr(props, "pci_bus_id", None)
-    sampler = ClockSampler(str(bus) if bus else str(local))
+    uuid = getattr(props, "uuid", None)
+    sampler = ClockSampler(f"GPU-{uuid}" if uuid is not None else str(local))
     sampler.start()
     time.sleep(0.3)
     torch_convnd.launch_count(reset=True)

@@ -254,16 +254,20 @@ def test_fp32_precision_modes():
     x = torch.randn(1, 8, 4, 4, 4, 4, 4, 4, generator=generator)
     w = torch.randn(16, 8, 3, 3, 3, 3, 3, 3, generator=generator) * (1 / 5832**0.5)
     expected = oracle.forward(x, w, None, (1,) * 6, (1,) * 6, (1,) * 6, 1)
-    errors = {}
+    errors, rel = {}, {}
     try:
         for mode in ("3xtf32", "tf32", "ieee"):
             torch_convnd.set_fp32_precision(mode)
-            y = conv_nd(x.cuda(), w.cuda(), padding=1)
-            errors[mode] = float((y.double().cpu() - expected).abs().max())
+            y = conv_nd(x.cuda(), w.cuda(), padding=1).double().cpu()
+            errors[mode] = float((y - expected).abs().max())
+            rel[mode] = float((y - expected).norm() / expected.norm())
     finally:
         torch_convnd.set_fp32_precision("3xtf32")
-    assert errors["3xtf32"] < 1e-5 and errors["ieee"] < 1e-5
-    assert errors["tf32"] < 5e-3
+    # BASELINE's float32 bar is rtol 1e-3 / atol 1e-4 against float64; 3xTF32 lands two
+    # orders of magnitude inside it, one TF32 product per term does not.
+    assert rel["3xtf32"] < 2e-5 and errors["3xtf32"] < 1e-3
+    assert rel["ieee"] < 1e-6
+    assert 1e-5 < rel["tf32"] < 2e-3
 
 
 def test_native_kernels_are_launched():

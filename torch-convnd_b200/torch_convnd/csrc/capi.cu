@@ -145,9 +145,14 @@ struct Plan {
   bool fast_fwd = false, fast_dgrad = false, fast_wgrad = false;
   ConvPass fwd{}, dgrad{};
   WgradPass wgrad{};
+  // weight-gradient operands: 16-bit problems reuse x_cl / dy_cl; float32 problems pack
+  // x and dy again as 3 (3xtf32 mode) or 2 (tf32 mode) bfloat16 terms.
+  int wg_op = 0, wg_parts = 1, wg_mode = 0;
+  int64_t wg_x_pad = 0, wg_dy_pad = 0;
   // workspace
   Region x_cl, x_cl_small, w_fwd, w_fwd_small, dy_cl, dy_cl_small, w_dg, w_dg_small, partial,
       bias_partial;
+  Region wg_x[3], wg_dy[3];
   size_t total = 0;
 };
 
@@ -178,8 +183,8 @@ void make_plan(const cnd_problem& p, bool forward, const int32_t* mask, Plan* pl
   plan->cin_g = p.channels / p.groups;
   plan->cout_g = p.output_channels / p.groups;
   const bool low = p.dtype == CND_BF16 || p.dtype == CND_F16;
-  const bool f32 = p.dtype == CND_F32 && p.fp32_mode != CND_FP32_SIMT;
-  plan->tensor_cores = (low || f32) && p.rank <= kMaxFastRank && p.batch > 0;
+  const bool f32_tensor = p.dtype == CND_F32 && p.fp32_mode != CND_FP32_SIMT;
+  plan->tensor_cores = (low || f32_tensor) && p.rank <= kMaxFastRank && p.batch > 0;
   if (!plan->tensor_cores) return;
   plan->op = operand_type(p.dtype);
   plan->split3 = (p.dtype == CND_F32 && p.fp32_mode == CND_FP32_3XTF32) ? 1 : 0;
@@ -243,33 +248,39 @@ void make_plan(const cnd_problem& p, bool forward, const int32_t* mask, Plan* pl
     dg.out_dtype = p.dtype;
     plan->fast_dgrad = !strided && !wide_pad && plan->cin_g <= 256 && conv_pass_supported(dg);
   }
+  const bool f32 = p.dtype == CND_F32;
+  plan->wg_op = f32 ? kOpBF16 : plan->op;
+  plan->wg_parts = f32 ? (plan->split3 ? 3 : 2) : 1;
+  plan->wg_mode = f32 ? (plan->split3 ? 3 : 4) : 0;
+  plan->wg_x_pad = f32 ? pad_channels(kOpBF16, plan->cin_g, 1) : plan->x_pad;
+  plan->wg_dy_pad = f32 ? pad_channels(kOpBF16, plan->cout_g, 16) : plan->dy_pad;
   if (mask[1]) {
     WgradPass& wg = plan->wgrad;
     wg.rank = p.rank;
     wg.batch = p.batch;
     wg.groups = p.groups;
     fill_spatial(p, wg.in, wg.out, wg.k, wg.s, wg.d, wg.p);
-    wg.c_pad = static_cast<int>(plan->x_pad);
+    wg.c_pad = static_cast<int>(plan->wg_x_pad);
     wg.cin_real = static_cast<int>(plan->cin_g);
-    wg.n_pad = static_cast<int>(plan->dy_pad);
+    wg.n_pad = static_cast<int>(plan->wg_dy_pad);
     wg.n_real = static_cast<int>(plan->cout_g);
-    wg.op = plan->op;
-    wg.split3 = plan->split3;
+    wg.op = plan->wg_op;
+    wg.parts = plan->wg_parts;
     plan->fast_wgrad = plan->cout_g <= 256 && wgrad_pass_supported(wg);
     if (plan->fast_wgrad) wg.splits = plan_wgrad_splits(wg, 0);
     if (wg.splits <= 0) plan->fast_wgrad = false;
   }
-  const bool need_dy = plan->fast_dgrad || plan->fast_wgrad;
+  const bool need_dy = plan->fast_dgrad || (plan->fast_wgrad && !f32);
   if (need_dy) {
     const size_t bytes =
         static_cast<size_t>(p.batch * p.groups * p.output_volume) * plan->dy_pad * es;
     plan->dy_cl = take(&cursor, bytes);
     if (plan->split3) plan->dy_cl_small = take(&cursor, bytes);
-    if (mask[2]) {
-      const size_t blocks = static_cast<size_t>(pack_blocks(p.output_volume));
-      plan->bias_partial = take(&cursor, static_cast<size_t>(p.batch * p.groups) * blocks *
-                                             plan->cout_g * sizeof(float));
-    }
+  }
+  if ((plan->fast_dgrad || plan->fast_wgrad) && mask[2]) {
+    const size_t blocks = static_cast<size_t>(pack_blocks(p.output_volume));
+    plan->bias_partial = take(&cursor, static_cast<size_t>(p.batch * p.groups) * blocks *
+                                           plan->cout_g * sizeof(float));
   }
   if (plan->fast_dgrad) {
     const size_t bytes =
@@ -278,9 +289,15 @@ void make_plan(const cnd_problem& p, bool forward, const int32_t* mask, Plan* pl
     if (plan->split3) plan->w_dg_small = take(&cursor, bytes);
   }
   if (plan->fast_wgrad) {
-    const size_t act = static_cast<size_t>(p.batch * p.groups * p.input_volume) * plan->x_pad * es;
-    plan->x_cl = take(&cursor, act);
-    if (plan->split3) plan->x_cl_small = take(&cursor, act);
+    const size_t wes = f32 ? 2 : es;
+    const size_t act =
+        static_cast<size_t>(p.batch * p.groups * p.input_volume) * plan->wg_x_pad * wes;
+    for (int part = 0; part < plan->wg_parts; ++part) plan->wg_x[part] = take(&cursor, act);
+    if (f32) {
+      const size_t grad =
+          static_cast<size_t>(p.batch * p.groups * p.output_volume) * plan->wg_dy_pad * wes;
+      for (int part = 0; part < plan->wg_parts; ++part) plan->wg_dy[part] = take(&cursor, grad);
+    }
     plan->partial = take(&cursor, static_cast<size_t>(plan->wgrad.splits) * p.groups * taps *
                                       plan->cin_g * plan->cout_g * sizeof(float));
   }
@@ -329,7 +346,8 @@ int cnd_forward(const cnd_problem* problem, const void* x, const void* w, const 
                 void* y, void* workspace, size_t workspace_bytes, void* stream_handle) {
   using namespace cnd;
   clear_error();
-  if (problem == nullptr || x == nullptr || w == nullptr || y == nullptr) {
+  if (problem == nullptr || w == nullptr ||
+      (problem->batch > 0 && (x == nullptr || y == nullptr))) {
     return fail(CND_ERR_INVALID, "cnd_forward: null argument");
   }
   const cnd_problem& p = *problem;
@@ -398,12 +416,14 @@ int cnd_backward(const cnd_problem* problem, const void* dy, const void* x, cons
                  size_t workspace_bytes, void* stream_handle) {
   using namespace cnd;
   clear_error();
-  if (problem == nullptr || output_mask == nullptr || dy == nullptr || x == nullptr ||
-      w == nullptr) {
+  if (problem == nullptr || output_mask == nullptr || w == nullptr) {
     return fail(CND_ERR_INVALID, "cnd_backward: null argument");
   }
-  if ((output_mask[0] && dx == nullptr) || (output_mask[1] && dw == nullptr) ||
-      (output_mask[2] && db == nullptr)) {
+  if (problem->batch > 0 && (dy == nullptr || x == nullptr)) {
+    return fail(CND_ERR_INVALID, "cnd_backward: null argument");
+  }
+  if ((output_mask[0] && dx == nullptr && problem->batch > 0) ||
+      (output_mask[1] && dw == nullptr) || (output_mask[2] && db == nullptr)) {
     return fail(CND_ERR_INVALID, "cnd_backward: missing gradient buffer");
   }
   const cnd_problem& p = *problem;
@@ -428,9 +448,11 @@ int cnd_backward(const cnd_problem* problem, const void* dy, const void* x, cons
                 workspace_bytes, plan.total);
   }
   int rc = CND_OK;
-  const bool packed_dy = plan.fast_dgrad || plan.fast_wgrad;
+  const bool f32 = p.dtype == CND_F32;
   const int blocks = static_cast<int>(pack_blocks(p.output_volume));
-  if (packed_dy) {
+  float* bias_partial = static_cast<float*>(at(workspace, plan.bias_partial));
+  bool bias_from_pack = false;
+  if (plan.dy_cl.bytes > 0) {
     PackActArgs pa{};
     pa.src = dy;
     pa.dst = at(workspace, plan.dy_cl);
@@ -442,7 +464,8 @@ int cnd_backward(const cnd_problem* problem, const void* dy, const void* x, cons
     pa.c_pad = static_cast<int>(plan.dy_pad);
     pa.dtype = p.dtype;
     pa.mode = plan.pack_mode;
-    pa.chan_partial = output_mask[2] ? static_cast<float*>(at(workspace, plan.bias_partial)) : nullptr;
+    pa.chan_partial = output_mask[2] ? bias_partial : nullptr;
+    bias_from_pack = output_mask[2] != 0;
     TimedPass timed(4, stream);
     rc = pack_activations(pa, stream);
     if (rc != CND_OK) return rc;
@@ -450,27 +473,49 @@ int cnd_backward(const cnd_problem* problem, const void* dy, const void* x, cons
   // ---- weight gradient ----
   if (output_mask[1]) {
     if (plan.fast_wgrad) {
-      PackActArgs pa{};
-      pa.src = x;
-      pa.dst = at(workspace, plan.x_cl);
-      pa.dst_small = at(workspace, plan.x_cl_small);
-      pa.batch = p.batch;
-      pa.groups = p.groups;
-      pa.spatial = p.input_volume;
-      pa.cg = static_cast<int>(plan.cin_g);
-      pa.c_pad = static_cast<int>(plan.x_pad);
-      pa.dtype = p.dtype;
-      pa.mode = plan.pack_mode;
+      WgradPass wg = plan.wgrad;
       {
+        PackActArgs pa{};
+        pa.src = x;
+        pa.dst = at(workspace, plan.wg_x[0]);
+        pa.dst_small = at(workspace, plan.wg_x[1]);
+        pa.dst_third = at(workspace, plan.wg_x[2]);
+        pa.batch = p.batch;
+        pa.groups = p.groups;
+        pa.spatial = p.input_volume;
+        pa.cg = static_cast<int>(plan.cin_g);
+        pa.c_pad = static_cast<int>(plan.wg_x_pad);
+        pa.dtype = p.dtype;
+        pa.mode = plan.wg_mode;
         TimedPass timed(4, stream);
         rc = pack_activations(pa, stream);
+        if (rc != CND_OK) return rc;
       }
-      if (rc != CND_OK) return rc;
-      WgradPass wg = plan.wgrad;
-      wg.act = pa.dst;
-      wg.act_small = pa.dst_small;
-      wg.grad = at(workspace, plan.dy_cl);
-      wg.grad_small = at(workspace, plan.dy_cl_small);
+      if (f32) {
+        PackActArgs pa{};
+        pa.src = dy;
+        pa.dst = at(workspace, plan.wg_dy[0]);
+        pa.dst_small = at(workspace, plan.wg_dy[1]);
+        pa.dst_third = at(workspace, plan.wg_dy[2]);
+        pa.batch = p.batch;
+        pa.groups = p.groups;
+        pa.spatial = p.output_volume;
+        pa.cg = static_cast<int>(plan.cout_g);
+        pa.c_pad = static_cast<int>(plan.wg_dy_pad);
+        pa.dtype = p.dtype;
+        pa.mode = plan.wg_mode;
+        if (output_mask[2] && !bias_from_pack) {
+          pa.chan_partial = bias_partial;
+          bias_from_pack = true;
+        }
+        TimedPass timed(4, stream);
+        rc = pack_activations(pa, stream);
+        if (rc != CND_OK) return rc;
+        for (int part = 0; part < 3; ++part) wg.grad[part] = at(workspace, plan.wg_dy[part]);
+      } else {
+        wg.grad[0] = at(workspace, plan.dy_cl);
+      }
+      for (int part = 0; part < 3; ++part) wg.act[part] = at(workspace, plan.wg_x[part]);
       wg.partial = static_cast<float*>(at(workspace, plan.partial));
       {
         TimedPass timed(3, stream);
@@ -529,8 +574,8 @@ int cnd_backward(const cnd_problem* problem, const void* dy, const void* x, cons
   }
   // ---- bias gradient ----
   if (output_mask[2]) {
-    TimedPass timed(packed_dy ? 6 : 7, stream);
-    if (packed_dy) {
+    TimedPass timed(bias_from_pack ? 6 : 7, stream);
+    if (bias_from_pack) {
       rc = reduce_bias(static_cast<const float*>(at(workspace, plan.bias_partial)), p.batch,
                        static_cast<int>(p.groups), blocks, static_cast<int>(plan.cout_g), db,
                        p.dtype, stream);

@@ -57,12 +57,36 @@ __device__ __forceinline__ __half from_float<__half>(float v) {
 
 constexpr int kPackPositions = 64;
 
+// Splits v into `parts` terms of type T whose sum reproduces v: TF32 big/small (kMode 1),
+// a TF32 rounding (kMode 2), or bf16 hi/mid/lo (kMode 3) and hi/lo (kMode 4), the
+// error-compensated operands of the split-product MMAs.
+template <typename T, int kMode>
+__device__ __forceinline__ void split_value(float v, T* out0, T* out1, T* out2, int64_t i) {
+  if constexpr (kMode == 1) {
+    const float big = tf32_round(v);
+    out0[i] = from_float<T>(big);
+    out1[i] = from_float<T>(tf32_round(v - big));
+  } else if constexpr (kMode == 2) {
+    out0[i] = from_float<T>(tf32_round(v));
+  } else if constexpr (kMode == 3 || kMode == 4) {
+    const T hi = from_float<T>(v);
+    const float r1 = v - to_float(hi);
+    const T mid = from_float<T>(r1);
+    out0[i] = hi;
+    out1[i] = mid;
+    if constexpr (kMode == 3) out2[i] = from_float<T>(r1 - to_float(mid));
+  } else {
+    out0[i] = from_float<T>(v);
+  }
+}
+
 // One block: 64 positions x all channels of one (n, g). Loads coalesced along positions,
 // stores coalesced along channels.
-template <typename T, int kMode>
-__global__ void __launch_bounds__(256) pack_act_kernel(const T* __restrict__ src,
-                                                       T* __restrict__ dst,
-                                                       T* __restrict__ dst_small, int64_t S,
+template <typename Tin, typename Tout, int kMode>
+__global__ void __launch_bounds__(256) pack_act_kernel(const Tin* __restrict__ src,
+                                                       Tout* __restrict__ dst0,
+                                                       Tout* __restrict__ dst1,
+                                                       Tout* __restrict__ dst2, int64_t S,
                                                        int Cg, int c_pad, int G,
                                                        float* __restrict__ chan_partial) {
   extern __shared__ float tile[];  // [c_pad][kPackPositions + 1]
@@ -70,7 +94,7 @@ __global__ void __launch_bounds__(256) pack_act_kernel(const T* __restrict__ src
   const int g = blockIdx.y;
   const int64_t n = blockIdx.z;
   const int width = kPackPositions + 1;
-  const T* in = src + (n * G + g) * static_cast<int64_t>(Cg) * S;
+  const Tin* in = src + (n * G + g) * static_cast<int64_t>(Cg) * S;
   for (int i = threadIdx.x; i < c_pad * kPackPositions; i += blockDim.x) {
     const int c = i / kPackPositions;
     const int s = i - c * kPackPositions;
@@ -79,22 +103,12 @@ __global__ void __launch_bounds__(256) pack_act_kernel(const T* __restrict__ src
     tile[c * width + s] = v;
   }
   __syncthreads();
-  T* out = dst + ((n * G + g) * S + s0) * c_pad;
-  T* out_small = kMode == 1 ? dst_small + ((n * G + g) * S + s0) * c_pad : nullptr;
+  const int64_t base = ((n * G + g) * S + s0) * c_pad;
   const int count = static_cast<int>(S - s0 < kPackPositions ? S - s0 : kPackPositions);
   for (int i = threadIdx.x; i < count * c_pad; i += blockDim.x) {
     const int s = i / c_pad;
     const int c = i - s * c_pad;
-    const float v = tile[c * width + s];
-    if constexpr (kMode == 1) {
-      const float big = tf32_round(v);
-      out[i] = from_float<T>(big);
-      out_small[i] = from_float<T>(tf32_round(v - big));
-    } else if constexpr (kMode == 2) {
-      out[i] = from_float<T>(tf32_round(v));
-    } else {
-      out[i] = from_float<T>(v);
-    }
+    split_value<Tout, kMode>(tile[c * width + s], dst0, dst1, dst2, base + i);
   }
   if (chan_partial != nullptr) {
     // Per-channel sum of this block's positions, in position order.
@@ -145,46 +159,52 @@ __global__ void pack_weight_kernel(const T* __restrict__ w, T* __restrict__ dst,
   }
 }
 
+// dw[(g*cout_g + co)*cin_g*taps + ci*taps + t] = sum over splits of
+// partial[s][g][t][ci][co], summed in split order. Threads walk the partial layout so the
+// split-strided reads are coalesced.
 template <typename T>
 __global__ void wgrad_reduce_kernel(const float* __restrict__ partial, int splits, int G,
                                     int taps, int cin_g, int cout_g, T* __restrict__ dw) {
-  const int64_t total = static_cast<int64_t>(G) * cout_g * cin_g * taps;
-  const int64_t per_split = total;
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    // dw index i = ((g*cout_g + co)*cin_g + ci)*taps + t
-    int64_t r = i;
-    const int t = static_cast<int>(r % taps);
-    r /= taps;
+  const int64_t total = static_cast<int64_t>(G) * taps * cin_g * cout_g;
+  for (int64_t p = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; p < total;
+       p += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    int64_t r = p;
+    const int co = static_cast<int>(r % cout_g);
+    r /= cout_g;
     const int ci = static_cast<int>(r % cin_g);
     r /= cin_g;
-    const int co = static_cast<int>(r % cout_g);
-    const int g = static_cast<int>(r / cout_g);
-    const int64_t p = ((static_cast<int64_t>(g) * taps + t) * cin_g + ci) * cout_g + co;
+    const int t = static_cast<int>(r % taps);
+    const int g = static_cast<int>(r / taps);
     float sum = 0.0f;
-    for (int s = 0; s < splits; ++s) sum += partial[s * per_split + p];
-    dw[i] = from_float<T>(sum);
+    for (int s = 0; s < splits; ++s) sum += partial[s * total + p];
+    dw[((static_cast<int64_t>(g) * cout_g + co) * cin_g + ci) * taps + t] = from_float<T>(sum);
   }
 }
 
+// db[g*cg + c] = sum over (n, block) of partial[n][g][block][c]: one CTA per channel,
+// strided per-thread sums then a fixed-shape tree, so the order never changes.
 template <typename T>
-__global__ void bias_reduce_kernel(const float* __restrict__ partial, int64_t rows, int G,
-                                   int blocks, int cg, T* __restrict__ db) {
-  // partial layout [N][G][blocks][cg]; db[g*cg + c] = sum over n, blocks (in order).
-  const int64_t total = static_cast<int64_t>(G) * cg;
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int g = static_cast<int>(i / cg);
-    const int c = static_cast<int>(i % cg);
-    float sum = 0.0f;
-    for (int64_t n = 0; n < rows; ++n) {
-      const float* p = partial + ((n * G + g) * blocks) * static_cast<int64_t>(cg) + c;
-      float part = 0.0f;
-      for (int b = 0; b < blocks; ++b) part += p[static_cast<int64_t>(b) * cg];
-      sum += part;
-    }
-    db[i] = from_float<T>(sum);
+__global__ void __launch_bounds__(256) bias_reduce_kernel(const float* __restrict__ partial,
+                                                          int64_t rows, int G, int blocks,
+                                                          int cg, T* __restrict__ db) {
+  __shared__ float scratch[256];
+  const int channel = blockIdx.x;  // over G*cg
+  const int g = channel / cg;
+  const int c = channel - g * cg;
+  const int64_t items = rows * blocks;
+  float sum = 0.0f;
+  for (int64_t i = threadIdx.x; i < items; i += blockDim.x) {
+    const int64_t n = i / blocks;
+    const int64_t b = i - n * blocks;
+    sum += partial[((n * G + g) * blocks + b) * static_cast<int64_t>(cg) + c];
   }
+  scratch[threadIdx.x] = sum;
+  __syncthreads();
+  for (int width = 128; width > 0; width >>= 1) {
+    if (threadIdx.x < width) scratch[threadIdx.x] += scratch[threadIdx.x + width];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) db[channel] = from_float<T>(scratch[0]);
 }
 
 int grid_for(int64_t total, int threads) {
@@ -194,8 +214,8 @@ int grid_for(int64_t total, int threads) {
   return static_cast<int>(blocks);
 }
 
-template <typename T>
-int pack_act_typed(const PackActArgs& a, cudaStream_t stream) {
+template <typename Tin, typename Tout, int kMode>
+int launch_pack_act(const PackActArgs& a, cudaStream_t stream) {
   const int64_t blocks = (a.spatial + kPackPositions - 1) / kPackPositions;
   if (blocks > 0x7FFFFFFF || a.groups > 65535 || a.batch > 65535) {
     return fail(CND_ERR_UNSUPPORTED, "pack_act: grid too large");
@@ -204,25 +224,13 @@ int pack_act_typed(const PackActArgs& a, cudaStream_t stream) {
                   static_cast<unsigned>(a.batch));
   const size_t smem = static_cast<size_t>(a.c_pad) * (kPackPositions + 1) * sizeof(float);
   if (smem > 200 * 1024) return fail(CND_ERR_UNSUPPORTED, "pack_act: too many channels");
-  const T* src = static_cast<const T*>(a.src);
-  T* dst = static_cast<T*>(a.dst);
-  T* dst_small = static_cast<T*>(a.dst_small);
-  if (a.mode == 1) {
-    auto k = pack_act_kernel<T, 1>;
-    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    k<<<grid, 256, smem, stream>>>(src, dst, dst_small, a.spatial, a.cg, a.c_pad,
-                                   static_cast<int>(a.groups), a.chan_partial);
-  } else if (a.mode == 2) {
-    auto k = pack_act_kernel<T, 2>;
-    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    k<<<grid, 256, smem, stream>>>(src, dst, dst_small, a.spatial, a.cg, a.c_pad,
-                                   static_cast<int>(a.groups), a.chan_partial);
-  } else {
-    auto k = pack_act_kernel<T, 0>;
-    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    k<<<grid, 256, smem, stream>>>(src, dst, dst_small, a.spatial, a.cg, a.c_pad,
-                                   static_cast<int>(a.groups), a.chan_partial);
-  }
+  auto kernel = pack_act_kernel<Tin, Tout, kMode>;
+  cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       static_cast<int>(smem));
+  kernel<<<grid, 256, smem, stream>>>(static_cast<const Tin*>(a.src), static_cast<Tout*>(a.dst),
+                                      static_cast<Tout*>(a.dst_small),
+                                      static_cast<Tout*>(a.dst_third), a.spatial, a.cg, a.c_pad,
+                                      static_cast<int>(a.groups), a.chan_partial);
   count_launch();
   return CND_OK;
 }
@@ -256,11 +264,26 @@ int pack_weight_typed(const PackWeightArgs& a, cudaStream_t stream) {
 int pack_activations(const PackActArgs& args, cudaStream_t stream) {
   int rc;
   if (args.dtype == CND_BF16) {
-    rc = pack_act_typed<__nv_bfloat16>(args, stream);
+    rc = launch_pack_act<__nv_bfloat16, __nv_bfloat16, 0>(args, stream);
   } else if (args.dtype == CND_F16) {
-    rc = pack_act_typed<__half>(args, stream);
+    rc = launch_pack_act<__half, __half, 0>(args, stream);
   } else if (args.dtype == CND_F32) {
-    rc = pack_act_typed<float>(args, stream);
+    switch (args.mode) {
+      case 1:
+        rc = launch_pack_act<float, float, 1>(args, stream);
+        break;
+      case 2:
+        rc = launch_pack_act<float, float, 2>(args, stream);
+        break;
+      case 3:
+        rc = launch_pack_act<float, __nv_bfloat16, 3>(args, stream);
+        break;
+      case 4:
+        rc = launch_pack_act<float, __nv_bfloat16, 4>(args, stream);
+        break;
+      default:
+        rc = launch_pack_act<float, float, 0>(args, stream);
+    }
   } else {
     return fail(CND_ERR_UNSUPPORTED, "pack_activations: unsupported dtype");
   }
@@ -311,16 +334,15 @@ int reduce_wgrad(const float* partial, int splits, int groups, int taps, int cin
 
 int reduce_bias(const float* partial, int64_t batch, int groups, int blocks, int cg, void* db,
                 int dtype, cudaStream_t stream) {
-  const int64_t total = static_cast<int64_t>(groups) * cg;
-  const int grid = grid_for(total, 128);
+  const int grid = groups * cg;
   if (dtype == CND_BF16) {
-    bias_reduce_kernel<<<grid, 128, 0, stream>>>(partial, batch, groups, blocks, cg,
+    bias_reduce_kernel<<<grid, 256, 0, stream>>>(partial, batch, groups, blocks, cg,
                                                  static_cast<__nv_bfloat16*>(db));
   } else if (dtype == CND_F16) {
-    bias_reduce_kernel<<<grid, 128, 0, stream>>>(partial, batch, groups, blocks, cg,
+    bias_reduce_kernel<<<grid, 256, 0, stream>>>(partial, batch, groups, blocks, cg,
                                                  static_cast<__half*>(db));
   } else {
-    bias_reduce_kernel<<<grid, 128, 0, stream>>>(partial, batch, groups, blocks, cg,
+    bias_reduce_kernel<<<grid, 256, 0, stream>>>(partial, batch, groups, blocks, cg,
                                                  static_cast<float*>(db));
   }
   count_launch();

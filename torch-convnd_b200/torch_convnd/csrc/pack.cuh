@@ -7,11 +7,13 @@
 
 namespace cnd {
 
-// mode: 0 = copy, 1 = 3xTF32 split into big + small, 2 = round to TF32.
+// mode: 0 = copy, 1 = TF32 big + small (3xTF32), 2 = round to TF32, 3 = fp32 -> bf16
+// hi + mid + lo, 4 = fp32 -> bf16 hi + lo (modes 3/4 write bfloat16 parts).
 struct PackActArgs {
   const void* src;      // channels-first [batch][groups*cg][spatial]
   void* dst;            // channels-last [batch][groups][spatial][c_pad]
-  void* dst_small;      // second part for mode 1
+  void* dst_small;      // second part (modes 1, 3, 4)
+  void* dst_third;      // third part (mode 3)
   int64_t batch, groups, spatial;
   int cg, c_pad, dtype, mode;
   float* chan_partial;  // optional [batch][groups][pack_blocks(spatial)][cg]

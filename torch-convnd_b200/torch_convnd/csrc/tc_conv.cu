@@ -364,12 +364,36 @@ __global__ void __launch_bounds__(kThreads, 1)
 // Weight-gradient kernel. Grid (split, tap chunk, group). Each CTA accumulates
 // mt_per_cta tiles of 128 (tap, channel) rows x n_pad output channels in TMEM over its
 // range of position tiles, then writes one fp32 partial.
-template <bool kTF32, bool kSplit>
+//
+// kParts > 1 runs error-compensated products for float32 problems: each operand arrives
+// as kParts bfloat16 terms (hi, mid[, lo]) and the MMA sums the cross products whose
+// combined magnitude is above fp32 rounding, smallest first: 3 products for two terms,
+// 6 for three (the latter is as accurate as fp32 accumulation).
+// Number of cross products for kParts terms per operand, and the term indices of
+// product q (smallest magnitude first).
+template <int kParts>
+__host__ __device__ constexpr int product_count() {
+  return kParts == 1 ? 1 : (kParts == 2 ? 3 : 6);
+}
+
+__host__ __device__ constexpr int product_a(int parts, int q) {
+  return parts == 2 ? (q == 0 ? 1 : 0)
+                    : (parts == 3 ? (q == 0 ? 2 : (q == 1 || q == 3) ? 1 : 0) : 0);
+}
+
+__host__ __device__ constexpr int product_b(int parts, int q) {
+  return parts == 2 ? (q == 1 ? 1 : 0)
+                    : (parts == 3 ? (q == 2 ? 2 : (q == 1 || q == 4) ? 1 : 0) : 0);
+}
+
+struct WgradMaps {
+  CUtensorMap act[3];
+  CUtensorMap grad[3];
+};
+
+template <int kParts>
 __global__ void __launch_bounds__(kThreads, 1)
-    wgrad_kernel(const __grid_constant__ CUtensorMap act_map,
-                 const __grid_constant__ CUtensorMap act_small_map,
-                 const __grid_constant__ CUtensorMap grad_map,
-                 const __grid_constant__ CUtensorMap grad_small_map,
+    wgrad_kernel(const __grid_constant__ WgradMaps maps,
                  const __grid_constant__ WgradKernelParams P) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
@@ -420,8 +444,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0 && lane == 0) {
     // ---------------- TMA producer ----------------
-    dev::prefetch_tensormap(&act_map);
-    dev::prefetch_tensormap(&grad_map);
+    for (int part = 0; part < kParts; ++part) {
+      dev::prefetch_tensormap(&maps.act[part]);
+      dev::prefetch_tensormap(&maps.grad[part]);
+    }
     int a_stage = 0, b_slot = 0;
     uint32_t a_phase = 0, b_phase = 0;
     bool ok = true;
@@ -437,16 +463,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       dev::mbar_arrive_expect_tx(&b_full[b_slot], P.b_tx);
       for (int j = 0; j < g.nb; ++j) {
         const int32_t mo = boxes[j].valid ? static_cast<int32_t>(boxes[j].out_merged) : -1;
+        const int32_t y2 = boxes[j].q[2] * g.b[2];
+        const int32_t y1 = boxes[j].q[1] * g.b[1];
+        const int32_t y0 = boxes[j].q[0] * g.b[0];
         for (int blk = 0; blk < P.b_blocks; ++blk) {
           uint8_t* dst = bs + blk * (P.kc_rows * 128) + j * g.box_rows * P.b_row_bytes;
           const int32_t c0 = blk * P.b_blk_elems;
-          const int32_t y2 = boxes[j].q[2] * g.b[2];
-          const int32_t y1 = boxes[j].q[1] * g.b[1];
-          const int32_t y0 = boxes[j].q[0] * g.b[0];
-          dev::tma_load_5d(dst, &grad_map, &b_full[b_slot], c0, y2, y1, y0, mo);
-          if constexpr (kSplit) {
-            dev::tma_load_5d(dst + P.b_part_bytes, &grad_small_map, &b_full[b_slot], c0, y2, y1,
-                             y0, mo);
+          for (int part = 0; part < kParts; ++part) {
+            dev::tma_load_5d(dst + part * P.b_part_bytes, &maps.grad[part], &b_full[b_slot], c0,
+                             y2, y1, y0, mo);
           }
         }
       }
@@ -475,10 +500,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int32_t x1 = boxes[j].ib[1] + t[1] * g.d[1];
             const int32_t x0 = boxes[j].ib[0] + t[0] * g.d[0];
             uint8_t* dst = as + jt * P.a_tile_bytes + j * g.box_rows * P.a_row_bytes;
-            dev::tma_load_5d(dst, &act_map, &a_full[a_stage], 0, x2, x1, x0, mc);
-            if constexpr (kSplit) {
-              dev::tma_load_5d(dst + P.a_part_bytes, &act_small_map, &a_full[a_stage], 0, x2, x1,
-                               x0, mc);
+            for (int part = 0; part < kParts; ++part) {
+              dev::tma_load_5d(dst + part * P.a_part_bytes, &maps.act[part], &a_full[a_stage], 0,
+                               x2, x1, x0, mc);
             }
           }
           if (real_tap) next_tap(g, t_o, t);
@@ -494,7 +518,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------- MMA issuer ----------------
     int a_stage = 0, b_slot = 0;
     uint32_t a_phase = 0, b_phase = 0;
-    const uint32_t k_rows = kTF32 ? 8u : 16u;
+    const uint32_t k_rows = 16u;
     const uint32_t a_sbo = 8u * P.a_row_bytes;
     const uint32_t b_sbo = 8u * P.b_row_bytes;
     const uint32_t b_lbo = static_cast<uint32_t>(P.kc_rows) * 128u;
@@ -513,19 +537,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int ks = 0; ks < P.ksteps; ++ks) {
           const uint32_t aoff = static_cast<uint32_t>(ks) * k_rows * P.a_row_bytes;
           const uint32_t boff = static_cast<uint32_t>(ks) * k_rows * P.b_row_bytes;
-          const uint64_t ad = dev::make_smem_desc(as + aoff, P.a_tile_bytes, a_sbo, P.a_layout);
-          const uint64_t bd = dev::make_smem_desc(bs + boff, b_lbo, b_sbo, P.b_layout);
-          const uint32_t acc = (pt != p_begin || ks != 0) ? 1u : 0u;
-          if constexpr (kSplit) {
-            const uint64_t ads =
-                dev::make_smem_desc(as + P.a_part_bytes + aoff, P.a_tile_bytes, a_sbo, P.a_layout);
-            const uint64_t bds =
-                dev::make_smem_desc(bs + P.b_part_bytes + boff, b_lbo, b_sbo, P.b_layout);
-            mma<true>(d, ads, bd, P.idesc, acc);
-            mma<true>(d, ad, bds, P.idesc, 1u);
-            mma<true>(d, ad, bd, P.idesc, 1u);
-          } else {
-            mma<kTF32>(d, ad, bd, P.idesc, acc);
+#pragma unroll
+          for (int q = 0; q < product_count<kParts>(); ++q) {
+            const uint64_t ad =
+                dev::make_smem_desc(as + product_a(kParts, q) * P.a_part_bytes + aoff,
+                                    P.a_tile_bytes, a_sbo, P.a_layout);
+            const uint64_t bd =
+                dev::make_smem_desc(bs + product_b(kParts, q) * P.b_part_bytes + boff, b_lbo,
+                                    b_sbo, P.b_layout);
+            const uint32_t acc = (pt != p_begin || ks != 0 || q != 0) ? 1u : 0u;
+            dev::mma_f16(d, ad, bd, P.idesc, acc);
           }
         }
         dev::mma_commit(&a_empty[a_stage]);
@@ -955,15 +976,16 @@ struct WgradPlan {
   WgradKernelParams P;
   size_t smem;
   int chunks;
+  int parts;
 };
 
 bool plan_wgrad(const WgradPass& pass, int splits_hint, WgradPlan* plan) {
   WgradKernelParams& P = plan->P;
   std::memset(&P, 0, sizeof(P));
+  if (pass.op == kOpF32) return false;  // wgrad runs on kind::f16 (bf16 parts for fp32)
   const int es = element_size(pass.op);
-  const bool tf32 = pass.op == kOpF32;
-  const bool split = tf32 && pass.split3;
-  const int parts = split ? 2 : 1;
+  const int parts = pass.parts < 1 ? 1 : pass.parts;
+  if (parts > 3) return false;
   const int a_row = pass.c_pad * es;
   if (!(a_row == 32 || a_row == 64 || a_row == 128)) return false;
   if (pass.n_pad < 16 || pass.n_pad > 256 || pass.n_pad % 16 != 0) return false;
@@ -997,7 +1019,7 @@ bool plan_wgrad(const WgradPass& pass, int splits_hint, WgradPlan* plan) {
     kc = 64;
   }
   P.kc_rows = kc;
-  P.ksteps = kc / (tf32 ? 8 : 16);
+  P.ksteps = kc / 16;
   if (!build_geom(pass.rank, pass.batch, pass.groups, pass.in, pass.out, pass.k, pass.s, pass.d,
                   pass.p, kc, &P.g)) {
     return false;
@@ -1009,6 +1031,7 @@ bool plan_wgrad(const WgradPass& pass, int splits_hint, WgradPlan* plan) {
   P.b_slot_bytes = P.b_part_bytes * parts;
   P.a_tx = P.a_tile_bytes * P.tpm * parts;
   P.b_tx = static_cast<uint32_t>(kc * b_row_full) * parts;
+  if (2 * P.b_slot_bytes + 2 * P.a_slot_bytes > 208 * 1024) return false;
   int stages = static_cast<int>((208 * 1024 - 2 * P.b_slot_bytes) / P.a_slot_bytes);
   if (stages > 6) stages = 6;
   if (stages < 2) return false;
@@ -1021,6 +1044,7 @@ bool plan_wgrad(const WgradPass& pass, int splits_hint, WgradPlan* plan) {
   plan->chunks = (P.mt_total + P.mt_per_cta - 1) / P.mt_per_cta;
   P.tmem_cols = tmem_columns(P.mt_per_cta * pass.n_pad);
   P.idesc = make_idesc(pass.op, 128, pass.n_pad, true, true);
+  plan->parts = parts;
   P.ptiles = (P.g.boxes_per_group + P.g.nb - 1) / P.g.nb;
   int splits = splits_hint;
   if (splits <= 0) {
@@ -1071,44 +1095,34 @@ int launch_wgrad_pass(const WgradPass& pass, cudaStream_t stream, uint64_t timeo
   const int box[3] = {P.g.b[0], P.g.b[1], P.g.b[2]};
   const int strd[3] = {P.g.s[0], P.g.s[1], P.g.s[2]};
   const int ones[3] = {1, 1, 1};
-  const bool split = pass.op == kOpF32 && pass.split3;
-  alignas(64) CUtensorMap maps[4];
-  std::memset(maps, 0, sizeof(maps));
-  int rc = encode_act_map(&maps[0], pass.act, pass.op, pass.c_pad, ext_in, merged_in, pass.c_pad,
-                          box, strd);
-  if (rc != CND_OK) return rc;
-  rc = encode_act_map(&maps[2], pass.grad, pass.op, pass.n_pad, ext_out, merged_out,
-                      P.b_blk_elems, box, ones);
-  if (rc != CND_OK) return rc;
-  if (split) {
-    rc = encode_act_map(&maps[1], pass.act_small, pass.op, pass.c_pad, ext_in, merged_in,
-                        pass.c_pad, box, strd);
+  alignas(64) WgradMaps maps;
+  std::memset(&maps, 0, sizeof(maps));
+  for (int part = 0; part < 3; ++part) {
+    const int source = part < plan.parts ? part : 0;
+    int rc = encode_act_map(&maps.act[part], pass.act[source], pass.op, pass.c_pad, ext_in,
+                            merged_in, pass.c_pad, box, strd);
     if (rc != CND_OK) return rc;
-    rc = encode_act_map(&maps[3], pass.grad_small, pass.op, pass.n_pad, ext_out, merged_out,
-                        P.b_blk_elems, box, ones);
+    rc = encode_act_map(&maps.grad[part], pass.grad[source], pass.op, pass.n_pad, ext_out,
+                        merged_out, P.b_blk_elems, box, ones);
     if (rc != CND_OK) return rc;
-  } else {
-    maps[1] = maps[0];
-    maps[3] = maps[2];
   }
   const dim3 grid(static_cast<unsigned>(P.splits), static_cast<unsigned>(plan.chunks),
                   static_cast<unsigned>(pass.groups));
-  const bool tf32 = pass.op == kOpF32;
-  if (split) {
-    auto kernel = wgrad_kernel<true, true>;
+  if (plan.parts == 3) {
+    auto kernel = wgrad_kernel<3>;
     cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          static_cast<int>(plan.smem));
-    kernel<<<grid, kThreads, plan.smem, stream>>>(maps[0], maps[1], maps[2], maps[3], P);
-  } else if (tf32) {
-    auto kernel = wgrad_kernel<true, false>;
+    kernel<<<grid, kThreads, plan.smem, stream>>>(maps, P);
+  } else if (plan.parts == 2) {
+    auto kernel = wgrad_kernel<2>;
     cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          static_cast<int>(plan.smem));
-    kernel<<<grid, kThreads, plan.smem, stream>>>(maps[0], maps[1], maps[2], maps[3], P);
+    kernel<<<grid, kThreads, plan.smem, stream>>>(maps, P);
   } else {
-    auto kernel = wgrad_kernel<false, false>;
+    auto kernel = wgrad_kernel<1>;
     cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          static_cast<int>(plan.smem));
-    kernel<<<grid, kThreads, plan.smem, stream>>>(maps[0], maps[1], maps[2], maps[3], P);
+    kernel<<<grid, kThreads, plan.smem, stream>>>(maps, P);
   }
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {

@@ -47,12 +47,10 @@ struct WgradPass {
   int cin_real;
   int n_pad;        // dy channels per group (packed), MMA N
   int n_real;
-  int op;
-  int split3;
-  const void* act;  // x packed [N][G][in...][c_pad]
-  const void* act_small;
-  const void* grad; // dy packed [N][G][out...][n_pad]
-  const void* grad_small;
+  int op;           // kOpBF16 or kOpF16 (float32 problems arrive as bf16 parts)
+  int parts;        // 1, or 2 / 3 bf16 terms per operand for float32 problems
+  const void* act[3];   // x packed [N][G][in...][c_pad], one array per part
+  const void* grad[3];  // dy packed [N][G][out...][n_pad], one array per part
   float* partial;   // [splits][G][taps][cin_real][n_real]
   int splits;       // chosen by plan_wgrad
 };
