@@ -136,6 +136,11 @@ CND_API int cnd_backward(const cnd_problem* problem, const void* dy, const void*
  * A clear bit means the generic CUDA-core kernels run that pass. */
 CND_API int cnd_fast_path_mask(const cnd_problem* problem);
 
+/* Writes a one-line-per-pass text description of how the library would run `problem`
+ * (kernel family, tile shape, halo and pipeline choices) into `buffer` (NUL-terminated,
+ * truncated to `size`). Returns the number of characters the full text needs. */
+CND_API int cnd_plan_summary(const cnd_problem* problem, char* buffer, size_t size);
+
 /* Reads and clears the library's device error word (set by a bounded wait that expired
  * inside a kernel). Returns CND_OK, or CND_ERR_TIMEOUT with the failing site in the
  * message. Synchronises `stream`. */

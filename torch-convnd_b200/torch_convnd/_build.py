@@ -27,8 +27,8 @@ LIB_DIR = PACKAGE / "_lib"
 CORE_LIBRARY = LIB_DIR / "libconvnd_b200.so"
 SHIM_LIBRARY = LIB_DIR / "_C.so"
 
-CORE_SOURCES = ["problem.cpp", "capi.cu", "tc_conv.cu", "pack.cu", "generic.cu"]
-CORE_HEADERS = ["internal.h", "ptx.cuh", "tc_conv.cuh", "pack.cuh", "generic.cuh"]
+CORE_SOURCES = ["problem.cpp", "capi.cu", "fprop.cu", "tc_conv.cu", "pack.cu", "generic.cu"]
+CORE_HEADERS = ["internal.h", "ptx.cuh", "fprop.cuh", "tc_conv.cuh", "pack.cuh", "generic.cuh"]
 SHIM_SOURCES = ["shim.cpp"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

@@ -11,6 +11,7 @@
 #include <cuda_runtime.h>
 
 #include <atomic>
+#include <cstdio>
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
@@ -19,6 +20,7 @@
 #include "generic.cuh"
 #include "internal.h"
 #include "pack.cuh"
+#include "fprop.cuh"
 #include "tc_conv.cuh"
 
 namespace cnd {
@@ -144,6 +146,7 @@ struct Plan {
   int64_t x_pad = 0, dy_pad = 0;
   bool fast_fwd = false, fast_dgrad = false, fast_wgrad = false;
   ConvPass fwd{}, dgrad{};
+  FpropPlan fwd_plan{}, dgrad_plan{};
   WgradPass wgrad{};
   // weight-gradient operands: 16-bit problems reuse x_cl / dy_cl; float32 problems pack
   // x and dy again as 3 (3xtf32 mode) or 2 (tf32 mode) bfloat16 terms.
@@ -208,7 +211,7 @@ void make_plan(const cnd_problem& p, bool forward, const int32_t* mask, Plan* pl
     f.op = plan->op;
     f.split3 = plan->split3;
     f.out_dtype = p.dtype;
-    plan->fast_fwd = plan->cout_g <= 256 && conv_pass_supported(f);
+    plan->fast_fwd = plan->cout_g <= 256 && plan_fprop(f, &plan->fwd_plan);
     if (plan->fast_fwd) {
       const size_t act = static_cast<size_t>(p.batch * p.groups * p.input_volume) * f.c_pad * es;
       const size_t wts = static_cast<size_t>(p.groups * taps * f.n_pad * f.c_pad) * es;
@@ -246,7 +249,8 @@ void make_plan(const cnd_problem& p, bool forward, const int32_t* mask, Plan* pl
     dg.op = plan->op;
     dg.split3 = plan->split3;
     dg.out_dtype = p.dtype;
-    plan->fast_dgrad = !strided && !wide_pad && plan->cin_g <= 256 && conv_pass_supported(dg);
+    plan->fast_dgrad =
+        !strided && !wide_pad && plan->cin_g <= 256 && plan_fprop(dg, &plan->dgrad_plan);
   }
   const bool f32 = p.dtype == CND_F32;
   plan->wg_op = f32 ? kOpBF16 : plan->op;
@@ -342,6 +346,45 @@ int cnd_fast_path_mask(const cnd_problem* problem) {
   return (fwd.fast_fwd ? 1 : 0) | (bwd.fast_dgrad ? 2 : 0) | (bwd.fast_wgrad ? 4 : 0);
 }
 
+int cnd_plan_summary(const cnd_problem* problem, char* buffer, size_t size) {
+  if (problem == nullptr) return 0;
+  cnd::Plan fwd, bwd;
+  const int32_t all[3] = {1, 1, 1};
+  cnd::make_plan(*problem, true, nullptr, &fwd);
+  cnd::make_plan(*problem, false, all, &bwd);
+  char text[1024];
+  int used = 0;
+  auto describe = [&](const char* name, bool fast, const cnd::FpropPlan& plan) {
+    const cnd::FpropParams& P = plan.params;
+    if (!fast) {
+      used += std::snprintf(text + used, sizeof(text) - used, "%s: generic CUDA cores\n", name);
+      return;
+    }
+    used += std::snprintf(text + used, sizeof(text) - used,
+                          "%s: tcgen05 tile [%d,%d,%d] x%d halo(a0=%d,a1=%d) box %dx%dx%d "
+                          "units=%d cblocks=%d N=%d stages=%d stage_bytes=%u nacc=%d parts=%d "
+                          "supers=%lld\n",
+                          name, P.e0, P.b1, P.b2, P.mt, P.nshift0, P.nshift1, P.h0, P.h1, P.b2,
+                          P.units, P.cblocks, P.n_pad, P.stages, P.stage_bytes, P.nacc,
+                          plan.parts, static_cast<long long>(P.supers_total));
+  };
+  describe("forward", fwd.fast_fwd, fwd.fwd_plan);
+  describe("dgrad", bwd.fast_dgrad, bwd.dgrad_plan);
+  if (bwd.fast_wgrad) {
+    used += std::snprintf(text + used, sizeof(text) - used,
+                          "wgrad: tcgen05 splits=%d parts=%d x_pad=%lld dy_pad=%lld\n",
+                          bwd.wgrad.splits, bwd.wgrad.parts,
+                          static_cast<long long>(bwd.wg_x_pad),
+                          static_cast<long long>(bwd.wg_dy_pad));
+  } else {
+    used += std::snprintf(text + used, sizeof(text) - used, "wgrad: generic CUDA cores\n");
+  }
+  if (buffer != nullptr && size > 0) {
+    std::snprintf(buffer, size, "%s", text);
+  }
+  return used;
+}
+
 int cnd_forward(const cnd_problem* problem, const void* x, const void* w, const void* b,
                 void* y, void* workspace, size_t workspace_bytes, void* stream_handle) {
   using namespace cnd;
@@ -395,6 +438,9 @@ int cnd_forward(const cnd_problem* problem, const void* x, const void* w, const 
   pw.dtype = p.dtype;
   pw.mode = plan.pack_mode;
   pw.dgrad = 0;
+  pw.shift0 = plan.fwd_plan.shift0;
+  pw.shift1 = plan.fwd_plan.shift1;
+  for (int a = 0; a < 3; ++a) pw.k_box[a] = plan.fwd_plan.k_box[a];
   {
     TimedPass timed(5, stream);
     rc = pack_weights(pw, stream);
@@ -408,7 +454,7 @@ int cnd_forward(const cnd_problem* problem, const void* x, const void* w, const 
   pass.dst = y;
   pass.bias = b;
   TimedPass timed(1, stream);
-  return launch_conv_pass(pass, stream, wait_timeout_ns(), 0);
+  return launch_fprop(pass, plan.fwd_plan, stream, wait_timeout_ns(), 0);
 }
 
 int cnd_backward(const cnd_problem* problem, const void* dy, const void* x, const void* w,
@@ -550,6 +596,9 @@ int cnd_backward(const cnd_problem* problem, const void* dy, const void* x, cons
       pw.dtype = p.dtype;
       pw.mode = plan.pack_mode;
       pw.dgrad = 1;
+      pw.shift0 = plan.dgrad_plan.shift0;
+      pw.shift1 = plan.dgrad_plan.shift1;
+      for (int a = 0; a < 3; ++a) pw.k_box[a] = plan.dgrad_plan.k_box[a];
       {
         TimedPass timed(5, stream);
         rc = pack_weights(pw, stream);
@@ -563,7 +612,7 @@ int cnd_backward(const cnd_problem* problem, const void* dy, const void* x, cons
       pass.dst = dx;
       pass.bias = nullptr;
       TimedPass timed(2, stream);
-      rc = launch_conv_pass(pass, stream, wait_timeout_ns(), 0);
+      rc = launch_fprop(pass, plan.dgrad_plan, stream, wait_timeout_ns(), 0);
       if (rc != CND_OK) return rc;
     } else {
       GenericCall call{GenericCall::kDgrad, problem, dy, w, nullptr, dx};
@@ -672,8 +721,13 @@ int cnd_debug_stall_test(int32_t timeout_ms, void* stream_handle) {
   pass.act = base;
   pass.wt = base + align_up(act);
   pass.dst = base + align_up(act) + align_up(wts);
-  int rc = launch_conv_pass(pass, stream,
-                            static_cast<uint64_t>(timeout_ms > 0 ? timeout_ms : 50) * 1000000ull, 1);
+  FpropPlan plan;
+  if (!plan_fprop(pass, &plan)) {
+    cudaFree(buffer);
+    return fail(CND_ERR_UNSUPPORTED, "cnd_debug_stall_test: planning failed");
+  }
+  int rc = launch_fprop(pass, plan, stream,
+                        static_cast<uint64_t>(timeout_ms > 0 ? timeout_ms : 50) * 1000000ull, 1);
   if (rc == CND_OK) rc = cnd_device_status(stream);
   cudaStreamSynchronize(stream);
   cudaFree(buffer);

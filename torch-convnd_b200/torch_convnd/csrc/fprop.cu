@@ -1,0 +1,753 @@
+// Persistent tcgen05 implicit-GEMM convolution pass (forward, and dgrad as a forward
+// pass over dy with flipped/transposed weights).
+//
+// Work decomposition. The last three spatial axes are "box axes" a0, a1, a2; the rest,
+// with batch and group, form the merged TMA dimension. An M tile is 128 output positions
+// [e0, b1, b2] along (a0, a1, a2); a CTA "super tile" is MT M tiles stacked along a0, all
+// sharing every weight tile it loads (weight reuse x MT). For each load unit — one value
+// of every tap axis that is not "shifted", and one channel block — TMA fetches a single
+// halo box of channels-last input [h0, h1, b2] that covers the super tile for every tap
+// of the shifted axes (a0 always when its stride is 1; a1 too when e0 == 1): the MMA for
+// tap (j0, j1) and tile m reads the box at row ((m*e0 + j0*d0)*h1 + j1*d1)*b2, a
+// multiple of 8 rows, so the 32/64/128-byte swizzle pattern lines up and no data moves
+// in shared memory. Out-of-range coordinates read zero (the reference's implicit zero
+// padding, src/torch_convnd/csrc/convnd.h:57-76). Weights are packed so that the taps of
+// one load unit are consecutive rows and arrive with one TMA box.
+//
+// Warp roles (192 threads): warp 0 lane 0 = TMA producer (warp 0 owns TMEM), warp 1 lane
+// 0 = MMA issuer, warps 2-5 = epilogue. Accumulators are double buffered in TMEM so the
+// epilogue of one super tile overlaps the main loop of the next. float32 problems
+// (kind::tf32) rotate taps over several accumulators and sum them in fp32 registers,
+// which keeps the tensor core's per-step accumulation error from growing with K.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <cstring>
+#include <mutex>
+
+#include "fprop.cuh"
+#include "ptx.cuh"
+
+namespace cnd {
+
+namespace {
+
+constexpr int kThreads = 192;
+constexpr uint32_t kSiteProducer = 0x301, kSiteMma = 0x302, kSiteEpilogue = 0x303,
+                   kSiteMmaAcc = 0x304, kSiteDrain = 0x305;
+
+struct FpropMaps {
+  CUtensorMap act[2];
+  CUtensorMap wt[2];
+};
+
+__device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
+  const uintptr_t v = reinterpret_cast<uintptr_t>(p);
+  return reinterpret_cast<uint8_t*>((v + 1023) & ~static_cast<uintptr_t>(1023));
+}
+
+// Position of a super tile: group, batch index, outer output coordinates and the tile
+// indices along the box axes (q0 counts super tiles along a0).
+struct Super {
+  int g;
+  int64_t n;
+  int64_t outer_lin;  // row-major index over the outer output axes
+  int o[kMaxOuter];
+  int q0, q1, q2;
+};
+
+__device__ __forceinline__ void decode_super(const FpropParams& P, int64_t st, Super& s) {
+  int64_t rest = st;
+  s.q2 = static_cast<int>(rest % P.nsup[2]);
+  rest /= P.nsup[2];
+  s.q1 = static_cast<int>(rest % P.nsup[1]);
+  rest /= P.nsup[1];
+  s.q0 = static_cast<int>(rest % P.nsup[0]);
+  rest /= P.nsup[0];
+  s.outer_lin = rest % P.out_outer_vol;
+  rest /= P.out_outer_vol;
+  s.n = rest % P.batch;
+  s.g = static_cast<int>(rest / P.batch);
+  int64_t o = s.outer_lin;
+#pragma unroll
+  for (int a = kMaxOuter - 1; a >= 0; --a) {
+    if (a < P.n_outer) {
+      s.o[a] = static_cast<int>(o % P.out_o[a]);
+      o /= P.out_o[a];
+    } else {
+      s.o[a] = 0;
+    }
+  }
+}
+
+__device__ __forceinline__ void store_value(void* out, int64_t index, float value, int dtype) {
+  if (dtype == CND_BF16) {
+    static_cast<__nv_bfloat16*>(out)[index] = __float2bfloat16_rn(value);
+  } else if (dtype == CND_F16) {
+    static_cast<__half*>(out)[index] = __float2half_rn(value);
+  } else {
+    static_cast<float*>(out)[index] = value;
+  }
+}
+
+__device__ __forceinline__ float load_value(const void* in, int64_t index, int dtype) {
+  if (dtype == CND_BF16) return __bfloat162float(static_cast<const __nv_bfloat16*>(in)[index]);
+  if (dtype == CND_F16) return __half2float(static_cast<const __half*>(in)[index]);
+  return static_cast<const float*>(in)[index];
+}
+
+template <bool kTF32>
+__device__ __forceinline__ void mma(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc,
+                                    uint32_t acc) {
+  if constexpr (kTF32) {
+    dev::mma_tf32(d, a, b, idesc, acc);
+  } else {
+    dev::mma_f16(d, a, b, idesc, acc);
+  }
+}
+
+template <bool kTF32, int kParts>
+__global__ void __launch_bounds__(kThreads, 1)
+    fprop_kernel(const __grid_constant__ FpropMaps maps, const __grid_constant__ FpropParams P) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + P.stages * P.stage_bytes);
+  uint64_t* empty = full + P.stages;
+  uint64_t* acc_full = empty + P.stages;
+  uint64_t* acc_empty = acc_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  volatile uint32_t* progress = tmem_slot + 1;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const dev::ErrorWord err{P.err};
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < P.stages; ++s) {
+      dev::mbar_init(&full[s], 1);
+      dev::mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      dev::mbar_init(&acc_full[b], 1);
+      dev::mbar_init(&acc_empty[b], 128);
+    }
+    *progress = 0;
+    dev::fence_barrier_init();
+  }
+  if (warp == 0) {
+    __syncwarp();
+    dev::tmem_alloc(tmem_slot, P.tmem_cols);
+  }
+  dev::tc_fence_before();
+  __syncthreads();
+  dev::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int nshift = P.nshift0 * P.nshift1;
+  const int work_per_super = P.units * nshift;
+
+  if (warp == 0 && lane == 0) {
+    // ------------------------------ TMA producer ------------------------------
+    for (int part = 0; part < kParts; ++part) {
+      dev::prefetch_tensormap(&maps.act[part]);
+      dev::prefetch_tensormap(&maps.wt[part]);
+    }
+    int stage = 0;
+    uint32_t phase = 0;
+    int64_t issued = 0;
+    bool ok = P.debug_stall == 0;
+    for (int64_t st = blockIdx.x; st < P.supers_total && ok; st += gridDim.x) {
+      Super S;
+      decode_super(P, st, S);
+      const int64_t m_base = (S.n * P.groups + S.g) * P.in_merged_per_gn;
+      int ibo[kMaxOuter];
+#pragma unroll
+      for (int a = 0; a < kMaxOuter; ++a) {
+        ibo[a] = a < P.n_outer ? S.o[a] * P.s_o[a] - P.p_o[a] : 0;
+      }
+      const int x0 = S.q0 * P.mt * P.e0 * P.s[0] - P.p[0];
+      const int x1 = S.q1 * P.b1 * P.s[1] - P.p[1];
+      const int x2 = S.q2 * P.b2 * P.s[2] - P.p[2];
+      int to[kMaxOuter];
+#pragma unroll
+      for (int a = 0; a < kMaxOuter; ++a) to[a] = 0;
+      int t0 = 0, t1 = 0, t2 = 0;
+      const int32_t w_base = S.g * P.taps;
+      for (int u = 0; u < P.units && ok; ++u) {
+        bool valid = true;
+        int64_t m = m_base;
+#pragma unroll
+        for (int a = 0; a < kMaxOuter; ++a) {
+          if (a < P.n_outer) {
+            const int c = ibo[a] + to[a] * P.d_o[a];
+            valid = valid && c >= 0 && c < P.in_o[a];
+            m += static_cast<int64_t>(c) * P.in_o_stride[a];
+          }
+        }
+        const int32_t mc = valid ? static_cast<int32_t>(m) : -1;
+        const int32_t c0 = x0 + (P.nshift0 > 1 ? 0 : t0 * P.d[0]);
+        const int32_t c1 = x1 + (P.nshift1 > 1 ? 0 : t1 * P.d[1]);
+        const int32_t c2 = x2 + t2 * P.d[2];
+        const int32_t w_row = w_base + u * nshift;
+        for (int cb = 0; cb < P.cblocks; ++cb) {
+          if (!dev::mbar_wait(&empty[stage], phase ^ 1u, err, kSiteProducer, P.timeout_ns)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sb = smem + stage * P.stage_bytes;
+          dev::mbar_arrive_expect_tx(&full[stage], P.tx_bytes);
+          const int32_t ch = cb * P.cblk_elems;
+#pragma unroll
+          for (int part = 0; part < kParts; ++part) {
+            dev::tma_load_5d(sb + part * P.a_part_bytes, &maps.act[part], &full[stage], ch, c2,
+                             c1, c0, mc);
+            dev::tma_load_3d(sb + P.b_off + part * P.b_part_bytes, &maps.wt[part], &full[stage],
+                             ch, 0, w_row);
+          }
+          ++issued;
+          if (++stage == P.stages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        // Next unit: t2 fastest, then the unshifted a1 / a0 taps, then the outer taps.
+        if (++t2 == P.k[2]) {
+          t2 = 0;
+          bool carry = true;
+          if (P.nshift1 == 1) {
+            if (++t1 == P.k[1]) {
+              t1 = 0;
+            } else {
+              carry = false;
+            }
+          }
+          if (carry && P.nshift0 == 1) {
+            if (++t0 == P.k[0]) {
+              t0 = 0;
+            } else {
+              carry = false;
+            }
+          }
+#pragma unroll
+          for (int a = kMaxOuter - 1; a >= 0; --a) {
+            if (carry && a < P.n_outer) {
+              if (++to[a] == P.k_o[a]) {
+                to[a] = 0;
+              } else {
+                carry = false;
+              }
+            }
+          }
+        }
+      }
+    }
+    if (!ok && issued > 0) {
+      // Let loads already in flight land before the CTA's shared memory goes away.
+      const int pending = issued < P.stages ? static_cast<int>(issued) : P.stages;
+      for (int i = 1; i <= pending; ++i) {
+        const int64_t kb = issued - i;
+        dev::mbar_wait(&full[kb % P.stages], static_cast<uint32_t>((kb / P.stages) & 1), err,
+                       kSiteDrain, P.timeout_ns / 8 + 1);
+      }
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ------------------------------ MMA issuer ------------------------------
+    int stage = 0;
+    uint32_t phase = 0;
+    uint32_t done = 0;
+    const uint32_t sbo = 8u * static_cast<uint32_t>(P.row_bytes);
+    const uint32_t b_tap_bytes = static_cast<uint32_t>(P.n_pad * P.row_bytes);
+    int iter = 0;
+    bool ok = true;
+    for (int64_t st = blockIdx.x; st < P.supers_total && ok; st += gridDim.x, ++iter) {
+      const int buf = iter & 1;
+      if (!dev::mbar_wait(&acc_empty[buf], (static_cast<uint32_t>(iter >> 1) & 1u) ^ 1u, err,
+                          kSiteMmaAcc, P.timeout_ns)) {
+        break;
+      }
+      dev::tc_fence_after();
+      const uint32_t dbase = tmem + static_cast<uint32_t>(buf * P.acc_stride);
+      for (int u = 0; u < P.units && ok; ++u) {
+        for (int cb = 0; cb < P.cblocks; ++cb) {
+          if (!dev::mbar_wait(&full[stage], phase, err, kSiteMma, P.timeout_ns)) {
+            ok = false;
+            break;
+          }
+          dev::tc_fence_after();
+          const uint32_t sa = dev::smem_u32(smem + stage * P.stage_bytes);
+          const uint32_t sbw = sa + P.b_off;
+          for (int j0 = 0; j0 < P.nshift0; ++j0) {
+            for (int j1 = 0; j1 < P.nshift1; ++j1) {
+              const int ls = j0 * P.nshift1 + j1;
+              const int w = u * nshift + ls;
+              const int acc_index = w % P.nacc;
+              const bool first_use = w < P.nacc && cb == 0;
+              const uint32_t b_addr = sbw + static_cast<uint32_t>(ls) * b_tap_bytes;
+              for (int m = 0; m < P.mt; ++m) {
+                const int row = ((m * P.e0 + j0 * P.d[0]) * P.h1 + j1 * P.d[1]) * P.b2;
+                const uint32_t a_addr = sa + static_cast<uint32_t>(row * P.row_bytes);
+                const uint32_t d =
+                    dbase + static_cast<uint32_t>((acc_index * P.mt + m) * P.n_pad);
+                for (int kk = 0; kk < P.ksteps; ++kk) {
+                  const uint32_t koff = static_cast<uint32_t>(kk) * 32u;
+                  const uint64_t ad = dev::make_smem_desc(a_addr + koff, 16, sbo, P.layout);
+                  const uint64_t bd = dev::make_smem_desc(b_addr + koff, 16, sbo, P.layout);
+                  const uint32_t acc = (first_use && kk == 0) ? 0u : 1u;
+                  if constexpr (kParts == 2) {
+                    const uint64_t ads =
+                        dev::make_smem_desc(a_addr + P.a_part_bytes + koff, 16, sbo, P.layout);
+                    const uint64_t bds =
+                        dev::make_smem_desc(b_addr + P.b_part_bytes + koff, 16, sbo, P.layout);
+                    mma<true>(d, ads, bd, P.idesc, acc);
+                    mma<true>(d, ad, bds, P.idesc, 1u);
+                    mma<true>(d, ad, bd, P.idesc, 1u);
+                  } else {
+                    mma<kTF32>(d, ad, bd, P.idesc, acc);
+                  }
+                }
+              }
+            }
+          }
+          dev::mma_commit(&empty[stage]);
+          *progress = ++done;
+          if (++stage == P.stages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      dev::mma_commit(&acc_full[buf]);
+    }
+  } else if (warp >= 2) {
+    // ------------------------------ epilogue ------------------------------
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const int i2 = row % P.b2;
+    const int i1 = (row / P.b2) % P.b1;
+    const int i0 = row / (P.b2 * P.b1);
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+    const int used = work_per_super < P.nacc ? work_per_super : P.nacc;
+    int iter = 0;
+    for (int64_t st = blockIdx.x; st < P.supers_total; st += gridDim.x, ++iter) {
+      const int buf = iter & 1;
+      dev::mbar_wait_progress(&acc_full[buf], static_cast<uint32_t>(iter >> 1) & 1u, progress,
+                              err, kSiteEpilogue, P.timeout_ns);
+      dev::tc_fence_after();
+      Super S;
+      decode_super(P, st, S);
+      const uint32_t dbase = lane_addr + static_cast<uint32_t>(buf * P.acc_stride);
+      const int o1 = S.q1 * P.b1 + i1;
+      const int o2 = S.q2 * P.b2 + i2;
+      const int64_t channel_base =
+          (S.n * P.out_channels_total + static_cast<int64_t>(S.g) * P.n_real) * P.out_volume;
+      for (int m = 0; m < P.mt; ++m) {
+        const int o0 = (S.q0 * P.mt + m) * P.e0 + i0;
+        const bool valid = o0 < P.out[0] && o1 < P.out[1] && o2 < P.out[2];
+        const int64_t sp = S.outer_lin * P.out_box_vol +
+                           (static_cast<int64_t>(o0) * P.out[1] + o1) * P.out[2] + o2;
+        for (int c = 0; c < P.n_pad / 16; ++c) {
+          float sum[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) sum[i] = 0.0f;
+          for (int a = 0; a < used; ++a) {
+            uint32_t v[16];
+            __syncwarp();
+            dev::tmem_load16(dbase + static_cast<uint32_t>((a * P.mt + m) * P.n_pad + c * 16), v);
+            dev::tmem_load_wait();
+#pragma unroll
+            for (int i = 0; i < 16; ++i) sum[i] += __uint_as_float(v[i]);
+          }
+          if (valid) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const int co = c * 16 + i;
+              if (co < P.n_real) {
+                float value = sum[i];
+                if (P.bias != nullptr) {
+                  value += load_value(P.bias, static_cast<int64_t>(S.g) * P.n_real + co,
+                                      P.out_dtype);
+                }
+                store_value(P.dst, channel_base + static_cast<int64_t>(co) * P.out_volume + sp,
+                            value, P.out_dtype);
+              }
+            }
+          }
+        }
+      }
+      dev::tc_fence_before();
+      dev::mbar_arrive(&acc_empty[buf]);
+    }
+  }
+  dev::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    dev::tc_fence_after();
+    dev::tmem_dealloc(tmem, P.tmem_cols);
+  }
+}
+
+// =======================================================================================
+// Host side
+// =======================================================================================
+
+PFN_cuTensorMapEncodeTiled_v12000 encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult status;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &status) ==
+            cudaSuccess &&
+        status == cudaDriverEntryPointSuccess) {
+      encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }
+  });
+  return encode;
+}
+
+int elem_size(int op) { return op == kOpF32 ? 4 : 2; }
+
+CUtensorMapDataType map_dtype(int op) {
+  if (op == kOpBF16) return CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  if (op == kOpF16) return CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  return CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+}
+
+CUtensorMapSwizzle swizzle_for(int row_bytes) {
+  if (row_bytes == 32) return CU_TENSOR_MAP_SWIZZLE_32B;
+  if (row_bytes == 64) return CU_TENSOR_MAP_SWIZZLE_64B;
+  return CU_TENSOR_MAP_SWIZZLE_128B;
+}
+
+uint32_t layout_for(int row_bytes) {
+  if (row_bytes == 32) return 6;
+  if (row_bytes == 64) return 4;
+  return 2;
+}
+
+int row_bytes_for(int op, int c_pad) {
+  const int row = c_pad * elem_size(op);
+  if (row == 32 || row == 64 || row == 128) return row;
+  if (row > 128 && row % 128 == 0) return 128;
+  return 0;
+}
+
+uint32_t round_up(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
+
+uint32_t pow2_columns(int needed) {
+  uint32_t cols = 32;
+  while (cols < static_cast<uint32_t>(needed)) cols <<= 1;
+  return cols;
+}
+
+int device_sms() {
+  static int count = 0;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, dev);
+    if (count <= 0) count = 148;
+  });
+  return count;
+}
+
+uint32_t make_idesc(int op, int m, int n) {
+  uint32_t desc = 1u << 4;  // fp32 accumulator
+  const uint32_t fmt = op == kOpBF16 ? 1u : (op == kOpF16 ? 0u : 2u);
+  desc |= fmt << 7;
+  desc |= fmt << 10;
+  desc |= static_cast<uint32_t>(n >> 3) << 17;
+  desc |= static_cast<uint32_t>(m >> 4) << 24;
+  return desc;
+}
+
+constexpr int64_t kInt32Max = (int64_t{1} << 31) - 1;
+
+// Fills the geometry part of the parameters (axes split, extents). False when a value
+// does not fit the kernel's 32-bit coordinates.
+bool fill_geometry(const ConvPass& pass, FpropParams* P) {
+  const int rank = pass.rank;
+  if (rank < 1 || rank > kMaxFastRank) return false;
+  const int n_outer = rank > 3 ? rank - 3 : 0;
+  const int lead = 3 - (rank - n_outer);
+  P->n_outer = n_outer;
+  for (int a = 0; a < 3; ++a) {
+    const int src = a - lead + n_outer;
+    if (a < lead) {
+      P->out[a] = P->in[a] = P->k[a] = P->s[a] = P->d[a] = 1;
+      P->p[a] = 0;
+      continue;
+    }
+    if (pass.in[src] > kInt32Max / 4 || pass.out[src] > 65536 || pass.k[src] > 4096 ||
+        pass.s[src] > 8 || pass.d[src] > 65536 || pass.p[src] > 65536) {
+      return false;
+    }
+    P->out[a] = static_cast<int>(pass.out[src]);
+    P->in[a] = static_cast<int>(pass.in[src]);
+    P->k[a] = static_cast<int>(pass.k[src]);
+    P->s[a] = static_cast<int>(pass.s[src]);
+    P->d[a] = static_cast<int>(pass.d[src]);
+    P->p[a] = static_cast<int>(pass.p[src]);
+  }
+  int64_t in_vol = 1, out_vol = 1, taps = 1;
+  for (int a = kMaxOuter - 1; a >= 0; --a) {
+    if (a >= n_outer) {
+      P->out_o[a] = P->in_o[a] = P->k_o[a] = P->s_o[a] = P->d_o[a] = 1;
+      P->p_o[a] = 0;
+      P->in_o_stride[a] = 0;
+      continue;
+    }
+    if (pass.in[a] > kInt32Max || pass.out[a] > kInt32Max || pass.k[a] > 4096 ||
+        pass.s[a] > 65536 || pass.d[a] > 65536 || pass.p[a] > 65536) {
+      return false;
+    }
+    P->out_o[a] = static_cast<int>(pass.out[a]);
+    P->in_o[a] = static_cast<int>(pass.in[a]);
+    P->k_o[a] = static_cast<int>(pass.k[a]);
+    P->s_o[a] = static_cast<int>(pass.s[a]);
+    P->d_o[a] = static_cast<int>(pass.d[a]);
+    P->p_o[a] = static_cast<int>(pass.p[a]);
+    P->in_o_stride[a] = in_vol;
+    in_vol *= pass.in[a];
+    out_vol *= pass.out[a];
+  }
+  for (int a = 0; a < rank; ++a) taps *= pass.k[a];
+  if (taps > 1 << 20) return false;
+  P->taps = static_cast<int>(taps);
+  P->batch = pass.batch;
+  P->groups = pass.groups;
+  P->in_merged_per_gn = in_vol;
+  P->out_outer_vol = out_vol;
+  P->out_box_vol = static_cast<int64_t>(P->out[0]) * P->out[1] * P->out[2];
+  P->out_volume = out_vol * P->out_box_vol;
+  if (pass.batch * pass.groups * in_vol > kInt32Max) return false;
+  return true;
+}
+
+struct Candidate {
+  int e0, b1, b2, mt, shift0, shift1;
+};
+
+// Shared-memory stage layout of a candidate; false when it does not fit.
+bool layout_candidate(const ConvPass& pass, FpropParams* P, const Candidate& c, int parts) {
+  const int row_bytes = row_bytes_for(pass.op, pass.c_pad);
+  const int k0 = P->k[0], k1 = P->k[1];
+  P->e0 = c.e0;
+  P->b1 = c.b1;
+  P->b2 = c.b2;
+  P->mt = c.mt;
+  P->nshift0 = c.shift0 ? k0 : 1;
+  P->nshift1 = c.shift1 ? k1 : 1;
+  P->h0 = c.mt * c.e0 + (c.shift0 ? (k0 - 1) * P->d[0] : 0);
+  P->h1 = c.b1 + (c.shift1 ? (k1 - 1) * P->d[1] : 0);
+  // TMA box extents (elements of the packed tensor, before element striding).
+  const int box0 = c.shift0 ? P->h0 : c.mt * c.e0 * P->s[0];
+  const int box1 = c.shift1 ? P->h1 : c.b1 * P->s[1];
+  const int box2 = c.b2 * P->s[2];
+  if (box0 > 256 || box1 > 256 || box2 > 256) return false;
+  const uint32_t rows = static_cast<uint32_t>(P->h0 * P->h1 * c.b2);
+  P->row_bytes = row_bytes;
+  P->a_part_bytes = round_up(rows * row_bytes, 1024);
+  const int nshift = P->nshift0 * P->nshift1;
+  P->b_part_bytes = round_up(static_cast<uint32_t>(nshift * pass.n_pad * row_bytes), 1024);
+  P->b_off = P->a_part_bytes * parts;
+  P->stage_bytes = P->b_off + P->b_part_bytes * parts;
+  P->tx_bytes = (rows * row_bytes + static_cast<uint32_t>(nshift * pass.n_pad * row_bytes)) * parts;
+  return P->stage_bytes <= 100 * 1024;
+}
+
+}  // namespace
+
+bool plan_fprop(const ConvPass& pass, FpropPlan* plan) {
+  std::memset(plan, 0, sizeof(*plan));
+  FpropParams& P = plan->params;
+  if (pass.n_pad < 16 || pass.n_pad > 256 || pass.n_pad % 16 != 0) return false;
+  const int row_bytes = row_bytes_for(pass.op, pass.c_pad);
+  if (row_bytes == 0) return false;
+  if (!fill_geometry(pass, &P)) return false;
+  const bool tf32 = pass.op == kOpF32;
+  const int parts = (tf32 && pass.split3) ? 2 : 1;
+  const int es = elem_size(pass.op);
+  P.cblk_elems = row_bytes / es;
+  P.cblocks = pass.c_pad / P.cblk_elems;
+  P.ksteps = row_bytes / 32;
+  P.layout = static_cast<int>(layout_for(row_bytes));
+  P.n_pad = pass.n_pad;
+  P.n_real = pass.n_real;
+  const int products = parts == 2 ? 3 : 1;
+  const int64_t outer_count = pass.batch * P.out_outer_vol * pass.groups;
+
+  double best = 1e300;
+  FpropParams chosen{};
+  bool found = false;
+  for (int e0 = 1; e0 <= 128; e0 *= 2) {
+    for (int b2 = 8; b2 <= 128; b2 *= 2) {
+      if (128 % (e0 * b2) != 0) continue;
+      const int b1 = 128 / (e0 * b2);
+      for (int mt = 1; mt <= 8; mt *= 2) {
+        for (int shift0 = 0; shift0 <= 1; ++shift0) {
+          if (shift0 && (P.s[0] != 1 || P.k[0] == 1)) continue;
+          for (int shift1 = 0; shift1 <= 1; ++shift1) {
+            if (shift1 && (P.s[1] != 1 || P.k[1] == 1 || e0 != 1)) continue;
+            FpropParams trial = P;
+            const Candidate cand{e0, b1, b2, mt, shift0, shift1};
+            if (!layout_candidate(pass, &trial, cand, parts)) continue;
+            int nacc = 1;
+            if (tf32) {
+              nacc = 8;
+              while (nacc > 1 && 2 * nacc * mt * pass.n_pad > 512) nacc /= 2;
+            }
+            if (2 * nacc * mt * pass.n_pad > 512) continue;
+            // Estimated cycles per useful output position.
+            const double tiles0 = (P.out[0] + mt * e0 - 1) / (mt * e0);
+            const double waste = (tiles0 * mt * e0 / P.out[0]) *
+                                 (double((P.out[1] + b1 - 1) / b1) * b1 / P.out[1]) *
+                                 (double((P.out[2] + b2 - 1) / b2) * b2 / P.out[2]);
+            const double mma_steps = double(mt) * P.taps * P.cblocks * P.ksteps * products;
+            const double mma_cycles = mma_steps * (pass.n_pad / 2.0);
+            const double feed_cycles = mma_steps * (128.0 * 32 + pass.n_pad * 32.0) / 128.0;
+            const int nshift = trial.nshift0 * trial.nshift1;
+            const double units = double(P.taps) / nshift * P.cblocks;
+            const double l2_cycles = units * trial.tx_bytes / 70.0;
+            const double issue_cycles = units * 250.0;
+            double cycles = mma_cycles;
+            if (feed_cycles > cycles) cycles = feed_cycles;
+            if (l2_cycles > cycles) cycles = l2_cycles;
+            if (issue_cycles > cycles) cycles = issue_cycles;
+            // Bound plus a small preference for less L2 traffic and fewer load units
+            // (both shorten the latency chain the bound ignores).
+            const double per_position =
+                (cycles + 0.15 * l2_cycles + 0.05 * issue_cycles) * waste / (mt * 128.0);
+            // Enough super tiles to fill the machine.
+            const double supers = double(outer_count) * tiles0 *
+                                  ((P.out[1] + b1 - 1) / b1) * ((P.out[2] + b2 - 1) / b2);
+            const double fill = supers >= device_sms() ? 1.0 : device_sms() / supers;
+            const double score = per_position * fill;
+            if (score < best) {
+              best = score;
+              chosen = trial;
+              chosen.nacc = nacc;
+              found = true;
+            }
+          }
+        }
+      }
+    }
+  }
+  if (!found) return false;
+  P = chosen;
+  P.units = P.taps / (P.nshift0 * P.nshift1);
+  P.nsup[0] = (P.out[0] + P.mt * P.e0 - 1) / (P.mt * P.e0);
+  P.nsup[1] = (P.out[1] + P.b1 - 1) / P.b1;
+  P.nsup[2] = (P.out[2] + P.b2 - 1) / P.b2;
+  P.supers_total = outer_count * P.nsup[0] * P.nsup[1] * P.nsup[2];
+  P.acc_stride = P.nacc * P.mt * pass.n_pad;
+  P.tmem_cols = pow2_columns(2 * P.acc_stride);
+  P.stages = static_cast<int>((200 * 1024) / P.stage_bytes);
+  if (P.stages > 8) P.stages = 8;
+  if (P.stages < 2) return false;
+  P.idesc = make_idesc(pass.op, 128, pass.n_pad);
+  P.out_dtype = pass.out_dtype;
+  P.out_channels_total = pass.groups * pass.n_real;
+  plan->parts = parts;
+  plan->smem = static_cast<size_t>(P.stages) * P.stage_bytes + 1024 + (2 * P.stages + 4) * 8 + 64;
+  // Weight packing order: one load unit's shifted taps are consecutive rows.
+  plan->shift0 = P.nshift0 > 1;
+  plan->shift1 = P.nshift1 > 1;
+  plan->k_box[0] = P.k[0];
+  plan->k_box[1] = P.k[1];
+  plan->k_box[2] = P.k[2];
+  return true;
+}
+
+int launch_fprop(const ConvPass& pass, const FpropPlan& plan_in, cudaStream_t stream,
+                 uint64_t timeout_ns, int debug_stall) {
+  FpropPlan plan = plan_in;
+  FpropParams& P = plan.params;
+  P.dst = pass.dst;
+  P.bias = pass.bias;
+  P.err = device_error_word();
+  P.timeout_ns = timeout_ns;
+  P.debug_stall = debug_stall;
+  if (P.supers_total == 0) return CND_OK;
+  auto encode = encoder();
+  if (encode == nullptr) return fail(CND_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  const int es = elem_size(pass.op);
+  alignas(64) FpropMaps maps;
+  std::memset(&maps, 0, sizeof(maps));
+  const void* act[2] = {pass.act, pass.act_small};
+  const void* wt[2] = {pass.wt, pass.wt_small};
+  for (int part = 0; part < plan.parts; ++part) {
+    cuuint64_t dims[5] = {static_cast<cuuint64_t>(pass.c_pad), static_cast<cuuint64_t>(P.in[2]),
+                          static_cast<cuuint64_t>(P.in[1]), static_cast<cuuint64_t>(P.in[0]),
+                          static_cast<cuuint64_t>(pass.batch * pass.groups * P.in_merged_per_gn)};
+    const cuuint64_t c = static_cast<cuuint64_t>(pass.c_pad) * es;
+    cuuint64_t strides[4] = {c, c * P.in[2], c * P.in[2] * P.in[1], c * P.in[2] * P.in[1] * P.in[0]};
+    const int box0 = P.nshift0 > 1 ? P.h0 : P.mt * P.e0 * P.s[0];
+    const int box1 = P.nshift1 > 1 ? P.h1 : P.b1 * P.s[1];
+    cuuint32_t boxd[5] = {static_cast<cuuint32_t>(P.cblk_elems),
+                          static_cast<cuuint32_t>(P.b2 * P.s[2]), static_cast<cuuint32_t>(box1),
+                          static_cast<cuuint32_t>(box0), 1};
+    cuuint32_t estr[5] = {1, static_cast<cuuint32_t>(P.s[2]),
+                          static_cast<cuuint32_t>(P.nshift1 > 1 ? 1 : P.s[1]),
+                          static_cast<cuuint32_t>(P.nshift0 > 1 ? 1 : P.s[0]), 1};
+    CUresult r = encode(&maps.act[part], map_dtype(pass.op), 5, const_cast<void*>(act[part]),
+                        dims, strides, boxd, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        swizzle_for(P.row_bytes), CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+      return fail(CND_ERR_CUDA, "cuTensorMapEncodeTiled (activations) failed with code %d",
+                  static_cast<int>(r));
+    }
+    const int nshift = P.nshift0 * P.nshift1;
+    cuuint64_t wdims[3] = {static_cast<cuuint64_t>(pass.c_pad), static_cast<cuuint64_t>(pass.n_pad),
+                           static_cast<cuuint64_t>(pass.groups * P.taps)};
+    cuuint64_t wstrides[2] = {c, c * pass.n_pad};
+    cuuint32_t wbox[3] = {static_cast<cuuint32_t>(P.cblk_elems),
+                          static_cast<cuuint32_t>(pass.n_pad), static_cast<cuuint32_t>(nshift)};
+    cuuint32_t westr[3] = {1, 1, 1};
+    r = encode(&maps.wt[part], map_dtype(pass.op), 3, const_cast<void*>(wt[part]), wdims,
+               wstrides, wbox, westr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle_for(P.row_bytes),
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+      return fail(CND_ERR_CUDA, "cuTensorMapEncodeTiled (weights) failed with code %d",
+                  static_cast<int>(r));
+    }
+  }
+  // Persistent grid: two CTAs per SM when both fit (shared memory and TMEM), else one,
+  // enforced through the shared-memory request.
+  const bool two_per_sm = plan.smem <= 110 * 1024 && P.tmem_cols <= 256;
+  size_t smem = plan.smem;
+  if (!two_per_sm && smem < 120 * 1024) smem = 120 * 1024;
+  int64_t grid = P.supers_total;
+  const int64_t resident = static_cast<int64_t>(device_sms()) * (two_per_sm ? 2 : 1);
+  if (grid > resident) grid = resident;
+  const bool tf32 = pass.op == kOpF32;
+  if (plan.parts == 2) {
+    auto kernel = fprop_kernel<true, 2>;
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         static_cast<int>(smem));
+    kernel<<<static_cast<unsigned>(grid), kThreads, smem, stream>>>(maps, P);
+  } else if (tf32) {
+    auto kernel = fprop_kernel<true, 1>;
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         static_cast<int>(smem));
+    kernel<<<static_cast<unsigned>(grid), kThreads, smem, stream>>>(maps, P);
+  } else {
+    auto kernel = fprop_kernel<false, 1>;
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         static_cast<int>(smem));
+    kernel<<<static_cast<unsigned>(grid), kThreads, smem, stream>>>(maps, P);
+  }
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    return fail(CND_ERR_CUDA, "fprop_kernel launch failed: %s", cudaGetErrorString(e));
+  }
+  count_launch();
+  return CND_OK;
+}
+
+}  // namespace cnd

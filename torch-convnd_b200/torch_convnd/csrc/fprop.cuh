@@ -1,0 +1,62 @@
+// Host interface of the persistent tcgen05 convolution pass in fprop.cu.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+
+#include "internal.h"
+#include "tc_conv.cuh"
+
+namespace cnd {
+
+// Kernel parameters (passed by value as a __grid_constant__).
+struct FpropParams {
+  // geometry: box axes a0..a2, outer axes (merged TMA dimension)
+  int n_outer;
+  int out_o[kMaxOuter], in_o[kMaxOuter], k_o[kMaxOuter], s_o[kMaxOuter], d_o[kMaxOuter],
+      p_o[kMaxOuter];
+  int64_t in_o_stride[kMaxOuter];
+  int out[3], in[3], k[3], s[3], d[3], p[3];
+  int64_t batch, groups, in_merged_per_gn, out_outer_vol, out_box_vol, out_volume,
+      out_channels_total;
+  int taps;
+  // tiling
+  int e0, b1, b2, mt;
+  int nshift0, nshift1;  // taps of a0 / a1 served by shared-memory shifts (1 = none)
+  int h0, h1;            // halo box extents (rows) along a0 / a1
+  int nsup[3];
+  int64_t supers_total;
+  int units;             // load units per super tile (taps / shifted taps)
+  // channels and MMA
+  int cblocks, cblk_elems, ksteps, row_bytes, layout;
+  int n_pad, n_real, nacc, acc_stride;
+  uint32_t a_part_bytes, b_part_bytes, b_off, stage_bytes, tx_bytes, idesc, tmem_cols;
+  int stages;
+  // output (channels-first)
+  void* dst;
+  const void* bias;
+  int out_dtype;
+  unsigned int* err;
+  uint64_t timeout_ns;
+  int debug_stall;
+};
+
+struct FpropPlan {
+  FpropParams params;
+  int parts;         // 2 for 3xTF32 (big + small operand arrays)
+  size_t smem;
+  // weight packing order (see PackWeightArgs::unit_order)
+  int shift0, shift1;
+  int k_box[3];
+};
+
+// Chooses tiling, halo and pipeline depth for a pass; false if the pass does not fit.
+bool plan_fprop(const ConvPass& pass, FpropPlan* plan);
+
+// Runs a planned pass. The packed weights must follow the plan's unit order.
+int launch_fprop(const ConvPass& pass, const FpropPlan& plan, cudaStream_t stream,
+                 uint64_t timeout_ns, int debug_stall);
+
+}  // namespace cnd

@@ -120,31 +120,56 @@ __global__ void __launch_bounds__(256) pack_act_kernel(const Tin* __restrict__ s
   }
 }
 
+// Original tap index of row `row` of the packed weights. Rows are grouped by load unit:
+// unit = (outer taps, t0 unless shifted, t1 unless shifted, t2) row-major, and within a
+// unit the shifted taps (t0 if shift0, t1 if shift1) row-major.
+__device__ __forceinline__ int packed_row_tap(int row, int k0, int k1, int k2, int shift0,
+                                              int shift1) {
+  const int n1 = shift1 ? k1 : 1;
+  const int n0 = shift0 ? k0 : 1;
+  const int ls = row % (n0 * n1);
+  int rest = row / (n0 * n1);
+  const int j1 = ls % n1;
+  const int j0 = ls / n1;
+  const int t2 = rest % k2;
+  rest /= k2;
+  int t1 = j1, t0 = j0;
+  if (!shift1) {
+    t1 = rest % k1;
+    rest /= k1;
+  }
+  if (!shift0) {
+    t0 = rest % k0;
+    rest /= k0;
+  }
+  return ((rest * k0 + t0) * k1 + t1) * k2 + t2;
+}
+
 template <typename T, int kMode>
 __global__ void pack_weight_kernel(const T* __restrict__ w, T* __restrict__ dst,
-                                   T* __restrict__ dst_small, int G, int cout_g, int cin_g,
-                                   int taps, int n_pad, int c_pad, int dgrad) {
-  const int64_t total = static_cast<int64_t>(G) * taps * n_pad * c_pad;
+                                   T* __restrict__ dst_small, PackWeightArgs a) {
+  const int64_t total = static_cast<int64_t>(a.groups) * a.taps * a.n_pad * a.c_pad;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     int64_t r = i;
-    const int c = static_cast<int>(r % c_pad);
-    r /= c_pad;
-    const int nn = static_cast<int>(r % n_pad);
-    r /= n_pad;
-    const int t = static_cast<int>(r % taps);
-    const int g = static_cast<int>(r / taps);
+    const int c = static_cast<int>(r % a.c_pad);
+    r /= a.c_pad;
+    const int nn = static_cast<int>(r % a.n_pad);
+    r /= a.n_pad;
+    const int row = static_cast<int>(r % a.taps);
+    const int g = static_cast<int>(r / a.taps);
+    const int t = packed_row_tap(row, a.k_box[0], a.k_box[1], a.k_box[2], a.shift0, a.shift1);
     float v = 0.0f;
-    if (!dgrad) {
+    if (!a.dgrad) {
       // forward operand: B[n = output channel][k = input channel] of tap t
-      if (nn < cout_g && c < cin_g) {
-        v = to_float(w[((static_cast<int64_t>(g) * cout_g + nn) * cin_g + c) * taps + t]);
+      if (nn < a.cout_g && c < a.cin_g) {
+        v = to_float(w[((static_cast<int64_t>(g) * a.cout_g + nn) * a.cin_g + c) * a.taps + t]);
       }
     } else {
       // dgrad operand: B[n = input channel][k = output channel] of the flipped tap
-      if (nn < cin_g && c < cout_g) {
-        v = to_float(
-            w[((static_cast<int64_t>(g) * cout_g + c) * cin_g + nn) * taps + (taps - 1 - t)]);
+      if (nn < a.cin_g && c < a.cout_g) {
+        v = to_float(w[((static_cast<int64_t>(g) * a.cout_g + c) * a.cin_g + nn) * a.taps +
+                       (a.taps - 1 - t)]);
       }
     }
     if constexpr (kMode == 1) {
@@ -243,17 +268,11 @@ int pack_weight_typed(const PackWeightArgs& a, cudaStream_t stream) {
   T* dst = static_cast<T*>(a.dst);
   T* dst_small = static_cast<T*>(a.dst_small);
   if (a.mode == 1) {
-    pack_weight_kernel<T, 1><<<blocks, 256, 0, stream>>>(w, dst, dst_small, a.groups, a.cout_g,
-                                                          a.cin_g, a.taps, a.n_pad, a.c_pad,
-                                                          a.dgrad);
+    pack_weight_kernel<T, 1><<<blocks, 256, 0, stream>>>(w, dst, dst_small, a);
   } else if (a.mode == 2) {
-    pack_weight_kernel<T, 2><<<blocks, 256, 0, stream>>>(w, dst, dst_small, a.groups, a.cout_g,
-                                                          a.cin_g, a.taps, a.n_pad, a.c_pad,
-                                                          a.dgrad);
+    pack_weight_kernel<T, 2><<<blocks, 256, 0, stream>>>(w, dst, dst_small, a);
   } else {
-    pack_weight_kernel<T, 0><<<blocks, 256, 0, stream>>>(w, dst, dst_small, a.groups, a.cout_g,
-                                                          a.cin_g, a.taps, a.n_pad, a.c_pad,
-                                                          a.dgrad);
+    pack_weight_kernel<T, 0><<<blocks, 256, 0, stream>>>(w, dst, dst_small, a);
   }
   count_launch();
   return CND_OK;

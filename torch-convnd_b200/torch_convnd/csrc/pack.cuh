@@ -19,11 +19,16 @@ struct PackActArgs {
   float* chan_partial;  // optional [batch][groups][pack_blocks(spatial)][cg]
 };
 
+// Weights [groups*cout_g][cin_g][taps] -> [groups][taps][n_pad][c_pad], rows in the
+// convolution pass's load-unit order (k_box = kernel extents of the three box axes,
+// shift0/shift1 = whether the a0 / a1 taps of a unit are served by shared-memory shifts).
 struct PackWeightArgs {
-  const void* w;        // [groups*cout_g][cin_g][taps]
-  void* dst;            // [groups][taps][n_pad][c_pad]
+  const void* w;
+  void* dst;
   void* dst_small;
   int groups, cout_g, cin_g, taps, n_pad, c_pad, dtype, mode, dgrad;
+  int k_box[3];
+  int shift0, shift1;
 };
 
 int pack_activations(const PackActArgs& args, cudaStream_t stream);

@@ -28,8 +28,6 @@ namespace cnd {
 namespace {
 
 constexpr int kThreads = 192;
-constexpr uint32_t kSiteProducer = 0x101, kSiteMma = 0x102, kSiteEpilogue = 0x103,
-                   kSiteDrain = 0x104;
 constexpr uint32_t kSiteWProducer = 0x201, kSiteWMma = 0x202, kSiteWEpilogue = 0x203;
 
 // Per-box bookkeeping, decoded once per tile.
@@ -42,20 +40,6 @@ struct BoxInfo {
   int64_t in_ng_base;            // merged input index of (n, g, outer origin 0)
   int64_t out_merged;            // merged output index (n, g, outer output position)
   int64_t outer_lin;             // linear outer output position (without n)
-};
-
-struct ConvKernelParams {
-  BoxGeom g;
-  int n_real, n_pad, cblocks, cblk_elems, ksteps, row_bytes, layout, stages, debug_stall;
-  uint32_t a_box_bytes, a_bytes, b_bytes, a_small_off, b_off, b_small_off, stage_bytes,
-      tx_bytes, idesc, tmem_cols;
-  void* out;
-  const void* bias;
-  int out_dtype;
-  int64_t out_channels_total;
-  int64_t out_volume;
-  unsigned int* err;
-  uint64_t timeout_ns;
 };
 
 struct WgradKernelParams {
@@ -169,194 +153,6 @@ __device__ __forceinline__ void mma(uint32_t d, uint64_t a, uint64_t b, uint32_t
     dev::mma_tf32(d, a, b, idesc, acc);
   } else {
     dev::mma_f16(d, a, b, idesc, acc);
-  }
-}
-
-// ---------------------------------------------------------------------------------------
-// Forward / dgrad pass kernel. One CTA = one 128-row tile of output positions (nb boxes)
-// of one group, all n_pad output channels.
-template <bool kTF32, bool kSplit>
-__global__ void __launch_bounds__(kThreads, 1)
-    conv_pass_kernel(const __grid_constant__ CUtensorMap act_map,
-                     const __grid_constant__ CUtensorMap act_small_map,
-                     const __grid_constant__ CUtensorMap wt_map,
-                     const __grid_constant__ CUtensorMap wt_small_map,
-                     const __grid_constant__ ConvKernelParams P) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = align1024(smem_raw);
-  uint8_t* stage_base = smem;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + P.stages * P.stage_bytes);
-  uint64_t* empty = full + P.stages;
-  uint64_t* acc_bar = empty + P.stages;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_bar + 1);
-  volatile uint32_t* progress = tmem_slot + 1;
-  BoxInfo* boxes = reinterpret_cast<BoxInfo*>(tmem_slot + 4);
-
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  const int grp = blockIdx.y;
-  const int64_t tile = blockIdx.x;
-  const BoxGeom& g = P.g;
-  const dev::ErrorWord err{P.err};
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < P.stages; ++s) {
-      dev::mbar_init(&full[s], 1);
-      dev::mbar_init(&empty[s], 1);
-    }
-    dev::mbar_init(acc_bar, 1);
-    *progress = 0;
-    dev::fence_barrier_init();
-  }
-  if (warp == 0) {
-    __syncwarp();
-    dev::tmem_alloc(tmem_slot, P.tmem_cols);
-  }
-  if (threadIdx.x >= 64 && threadIdx.x < 64 + g.nb) {
-    const int j = threadIdx.x - 64;
-    decode_box(g, tile * g.nb + j, grp, boxes[j]);
-  }
-  dev::tc_fence_before();
-  __syncthreads();
-  dev::tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-  const int nkb = g.taps * P.cblocks;
-
-  if (warp == 0 && lane == 0) {
-    // ---------------- TMA producer ----------------
-    dev::prefetch_tensormap(&act_map);
-    dev::prefetch_tensormap(&wt_map);
-    int t_o[kMaxOuter] = {0, 0, 0, 0, 0, 0};
-    int t[3] = {0, 0, 0};
-    int stage = 0;
-    uint32_t phase = 0;
-    int issued = 0;
-    bool ok = P.debug_stall == 0;
-    for (int tap = 0; tap < g.taps && ok; ++tap) {
-      int32_t mc[kMaxBoxes];
-      for (int j = 0; j < g.nb; ++j) mc[j] = merged_input(g, boxes[j], t_o);
-      const int32_t w_row = grp * g.taps + tap;
-      for (int cb = 0; cb < P.cblocks; ++cb) {
-        if (!dev::mbar_wait(&empty[stage], phase ^ 1u, err, kSiteProducer, P.timeout_ns)) {
-          ok = false;
-          break;
-        }
-        uint8_t* sb = stage_base + stage * P.stage_bytes;
-        dev::mbar_arrive_expect_tx(&full[stage], P.tx_bytes);
-        const int32_t c0 = cb * P.cblk_elems;
-        for (int j = 0; j < g.nb; ++j) {
-          const int32_t x2 = boxes[j].ib[2] + t[2] * g.d[2];
-          const int32_t x1 = boxes[j].ib[1] + t[1] * g.d[1];
-          const int32_t x0 = boxes[j].ib[0] + t[0] * g.d[0];
-          dev::tma_load_5d(sb + j * P.a_box_bytes, &act_map, &full[stage], c0, x2, x1, x0,
-                           mc[j]);
-          if constexpr (kSplit) {
-            dev::tma_load_5d(sb + P.a_small_off + j * P.a_box_bytes, &act_small_map,
-                             &full[stage], c0, x2, x1, x0, mc[j]);
-          }
-        }
-        dev::tma_load_3d(sb + P.b_off, &wt_map, &full[stage], c0, 0, w_row);
-        if constexpr (kSplit) {
-          dev::tma_load_3d(sb + P.b_small_off, &wt_small_map, &full[stage], c0, 0, w_row);
-        }
-        ++issued;
-        if (++stage == P.stages) {
-          stage = 0;
-          phase ^= 1u;
-        }
-      }
-      next_tap(g, t_o, t);
-    }
-    if (!ok && issued > 0) {
-      // Let loads already in flight land before the CTA's shared memory goes away.
-      const int pending = issued < P.stages ? issued : P.stages;
-      for (int i = 1; i <= pending; ++i) {
-        const int kb = issued - i;
-        dev::mbar_wait(&full[kb % P.stages], static_cast<uint32_t>((kb / P.stages) & 1), err,
-                       kSiteDrain, P.timeout_ns / 8 + 1);
-      }
-    }
-  } else if (warp == 1 && lane == 0) {
-    // ---------------- MMA issuer ----------------
-    int stage = 0;
-    uint32_t phase = 0;
-    const uint32_t sbo = 8u * static_cast<uint32_t>(P.row_bytes);
-    for (int kb = 0; kb < nkb; ++kb) {
-      if (!dev::mbar_wait(&full[stage], phase, err, kSiteMma, P.timeout_ns)) break;
-      dev::tc_fence_after();
-      const uint32_t sb = dev::smem_u32(stage_base + stage * P.stage_bytes);
-      for (int kk = 0; kk < P.ksteps; ++kk) {
-        const uint32_t koff = static_cast<uint32_t>(kk) * 32u;
-        const uint64_t ad = dev::make_smem_desc(sb + koff, 16, sbo, P.layout);
-        const uint64_t bd = dev::make_smem_desc(sb + P.b_off + koff, 16, sbo, P.layout);
-        const uint32_t acc = (kb | kk) != 0 ? 1u : 0u;
-        if constexpr (kSplit) {
-          const uint64_t ads = dev::make_smem_desc(sb + P.a_small_off + koff, 16, sbo, P.layout);
-          const uint64_t bds = dev::make_smem_desc(sb + P.b_small_off + koff, 16, sbo, P.layout);
-          mma<true>(tmem, ads, bd, P.idesc, acc);
-          mma<true>(tmem, ad, bds, P.idesc, 1u);
-          mma<true>(tmem, ad, bd, P.idesc, 1u);
-        } else {
-          mma<kTF32>(tmem, ad, bd, P.idesc, acc);
-        }
-      }
-      dev::mma_commit(&empty[stage]);
-      *progress = static_cast<uint32_t>(kb + 1);
-      if (++stage == P.stages) {
-        stage = 0;
-        phase ^= 1u;
-      }
-    }
-    dev::mma_commit(acc_bar);
-  } else if (warp >= 2) {
-    // ---------------- epilogue ----------------
-    dev::mbar_wait_progress(acc_bar, 0, progress, err, kSiteEpilogue, P.timeout_ns);
-    dev::tc_fence_after();
-    const int quarter = warp & 3;
-    const int row = quarter * 32 + lane;
-    const int j = row / g.box_rows;
-    const int local = row - j * g.box_rows;
-    const int i2 = local % g.b[2];
-    const int i1 = (local / g.b[2]) % g.b[1];
-    const int i0 = local / (g.b[2] * g.b[1]);
-    const BoxInfo& B = boxes[j];
-    const int o0 = B.q[0] * g.b[0] + i0;
-    const int o1 = B.q[1] * g.b[1] + i1;
-    const int o2 = B.q[2] * g.b[2] + i2;
-    const bool valid = B.valid && o0 < g.out[0] && o1 < g.out[1] && o2 < g.out[2];
-    const int64_t sp = B.outer_lin * g.out_box_vol +
-                       (static_cast<int64_t>(o0) * g.out[1] + o1) * g.out[2] + o2;
-    const int64_t base =
-        (static_cast<int64_t>(B.n) * P.out_channels_total + static_cast<int64_t>(grp) * P.n_real) *
-            P.out_volume +
-        sp;
-    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
-    for (int c = 0; c < P.n_pad / 16; ++c) {
-      uint32_t v[16];
-      __syncwarp();
-      dev::tmem_load16(lane_addr + static_cast<uint32_t>(c * 16), v);
-      dev::tmem_load_wait();
-      if (valid) {
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int co = c * 16 + i;
-          if (co < P.n_real) {
-            float value = __uint_as_float(v[i]);
-            if (P.bias != nullptr) {
-              value += load_value(P.bias, static_cast<int64_t>(grp) * P.n_real + co, P.out_dtype);
-            }
-            store_value(P.out, base + static_cast<int64_t>(co) * P.out_volume, value,
-                        P.out_dtype);
-          }
-        }
-      }
-    }
-  }
-  dev::tc_fence_before();
-  __syncthreads();
-  if (warp == 0) {
-    dev::tc_fence_after();
-    dev::tmem_dealloc(tmem, P.tmem_cols);
   }
 }
 
@@ -677,29 +473,6 @@ int encode_act_map(CUtensorMap* map, const void* base, int op, int64_t channels,
   return CND_OK;
 }
 
-// 3-D map over packed weights [rows][n_pad][c_pad], box (cblk, n_pad, 1).
-int encode_weight_map(CUtensorMap* map, const void* base, int op, int64_t c_pad, int64_t n_pad,
-                      int64_t rows, int cblk) {
-  auto encode = tensor_map_encoder();
-  if (encode == nullptr) return fail(CND_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
-  const int64_t es = element_size(op);
-  cuuint64_t dims[3] = {static_cast<cuuint64_t>(c_pad), static_cast<cuuint64_t>(n_pad),
-                        static_cast<cuuint64_t>(rows)};
-  cuuint64_t strides[2] = {static_cast<cuuint64_t>(c_pad * es),
-                           static_cast<cuuint64_t>(c_pad * n_pad * es)};
-  cuuint32_t boxd[3] = {static_cast<cuuint32_t>(cblk), static_cast<cuuint32_t>(n_pad), 1};
-  cuuint32_t estr[3] = {1, 1, 1};
-  const CUresult r = encode(map, map_type(op), 3, const_cast<void*>(base), dims, strides, boxd,
-                            estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                            map_swizzle(static_cast<int>(cblk * es)),
-                            CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) {
-    return fail(CND_ERR_CUDA, "cuTensorMapEncodeTiled (weights) failed with code %d",
-                static_cast<int>(r));
-  }
-  return CND_OK;
-}
-
 // Chooses the box shape (outer->inner) and boxes per tile for `rows` positions per tile.
 bool plan_boxes(const int out[3], const int stride[3], int rows, int* nb_out, int b_out[3]) {
   double best = 1e30;
@@ -848,127 +621,6 @@ int channel_block_bytes(int op, int c_pad) {
 }
 
 }  // namespace
-
-bool conv_pass_supported(const ConvPass& pass) {
-  if (pass.rank < 1 || pass.rank > kMaxFastRank) return false;
-  if (pass.n_pad < 16 || pass.n_pad > 256 || pass.n_pad % 16 != 0) return false;
-  if (channel_block_bytes(pass.op, pass.c_pad) == 0) return false;
-  BoxGeom g;
-  return build_geom(pass.rank, pass.batch, pass.groups, pass.in, pass.out, pass.k, pass.s,
-                    pass.d, pass.p, kTileRows, &g);
-}
-
-int launch_conv_pass(const ConvPass& pass, cudaStream_t stream, uint64_t timeout_ns,
-                     int debug_stall) {
-  ConvKernelParams P;
-  std::memset(&P, 0, sizeof(P));
-  if (!build_geom(pass.rank, pass.batch, pass.groups, pass.in, pass.out, pass.k, pass.s, pass.d,
-                  pass.p, kTileRows, &P.g)) {
-    return fail(CND_ERR_UNSUPPORTED, "geometry outside the tcgen05 path");
-  }
-  const int es = element_size(pass.op);
-  const int row_bytes = channel_block_bytes(pass.op, pass.c_pad);
-  if (row_bytes == 0) return fail(CND_ERR_UNSUPPORTED, "channel count outside the tcgen05 path");
-  const bool tf32 = pass.op == kOpF32;
-  const bool split = tf32 && pass.split3;
-  P.n_real = pass.n_real;
-  P.n_pad = pass.n_pad;
-  P.row_bytes = row_bytes;
-  P.cblk_elems = row_bytes / es;
-  P.cblocks = pass.c_pad / P.cblk_elems;
-  P.ksteps = row_bytes / 32;
-  P.layout = desc_layout(row_bytes);
-  P.debug_stall = debug_stall;
-  P.a_box_bytes = static_cast<uint32_t>(P.g.box_rows * row_bytes);
-  P.a_bytes = P.a_box_bytes * P.g.nb;
-  P.b_bytes = static_cast<uint32_t>(pass.n_pad * row_bytes);
-  const int parts = split ? 2 : 1;
-  P.a_small_off = round_up(P.a_bytes, 1024);
-  P.b_off = round_up(P.a_bytes, 1024) * parts;
-  P.b_small_off = P.b_off + round_up(P.b_bytes, 1024);
-  P.stage_bytes = P.b_off + round_up(P.b_bytes, 1024) * parts;
-  P.tx_bytes = (P.a_bytes + P.b_bytes) * parts;
-  // Two CTAs per SM when the pipeline is at least four stages deep.
-  const uint32_t budget = 100 * 1024;
-  int stages = static_cast<int>(budget / P.stage_bytes);
-  if (stages > 8) stages = 8;
-  if (stages < 4) {
-    stages = static_cast<int>((200 * 1024) / P.stage_bytes);
-    if (stages > 4) stages = 4;
-  }
-  if (stages < 2) return fail(CND_ERR_UNSUPPORTED, "tile does not fit in shared memory");
-  P.stages = stages;
-  P.idesc = make_idesc(pass.op, 128, pass.n_pad, false, false);
-  P.tmem_cols = tmem_columns(pass.n_pad);
-  P.out = pass.dst;
-  P.bias = pass.bias;
-  P.out_dtype = pass.out_dtype;
-  P.out_channels_total = static_cast<int64_t>(pass.groups) * pass.n_real;
-  P.out_volume = 1;
-  for (int a = 0; a < pass.rank; ++a) P.out_volume *= pass.out[a];
-  P.err = device_error_word();
-  P.timeout_ns = timeout_ns;
-
-  const int64_t mtiles = (P.g.boxes_per_group + P.g.nb - 1) / P.g.nb;
-  if (mtiles > 0x7FFFFFFF || pass.groups > 65535) {
-    return fail(CND_ERR_UNSUPPORTED, "grid too large for the tcgen05 path");
-  }
-  if (mtiles == 0) return CND_OK;
-
-  // Packed activation extents: the three box axes and the merged outer dimension.
-  int64_t ext[3];
-  const int n_outer = P.g.n_outer;
-  for (int a = 0; a < 3; ++a) ext[a] = P.g.in[a];
-  const int64_t merged = pass.batch * pass.groups * P.g.in_merged_per_ng;
-  const int box[3] = {P.g.b[0], P.g.b[1], P.g.b[2]};
-  const int strd[3] = {P.g.s[0], P.g.s[1], P.g.s[2]};
-  (void)n_outer;
-  alignas(64) CUtensorMap maps[4];
-  std::memset(maps, 0, sizeof(maps));
-  int rc = encode_act_map(&maps[0], pass.act, pass.op, pass.c_pad, ext, merged, P.cblk_elems, box,
-                          strd);
-  if (rc != CND_OK) return rc;
-  rc = encode_weight_map(&maps[2], pass.wt, pass.op, pass.c_pad, pass.n_pad,
-                         pass.groups * P.g.taps, P.cblk_elems);
-  if (rc != CND_OK) return rc;
-  if (split) {
-    rc = encode_act_map(&maps[1], pass.act_small, pass.op, pass.c_pad, ext, merged, P.cblk_elems,
-                        box, strd);
-    if (rc != CND_OK) return rc;
-    rc = encode_weight_map(&maps[3], pass.wt_small, pass.op, pass.c_pad, pass.n_pad,
-                           pass.groups * P.g.taps, P.cblk_elems);
-    if (rc != CND_OK) return rc;
-  } else {
-    maps[1] = maps[0];
-    maps[3] = maps[2];
-  }
-  const size_t smem = static_cast<size_t>(P.stages) * P.stage_bytes + 1024 +
-                      (2 * P.stages + 1) * 8 + 16 + sizeof(BoxInfo) * kMaxBoxes + 64;
-  const dim3 grid(static_cast<unsigned>(mtiles), static_cast<unsigned>(pass.groups));
-  cudaError_t e;
-  if (split) {
-    auto kernel = conv_pass_kernel<true, true>;
-    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         static_cast<int>(smem));
-    kernel<<<grid, kThreads, smem, stream>>>(maps[0], maps[1], maps[2], maps[3], P);
-  } else if (tf32) {
-    auto kernel = conv_pass_kernel<true, false>;
-    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         static_cast<int>(smem));
-    kernel<<<grid, kThreads, smem, stream>>>(maps[0], maps[1], maps[2], maps[3], P);
-  } else {
-    auto kernel = conv_pass_kernel<false, false>;
-    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         static_cast<int>(smem));
-    kernel<<<grid, kThreads, smem, stream>>>(maps[0], maps[1], maps[2], maps[3], P);
-  }
-  e = cudaGetLastError();
-  if (e != cudaSuccess) {
-    return fail(CND_ERR_CUDA, "conv_pass_kernel launch failed: %s", cudaGetErrorString(e));
-  }
-  count_launch();
-  return CND_OK;
-}
 
 namespace {
 

@@ -55,15 +55,12 @@ struct WgradPass {
   int splits;       // chosen by plan_wgrad
 };
 
-// Returns true when the tcgen05 kernels can run the pass (geometry within TMA limits).
-bool conv_pass_supported(const ConvPass& pass);
+// Returns true when the tcgen05 weight-gradient kernel can run the pass.
 bool wgrad_pass_supported(const WgradPass& pass);
 
 // Number of fp32 partial sets the wgrad kernel will write for this pass.
 int plan_wgrad_splits(const WgradPass& pass, int sm_count);
 
-int launch_conv_pass(const ConvPass& pass, cudaStream_t stream, uint64_t timeout_ns,
-                     int debug_stall);
 int launch_wgrad_pass(const WgradPass& pass, cudaStream_t stream, uint64_t timeout_ns);
 
 }  // namespace cnd
