@@ -83,22 +83,6 @@ __device__ __forceinline__ void decode_super(const FpropParams& P, int64_t st, S
   }
 }
 
-__device__ __forceinline__ void store_value(void* out, int64_t index, float value, int dtype) {
-  if (dtype == CND_BF16) {
-    static_cast<__nv_bfloat16*>(out)[index] = __float2bfloat16_rn(value);
-  } else if (dtype == CND_F16) {
-    static_cast<__half*>(out)[index] = __float2half_rn(value);
-  } else {
-    static_cast<float*>(out)[index] = value;
-  }
-}
-
-__device__ __forceinline__ float load_value(const void* in, int64_t index, int dtype) {
-  if (dtype == CND_BF16) return __bfloat162float(static_cast<const __nv_bfloat16*>(in)[index]);
-  if (dtype == CND_F16) return __half2float(static_cast<const __half*>(in)[index]);
-  return static_cast<const float*>(in)[index];
-}
-
 template <bool kTF32>
 __device__ __forceinline__ void mma(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc,
                                     uint32_t acc) {
@@ -109,9 +93,52 @@ __device__ __forceinline__ void mma(uint32_t d, uint64_t a, uint64_t b, uint32_t
   }
 }
 
-template <bool kTF32, int kParts>
+// Operand kinds of the kernel instantiations: the element type of activations, weights
+// and output, and whether float32 runs as one or three TF32 products.
+enum KernelOp { kKindF16 = 0, kKindBF16 = 1, kKindTF32 = 2, kKind3xTF32 = 3 };
+
+template <int kOp>
+struct OpTraits;
+template <>
+struct OpTraits<kKindF16> {
+  using Out = __half;
+  static constexpr bool tf32 = false;
+  static constexpr int parts = 1;
+  static __device__ __forceinline__ Out cast(float v) { return __float2half_rn(v); }
+  static __device__ __forceinline__ float load(const Out* p) { return __half2float(*p); }
+};
+template <>
+struct OpTraits<kKindBF16> {
+  using Out = __nv_bfloat16;
+  static constexpr bool tf32 = false;
+  static constexpr int parts = 1;
+  static __device__ __forceinline__ Out cast(float v) { return __float2bfloat16_rn(v); }
+  static __device__ __forceinline__ float load(const Out* p) { return __bfloat162float(*p); }
+};
+template <>
+struct OpTraits<kKindTF32> {
+  using Out = float;
+  static constexpr bool tf32 = true;
+  static constexpr int parts = 1;
+  static __device__ __forceinline__ Out cast(float v) { return v; }
+  static __device__ __forceinline__ float load(const Out* p) { return *p; }
+};
+template <>
+struct OpTraits<kKind3xTF32> {
+  using Out = float;
+  static constexpr bool tf32 = true;
+  static constexpr int parts = 2;
+  static __device__ __forceinline__ Out cast(float v) { return v; }
+  static __device__ __forceinline__ float load(const Out* p) { return *p; }
+};
+
+template <int kOp, int kKSteps>
 __global__ void __launch_bounds__(kThreads, 1)
     fprop_kernel(const __grid_constant__ FpropMaps maps, const __grid_constant__ FpropParams P) {
+  using Traits = OpTraits<kOp>;
+  using OutT = typename Traits::Out;
+  constexpr bool kTF32 = Traits::tf32;
+  constexpr int kParts = Traits::parts;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + P.stages * P.stage_bytes);
@@ -254,11 +281,23 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1 && lane == 0) {
     // ------------------------------ MMA issuer ------------------------------
+    // Descriptors differ only in their start-address field (bits 0-13, address >> 4):
+    // build the constant part once and add offsets in 16-byte units. Shared memory is
+    // below 256 KB, so the field never carries into the next one.
+    const uint64_t desc_hi =
+        dev::make_smem_desc(0, 16, 8u * static_cast<uint32_t>(P.row_bytes), P.layout);
+    const uint32_t row_units = static_cast<uint32_t>(P.row_bytes) >> 4;
+    const uint32_t tile_units = static_cast<uint32_t>(P.e0 * P.h1 * P.b2) * row_units;
+    const uint32_t j0_units = static_cast<uint32_t>(P.d[0] * P.h1 * P.b2) * row_units;
+    const uint32_t j1_units = static_cast<uint32_t>(P.d[1] * P.b2) * row_units;
+    const uint32_t btap_units = static_cast<uint32_t>(P.n_pad) * row_units;
+    const uint32_t a_small_units = P.a_part_bytes >> 4;
+    const uint32_t b_small_units = P.b_part_bytes >> 4;
+    const uint32_t tile_cols = static_cast<uint32_t>(P.n_pad);
+    const uint32_t acc_cols = static_cast<uint32_t>(P.mt * P.n_pad);
     int stage = 0;
     uint32_t phase = 0;
     uint32_t done = 0;
-    const uint32_t sbo = 8u * static_cast<uint32_t>(P.row_bytes);
-    const uint32_t b_tap_bytes = static_cast<uint32_t>(P.n_pad * P.row_bytes);
     int iter = 0;
     bool ok = true;
     for (int64_t st = blockIdx.x; st < P.supers_total && ok; st += gridDim.x, ++iter) {
@@ -269,39 +308,36 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       dev::tc_fence_after();
       const uint32_t dbase = tmem + static_cast<uint32_t>(buf * P.acc_stride);
+      int w = 0;  // work item (unit, shifted tap) within the super tile
       for (int u = 0; u < P.units && ok; ++u) {
+        const int w_unit = w;
         for (int cb = 0; cb < P.cblocks; ++cb) {
           if (!dev::mbar_wait(&full[stage], phase, err, kSiteMma, P.timeout_ns)) {
             ok = false;
             break;
           }
           dev::tc_fence_after();
-          const uint32_t sa = dev::smem_u32(smem + stage * P.stage_bytes);
-          const uint32_t sbw = sa + P.b_off;
+          const uint32_t sa = dev::smem_u32(smem + stage * P.stage_bytes) >> 4;
+          const uint32_t sbw = sa + (P.b_off >> 4);
+          int wi = w_unit;
           for (int j0 = 0; j0 < P.nshift0; ++j0) {
-            for (int j1 = 0; j1 < P.nshift1; ++j1) {
-              const int ls = j0 * P.nshift1 + j1;
-              const int w = u * nshift + ls;
-              const int acc_index = w % P.nacc;
-              const bool first_use = w < P.nacc && cb == 0;
-              const uint32_t b_addr = sbw + static_cast<uint32_t>(ls) * b_tap_bytes;
-              for (int m = 0; m < P.mt; ++m) {
-                const int row = ((m * P.e0 + j0 * P.d[0]) * P.h1 + j1 * P.d[1]) * P.b2;
-                const uint32_t a_addr = sa + static_cast<uint32_t>(row * P.row_bytes);
-                const uint32_t d =
-                    dbase + static_cast<uint32_t>((acc_index * P.mt + m) * P.n_pad);
-                for (int kk = 0; kk < P.ksteps; ++kk) {
-                  const uint32_t koff = static_cast<uint32_t>(kk) * 32u;
-                  const uint64_t ad = dev::make_smem_desc(a_addr + koff, 16, sbo, P.layout);
-                  const uint64_t bd = dev::make_smem_desc(b_addr + koff, 16, sbo, P.layout);
-                  const uint32_t acc = (first_use && kk == 0) ? 0u : 1u;
+            for (int j1 = 0; j1 < P.nshift1; ++j1, ++wi) {
+              const int acc_index = wi % P.nacc;
+              const uint32_t first = (wi < P.nacc && cb == 0) ? 1u : 0u;
+              const uint32_t b_addr =
+                  sbw + static_cast<uint32_t>(j0 * P.nshift1 + j1) * btap_units;
+              uint32_t a_addr = sa + static_cast<uint32_t>(j0) * j0_units +
+                                static_cast<uint32_t>(j1) * j1_units;
+              uint32_t d = dbase + static_cast<uint32_t>(acc_index) * acc_cols;
+              for (int m = 0; m < P.mt; ++m, a_addr += tile_units, d += tile_cols) {
+#pragma unroll
+                for (int kk = 0; kk < kKSteps; ++kk) {
+                  const uint64_t ad = desc_hi | (a_addr + 2u * kk);
+                  const uint64_t bd = desc_hi | (b_addr + 2u * kk);
+                  const uint32_t acc = (first != 0u && kk == 0) ? 0u : 1u;
                   if constexpr (kParts == 2) {
-                    const uint64_t ads =
-                        dev::make_smem_desc(a_addr + P.a_part_bytes + koff, 16, sbo, P.layout);
-                    const uint64_t bds =
-                        dev::make_smem_desc(b_addr + P.b_part_bytes + koff, 16, sbo, P.layout);
-                    mma<true>(d, ads, bd, P.idesc, acc);
-                    mma<true>(d, ad, bds, P.idesc, 1u);
+                    mma<true>(d, desc_hi | (a_addr + a_small_units + 2u * kk), bd, P.idesc, acc);
+                    mma<true>(d, ad, desc_hi | (b_addr + b_small_units + 2u * kk), P.idesc, 1u);
                     mma<true>(d, ad, bd, P.idesc, 1u);
                   } else {
                     mma<kTF32>(d, ad, bd, P.idesc, acc);
@@ -317,6 +353,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             phase ^= 1u;
           }
         }
+        w += P.nshift0 * P.nshift1;
       }
       dev::mma_commit(&acc_full[buf]);
     }
@@ -329,6 +366,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int i0 = row / (P.b2 * P.b1);
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
     const int used = work_per_super < P.nacc ? work_per_super : P.nacc;
+    const OutT* bias = static_cast<const OutT*>(P.bias);
+    OutT* out = static_cast<OutT*>(P.dst);
     int iter = 0;
     for (int64_t st = blockIdx.x; st < P.supers_total; st += gridDim.x, ++iter) {
       const int buf = iter & 1;
@@ -342,19 +381,28 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int o2 = S.q2 * P.b2 + i2;
       const int64_t channel_base =
           (S.n * P.out_channels_total + static_cast<int64_t>(S.g) * P.n_real) * P.out_volume;
+      const OutT* group_bias = bias != nullptr ? bias + static_cast<int64_t>(S.g) * P.n_real : nullptr;
       for (int m = 0; m < P.mt; ++m) {
         const int o0 = (S.q0 * P.mt + m) * P.e0 + i0;
         const bool valid = o0 < P.out[0] && o1 < P.out[1] && o2 < P.out[2];
         const int64_t sp = S.outer_lin * P.out_box_vol +
                            (static_cast<int64_t>(o0) * P.out[1] + o1) * P.out[2] + o2;
+        OutT* dst = out + channel_base + sp;
         for (int c = 0; c < P.n_pad / 16; ++c) {
           float sum[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i) sum[i] = 0.0f;
-          for (int a = 0; a < used; ++a) {
+          {
             uint32_t v[16];
             __syncwarp();
-            dev::tmem_load16(dbase + static_cast<uint32_t>((a * P.mt + m) * P.n_pad + c * 16), v);
+            dev::tmem_load16(dbase + static_cast<uint32_t>(m * P.n_pad + c * 16), v);
+            dev::tmem_load_wait();
+#pragma unroll
+            for (int i = 0; i < 16; ++i) sum[i] = __uint_as_float(v[i]);
+          }
+          for (int a = 1; a < used; ++a) {
+            uint32_t v[16];
+            __syncwarp();
+            dev::tmem_load16(
+                dbase + static_cast<uint32_t>((a * P.mt + m) * P.n_pad + c * 16), v);
             dev::tmem_load_wait();
 #pragma unroll
             for (int i = 0; i < 16; ++i) sum[i] += __uint_as_float(v[i]);
@@ -365,12 +413,8 @@ __global__ void __launch_bounds__(kThreads, 1)
               const int co = c * 16 + i;
               if (co < P.n_real) {
                 float value = sum[i];
-                if (P.bias != nullptr) {
-                  value += load_value(P.bias, static_cast<int64_t>(S.g) * P.n_real + co,
-                                      P.out_dtype);
-                }
-                store_value(P.dst, channel_base + static_cast<int64_t>(co) * P.out_volume + sp,
-                            value, P.out_dtype);
+                if (group_bias != nullptr) value += Traits::load(group_bias + co);
+                dst[static_cast<int64_t>(co) * P.out_volume] = Traits::cast(value);
               }
             }
           }
@@ -725,23 +769,22 @@ int launch_fprop(const ConvPass& pass, const FpropPlan& plan_in, cudaStream_t st
   int64_t grid = P.supers_total;
   const int64_t resident = static_cast<int64_t>(device_sms()) * (two_per_sm ? 2 : 1);
   if (grid > resident) grid = resident;
-  const bool tf32 = pass.op == kOpF32;
-  if (plan.parts == 2) {
-    auto kernel = fprop_kernel<true, 2>;
-    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         static_cast<int>(smem));
-    kernel<<<static_cast<unsigned>(grid), kThreads, smem, stream>>>(maps, P);
-  } else if (tf32) {
-    auto kernel = fprop_kernel<true, 1>;
-    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         static_cast<int>(smem));
-    kernel<<<static_cast<unsigned>(grid), kThreads, smem, stream>>>(maps, P);
-  } else {
-    auto kernel = fprop_kernel<false, 1>;
-    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         static_cast<int>(smem));
-    kernel<<<static_cast<unsigned>(grid), kThreads, smem, stream>>>(maps, P);
-  }
+  using Kernel = void (*)(FpropMaps, FpropParams);
+  Kernel kernel = nullptr;
+  const int kind = pass.op == kOpF16 ? kKindF16
+                   : pass.op == kOpBF16 ? kKindBF16
+                   : (plan.parts == 2 ? kKind3xTF32 : kKindTF32);
+#define CND_FPROP_CASE(KIND, KSTEPS) \
+  if (kind == KIND && P.ksteps == KSTEPS) kernel = fprop_kernel<KIND, KSTEPS>;
+  CND_FPROP_CASE(kKindF16, 1) CND_FPROP_CASE(kKindF16, 2) CND_FPROP_CASE(kKindF16, 4)
+  CND_FPROP_CASE(kKindBF16, 1) CND_FPROP_CASE(kKindBF16, 2) CND_FPROP_CASE(kKindBF16, 4)
+  CND_FPROP_CASE(kKindTF32, 1) CND_FPROP_CASE(kKindTF32, 2) CND_FPROP_CASE(kKindTF32, 4)
+  CND_FPROP_CASE(kKind3xTF32, 1) CND_FPROP_CASE(kKind3xTF32, 2) CND_FPROP_CASE(kKind3xTF32, 4)
+#undef CND_FPROP_CASE
+  if (kernel == nullptr) return fail(CND_ERR_UNSUPPORTED, "no fprop kernel for this operand");
+  cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       static_cast<int>(smem));
+  kernel<<<static_cast<unsigned>(grid), kThreads, smem, stream>>>(maps, P);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     return fail(CND_ERR_CUDA, "fprop_kernel launch failed: %s", cudaGetErrorString(e));

@@ -77,10 +77,15 @@ __device__ void decode_box(const BoxGeom& g, int64_t bt, int grp, BoxInfo& info)
   info.n = static_cast<int32_t>(n);
   info.outer_lin = outer_lin;
   int64_t o = outer_lin;
-  for (int a = g.n_outer - 1; a >= 0; --a) {
-    const int64_t coord = o % g.out_o[a];
-    o /= g.out_o[a];
-    info.ib_o[a] = static_cast<int32_t>(coord * g.s_o[a] - g.p_o[a]);
+#pragma unroll
+  for (int a = kMaxOuter - 1; a >= 0; --a) {
+    if (a < g.n_outer) {
+      const int64_t coord = o % g.out_o[a];
+      o /= g.out_o[a];
+      info.ib_o[a] = static_cast<int32_t>(coord * g.s_o[a] - g.p_o[a]);
+    } else {
+      info.ib_o[a] = 0;
+    }
   }
   for (int a = 0; a < 3; ++a) {
     info.ib[a] = info.q[a] * g.b[a] * g.s[a] - g.p[a];
@@ -93,14 +98,17 @@ __device__ void decode_box(const BoxGeom& g, int64_t bt, int grp, BoxInfo& info)
 // falls into the zero padding (TMA then fills the whole box with zeros).
 __device__ __forceinline__ int32_t merged_input(const BoxGeom& g, const BoxInfo& info,
                                                 const int* t_o) {
-  if (!info.valid) return -1;
+  bool valid = info.valid != 0;
   int64_t m = info.in_ng_base;
-  for (int a = 0; a < g.n_outer; ++a) {
-    const int c = info.ib_o[a] + t_o[a] * g.d_o[a];
-    if (c < 0 || c >= g.in_o[a]) return -1;
-    m += static_cast<int64_t>(c) * g.in_o_stride[a];
+#pragma unroll
+  for (int a = 0; a < kMaxOuter; ++a) {
+    if (a < g.n_outer) {
+      const int c = info.ib_o[a] + t_o[a] * g.d_o[a];
+      valid = valid && c >= 0 && c < g.in_o[a];
+      m += static_cast<int64_t>(c) * g.in_o_stride[a];
+    }
   }
-  return static_cast<int32_t>(m);
+  return valid ? static_cast<int32_t>(m) : -1;
 }
 
 // Advances a row-major tap odometer (outer axes, then the three box axes).
@@ -111,9 +119,16 @@ __device__ __forceinline__ void next_tap(const BoxGeom& g, int* t_o, int* t) {
   t[1] = 0;
   if (++t[0] < g.k[0]) return;
   t[0] = 0;
-  for (int a = g.n_outer - 1; a >= 0; --a) {
-    if (++t_o[a] < g.k_o[a]) return;
-    t_o[a] = 0;
+  bool carry = true;
+#pragma unroll
+  for (int a = kMaxOuter - 1; a >= 0; --a) {
+    if (carry && a < g.n_outer) {
+      if (++t_o[a] < g.k_o[a]) {
+        carry = false;
+      } else {
+        t_o[a] = 0;
+      }
+    }
   }
 }
 
@@ -124,9 +139,14 @@ __device__ __forceinline__ void set_tap(const BoxGeom& g, int tap, int* t_o, int
   tap /= g.k[1];
   t[0] = tap % g.k[0];
   tap /= g.k[0];
-  for (int a = g.n_outer - 1; a >= 0; --a) {
-    t_o[a] = tap % g.k_o[a];
-    tap /= g.k_o[a];
+#pragma unroll
+  for (int a = kMaxOuter - 1; a >= 0; --a) {
+    if (a < g.n_outer) {
+      t_o[a] = tap % g.k_o[a];
+      tap /= g.k_o[a];
+    } else {
+      t_o[a] = 0;
+    }
   }
 }
 
@@ -203,6 +223,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* acc_bar = a_empty + P.a_stages;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_bar + 1);
   volatile uint32_t* progress = tmem_slot + 1;
+  BoxInfo* boxes = reinterpret_cast<BoxInfo*>(tmem_slot + 4);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -247,7 +268,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     int a_stage = 0, b_slot = 0;
     uint32_t a_phase = 0, b_phase = 0;
     bool ok = true;
-    BoxInfo boxes[kMaxBoxes];
     for (int64_t pt = p_begin; pt < p_end && ok; ++pt) {
       for (int j = 0; j < g.nb; ++j) decode_box(g, pt * g.nb + j, grp, boxes[j]);
       // Output-gradient tile (B operand), shared by every tap tile of this CTA.
@@ -314,33 +334,34 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------- MMA issuer ----------------
     int a_stage = 0, b_slot = 0;
     uint32_t a_phase = 0, b_phase = 0;
-    const uint32_t k_rows = 16u;
-    const uint32_t a_sbo = 8u * P.a_row_bytes;
-    const uint32_t b_sbo = 8u * P.b_row_bytes;
-    const uint32_t b_lbo = static_cast<uint32_t>(P.kc_rows) * 128u;
+    // Constant descriptor parts; per MMA only the start-address field (address >> 4)
+    // changes, and it never carries (shared memory is below 256 KB).
+    const uint64_t a_hi = dev::make_smem_desc(0, P.a_tile_bytes, 8u * P.a_row_bytes, P.a_layout);
+    const uint64_t b_hi = dev::make_smem_desc(0, static_cast<uint32_t>(P.kc_rows) * 128u,
+                                              8u * P.b_row_bytes, P.b_layout);
+    const uint32_t a_step = (16u * P.a_row_bytes) >> 4;  // one K step = 16 positions
+    const uint32_t b_step = (16u * P.b_row_bytes) >> 4;
+    const uint32_t a_part = P.a_part_bytes >> 4;
+    const uint32_t b_part = P.b_part_bytes >> 4;
     bool ok = true;
     for (int64_t pt = p_begin; pt < p_end && ok; ++pt) {
       if (!dev::mbar_wait(&b_full[b_slot], b_phase, err, kSiteWMma, P.timeout_ns)) break;
-      const uint32_t bs = dev::smem_u32(b_base + b_slot * P.b_slot_bytes);
+      const uint32_t bs = dev::smem_u32(b_base + b_slot * P.b_slot_bytes) >> 4;
       for (int mt = 0; mt < mt_count; ++mt) {
         if (!dev::mbar_wait(&a_full[a_stage], a_phase, err, kSiteWMma, P.timeout_ns)) {
           ok = false;
           break;
         }
         dev::tc_fence_after();
-        const uint32_t as = dev::smem_u32(a_base + a_stage * P.a_slot_bytes);
+        const uint32_t as = dev::smem_u32(a_base + a_stage * P.a_slot_bytes) >> 4;
         const uint32_t d = tmem + static_cast<uint32_t>(mt * P.n_pad);
         for (int ks = 0; ks < P.ksteps; ++ks) {
-          const uint32_t aoff = static_cast<uint32_t>(ks) * k_rows * P.a_row_bytes;
-          const uint32_t boff = static_cast<uint32_t>(ks) * k_rows * P.b_row_bytes;
+          const uint32_t aoff = as + static_cast<uint32_t>(ks) * a_step;
+          const uint32_t boff = bs + static_cast<uint32_t>(ks) * b_step;
 #pragma unroll
           for (int q = 0; q < product_count<kParts>(); ++q) {
-            const uint64_t ad =
-                dev::make_smem_desc(as + product_a(kParts, q) * P.a_part_bytes + aoff,
-                                    P.a_tile_bytes, a_sbo, P.a_layout);
-            const uint64_t bd =
-                dev::make_smem_desc(bs + product_b(kParts, q) * P.b_part_bytes + boff, b_lbo,
-                                    b_sbo, P.b_layout);
+            const uint64_t ad = a_hi | (aoff + product_a(kParts, q) * a_part);
+            const uint64_t bd = b_hi | (boff + product_b(kParts, q) * b_part);
             const uint32_t acc = (pt != p_begin || ks != 0 || q != 0) ? 1u : 0u;
             dev::mma_f16(d, ad, bd, P.idesc, acc);
           }
@@ -707,7 +728,7 @@ bool plan_wgrad(const WgradPass& pass, int splits_hint, WgradPlan* plan) {
     splits = static_cast<int>(s);
   }
   P.splits = splits;
-  plan->smem = P.bar_off + (4 + 2 * stages + 1) * 8 + 16 + 1024;
+  plan->smem = P.bar_off + (4 + 2 * stages + 1) * 8 + 16 + sizeof(BoxInfo) * kMaxBoxes + 1024;
   return true;
 }
 
