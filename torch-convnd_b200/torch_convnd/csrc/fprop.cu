@@ -279,8 +279,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                        kSiteDrain, P.timeout_ns / 8 + 1);
       }
     }
-  } else if (warp == 1 && lane == 0) {
+  } else if (warp == 1) {
     // ------------------------------ MMA issuer ------------------------------
+    // The whole warp runs the loop and waits; one elected lane issues the MMAs and
+    // commits (tcgen05.mma from a converged warp issues at the operand-bandwidth rate).
+    const bool leader = dev::elect_one();
     // Descriptors differ only in their start-address field (bits 0-13, address >> 4):
     // build the constant part once and add offsets in 16-byte units. Shared memory is
     // below 256 KB, so the field never carries into the next one.
@@ -329,25 +332,33 @@ __global__ void __launch_bounds__(kThreads, 1)
               uint32_t a_addr = sa + static_cast<uint32_t>(j0) * j0_units +
                                 static_cast<uint32_t>(j1) * j1_units;
               uint32_t d = dbase + static_cast<uint32_t>(acc_index) * acc_cols;
-              for (int m = 0; m < P.mt; ++m, a_addr += tile_units, d += tile_cols) {
+              if (leader) {
+                for (int m = 0; m < P.mt; ++m, a_addr += tile_units, d += tile_cols) {
 #pragma unroll
-                for (int kk = 0; kk < kKSteps; ++kk) {
-                  const uint64_t ad = desc_hi | (a_addr + 2u * kk);
-                  const uint64_t bd = desc_hi | (b_addr + 2u * kk);
-                  const uint32_t acc = (first != 0u && kk == 0) ? 0u : 1u;
-                  if constexpr (kParts == 2) {
-                    mma<true>(d, desc_hi | (a_addr + a_small_units + 2u * kk), bd, P.idesc, acc);
-                    mma<true>(d, ad, desc_hi | (b_addr + b_small_units + 2u * kk), P.idesc, 1u);
-                    mma<true>(d, ad, bd, P.idesc, 1u);
-                  } else {
-                    mma<kTF32>(d, ad, bd, P.idesc, acc);
+                  for (int kk = 0; kk < kKSteps; ++kk) {
+                    const uint64_t ad = desc_hi | (a_addr + 2u * kk);
+                    const uint64_t bd = desc_hi | (b_addr + 2u * kk);
+                    const uint32_t acc = (first != 0u && kk == 0) ? 0u : 1u;
+                    if constexpr (kParts == 2) {
+                      mma<true>(d, desc_hi | (a_addr + a_small_units + 2u * kk), bd, P.idesc,
+                                acc);
+                      mma<true>(d, ad, desc_hi | (b_addr + b_small_units + 2u * kk), P.idesc,
+                                1u);
+                      mma<true>(d, ad, bd, P.idesc, 1u);
+                    } else {
+                      mma<kTF32>(d, ad, bd, P.idesc, acc);
+                    }
                   }
                 }
               }
+              __syncwarp();
             }
           }
-          dev::mma_commit(&empty[stage]);
-          *progress = ++done;
+          if (leader) {
+            dev::mma_commit(&empty[stage]);
+            *progress = ++done;
+          }
+          __syncwarp();
           if (++stage == P.stages) {
             stage = 0;
             phase ^= 1u;
@@ -355,7 +366,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         w += P.nshift0 * P.nshift1;
       }
-      dev::mma_commit(&acc_full[buf]);
+      if (leader) dev::mma_commit(&acc_full[buf]);
+      __syncwarp();
     }
   } else if (warp >= 2) {
     // ------------------------------ epilogue ------------------------------

@@ -49,10 +49,26 @@ struct WgradKernelParams {
   uint32_t a_tile_bytes, a_part_bytes, a_slot_bytes, b_part_bytes, b_slot_bytes, a_tx, b_tx,
       idesc, tmem_cols, a_base_off, bar_off;
   int64_t ptiles;
+  int outer_combos;  // product of the outer axes' kernel extents (<= 64)
   float* partial;
   unsigned int* err;
   uint64_t timeout_ns;
 };
+
+// One kernel tap of a weight-gradient CTA: offsets along the three box axes, the index
+// of its outer-axis tap combination and that combination's merged-coordinate delta.
+struct TapEntry {
+  int32_t dx0, dx1, dx2;
+  int32_t outer;
+  int32_t delta;
+};
+
+// Offsets (t * dilation) of one outer-axis tap combination.
+struct OuterCombo {
+  int32_t off[kMaxOuter];
+};
+
+constexpr int kMaxOuterCombos = 64;
 
 __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
   const uintptr_t v = reinterpret_cast<uintptr_t>(p);
@@ -92,88 +108,6 @@ __device__ void decode_box(const BoxGeom& g, int64_t bt, int grp, BoxInfo& info)
   }
   info.in_ng_base = (n * g.groups + grp) * g.in_merged_per_ng;
   info.out_merged = (n * g.groups + grp) * g.out_outer_vol + outer_lin;
-}
-
-// Merged input coordinate of a box for the outer taps t_o, or -1 when any outer axis
-// falls into the zero padding (TMA then fills the whole box with zeros).
-__device__ __forceinline__ int32_t merged_input(const BoxGeom& g, const BoxInfo& info,
-                                                const int* t_o) {
-  bool valid = info.valid != 0;
-  int64_t m = info.in_ng_base;
-#pragma unroll
-  for (int a = 0; a < kMaxOuter; ++a) {
-    if (a < g.n_outer) {
-      const int c = info.ib_o[a] + t_o[a] * g.d_o[a];
-      valid = valid && c >= 0 && c < g.in_o[a];
-      m += static_cast<int64_t>(c) * g.in_o_stride[a];
-    }
-  }
-  return valid ? static_cast<int32_t>(m) : -1;
-}
-
-// Advances a row-major tap odometer (outer axes, then the three box axes).
-__device__ __forceinline__ void next_tap(const BoxGeom& g, int* t_o, int* t) {
-  if (++t[2] < g.k[2]) return;
-  t[2] = 0;
-  if (++t[1] < g.k[1]) return;
-  t[1] = 0;
-  if (++t[0] < g.k[0]) return;
-  t[0] = 0;
-  bool carry = true;
-#pragma unroll
-  for (int a = kMaxOuter - 1; a >= 0; --a) {
-    if (carry && a < g.n_outer) {
-      if (++t_o[a] < g.k_o[a]) {
-        carry = false;
-      } else {
-        t_o[a] = 0;
-      }
-    }
-  }
-}
-
-__device__ __forceinline__ void set_tap(const BoxGeom& g, int tap, int* t_o, int* t) {
-  t[2] = tap % g.k[2];
-  tap /= g.k[2];
-  t[1] = tap % g.k[1];
-  tap /= g.k[1];
-  t[0] = tap % g.k[0];
-  tap /= g.k[0];
-#pragma unroll
-  for (int a = kMaxOuter - 1; a >= 0; --a) {
-    if (a < g.n_outer) {
-      t_o[a] = tap % g.k_o[a];
-      tap /= g.k_o[a];
-    } else {
-      t_o[a] = 0;
-    }
-  }
-}
-
-__device__ __forceinline__ void store_value(void* out, int64_t index, float value, int dtype) {
-  if (dtype == CND_BF16) {
-    static_cast<__nv_bfloat16*>(out)[index] = __float2bfloat16_rn(value);
-  } else if (dtype == CND_F16) {
-    static_cast<__half*>(out)[index] = __float2half_rn(value);
-  } else {
-    static_cast<float*>(out)[index] = value;
-  }
-}
-
-__device__ __forceinline__ float load_value(const void* in, int64_t index, int dtype) {
-  if (dtype == CND_BF16) return __bfloat162float(static_cast<const __nv_bfloat16*>(in)[index]);
-  if (dtype == CND_F16) return __half2float(static_cast<const __half*>(in)[index]);
-  return static_cast<const float*>(in)[index];
-}
-
-template <bool kTF32>
-__device__ __forceinline__ void mma(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc,
-                                    uint32_t acc) {
-  if constexpr (kTF32) {
-    dev::mma_tf32(d, a, b, idesc, acc);
-  } else {
-    dev::mma_f16(d, a, b, idesc, acc);
-  }
 }
 
 // ---------------------------------------------------------------------------------------
@@ -224,6 +158,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_bar + 1);
   volatile uint32_t* progress = tmem_slot + 1;
   BoxInfo* boxes = reinterpret_cast<BoxInfo*>(tmem_slot + 4);
+  uint64_t* box_mask = reinterpret_cast<uint64_t*>(boxes + kMaxBoxes);
+  OuterCombo* combos = reinterpret_cast<OuterCombo*>(box_mask + kMaxBoxes);
+  TapEntry* taps = reinterpret_cast<TapEntry*>(combos + kMaxOuterCombos);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -236,6 +173,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int64_t p_end = P.ptiles * (split + 1) / P.splits;
   const int mt_first = chunk * P.mt_per_cta;
   const int mt_count = min(P.mt_per_cta, P.mt_total - mt_first);
+  const int tap_first = mt_first * P.tpm;
+  const int tap_count = mt_count * P.tpm;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < 2; ++s) {
@@ -254,6 +193,49 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
     dev::tmem_alloc(tmem_slot, P.tmem_cols);
   }
+  // Tables of this CTA's taps and of the outer-axis tap combinations (epilogue warps,
+  // which are idle until the main loop ends).
+  if (warp >= 2) {
+    const int t = threadIdx.x - 64;
+    for (int c = t; c < P.outer_combos; c += 128) {
+      int rest = c;
+#pragma unroll
+      for (int a = kMaxOuter - 1; a >= 0; --a) {
+        if (a < g.n_outer) {
+          combos[c].off[a] = (rest % g.k_o[a]) * g.d_o[a];
+          rest /= g.k_o[a];
+        } else {
+          combos[c].off[a] = 0;
+        }
+      }
+    }
+    for (int i = t; i < tap_count; i += 128) {
+      const int tap = tap_first + i;
+      TapEntry e{0, 0, 0, 0, 0};
+      if (tap < g.taps) {
+        int rest = tap;
+        e.dx2 = (rest % g.k[2]) * g.d[2];
+        rest /= g.k[2];
+        e.dx1 = (rest % g.k[1]) * g.d[1];
+        rest /= g.k[1];
+        e.dx0 = (rest % g.k[0]) * g.d[0];
+        rest /= g.k[0];
+        e.outer = rest;  // row-major index over the outer tap axes
+        int64_t delta = 0;
+#pragma unroll
+        for (int a = kMaxOuter - 1; a >= 0; --a) {
+          if (a < g.n_outer) {
+            delta += static_cast<int64_t>(rest % g.k_o[a]) * g.d_o[a] * g.in_o_stride[a];
+            rest /= g.k_o[a];
+          }
+        }
+        e.delta = static_cast<int32_t>(delta);
+      } else {
+        e.outer = -1;  // padding slot of the last M tile: loads read zeros
+      }
+      taps[i] = e;
+    }
+  }
   dev::tc_fence_before();
   __syncthreads();
   dev::tc_fence_after();
@@ -269,7 +251,34 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t a_phase = 0, b_phase = 0;
     bool ok = true;
     for (int64_t pt = p_begin; pt < p_end && ok; ++pt) {
-      for (int j = 0; j < g.nb; ++j) decode_box(g, pt * g.nb + j, grp, boxes[j]);
+      // Boxes of this position tile and, per box, which outer tap combinations stay
+      // inside the input (bit c of box_mask).
+      for (int j = 0; j < g.nb; ++j) {
+        BoxInfo& B = boxes[j];
+        decode_box(g, pt * g.nb + j, grp, B);
+        uint64_t mask = 0;
+        if (B.valid) {
+          for (int c = 0; c < P.outer_combos; ++c) {
+            bool inside = true;
+#pragma unroll
+            for (int a = 0; a < kMaxOuter; ++a) {
+              if (a < g.n_outer) {
+                const int coord = B.ib_o[a] + combos[c].off[a];
+                inside = inside && coord >= 0 && coord < g.in_o[a];
+              }
+            }
+            if (inside) mask |= uint64_t{1} << c;
+          }
+        }
+        box_mask[j] = mask;
+        // merged base: input index of (n, g) plus the outer origins of tap 0
+        int64_t base = B.in_ng_base;
+#pragma unroll
+        for (int a = 0; a < kMaxOuter; ++a) {
+          if (a < g.n_outer) base += static_cast<int64_t>(B.ib_o[a]) * g.in_o_stride[a];
+        }
+        B.in_ng_base = base;
+      }
       // Output-gradient tile (B operand), shared by every tap tile of this CTA.
       if (!dev::mbar_wait(&b_empty[b_slot], b_phase ^ 1u, err, kSiteWProducer, P.timeout_ns)) {
         ok = false;
@@ -295,11 +304,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         b_slot = 0;
         b_phase ^= 1u;
       }
-      // Activation tiles: tpm taps per M tile.
-      int t_o[kMaxOuter] = {0, 0, 0, 0, 0, 0};
-      int t[3] = {0, 0, 0};
-      int tap = mt_first * P.tpm;
-      if (tap < g.taps) set_tap(g, tap, t_o, t);
+      // Activation tiles: tpm taps per M tile, coordinates from the tap table.
+      int ti = 0;
       for (int mt = 0; mt < mt_count && ok; ++mt) {
         if (!dev::mbar_wait(&a_empty[a_stage], a_phase ^ 1u, err, kSiteWProducer,
                             P.timeout_ns)) {
@@ -308,20 +314,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         uint8_t* as = a_base + a_stage * P.a_slot_bytes;
         dev::mbar_arrive_expect_tx(&a_full[a_stage], P.a_tx);
-        for (int jt = 0; jt < P.tpm; ++jt, ++tap) {
-          const bool real_tap = tap < g.taps;
+        for (int jt = 0; jt < P.tpm; ++jt, ++ti) {
+          const TapEntry e = taps[ti];
           for (int j = 0; j < g.nb; ++j) {
-            const int32_t mc = real_tap ? merged_input(g, boxes[j], t_o) : -1;
-            const int32_t x2 = boxes[j].ib[2] + t[2] * g.d[2];
-            const int32_t x1 = boxes[j].ib[1] + t[1] * g.d[1];
-            const int32_t x0 = boxes[j].ib[0] + t[0] * g.d[0];
+            const BoxInfo& B = boxes[j];
+            const bool inside = e.outer >= 0 && ((box_mask[j] >> e.outer) & 1u);
+            const int32_t mc = inside ? static_cast<int32_t>(B.in_ng_base + e.delta) : -1;
             uint8_t* dst = as + jt * P.a_tile_bytes + j * g.box_rows * P.a_row_bytes;
             for (int part = 0; part < kParts; ++part) {
               dev::tma_load_5d(dst + part * P.a_part_bytes, &maps.act[part], &a_full[a_stage], 0,
-                               x2, x1, x0, mc);
+                               B.ib[2] + e.dx2, B.ib[1] + e.dx1, B.ib[0] + e.dx0, mc);
             }
           }
-          if (real_tap) next_tap(g, t_o, t);
         }
         if (++a_stage == P.a_stages) {
           a_stage = 0;
@@ -330,8 +334,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     (void)ok;
-  } else if (warp == 1 && lane == 0) {
-    // ---------------- MMA issuer ----------------
+  } else if (warp == 1) {
+    // ---------------- MMA issuer (converged warp, one elected lane issues) ----------------
+    const bool leader = dev::elect_one();
     int a_stage = 0, b_slot = 0;
     uint32_t a_phase = 0, b_phase = 0;
     // Constant descriptor parts; per MMA only the start-address field (address >> 4)
@@ -347,39 +352,47 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int64_t pt = p_begin; pt < p_end && ok; ++pt) {
       if (!dev::mbar_wait(&b_full[b_slot], b_phase, err, kSiteWMma, P.timeout_ns)) break;
       const uint32_t bs = dev::smem_u32(b_base + b_slot * P.b_slot_bytes) >> 4;
+      const uint32_t first_tile = pt == p_begin ? 1u : 0u;
       for (int mt = 0; mt < mt_count; ++mt) {
         if (!dev::mbar_wait(&a_full[a_stage], a_phase, err, kSiteWMma, P.timeout_ns)) {
           ok = false;
           break;
         }
         dev::tc_fence_after();
-        const uint32_t as = dev::smem_u32(a_base + a_stage * P.a_slot_bytes) >> 4;
-        const uint32_t d = tmem + static_cast<uint32_t>(mt * P.n_pad);
-        for (int ks = 0; ks < P.ksteps; ++ks) {
-          const uint32_t aoff = as + static_cast<uint32_t>(ks) * a_step;
-          const uint32_t boff = bs + static_cast<uint32_t>(ks) * b_step;
+        if (leader) {
+          const uint32_t as = dev::smem_u32(a_base + a_stage * P.a_slot_bytes) >> 4;
+          const uint32_t d = tmem + static_cast<uint32_t>(mt * P.n_pad);
+          for (int ks = 0; ks < P.ksteps; ++ks) {
+            const uint32_t aoff = as + static_cast<uint32_t>(ks) * a_step;
+            const uint32_t boff = bs + static_cast<uint32_t>(ks) * b_step;
 #pragma unroll
-          for (int q = 0; q < product_count<kParts>(); ++q) {
-            const uint64_t ad = a_hi | (aoff + product_a(kParts, q) * a_part);
-            const uint64_t bd = b_hi | (boff + product_b(kParts, q) * b_part);
-            const uint32_t acc = (pt != p_begin || ks != 0 || q != 0) ? 1u : 0u;
-            dev::mma_f16(d, ad, bd, P.idesc, acc);
+            for (int q = 0; q < product_count<kParts>(); ++q) {
+              const uint64_t ad = a_hi | (aoff + product_a(kParts, q) * a_part);
+              const uint64_t bd = b_hi | (boff + product_b(kParts, q) * b_part);
+              const uint32_t acc = (first_tile != 0u && ks == 0 && q == 0) ? 0u : 1u;
+              dev::mma_f16(d, ad, bd, P.idesc, acc);
+            }
           }
+          dev::mma_commit(&a_empty[a_stage]);
         }
-        dev::mma_commit(&a_empty[a_stage]);
+        __syncwarp();
         if (++a_stage == P.a_stages) {
           a_stage = 0;
           a_phase ^= 1u;
         }
       }
-      dev::mma_commit(&b_empty[b_slot]);
-      *progress = static_cast<uint32_t>(pt - p_begin + 1);
+      if (leader) {
+        dev::mma_commit(&b_empty[b_slot]);
+        *progress = static_cast<uint32_t>(pt - p_begin + 1);
+      }
+      __syncwarp();
       if (++b_slot == 2) {
         b_slot = 0;
         b_phase ^= 1u;
       }
     }
-    dev::mma_commit(acc_bar);
+    if (leader) dev::mma_commit(acc_bar);
+    __syncwarp();
   } else if (warp >= 2) {
     // ---------------- epilogue: TMEM -> fp32 partial ----------------
     dev::mbar_wait_progress(acc_bar, 0, progress, err, kSiteWEpilogue, P.timeout_ns);
@@ -711,6 +724,10 @@ bool plan_wgrad(const WgradPass& pass, int splits_hint, WgradPlan* plan) {
   P.a_stages = stages;
   P.a_base_off = 2 * P.b_slot_bytes;
   P.bar_off = P.a_base_off + stages * P.a_slot_bytes;
+  int64_t combos = 1;
+  for (int a = 0; a < P.g.n_outer; ++a) combos *= P.g.k_o[a];
+  if (combos > kMaxOuterCombos) return false;
+  P.outer_combos = static_cast<int>(combos);
   P.mt_total = (P.g.taps + P.tpm - 1) / P.tpm;
   P.mt_per_cta = 512 / pass.n_pad;
   if (P.mt_per_cta > P.mt_total) P.mt_per_cta = P.mt_total;
@@ -728,7 +745,10 @@ bool plan_wgrad(const WgradPass& pass, int splits_hint, WgradPlan* plan) {
     splits = static_cast<int>(s);
   }
   P.splits = splits;
-  plan->smem = P.bar_off + (4 + 2 * stages + 1) * 8 + 16 + sizeof(BoxInfo) * kMaxBoxes + 1024;
+  plan->smem = P.bar_off + (4 + 2 * stages + 1) * 8 + 16 +
+               (sizeof(BoxInfo) + sizeof(uint64_t)) * kMaxBoxes +
+               sizeof(OuterCombo) * kMaxOuterCombos +
+               sizeof(TapEntry) * static_cast<size_t>(P.mt_per_cta) * P.tpm + 1024;
   return true;
 }
 
