@@ -44,6 +44,11 @@ struct BoxInfo {
 
 struct WgradKernelParams {
   BoxGeom g;
+  // A load unit is one A slot: tpm separate tap tiles (halo == 0), or one halo box along
+  // a1 holding all k1 taps of a (outer, t0, t2) combination, read as mtpu M tiles whose
+  // atoms sit d1*b2 rows apart (halo == 1).
+  int halo, mtpu, units_total, units_per_cta, entries_per_unit;
+  uint32_t atom_bytes;  // LBO of the A operand: distance between the stacked taps
   int c_pad, cin_real, n_pad, n_real, tpm, mt_per_cta, mt_total, splits, kc_rows, ksteps;
   int a_row_bytes, a_layout, b_row_bytes, b_layout, b_blocks, b_blk_elems, a_stages;
   uint32_t a_tile_bytes, a_part_bytes, a_slot_bytes, b_part_bytes, b_slot_bytes, a_tx, b_tx,
@@ -171,10 +176,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const dev::ErrorWord err{P.err};
   const int64_t p_begin = P.ptiles * split / P.splits;
   const int64_t p_end = P.ptiles * (split + 1) / P.splits;
-  const int mt_first = chunk * P.mt_per_cta;
-  const int mt_count = min(P.mt_per_cta, P.mt_total - mt_first);
-  const int tap_first = mt_first * P.tpm;
-  const int tap_count = mt_count * P.tpm;
+  const int unit_first = chunk * P.units_per_cta;
+  const int unit_count = min(P.units_per_cta, P.units_total - unit_first);
+  const int entry_count = unit_count * P.entries_per_unit;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < 2; ++s) {
@@ -209,8 +213,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-    for (int i = t; i < tap_count; i += 128) {
-      const int tap = tap_first + i;
+    for (int i = t; i < entry_count; i += 128) {
+      // Non-halo: entry = one tap. Halo: entry = one unit, i.e. a (outer, t0, t2)
+      // combination whose k1 taps along a1 share one box (t1 = 0 here).
+      int tap;
+      if (P.halo) {
+        const int unit = unit_first + i;
+        const int t2 = unit % g.k[2];
+        const int rest = unit / g.k[2];  // (outer, t0) row-major
+        tap = (rest * g.k[1]) * g.k[2] + t2;
+      } else {
+        tap = unit_first * P.tpm + i;
+      }
       TapEntry e{0, 0, 0, 0, 0};
       if (tap < g.taps) {
         int rest = tap;
@@ -304,9 +318,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         b_slot = 0;
         b_phase ^= 1u;
       }
-      // Activation tiles: tpm taps per M tile, coordinates from the tap table.
+      // Activation units, coordinates from the tap table.
       int ti = 0;
-      for (int mt = 0; mt < mt_count && ok; ++mt) {
+      for (int unit = 0; unit < unit_count && ok; ++unit) {
         if (!dev::mbar_wait(&a_empty[a_stage], a_phase ^ 1u, err, kSiteWProducer,
                             P.timeout_ns)) {
           ok = false;
@@ -314,7 +328,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         uint8_t* as = a_base + a_stage * P.a_slot_bytes;
         dev::mbar_arrive_expect_tx(&a_full[a_stage], P.a_tx);
-        for (int jt = 0; jt < P.tpm; ++jt, ++ti) {
+        for (int jt = 0; jt < P.entries_per_unit; ++jt, ++ti) {
           const TapEntry e = taps[ti];
           for (int j = 0; j < g.nb; ++j) {
             const BoxInfo& B = boxes[j];
@@ -341,7 +355,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t a_phase = 0, b_phase = 0;
     // Constant descriptor parts; per MMA only the start-address field (address >> 4)
     // changes, and it never carries (shared memory is below 256 KB).
-    const uint64_t a_hi = dev::make_smem_desc(0, P.a_tile_bytes, 8u * P.a_row_bytes, P.a_layout);
+    const uint64_t a_hi = dev::make_smem_desc(0, P.atom_bytes, 8u * P.a_row_bytes, P.a_layout);
+    const uint32_t group_units = (static_cast<uint32_t>(P.tpm) * P.atom_bytes) >> 4;
     const uint64_t b_hi = dev::make_smem_desc(0, static_cast<uint32_t>(P.kc_rows) * 128u,
                                               8u * P.b_row_bytes, P.b_layout);
     const uint32_t a_step = (16u * P.a_row_bytes) >> 4;  // one K step = 16 positions
@@ -353,7 +368,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!dev::mbar_wait(&b_full[b_slot], b_phase, err, kSiteWMma, P.timeout_ns)) break;
       const uint32_t bs = dev::smem_u32(b_base + b_slot * P.b_slot_bytes) >> 4;
       const uint32_t first_tile = pt == p_begin ? 1u : 0u;
-      for (int mt = 0; mt < mt_count; ++mt) {
+      for (int unit = 0; unit < unit_count; ++unit) {
         if (!dev::mbar_wait(&a_full[a_stage], a_phase, err, kSiteWMma, P.timeout_ns)) {
           ok = false;
           break;
@@ -361,16 +376,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         dev::tc_fence_after();
         if (leader) {
           const uint32_t as = dev::smem_u32(a_base + a_stage * P.a_slot_bytes) >> 4;
-          const uint32_t d = tmem + static_cast<uint32_t>(mt * P.n_pad);
-          for (int ks = 0; ks < P.ksteps; ++ks) {
-            const uint32_t aoff = as + static_cast<uint32_t>(ks) * a_step;
-            const uint32_t boff = bs + static_cast<uint32_t>(ks) * b_step;
+          for (int gi = 0; gi < P.mtpu; ++gi) {
+            const uint32_t d =
+                tmem + static_cast<uint32_t>((unit * P.mtpu + gi) * P.n_pad);
+            const uint32_t ag = as + static_cast<uint32_t>(gi) * group_units;
+            for (int ks = 0; ks < P.ksteps; ++ks) {
+              const uint32_t aoff = ag + static_cast<uint32_t>(ks) * a_step;
+              const uint32_t boff = bs + static_cast<uint32_t>(ks) * b_step;
 #pragma unroll
-            for (int q = 0; q < product_count<kParts>(); ++q) {
-              const uint64_t ad = a_hi | (aoff + product_a(kParts, q) * a_part);
-              const uint64_t bd = b_hi | (boff + product_b(kParts, q) * b_part);
-              const uint32_t acc = (first_tile != 0u && ks == 0 && q == 0) ? 0u : 1u;
-              dev::mma_f16(d, ad, bd, P.idesc, acc);
+              for (int q = 0; q < product_count<kParts>(); ++q) {
+                const uint64_t ad = a_hi | (aoff + product_a(kParts, q) * a_part);
+                const uint64_t bd = b_hi | (boff + product_b(kParts, q) * b_part);
+                const uint32_t acc = (first_tile != 0u && ks == 0 && q == 0) ? 0u : 1u;
+                dev::mma_f16(d, ad, bd, P.idesc, acc);
+              }
             }
           }
           dev::mma_commit(&a_empty[a_stage]);
@@ -403,9 +422,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int ci = row - jt * P.c_pad;
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
     const bool empty_range = p_begin >= p_end;
+    const int mt_count = unit_count * P.mtpu;
     for (int mt = 0; mt < mt_count; ++mt) {
-      const int tap = (mt_first + mt) * P.tpm + jt;
-      const bool valid = tap < g.taps && ci < P.cin_real;
+      int tap;
+      bool valid;
+      if (P.halo) {
+        const int unit = unit_first + mt / P.mtpu;
+        const int t1 = (mt % P.mtpu) * P.tpm + jt;
+        const int t2 = unit % g.k[2];
+        const int rest = unit / g.k[2];
+        tap = (rest * g.k[1] + t1) * g.k[2] + t2;
+        valid = t1 < g.k[1] && ci < P.cin_real;
+      } else {
+        tap = (unit_first + mt) * P.tpm + jt;
+        valid = tap < g.taps && ci < P.cin_real;
+      }
       float* dst = P.partial +
                    ((((static_cast<int64_t>(split) * g.groups + grp) * g.taps + tap) *
                          P.cin_real +
@@ -546,7 +577,7 @@ bool plan_boxes(const int out[3], const int stride[3], int rows, int* nb_out, in
 // BoxGeom; `rows` is the number of positions per tile.
 bool build_geom(int rank, int64_t batch, int64_t groups, const int64_t* in, const int64_t* out,
                 const int64_t* k, const int64_t* s, const int64_t* d, const int64_t* p, int rows,
-                BoxGeom* g) {
+                BoxGeom* g, const int* forced_box = nullptr) {
   std::memset(g, 0, sizeof(*g));
   if (rank < 1 || rank > kMaxFastRank) return false;
   const int n_outer = rank > 3 ? rank - 3 : 0;
@@ -600,7 +631,12 @@ bool build_geom(int rank, int64_t batch, int64_t groups, const int64_t* in, cons
   // Merged TMA coordinates are int32.
   if (batch * groups * in_vol > limit || batch * groups * out_vol > limit) return false;
   int nb = 0, b[3] = {0, 0, 0};
-  if (!plan_boxes(g->out, g->s, rows, &nb, b)) return false;
+  if (forced_box != nullptr) {
+    nb = 1;
+    for (int a = 0; a < 3; ++a) b[a] = forced_box[a];
+  } else if (!plan_boxes(g->out, g->s, rows, &nb, b)) {
+    return false;
+  }
   g->nb = nb;
   g->box_rows = rows / nb;
   for (int a = 0; a < 3; ++a) {
@@ -663,6 +699,7 @@ struct WgradPlan {
   size_t smem;
   int chunks;
   int parts;
+  int halo_rows;  // box rows along a1 in halo mode
 };
 
 bool plan_wgrad(const WgradPass& pass, int splits_hint, WgradPlan* plan) {
@@ -695,31 +732,93 @@ bool plan_wgrad(const WgradPass& pass, int splits_hint, WgradPlan* plan) {
   P.b_layout = static_cast<int>(desc_layout(b_row));
   P.b_blocks = b_row_full / b_row;
   P.b_blk_elems = b_row / es;
-  // Position rows per K chunk: 128, or 64 when the 128-row slots do not fit twice.
-  int kc = 128;
-  for (;;) {
-    const uint32_t a_tile = static_cast<uint32_t>(kc * a_row);
-    const uint32_t a_slot = round_up(a_tile * P.tpm, 1024) * parts;
-    const uint32_t b_slot = round_up(static_cast<uint32_t>(kc * b_row_full), 1024) * parts;
-    if (2 * a_slot + 2 * b_slot <= 200 * 1024 || kc == 64) break;
-    kc = 64;
+  // Kernel extent, stride and dilation of box axis a1 (the second-to-last spatial axis).
+  const int a1 = pass.rank >= 2 ? pass.rank - 2 : -1;
+  const int k1 = a1 >= 0 ? static_cast<int>(pass.k[a1]) : 1;
+  const int64_t s1 = a1 >= 0 ? pass.s[a1] : 1;
+  const int64_t d1 = a1 >= 0 ? pass.d[a1] : 1;
+  const int64_t o1 = a1 >= 0 ? pass.out[a1] : 1;
+  const int64_t o2 = pass.out[pass.rank - 1];
+  const int mtpu = (k1 + P.tpm - 1) / P.tpm;
+  const bool halo_ok = k1 >= 2 && s1 == 1 && d1 <= 16 &&
+                       static_cast<double>(k1) / (mtpu * P.tpm) >= 0.6;
+  bool planned = false;
+  if (halo_ok) {
+    // Position tile [1, b1, b2] with b2 a power of two >= 8 (8-row alignment of every
+    // tap window), least padding waste first.
+    for (int kc : {128, 64}) {
+      double best_waste = 1e30;
+      int best_b2 = 0;
+      for (int b2 = 8; b2 <= kc; b2 *= 2) {
+        const int b1 = kc / b2;
+        const double waste = double((o1 + b1 - 1) / b1 * b1) / o1 *
+                             double((o2 + b2 - 1) / b2 * b2) / o2;
+        if (waste < best_waste - 1e-9) {
+          best_waste = waste;
+          best_b2 = b2;
+        }
+      }
+      const int b2 = best_b2;
+      const int b1 = kc / b2;
+      const int h1 = b1 + (mtpu * P.tpm - 1) * static_cast<int>(d1);
+      if (h1 > 256) continue;
+      const uint32_t rows = static_cast<uint32_t>(h1 * b2);
+      const uint32_t a_part = round_up(rows * a_row, 1024);
+      const uint32_t b_part = round_up(static_cast<uint32_t>(kc * b_row_full), 1024);
+      if (2 * b_part * parts + 3 * a_part * parts > 208 * 1024) continue;
+      const int box[3] = {1, b1, b2};
+      if (!build_geom(pass.rank, pass.batch, pass.groups, pass.in, pass.out, pass.k, pass.s,
+                      pass.d, pass.p, kc, &P.g, box)) {
+        continue;
+      }
+      P.halo = 1;
+      P.mtpu = mtpu;
+      P.kc_rows = kc;
+      P.a_part_bytes = a_part;
+      P.a_tx = rows * a_row * parts;
+      P.atom_bytes = static_cast<uint32_t>(d1 * b2 * a_row);
+      P.units_total = P.g.taps / k1;
+      P.entries_per_unit = 1;
+      plan->halo_rows = h1;
+      planned = true;
+      break;
+    }
   }
-  P.kc_rows = kc;
+  if (!planned) {
+    // Position rows per K chunk: 128, or 64 when the 128-row slots do not fit twice.
+    int kc = 128;
+    for (;;) {
+      const uint32_t a_tile = static_cast<uint32_t>(kc * a_row);
+      const uint32_t a_slot = round_up(a_tile * P.tpm, 1024) * parts;
+      const uint32_t b_slot = round_up(static_cast<uint32_t>(kc * b_row_full), 1024) * parts;
+      if (2 * a_slot + 2 * b_slot <= 200 * 1024 || kc == 64) break;
+      kc = 64;
+    }
+    if (!build_geom(pass.rank, pass.batch, pass.groups, pass.in, pass.out, pass.k, pass.s,
+                    pass.d, pass.p, kc, &P.g)) {
+      return false;
+    }
+    P.halo = 0;
+    P.mtpu = 1;
+    P.kc_rows = kc;
+    P.a_tile_bytes = static_cast<uint32_t>(kc * a_row);
+    P.a_part_bytes = round_up(P.a_tile_bytes * P.tpm, 1024);
+    P.a_tx = P.a_tile_bytes * P.tpm * parts;
+    P.atom_bytes = P.a_tile_bytes;
+    P.units_total = (P.g.taps + P.tpm - 1) / P.tpm;
+    P.entries_per_unit = P.tpm;
+    plan->halo_rows = 0;
+  }
+  const int kc = P.kc_rows;
   P.ksteps = kc / 16;
-  if (!build_geom(pass.rank, pass.batch, pass.groups, pass.in, pass.out, pass.k, pass.s, pass.d,
-                  pass.p, kc, &P.g)) {
-    return false;
-  }
   P.a_tile_bytes = static_cast<uint32_t>(kc * a_row);
-  P.a_part_bytes = round_up(P.a_tile_bytes * P.tpm, 1024);
   P.a_slot_bytes = P.a_part_bytes * parts;
   P.b_part_bytes = round_up(static_cast<uint32_t>(kc * b_row_full), 1024);
   P.b_slot_bytes = P.b_part_bytes * parts;
-  P.a_tx = P.a_tile_bytes * P.tpm * parts;
   P.b_tx = static_cast<uint32_t>(kc * b_row_full) * parts;
   if (2 * P.b_slot_bytes + 2 * P.a_slot_bytes > 208 * 1024) return false;
   int stages = static_cast<int>((208 * 1024 - 2 * P.b_slot_bytes) / P.a_slot_bytes);
-  if (stages > 6) stages = 6;
+  if (stages > 12) stages = 12;
   if (stages < 2) return false;
   P.a_stages = stages;
   P.a_base_off = 2 * P.b_slot_bytes;
@@ -728,10 +827,12 @@ bool plan_wgrad(const WgradPass& pass, int splits_hint, WgradPlan* plan) {
   for (int a = 0; a < P.g.n_outer; ++a) combos *= P.g.k_o[a];
   if (combos > kMaxOuterCombos) return false;
   P.outer_combos = static_cast<int>(combos);
-  P.mt_total = (P.g.taps + P.tpm - 1) / P.tpm;
-  P.mt_per_cta = 512 / pass.n_pad;
-  if (P.mt_per_cta > P.mt_total) P.mt_per_cta = P.mt_total;
-  plan->chunks = (P.mt_total + P.mt_per_cta - 1) / P.mt_per_cta;
+  P.mt_total = P.units_total * P.mtpu;
+  const int max_units = (512 / pass.n_pad) / P.mtpu;
+  if (max_units < 1) return false;
+  plan->chunks = (P.units_total + max_units - 1) / max_units;
+  P.units_per_cta = (P.units_total + plan->chunks - 1) / plan->chunks;
+  P.mt_per_cta = P.units_per_cta * P.mtpu;
   P.tmem_cols = tmem_columns(P.mt_per_cta * pass.n_pad);
   P.idesc = make_idesc(pass.op, 128, pass.n_pad, true, true);
   plan->parts = parts;
@@ -748,7 +849,8 @@ bool plan_wgrad(const WgradPass& pass, int splits_hint, WgradPlan* plan) {
   plan->smem = P.bar_off + (4 + 2 * stages + 1) * 8 + 16 +
                (sizeof(BoxInfo) + sizeof(uint64_t)) * kMaxBoxes +
                sizeof(OuterCombo) * kMaxOuterCombos +
-               sizeof(TapEntry) * static_cast<size_t>(P.mt_per_cta) * P.tpm + 1024;
+               sizeof(TapEntry) * static_cast<size_t>(P.units_per_cta) * P.entries_per_unit +
+               1024;
   return true;
 }
 
@@ -790,10 +892,16 @@ int launch_wgrad_pass(const WgradPass& pass, cudaStream_t stream, uint64_t timeo
   const int ones[3] = {1, 1, 1};
   alignas(64) WgradMaps maps;
   std::memset(&maps, 0, sizeof(maps));
+  int act_box[3] = {box[0], box[1], box[2]};
+  int act_strd[3] = {strd[0], strd[1], strd[2]};
+  if (P.halo) {
+    act_box[1] = plan.halo_rows;
+    act_strd[1] = 1;
+  }
   for (int part = 0; part < 3; ++part) {
     const int source = part < plan.parts ? part : 0;
     int rc = encode_act_map(&maps.act[part], pass.act[source], pass.op, pass.c_pad, ext_in,
-                            merged_in, pass.c_pad, box, strd);
+                            merged_in, pass.c_pad, act_box, act_strd);
     if (rc != CND_OK) return rc;
     rc = encode_act_map(&maps.grad[part], pass.grad[source], pass.op, pass.n_pad, ext_out,
                         merged_out, P.b_blk_elems, box, ones);
