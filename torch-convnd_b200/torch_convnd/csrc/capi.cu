@@ -282,7 +282,8 @@ void make_plan(const cnd_problem& p, bool forward, const int32_t* mask, Plan* pl
     if (plan->split3) plan->dy_cl_small = take(&cursor, bytes);
   }
   if ((plan->fast_dgrad || plan->fast_wgrad) && mask[2]) {
-    const size_t blocks = static_cast<size_t>(pack_blocks(p.output_volume));
+    // Upper bound of the partial count (the generic pack uses the smallest blocks).
+    const size_t blocks = static_cast<size_t>((p.output_volume + 63) / 64);
     plan->bias_partial = take(&cursor, static_cast<size_t>(p.batch * p.groups) * blocks *
                                            plan->cout_g * sizeof(float));
   }
@@ -495,7 +496,7 @@ int cnd_backward(const cnd_problem* problem, const void* dy, const void* x, cons
   }
   int rc = CND_OK;
   const bool f32 = p.dtype == CND_F32;
-  const int blocks = static_cast<int>(pack_blocks(p.output_volume));
+  int blocks = 0;  // bias-gradient partials per (n, g), set by the pack that makes them
   float* bias_partial = static_cast<float*>(at(workspace, plan.bias_partial));
   bool bias_from_pack = false;
   if (plan.dy_cl.bytes > 0) {
@@ -512,6 +513,7 @@ int cnd_backward(const cnd_problem* problem, const void* dy, const void* x, cons
     pa.mode = plan.pack_mode;
     pa.chan_partial = output_mask[2] ? bias_partial : nullptr;
     bias_from_pack = output_mask[2] != 0;
+    if (bias_from_pack) blocks = static_cast<int>(pack_blocks(pa));
     TimedPass timed(4, stream);
     rc = pack_activations(pa, stream);
     if (rc != CND_OK) return rc;
@@ -553,6 +555,7 @@ int cnd_backward(const cnd_problem* problem, const void* dy, const void* x, cons
         if (output_mask[2] && !bias_from_pack) {
           pa.chan_partial = bias_partial;
           bias_from_pack = true;
+          blocks = static_cast<int>(pack_blocks(pa));
         }
         TimedPass timed(4, stream);
         rc = pack_activations(pa, stream);

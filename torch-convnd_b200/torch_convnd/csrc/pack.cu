@@ -145,6 +145,62 @@ __device__ __forceinline__ int packed_row_tap(int row, int k0, int k1, int k2, i
   return ((rest * k0 + t0) * k1 + t1) * k2 + t2;
 }
 
+// Fast path for 16-bit activations without splitting (bf16/fp16 problems): 128 positions
+// per block, 16-byte loads of 8 consecutive positions of one channel and 16-byte stores of
+// 8 consecutive channels of one position, through a [c_pad][128] shared tile.
+// Requirements (checked by the host): c_pad a multiple of 8 and <= 64, S % 8 == 0.
+constexpr int kFastPositions = 128;
+
+template <typename T>
+__global__ void __launch_bounds__(256) pack_act16_kernel(const T* __restrict__ src,
+                                                         T* __restrict__ dst, int64_t S, int Cg,
+                                                         int c_pad, int G,
+                                                         float* __restrict__ chan_partial) {
+  __shared__ __align__(16) uint16_t tile[64][kFastPositions + 8];
+  const int64_t s0 = static_cast<int64_t>(blockIdx.x) * kFastPositions;
+  const int g = blockIdx.y;
+  const int64_t n = blockIdx.z;
+  const uint16_t* in = reinterpret_cast<const uint16_t*>(src) + (n * G + g) * Cg * S;
+  const int count = static_cast<int>(S - s0 < kFastPositions ? S - s0 : kFastPositions);
+  // Load: (channel, 8-position vector) pairs.
+  for (int i = threadIdx.x; i < c_pad * (kFastPositions / 8); i += blockDim.x) {
+    const int c = i >> 4;
+    const int v = i & 15;
+    uint4 value = make_uint4(0, 0, 0, 0);
+    if (c < Cg && v * 8 < count) value = *reinterpret_cast<const uint4*>(in + c * S + s0 + v * 8);
+    *reinterpret_cast<uint4*>(&tile[c][v * 8]) = value;
+  }
+  __syncthreads();
+  // Store: (position, 8-channel vector) pairs.
+  const int vectors = c_pad >> 3;
+  uint16_t* out = reinterpret_cast<uint16_t*>(dst) + ((n * G + g) * S + s0) * c_pad;
+  for (int i = threadIdx.x; i < count * vectors; i += blockDim.x) {
+    const int p = i / vectors;
+    const int k = i - p * vectors;
+    uint16_t lane[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) lane[j] = tile[k * 8 + j][p];
+    uint4 value;
+    value.x = lane[0] | (static_cast<uint32_t>(lane[1]) << 16);
+    value.y = lane[2] | (static_cast<uint32_t>(lane[3]) << 16);
+    value.z = lane[4] | (static_cast<uint32_t>(lane[5]) << 16);
+    value.w = lane[6] | (static_cast<uint32_t>(lane[7]) << 16);
+    *reinterpret_cast<uint4*>(out + static_cast<int64_t>(p) * c_pad + k * 8) = value;
+  }
+  if (chan_partial != nullptr) {
+    // Per-channel sum of this block's positions, in position order.
+    for (int c = threadIdx.x; c < Cg; c += blockDim.x) {
+      float sum = 0.0f;
+      for (int p = 0; p < count; ++p) {
+        T v;
+        *reinterpret_cast<uint16_t*>(&v) = tile[c][p];
+        sum += to_float(v);
+      }
+      chan_partial[((n * G + g) * gridDim.x + blockIdx.x) * Cg + c] = sum;
+    }
+  }
+}
+
 template <typename T, int kMode>
 __global__ void pack_weight_kernel(const T* __restrict__ w, T* __restrict__ dst,
                                    T* __restrict__ dst_small, PackWeightArgs a) {
@@ -280,9 +336,32 @@ int pack_weight_typed(const PackWeightArgs& a, cudaStream_t stream) {
 
 }  // namespace
 
+template <typename T>
+int launch_pack_act16(const PackActArgs& a, cudaStream_t stream) {
+  const int64_t blocks = (a.spatial + kFastPositions - 1) / kFastPositions;
+  const dim3 grid(static_cast<unsigned>(blocks), static_cast<unsigned>(a.groups),
+                  static_cast<unsigned>(a.batch));
+  pack_act16_kernel<T><<<grid, 256, 0, stream>>>(static_cast<const T*>(a.src),
+                                                 static_cast<T*>(a.dst), a.spatial, a.cg,
+                                                 a.c_pad, static_cast<int>(a.groups),
+                                                 a.chan_partial);
+  count_launch();
+  return CND_OK;
+}
+
+bool pack16_fast_ok(const PackActArgs& a) {
+  return a.mode == 0 && a.c_pad % 8 == 0 && a.c_pad <= 64 && a.spatial % 8 == 0 &&
+         (a.spatial + kFastPositions - 1) / kFastPositions <= 0x7FFFFFFF && a.groups <= 65535 &&
+         a.batch <= 65535 && reinterpret_cast<uintptr_t>(a.src) % 16 == 0 &&
+         reinterpret_cast<uintptr_t>(a.dst) % 16 == 0;
+}
+
 int pack_activations(const PackActArgs& args, cudaStream_t stream) {
   int rc;
-  if (args.dtype == CND_BF16) {
+  if ((args.dtype == CND_BF16 || args.dtype == CND_F16) && pack16_fast_ok(args)) {
+    rc = args.dtype == CND_BF16 ? launch_pack_act16<__nv_bfloat16>(args, stream)
+                                : launch_pack_act16<__half>(args, stream);
+  } else if (args.dtype == CND_BF16) {
     rc = launch_pack_act<__nv_bfloat16, __nv_bfloat16, 0>(args, stream);
   } else if (args.dtype == CND_F16) {
     rc = launch_pack_act<__half, __half, 0>(args, stream);
@@ -370,6 +449,11 @@ int reduce_bias(const float* partial, int64_t batch, int groups, int blocks, int
   return CND_OK;
 }
 
-int64_t pack_blocks(int64_t spatial) { return (spatial + kPackPositions - 1) / kPackPositions; }
+int64_t pack_blocks(const PackActArgs& args) {
+  if ((args.dtype == CND_BF16 || args.dtype == CND_F16) && pack16_fast_ok(args)) {
+    return (args.spatial + kFastPositions - 1) / kFastPositions;
+  }
+  return (args.spatial + kPackPositions - 1) / kPackPositions;
+}
 
 }  // namespace cnd

@@ -37,6 +37,8 @@ int reduce_wgrad(const float* partial, int splits, int groups, int taps, int cin
                  void* dw, int dtype, cudaStream_t stream);
 int reduce_bias(const float* partial, int64_t batch, int groups, int blocks, int cg, void* db,
                 int dtype, cudaStream_t stream);
-int64_t pack_blocks(int64_t spatial);
+// Number of position blocks (and so of bias-gradient partials per (n, g)) the activation
+// pack of `args` produces.
+int64_t pack_blocks(const PackActArgs& args);
 
 }  // namespace cnd

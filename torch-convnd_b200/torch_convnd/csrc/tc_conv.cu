@@ -115,6 +115,78 @@ __device__ void decode_box(const BoxGeom& g, int64_t bt, int grp, BoxInfo& info)
   info.out_merged = (n * g.groups + grp) * g.out_outer_vol + outer_lin;
 }
 
+// Walks box indices in order (q2 fastest, then q1, q0, outer position, batch) without
+// divisions; the outer coordinates are re-derived only when the outer position changes.
+struct BoxCursor {
+  int64_t bt;
+  int q[3];
+  int64_t outer_lin, n;
+  bool outer_changed;
+};
+
+__device__ __forceinline__ void cursor_init(const BoxGeom& g, int64_t bt, BoxCursor& c) {
+  c.bt = bt;
+  int64_t rest = bt;
+  c.q[2] = static_cast<int>(rest % g.nbox[2]);
+  rest /= g.nbox[2];
+  c.q[1] = static_cast<int>(rest % g.nbox[1]);
+  rest /= g.nbox[1];
+  c.q[0] = static_cast<int>(rest % g.nbox[0]);
+  rest /= g.nbox[0];
+  c.outer_lin = rest % g.out_outer_vol;
+  c.n = rest / g.out_outer_vol;
+  c.outer_changed = true;
+}
+
+__device__ __forceinline__ void cursor_next(const BoxGeom& g, BoxCursor& c) {
+  ++c.bt;
+  c.outer_changed = false;
+  if (++c.q[2] < g.nbox[2]) return;
+  c.q[2] = 0;
+  if (++c.q[1] < g.nbox[1]) return;
+  c.q[1] = 0;
+  if (++c.q[0] < g.nbox[0]) return;
+  c.q[0] = 0;
+  c.outer_changed = true;
+  if (++c.outer_lin < g.out_outer_vol) return;
+  c.outer_lin = 0;
+  ++c.n;
+}
+
+// Fills a BoxInfo from the cursor. The outer-axis fields (ib_o, in_ng_base without the
+// tap-0 origins, out_merged) are recomputed only when `refresh_outer` is set.
+__device__ __forceinline__ void cursor_box(const BoxGeom& g, const BoxCursor& c, int grp,
+                                           bool refresh_outer, BoxInfo& info) {
+  info.valid = c.bt < g.boxes_per_group ? 1 : 0;
+  info.q[0] = c.q[0];
+  info.q[1] = c.q[1];
+  info.q[2] = c.q[2];
+#pragma unroll
+  for (int a = 0; a < 3; ++a) info.ib[a] = c.q[a] * g.b[a] * g.s[a] - g.p[a];
+  if (refresh_outer) {
+    info.n = static_cast<int32_t>(c.n);
+    info.outer_lin = c.outer_lin;
+    int64_t o = c.outer_lin;
+#pragma unroll
+    for (int a = kMaxOuter - 1; a >= 0; --a) {
+      if (a < g.n_outer) {
+        const int64_t coord = o % g.out_o[a];
+        o /= g.out_o[a];
+        info.ib_o[a] = static_cast<int32_t>(coord * g.s_o[a] - g.p_o[a]);
+      } else {
+        info.ib_o[a] = 0;
+      }
+    }
+    int64_t base = (c.n * g.groups + grp) * g.in_merged_per_ng;
+#pragma unroll
+    for (int a = 0; a < kMaxOuter; ++a) {
+      if (a < g.n_outer) base += static_cast<int64_t>(info.ib_o[a]) * g.in_o_stride[a];
+    }
+    info.in_ng_base = base;
+    info.out_merged = (c.n * g.groups + grp) * g.out_outer_vol + c.outer_lin;
+  }
+}
+
 // ---------------------------------------------------------------------------------------
 // Weight-gradient kernel. Grid (split, tap chunk, group). Each CTA accumulates
 // mt_per_cta tiles of 128 (tap, channel) rows x n_pad output channels in TMEM over its
@@ -264,14 +336,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     int a_stage = 0, b_slot = 0;
     uint32_t a_phase = 0, b_phase = 0;
     bool ok = true;
+    BoxCursor cursor;
+    cursor_init(g, p_begin * g.nb, cursor);
     for (int64_t pt = p_begin; pt < p_end && ok; ++pt) {
       // Boxes of this position tile and, per box, which outer tap combinations stay
-      // inside the input (bit c of box_mask).
+      // inside the input (bit c of box_mask; recomputed when the outer position moves).
       for (int j = 0; j < g.nb; ++j) {
         BoxInfo& B = boxes[j];
-        decode_box(g, pt * g.nb + j, grp, B);
-        uint64_t mask = 0;
-        if (B.valid) {
+        const bool refresh = cursor.outer_changed || g.nb > 1;
+        cursor_box(g, cursor, grp, refresh, B);
+        if (refresh) {
+          uint64_t mask = 0;
           for (int c = 0; c < P.outer_combos; ++c) {
             bool inside = true;
 #pragma unroll
@@ -283,15 +358,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             if (inside) mask |= uint64_t{1} << c;
           }
+          box_mask[j] = mask;
         }
-        box_mask[j] = mask;
-        // merged base: input index of (n, g) plus the outer origins of tap 0
-        int64_t base = B.in_ng_base;
-#pragma unroll
-        for (int a = 0; a < kMaxOuter; ++a) {
-          if (a < g.n_outer) base += static_cast<int64_t>(B.ib_o[a]) * g.in_o_stride[a];
-        }
-        B.in_ng_base = base;
+        cursor_next(g, cursor);
       }
       // Output-gradient tile (B operand), shared by every tap tile of this CTA.
       if (!dev::mbar_wait(&b_empty[b_slot], b_phase ^ 1u, err, kSiteWProducer, P.timeout_ns)) {
@@ -332,7 +401,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           const TapEntry e = taps[ti];
           for (int j = 0; j < g.nb; ++j) {
             const BoxInfo& B = boxes[j];
-            const bool inside = e.outer >= 0 && ((box_mask[j] >> e.outer) & 1u);
+            const bool inside =
+                B.valid && e.outer >= 0 && ((box_mask[j] >> e.outer) & 1u);
             const int32_t mc = inside ? static_cast<int32_t>(B.in_ng_base + e.delta) : -1;
             uint8_t* dst = as + jt * P.a_tile_bytes + j * g.box_rows * P.a_row_bytes;
             for (int part = 0; part < kParts; ++part) {
