@@ -121,6 +121,29 @@ CND_API size_t cnd_backward_workspace_size(const cnd_problem* problem, const int
 CND_API int cnd_forward(const cnd_problem* problem, const void* x, const void* w, const void* b,
                 void* y, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Capacity of the static device scratch that cnd_forward_noalloc uses (bytes). */
+#define CND_NOALLOC_SCRATCH_BYTES (16u * 1024u * 1024u)
+
+/* Forward without any device allocation by the caller or the library.
+ * For callers that cannot allocate device memory: hosts that drive this C ABI through
+ * thin bindings that hold no device allocator of their own (cgo, JNI, N-API or ctypes
+ * code that only has the input/output pointers it was handed), and processes whose
+ * device memory belongs to another allocator with a fixed budget (a serving process
+ * where a PyTorch caching allocator or a pre-sized pool owns the GPU), for which an extra
+ * workspace allocation would fail or fragment the pool.
+ * This variant has no counterpart in the reference. It computes exactly what
+ * cnd_forward computes, using as workspace a file-scope device array of
+ * CND_NOALLOC_SCRATCH_BYTES that every GPU which loads this library keeps until process
+ * exit. Problems whose workspace (cnd_forward_workspace_size) exceeds that size are
+ * rejected with CND_ERR_WORKSPACE and a message naming both sizes. The first call on a
+ * device looks up the array's device address (cudaGetSymbolAddress) with that device
+ * current, so make that first call before any stream capture. All calls share the one
+ * array and it keeps the last call's contents (every byte a call reads is written by
+ * the same call first); calls that overlap on the GPU, e.g. on two streams at once,
+ * race on it. */
+CND_API int cnd_forward_noalloc(const cnd_problem* problem, const void* x, const void* w,
+                                const void* b, void* y, void* stream);
+
 /* Backward: fills the gradients selected by output_mask = {dx, dw, db}.
  * Replaces torch_convnd::conv_nd_backward's CUDA kernel (reference
  * csrc/convnd.cpp:345-415 for fp32/fp64 and csrc/convnd_mixed.cpp:11-59 for fp16/bf16).

@@ -27,6 +27,9 @@ namespace cnd {
 
 __device__ unsigned int g_error_word;
 
+// Workspace of cnd_forward_noalloc: a fixed device array instead of an allocation.
+static __device__ __align__(256) unsigned char g_forward_scratch[CND_NOALLOC_SCRATCH_BYTES];
+
 namespace {
 
 std::atomic<int64_t> g_launches{0};
@@ -456,6 +459,45 @@ int cnd_forward(const cnd_problem* problem, const void* x, const void* w, const 
   pass.bias = b;
   TimedPass timed(1, stream);
   return launch_fprop(pass, plan.fwd_plan, stream, wait_timeout_ns(), 0);
+}
+
+int cnd_forward_noalloc(const cnd_problem* problem, const void* x, const void* w,
+                        const void* b, void* y, void* stream_handle) {
+  using namespace cnd;
+  clear_error();
+  if (problem == nullptr) return fail(CND_ERR_INVALID, "cnd_forward_noalloc: null argument");
+  const size_t needed = cnd_forward_workspace_size(problem);
+  if (needed > CND_NOALLOC_SCRATCH_BYTES) {
+    return fail(CND_ERR_WORKSPACE,
+                "cnd_forward_noalloc: this problem needs %zu bytes of workspace, more than "
+                "the %u-byte static scratch; use cnd_forward with a caller workspace",
+                needed, static_cast<unsigned>(CND_NOALLOC_SCRATCH_BYTES));
+  }
+  // Device address of the static scratch, looked up once per device with it current.
+  static std::mutex mutex;
+  static void* addresses[128] = {};
+  int device = 0;
+  cudaError_t e = cudaGetDevice(&device);
+  if (e != cudaSuccess || device < 0 || device >= 128) {
+    return fail(CND_ERR_CUDA, "cnd_forward_noalloc: cudaGetDevice failed");
+  }
+  void* scratch = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(mutex);
+    if (addresses[device] == nullptr) {
+      void* address = nullptr;
+      e = cudaGetSymbolAddress(&address, g_forward_scratch);
+      if (e != cudaSuccess || address == nullptr) {
+        return fail(CND_ERR_CUDA, "cnd_forward_noalloc: cudaGetSymbolAddress failed: %s",
+                    cudaGetErrorString(e));
+      }
+      addresses[device] = address;
+    }
+    scratch = addresses[device];
+  }
+  const int rc = cnd_forward(problem, x, w, b, y, needed > 0 ? scratch : nullptr, needed,
+                             stream_handle);
+  return rc;
 }
 
 int cnd_backward(const cnd_problem* problem, const void* dy, const void* x, const void* w,
