@@ -438,14 +438,14 @@ def run_b200(args):
 
 def traffic_from_profiles(config_name, kind):
     """DRAM bytes per launch of a pass, from the committed ncu summary (if any)."""
-    path = ROOT / "profiles" / "traffic.json"
+    path = ROOT / "profiles" / "traffic.txt"
     if not path.exists():
         return None
-    try:
-        data = json.loads(path.read_text())
-        return data.get(config_name, {}).get(kind)
-    except (ValueError, OSError):
-        return None
+    for line in path.read_text().splitlines():
+        parts = line.split()
+        if len(parts) == 3 and not line.startswith("#") and parts[:2] == [config_name, kind]:
+            return int(parts[2])
+    return None
 
 
 def run_e2e(args, cfg, inputs, device, world, dist, rank):
