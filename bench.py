@@ -1,20 +1,23 @@
 #!/usr/bin/env python
 """Benchmark of the N-D convolution hot path on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2|c3|c4|c1]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c1|c2|c3|c4|c5]
     python -m torch.distributed.run --nproc-per-node N ... bench.py --gpus N ...
     python bench.py --impl reference ...      # the reference's own CPU implementation
 
-A step is one forward + dgrad + wgrad (+ bias gradient) of the configuration's
-convolution over one batch of synthetic input that is already resident in HBM; with
-N > 1 GPUs every rank convolves its own batch (weak scaling: per-GPU work fixed) and the
-weight/bias gradients are all-reduced with NCCL, as data-parallel training does.
+For c1-c4 a step is one forward + dgrad + wgrad (+ bias gradient) of the configuration's
+convolution over one batch of synthetic input already resident in HBM; with N > 1 GPUs
+every rank convolves its own batch (weak scaling: per-GPU work fixed) and the weight/bias
+gradients are all-reduced with NCCL, as data-parallel training does. For c5 a step is
+the three-layer training step over a global batch of 64 split across the ranks (strong
+scaling), with bucketed gradient all-reduce and an SGD update.
 `value` is whole-job TFLOP/s (all ranks' algorithmic FLOPs / max-over-ranks time).
 `e2e` is the same metric through the public module API with the step's inputs copied
-from pinned host memory and the parameter gradients read back, inside the timed region.
-`roofline` reports the dominant tcgen05 pass; `cpu_baseline` times the reference's
-native CPU implementation (compiled from its sources into oracle/_ref) on a bounded
-sample of the same workload.
+from pinned host memory and the step's result read back, inside the timed region.
+`roofline` reports the pass (layer x forward/dgrad/wgrad) with the largest share of the
+step against the bound its arithmetic intensity sets; `cpu_baseline` times the
+reference's native CPU implementation (compiled from its sources into oracle/_ref) on a
+bounded sample of the same workload.
 """
 
 from __future__ import annotations
@@ -46,7 +49,7 @@ def parse_args(argv=None):
     parser.add_argument("--steps", type=int, default=20)
     parser.add_argument("--warmup", type=int, default=5)
     parser.add_argument("--impl", choices=("b200", "reference"), default="b200")
-    parser.add_argument("--config", default="c2", choices=("c1", "c2", "c3", "c4"))
+    parser.add_argument("--config", default="c2", choices=("c1", "c2", "c3", "c4", "c5"))
     parser.add_argument("--fp32-precision", default="3xtf32", choices=("3xtf32", "tf32", "ieee"))
     parser.add_argument("--no-e2e", action="store_true")
     parser.add_argument("--no-cpu-baseline", action="store_true")
@@ -172,41 +175,105 @@ def geometry_args(cfg, workspace=64 * 1024 * 1024):
 # CPU baseline: the reference's own native CPU operators (oracle/_ref), or the oracle.
 # ------------------------------------------------------------------------------------
 
+def _cpu_conv_function(kind):
+    """A torch.autograd.Function running one convolution layer on the CPU through the
+    reference's compiled operators (kind 'reference') or the oracle port ('port')."""
+    import torch
+
+    if kind == "reference":
+        op = torch.ops.torch_convnd
+
+        def forward(x, w, b, geo):
+            return op.conv_nd(x, w, b, *geo)
+
+        def backward(dy, x, w, geo, mask):
+            return op.conv_nd_backward(dy, x, w, *geo, mask)
+    else:
+        from oracle import convnd_oracle as oracle
+
+        def forward(x, w, b, geo):
+            return oracle.forward(x, w, b, *geo[:4]).to(x.dtype)
+
+        def backward(dy, x, w, geo, mask):
+            grads = oracle.backward(dy, x, w, *geo[:4], mask=mask)
+            return tuple(None if g is None else g.to(x.dtype) for g in grads)
+
+    class Conv(torch.autograd.Function):
+        @staticmethod
+        def forward(ctx, x, w, b, geo):
+            ctx.save_for_backward(x, w)
+            ctx.geo = geo
+            return forward(x, w, b, geo)
+
+        @staticmethod
+        def backward(ctx, dy):
+            x, w = ctx.saved_tensors
+            mask = [ctx.needs_input_grad[0], True, True]
+            dx, dw, db = backward(dy.contiguous(), x, w, ctx.geo, mask)
+            return dx, dw, db, None
+
+    return Conv
+
+
 def cpu_baseline_worker(args):
     """Subprocess entry: print one JSON object with the CPU timing of a bounded sample."""
     import torch
 
     configs = load_configs()
-    cfg = config_for(args.config)
-    sample = cfg.with_batch(args.cpu_sample_images)
     cores = os.cpu_count() or 1
     torch.set_num_threads(cores)
-    inputs = configs.make_inputs(sample)
-    geo = geometry_args(sample)
     ref_so = ROOT / "oracle" / "_ref" / "libtorch_convnd_ref_cpu.so"
+    keep = None
     if ref_so.exists():
         from oracle import build_ref
 
         keep = build_ref.load(ref_so)  # noqa: F841  (the schema library must stay alive)
         kind = "reference"
-
-        def step():
-            y = torch.ops.torch_convnd.conv_nd(inputs.x, inputs.weight, inputs.bias, *geo)
-            grads = torch.ops.torch_convnd.conv_nd_backward(
-                inputs.grad, inputs.x, inputs.weight, *geo, [True, True, True])
-            return y, grads
     else:
-        from oracle import convnd_oracle as oracle
-
         kind = "port"
-        cores = torch.get_num_threads()
+    conv = _cpu_conv_function(kind)
+    images = args.cpu_sample_images
+    if args.config == "c5":
+        full_batch = configs.C5_BATCH
+        data = configs.make_c5_inputs()
+        x = data.x[:images].contiguous()
+        target = data.target[:images].contiguous()
+        params = [(w.clone().requires_grad_(), b.clone().requires_grad_())
+                  for w, b in data.parameters]
+        layers = configs.C5_LAYERS
+        flops = configs.C5_STEP_FLOPS * images / full_batch
+        name = "c5 three-layer training step (conv, GELU, conv, GELU, conv, MSE)"
 
         def step():
-            y = oracle.forward(inputs.x, inputs.weight, inputs.bias, sample.stride,
-                               sample.padding, sample.dilation, sample.groups)
-            grads = oracle.backward(inputs.grad, inputs.x, inputs.weight, sample.stride,
-                                    sample.padding, sample.dilation, sample.groups)
-            return y, grads
+            h = x
+            for index, (layer, (w, b)) in enumerate(zip(layers, params)):
+                h = conv.apply(h, w, b, geometry_args(layer))
+                if index + 1 < len(layers):
+                    h = torch.nn.functional.gelu(h)
+            loss = torch.nn.functional.mse_loss(h, target)
+            loss.backward()
+            for w, b in params:
+                w.grad = b.grad = None
+            return loss
+    else:
+        cfg = config_for(args.config)
+        full_batch = cfg.batch
+        sample = cfg.with_batch(images)
+        inputs = configs.make_inputs(sample)
+        x = inputs.x.clone().requires_grad_(cfg.input_grad)
+        w = inputs.weight.clone().requires_grad_()
+        b = inputs.bias.clone().requires_grad_() if inputs.bias is not None else None
+        geo = geometry_args(sample)
+        flops = sample.step_flops
+        name = f"{cfg.name} (fwd+dgrad+wgrad+dbias)"
+
+        def step():
+            y = conv.apply(x, w, b, geo)
+            y.backward(inputs.grad)
+            x.grad = w.grad = None
+            if b is not None:
+                b.grad = None
+            return y
     steps = max(1, args.steps)
     warmup = max(0, args.warmup)
     for _ in range(warmup):
@@ -215,14 +282,13 @@ def cpu_baseline_worker(args):
     for _ in range(steps):
         step()
     seconds = (time.perf_counter() - start) / steps
-    value = sample.step_flops / seconds / 1e12
     print(json.dumps({
-        "value": value, "unit": "TFLOP/s", "cores": cores, "kind": kind,
+        "value": flops / seconds / 1e12, "unit": "TFLOP/s", "cores": cores, "kind": kind,
         "seconds_per_step": seconds,
-        "sample": f"{args.cpu_sample_images} of {cfg.batch} images of {cfg.name} per step "
-                  f"(fwd+dgrad+wgrad+dbias, {dtype_name(cfg.dtype)} inputs), "
-                  f"torch.set_num_threads({cores})",
+        "sample": f"{images} of {full_batch} images of {name} per step, "
+                  f"{args.config} dtype inputs, torch.set_num_threads({cores})",
     }))
+    del keep
 
 
 def cpu_baseline(args, steps=1, warmup=0):
@@ -253,8 +319,12 @@ def run_reference_arm(args):
     result = cpu_baseline(worker_args, steps=steps, warmup=warmup)
     import torch  # noqa: F401
 
-    cfg = config_for(args.config)
     value = result.get("value")
+    if args.config == "c5":
+        dtype, workload, batch = "bf16", C5_WORKLOAD, load_configs().C5_BATCH
+    else:
+        cfg = config_for(args.config)
+        dtype, workload, batch = dtype_name(cfg.dtype), workload_text(cfg), cfg.batch
     line = {
         "metric": METRIC,
         "impl": "reference",
@@ -265,12 +335,12 @@ def run_reference_arm(args):
         "warmup": warmup,
         "ms_per_step": None if value is None else result["seconds_per_step"] * 1e3,
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong" if args.config == "c5" else "weak",
         "vs_baseline": None,
-        "dtype": dtype_name(cfg.dtype),
+        "dtype": dtype,
         "data": "synthetic (seeded N(0,1) activations and gradients, kaiming-uniform weights)",
-        "config": {"workload": workload_text(cfg) + "; reference CPU path on a bounded sample",
-                   "per_gpu_batch": cfg.batch, "parallelism": "host cores"},
+        "config": {"workload": workload + "; reference CPU path on a bounded sample",
+                   "batch": batch, "parallelism": "host cores"},
         "cpu_baseline": {k: result.get(k) for k in ("value", "unit", "cores", "kind", "sample")},
         "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
@@ -279,8 +349,217 @@ def run_reference_arm(args):
 
 
 # ------------------------------------------------------------------------------------
-# B200 arm
+# B200 arm: workloads
 # ------------------------------------------------------------------------------------
+
+C5_WORKLOAD = ("c5: 3-layer Conv4d bf16 training step, x[64,16,32,32,16,16] -> L1 16->32 "
+               "k3 s2 p1 -> GELU -> L2 32->32 k(3,3,1,1) p(2,2,0,0) d(2,2,1,1) g4 -> GELU -> "
+               "L3 32->8 k1 -> MSE; fwd + bwd (no dgrad of L1) + gradient all-reduce + SGD")
+
+
+class SingleOp:
+    """c1-c4: one convolution's forward + dgrad + wgrad + dbias per step. Every rank
+    convolves its own batch of the config's size (weak scaling); the weight and bias
+    gradients are all-reduced in one fp32 bucket."""
+
+    scaling = "weak"
+
+    def __init__(self, args, device, rank, world, dist):
+        import torch
+
+        configs = load_configs()
+        self.cfg = cfg = config_for(args.config)
+        self.world, self.dist, self.device = world, dist, device
+        self.inputs = configs.make_inputs(cfg, device=device, generator_seed=cfg.seed + 1000 * rank)
+        self.geo = geometry_args(cfg)
+        self.layers = [cfg]
+        self.job_flops = world * cfg.step_flops
+        self.dtype = dtype_name(cfg.dtype)
+        self.op = torch.ops.torch_convnd
+
+    def _allreduce(self, grads):
+        import torch
+
+        if self.world == 1:
+            return
+        bucket = torch.cat([g.reshape(-1).float() for g in grads])
+        self.dist.all_reduce(bucket)
+        bucket.div_(self.world)
+        offset = 0
+        for g in grads:
+            g.copy_(bucket[offset: offset + g.numel()].view_as(g))
+            offset += g.numel()
+
+    def step(self):
+        i = self.inputs
+        y = self.op.conv_nd.default(i.x, i.weight, i.bias, *self.geo)
+        dx, dw, db = self.op.conv_nd_backward.default(i.grad, i.x, i.weight, *self.geo,
+                                                      [True, True, i.bias is not None])
+        self._allreduce([g for g in (dw, db) if g is not None])
+        return y
+
+    def config(self):
+        cfg = self.cfg
+        return {"workload": workload_text(cfg), "per_gpu_batch": cfg.batch,
+                "global_batch": cfg.batch * self.world, "parallelism": f"dp{self.world}",
+                "step_gflop_per_gpu": cfg.step_flops / 1e9,
+                "l2": "inputs larger than L2 (x, dy, y and dx together exceed 126 MB)"}
+
+    def e2e_step_factory(self):
+        """Through the public module API: pinned host x and dy copied in, parameter
+        gradients read back, every step."""
+        import torch
+
+        import torch_convnd
+
+        cfg, inputs, device = self.cfg, self.inputs, self.device
+        layer = torch_convnd.ConvNd(cfg.in_channels, cfg.out_channels, cfg.kernel, cfg.stride,
+                                    cfg.padding, cfg.dilation, cfg.groups, bias=cfg.bias,
+                                    device=device, dtype=cfg.dtype, dimensions=cfg.rank)
+        with torch.no_grad():
+            layer.weight.copy_(inputs.weight)
+            if cfg.bias:
+                layer.bias.copy_(inputs.bias)
+        x_host = inputs.x.cpu().pin_memory()
+        dy_host = inputs.grad.cpu().pin_memory()
+        params = list(layer.parameters())
+        grad_host = [torch.empty(p.shape, dtype=p.dtype, pin_memory=True) for p in params]
+
+        def step():
+            x = x_host.to(device, non_blocking=True).requires_grad_()
+            dy = dy_host.to(device, non_blocking=True)
+            layer(x).backward(dy)
+            self._allreduce([p.grad for p in params])
+            for host, p in zip(grad_host, params):
+                host.copy_(p.grad, non_blocking=True)
+                p.grad = None
+
+        h2d = sum(t.numel() * t.element_size() for t in (x_host, dy_host))
+        d2h = sum(g.numel() * g.element_size() for g in grad_host)
+        return step, h2d, d2h, "torch_convnd.ConvNd forward + autograd backward"
+
+
+class C5Step:
+    """c5: the three-layer training step over a global batch of 64 split across the
+    ranks (strong scaling): forward, MSE loss, backward (L1's input needs no gradient),
+    bucketed gradient all-reduce started from gradient hooks, SGD update."""
+
+    scaling = "strong"
+
+    def __init__(self, args, device, rank, world, dist):
+        import torch
+
+        import torch_convnd
+        from torch_convnd.data_parallel import GradientBucketer
+
+        configs = load_configs()
+        self.world, self.device, self.rank = world, device, rank
+        self.data = configs.make_c5_inputs(device=device, rank=rank, world=world)
+        shard = self.data.x.shape[0]
+        self.layers = [layer.with_batch(shard) for layer in configs.C5_LAYERS]
+        self.job_flops = configs.C5_STEP_FLOPS
+        self.dtype = "bf16"
+        self.net = configs.c5_network(torch_convnd.ConvNd, self.data.parameters, device)
+        self.bucketer = GradientBucketer(self.net.parameters())
+        self.optimizer = torch.optim.SGD(self.net.parameters(), lr=1e-4)
+        self.mse = torch.nn.functional.mse_loss
+
+    def _train(self, x, target):
+        loss = self.mse(self.net(x), target)
+        loss.backward()
+        self.bucketer.finish()
+        self.optimizer.step()
+        self.optimizer.zero_grad(set_to_none=True)
+        return loss
+
+    def step(self):
+        return self._train(self.data.x, self.data.target)
+
+    def config(self):
+        configs = load_configs()
+        return {"workload": C5_WORKLOAD, "global_batch": configs.C5_BATCH,
+                "per_gpu_batch": self.layers[0].batch, "parallelism": f"dp{self.world}",
+                "step_gflop_per_gpu": sum(l.step_flops for l in self.layers) / 1e9,
+                "gradient_buckets": len(self.bucketer.buckets),
+                "l2": "inputs larger than L2 (x alone is 537 MB at batch 64)"}
+
+    def e2e_step_factory(self):
+        import torch
+
+        device = self.device
+        x_host = self.data.x.cpu().pin_memory()
+        target_host = self.data.target.cpu().pin_memory()
+        loss_host = torch.empty((), dtype=torch.bfloat16, pin_memory=True)
+
+        def step():
+            x = x_host.to(device, non_blocking=True)
+            target = target_host.to(device, non_blocking=True)
+            loss_host.copy_(self._train(x, target).detach(), non_blocking=True)
+
+        h2d = sum(t.numel() * t.element_size() for t in (x_host, target_host))
+        return step, h2d, 2, "torch_convnd.ConvNd x3 + GELU + MSE, autograd backward, SGD"
+
+
+# ------------------------------------------------------------------------------------
+# B200 arm: timing and attribution
+# ------------------------------------------------------------------------------------
+
+def timed_ms(step, steps, world, dist, device):
+    """Mean device time of `steps` steps (CUDA events on the current stream, barrier and
+    synchronize on both sides), max over ranks."""
+    import torch
+
+    stream = torch.cuda.current_stream()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    start.record(stream)
+    for _ in range(steps):
+        step()
+    end.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms = start.elapsed_time(end) / steps
+    if world > 1:
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return ms
+
+
+def pass_bytes(layer) -> int:
+    """Minimum HBM bytes of one pass: read x (or dy) and the weights, write y (or dx / dw):
+    x, y and w once each in the layer dtype."""
+    import torch
+
+    size = torch.empty((), dtype=layer.dtype).element_size()
+    x = layer.batch * layer.in_channels * math.prod(layer.spatial)
+    y = layer.batch * layer.out_channels * math.prod(layer.output)
+    w = layer.out_channels * (layer.in_channels // layer.groups) * math.prod(layer.kernel)
+    return size * (x + y + w)
+
+
+def attribute_passes(timings, layers, steps):
+    """Splits the launch-ordered pass timings of `steps` steps by layer: forward passes run
+    in layer order, dgrad and wgrad in reverse layer order (dgrad only where the layer's
+    input needs a gradient)."""
+    orders = {
+        "forward": [l.name for l in layers],
+        "dgrad": [l.name for l in reversed(layers) if l.input_grad],
+        "wgrad": [l.name for l in reversed(layers)],
+    }
+    seen = {k: 0 for k in orders}
+    per_layer = {}
+    for kind, ms in timings:
+        if kind not in orders or not orders[kind]:
+            continue
+        name = orders[kind][seen[kind] % len(orders[kind])]
+        seen[kind] += 1
+        per_layer.setdefault((kind, name), []).append(ms)
+    return per_layer
+
 
 def run_b200(args):
     import torch
@@ -296,134 +575,118 @@ def run_b200(args):
 
     import torch_convnd
 
-    configs = load_configs()
     torch_convnd.set_fp32_precision(args.fp32_precision)
-    cfg = config_for(args.config)
-    inputs = configs.make_inputs(cfg, device=device, generator_seed=cfg.seed + 1000 * rank)
-    x, w, b, dy = inputs.x, inputs.weight, inputs.bias, inputs.grad
-    geo = geometry_args(cfg)
-    op = torch.ops.torch_convnd
-    bucket_numel = w.numel() + (b.numel() if b is not None else 0)
-
-    def allreduce(dw, db):
-        if world == 1:
-            return
-        bucket = torch.cat([dw.reshape(-1).float(), db.reshape(-1).float()])
-        dist.all_reduce(bucket)
-        bucket.div_(world)
-        dw.copy_(bucket[: dw.numel()].view_as(dw))
-        db.copy_(bucket[dw.numel():].view_as(db))
-
-    def step():
-        y = op.conv_nd.default(x, w, b, *geo)
-        dx, dw, db = op.conv_nd_backward.default(dy, x, w, *geo, [True, True, True])
-        allreduce(dw, db)
-        return y, dx, dw, db
-
-    def barrier():
-        if world > 1:
-            dist.barrier()
-
-    for _ in range(max(args.warmup, 3)):
-        step()
+    workload = (C5Step if args.config == "c5" else SingleOp)(args, device, rank, world, dist)
+    warmup = max(args.warmup, 3)
+    for _ in range(warmup):
+        workload.step()
     torch.cuda.synchronize()
     torch_convnd.device_status()
-    barrier()
     props = torch.cuda.get_device_properties(device)
     uuid = getattr(props, "uuid", None)
     sampler = ClockSampler(f"GPU-{uuid}" if uuid is not None else str(local))
     sampler.start()
     time.sleep(0.3)
     torch_convnd.launch_count(reset=True)
-    stream = torch.cuda.current_stream()
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier()
-    torch.cuda.synchronize()
-    start.record(stream)
-    for _ in range(args.steps):
-        step()
-    end.record(stream)
-    torch.cuda.synchronize()
-    barrier()
+    ms = timed_ms(workload.step, args.steps, world, dist, device)
     clocks = sampler.stop()
     launches = torch_convnd.launch_count()
-    ms = start.elapsed_time(end) / args.steps
-    if world > 1:
-        t = torch.tensor([ms], device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    value = world * cfg.step_flops / (ms / 1e3) / 1e12
+    value = workload.job_flops / (ms / 1e3) / 1e12
     torch_convnd.device_status()
 
-    # Per-pass durations with CUDA events on the launching stream (separate loop).
+    # Per-pass durations with CUDA events on the launching stream (a separate loop).
     torch_convnd._native.set_kernel_timing(True)
     timing_steps = min(args.steps, 5)
     for _ in range(timing_steps):
-        step()
+        workload.step()
     torch.cuda.synchronize()
     timings = torch_convnd._native.collect_kernel_timings()
     torch_convnd._native.set_kernel_timing(False)
-    per_kind = {}
-    for kind, t in timings:
-        per_kind.setdefault(kind, []).append(t)
     kernels = {}
-    for kind, values in per_kind.items():
-        kernels[kind] = {"launches": len(values), "avg_ms": sum(values) / len(values),
-                         "share_of_step": sum(values) / timing_steps / ms}
-    peaks, source = measured_peaks()
-    tensor_passes = {k: v for k, v in kernels.items() if k in ("forward", "dgrad", "wgrad")}
-    roofline = None
-    if tensor_passes:
-        dominant = max(tensor_passes, key=lambda k: tensor_passes[k]["avg_ms"] *
-                       tensor_passes[k]["launches"])
-        achieved = cfg.forward_flops / (tensor_passes[dominant]["avg_ms"] / 1e3) / 1e12
-        peak = float(peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"]))
-        peak_note = f"{source} cuBLAS bf16 sustained"
-        if cfg.dtype == torch.float32:
-            peak = peak / 2
-            peak_note = f"{source} cuBLAS bf16 sustained / 2 (dense TF32 rate)"
-        traffic = traffic_from_profiles(cfg.name, dominant)
-        roofline = {"kernel": f"{dominant} pass (tcgen05)", "bound": "tensor",
-                    "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                    "frac": achieved / peak, "peak_source": peak_note, "traffic": traffic}
-        for kind, info in tensor_passes.items():
-            info["tflops"] = cfg.forward_flops / (info["avg_ms"] / 1e3) / 1e12
+    for kind, t in timings:
+        entry = kernels.setdefault(kind, {"launches": 0, "total_ms": 0.0})
+        entry["launches"] += 1
+        entry["total_ms"] += t
+    for entry in kernels.values():
+        entry["avg_ms"] = entry["total_ms"] / entry["launches"]
+        entry["share_of_step"] = entry.pop("total_ms") / timing_steps / ms
 
-    # End-to-end through the public API with host buffers.
+    peaks, source = measured_peaks()
+    hbm = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
+    tensor_peak = float(peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"]))
+    passes = {}
+    by_name = {l.name: l for l in workload.layers}
+    for (kind, name), values in attribute_passes(timings, workload.layers, timing_steps).items():
+        layer = by_name[name]
+        avg = sum(values) / len(values)
+        peak_t = tensor_peak / (2 if layer.dtype == torch.float32 else 1)
+        t_flop = layer.forward_flops / (peak_t * 1e12)
+        t_byte = pass_bytes(layer) / (hbm * 1e9)
+        passes[f"{name} {kind}"] = {
+            "layer": name, "kind": kind, "launches": len(values), "avg_ms": avg,
+            "tflops": layer.forward_flops / (avg / 1e3) / 1e12,
+            "gbs": pass_bytes(layer) / (avg / 1e3) / 1e9,
+            "bound": "tensor" if t_flop >= t_byte else "hbm",
+            "share_of_step": sum(values) / timing_steps / ms,
+        }
+    roofline = None
+    if passes:
+        key = max(passes, key=lambda k: passes[k]["share_of_step"])
+        info = passes[key]
+        layer = by_name[info["layer"]]
+        traffic = traffic_from_profiles(layer.name, info["kind"])
+        if info["bound"] == "tensor":
+            peak = tensor_peak / (2 if layer.dtype == torch.float32 else 1)
+            note = f"{source} cuBLAS bf16 sustained" + (
+                " / 2 (dense TF32 rate)" if layer.dtype == torch.float32 else "")
+            achieved, unit = info["tflops"], "TFLOP/s"
+            algorithmic = f"{layer.forward_flops / 1e9:.1f} GFLOP per launch"
+        else:
+            peak, note = hbm, f"{source} HBM copy bandwidth"
+            achieved, unit = info["gbs"], "GB/s"
+            algorithmic = f"{pass_bytes(layer) / 1e6:.1f} MB per launch"
+        roofline = {"kernel": f"{key} pass (tcgen05)", "bound": info["bound"],
+                    "achieved": achieved, "peak": peak, "unit": unit,
+                    "frac": achieved / peak, "peak_source": note,
+                    "algorithmic": algorithmic, "traffic": traffic}
+
     e2e = None
     if not args.no_e2e:
-        e2e = run_e2e(args, cfg, inputs, device, world, dist, rank)
+        step, h2d, d2h, api = workload.e2e_step_factory()
+        for _ in range(3):
+            step()
+        torch.cuda.synchronize()
+        e2e_ms = timed_ms(step, args.steps, world, dist, device)
+        e2e = {"value": workload.job_flops / (e2e_ms / 1e3) / 1e12, "unit": "TFLOP/s",
+               "ms_per_step": e2e_ms, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+               "api": api}
 
     baseline = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         baseline = cpu_baseline(args, steps=1, warmup=0)
 
     if rank == 0:
+        config = workload.config()
+        if workload.dtype == "fp32":
+            config["fp32_precision"] = args.fp32_precision
         line = {
             "metric": METRIC,
             "value": value,
             "unit": "TFLOP/s",
             "n_gpus": world,
             "steps": args.steps,
-            "warmup": max(args.warmup, 3),
+            "warmup": warmup,
             "ms_per_step": ms,
             "higher_is_better": True,
-            "scaling": "weak",
+            "scaling": workload.scaling,
             "vs_baseline": None,
-            "dtype": dtype_name(cfg.dtype),
+            "dtype": workload.dtype,
             "data": "synthetic (seeded N(0,1) activations and gradients, kaiming-uniform "
                     "weights, uniform bias; the reference config's shapes)",
-            "config": {
-                "workload": workload_text(cfg),
-                "per_gpu_batch": cfg.batch,
-                "global_batch": cfg.batch * world,
-                "parallelism": f"dp{world}",
-                "step_gflop_per_gpu": cfg.step_flops / 1e9,
-                "fp32_precision": args.fp32_precision if cfg.dtype == torch.float32 else None,
-                "l2": "inputs larger than L2 (x, dy, y and dx together exceed 126 MB)",
-            },
+            "config": config,
             "value_per_gpu": value / world,
             "roofline": roofline,
+            "passes": passes,
             "kernels": kernels,
             "cpu_baseline": baseline,
             "e2e": e2e,
@@ -446,63 +709,6 @@ def traffic_from_profiles(config_name, kind):
         if len(parts) == 3 and not line.startswith("#") and parts[:2] == [config_name, kind]:
             return int(parts[2])
     return None
-
-
-def run_e2e(args, cfg, inputs, device, world, dist, rank):
-    import torch
-
-    import torch_convnd
-
-    layer = torch_convnd.ConvNd(cfg.in_channels, cfg.out_channels, cfg.kernel, cfg.stride,
-                                cfg.padding, cfg.dilation, cfg.groups, bias=cfg.bias,
-                                device=device, dtype=cfg.dtype, dimensions=cfg.rank)
-    with torch.no_grad():
-        layer.weight.copy_(inputs.weight)
-        if cfg.bias:
-            layer.bias.copy_(inputs.bias)
-    x_host = inputs.x.cpu().pin_memory()
-    dy_host = inputs.grad.cpu().pin_memory()
-    grad_host = [torch.empty(p.shape, dtype=p.dtype, pin_memory=True) for p in layer.parameters()]
-
-    def step():
-        x = x_host.to(device, non_blocking=True).requires_grad_()
-        dy = dy_host.to(device, non_blocking=True)
-        layer(x).backward(dy)
-        params = list(layer.parameters())
-        if world > 1:
-            bucket = torch.cat([p.grad.reshape(-1).float() for p in params])
-            dist.all_reduce(bucket)
-            bucket.div_(world)
-            offset = 0
-            for p in params:
-                p.grad.copy_(bucket[offset: offset + p.numel()].view_as(p))
-                offset += p.numel()
-        for host, p in zip(grad_host, params):
-            host.copy_(p.grad, non_blocking=True)
-            p.grad = None
-        return x
-
-    for _ in range(3):
-        step()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    start.record()
-    for _ in range(args.steps):
-        step()
-    end.record()
-    torch.cuda.synchronize()
-    ms = start.elapsed_time(end) / args.steps
-    if world > 1:
-        t = torch.tensor([ms], device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    h2d = x_host.numel() * x_host.element_size() + dy_host.numel() * dy_host.element_size()
-    d2h = sum(g.numel() * g.element_size() for g in grad_host)
-    return {"value": world * cfg.step_flops / (ms / 1e3) / 1e12, "unit": "TFLOP/s",
-            "ms_per_step": ms, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-            "api": "torch_convnd.ConvNd forward + autograd backward"}
 
 
 def main(argv=None):

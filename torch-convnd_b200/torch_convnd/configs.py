@@ -124,3 +124,59 @@ def make_inputs(config: ConvConfig, device="cpu", generator_seed: int | None = N
         return None if t is None else t.to(dtype=config.dtype).to(device)
 
     return ConvInputs(cast(x), cast(weight), cast(bias), cast(grad))
+
+
+# ------------------------------------------------------------------------------------
+# c5: the three-layer training step
+# ------------------------------------------------------------------------------------
+
+C5_STEP_FLOPS = sum(layer.step_flops for layer in C5_LAYERS)  # 190.0 GFLOP per global batch
+
+
+@dataclass
+class C5Inputs:
+    x: torch.Tensor
+    target: torch.Tensor
+    parameters: list  # [(weight, bias)] per layer, in layer order
+
+
+def make_c5_inputs(device="cpu", rank: int = 0, world: int = 1) -> C5Inputs:
+    """Seeded c5 inputs: x, then each layer's weight and bias, then the MSE target, all
+    drawn on the CPU for the whole global batch; rank `rank` of `world` keeps its
+    contiguous batch shard (the first ``64 % world`` ranks one extra row)."""
+    generator = torch.Generator().manual_seed(C5_LAYERS[0].seed)
+    first = C5_LAYERS[0]
+    x = torch.randn((C5_BATCH, first.in_channels, *first.spatial), generator=generator)
+    parameters = []
+    for layer in C5_LAYERS:
+        fan_in = layer.in_channels // layer.groups * math.prod(layer.kernel)
+        bound = 1.0 / math.sqrt(fan_in)
+        weight = torch.empty(
+            (layer.out_channels, layer.in_channels // layer.groups, *layer.kernel)
+        ).uniform_(-bound, bound, generator=generator)
+        bias = torch.empty(layer.out_channels).uniform_(-bound, bound, generator=generator)
+        parameters.append((weight.to(first.dtype).to(device), bias.to(first.dtype).to(device)))
+    last = C5_LAYERS[-1]
+    target = torch.randn((C5_BATCH, last.out_channels, *last.output), generator=generator)
+    base, extra = divmod(C5_BATCH, world)
+    start = rank * base + min(rank, extra)
+    stop = start + base + (1 if rank < extra else 0)
+    return C5Inputs(x[start:stop].to(first.dtype).to(device),
+                    target[start:stop].to(first.dtype).to(device), parameters)
+
+
+def c5_network(conv_class, parameters, device=None):
+    """conv L1 -> GELU -> conv L2 -> GELU -> conv L3, built from `conv_class` (a ConvNd
+    with the reference's constructor) and loaded with `parameters`."""
+    layers = []
+    for index, (layer, (weight, bias)) in enumerate(zip(C5_LAYERS, parameters, strict=True)):
+        conv = conv_class(layer.in_channels, layer.out_channels, layer.kernel, layer.stride,
+                          layer.padding, layer.dilation, layer.groups, bias=True,
+                          device=device, dtype=layer.dtype, dimensions=layer.rank)
+        with torch.no_grad():
+            conv.weight.copy_(weight)
+            conv.bias.copy_(bias)
+        layers.append(conv)
+        if index + 1 < len(C5_LAYERS):
+            layers.append(torch.nn.GELU())
+    return torch.nn.Sequential(*layers)
