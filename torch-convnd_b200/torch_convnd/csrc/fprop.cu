@@ -83,13 +83,14 @@ __device__ __forceinline__ void decode_super(const FpropParams& P, int64_t st, S
   }
 }
 
+// One MMA issued by the converged MMA warp (one elected lane).
 template <bool kTF32>
 __device__ __forceinline__ void mma(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc,
                                     uint32_t acc) {
   if constexpr (kTF32) {
-    dev::mma_tf32(d, a, b, idesc, acc);
+    dev::mma_tf32_warp(d, a, b, idesc, acc);
   } else {
-    dev::mma_f16(d, a, b, idesc, acc);
+    dev::mma_f16_warp(d, a, b, idesc, acc);
   }
 }
 
@@ -132,7 +133,7 @@ struct OpTraits<kKind3xTF32> {
   static __device__ __forceinline__ float load(const Out* p) { return *p; }
 };
 
-template <int kOp, int kKSteps>
+template <int kOp, int kKSteps, int kMT>
 __global__ void __launch_bounds__(kThreads, 1)
     fprop_kernel(const __grid_constant__ FpropMaps maps, const __grid_constant__ FpropParams P) {
   using Traits = OpTraits<kOp>;
@@ -194,7 +195,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int a = 0; a < kMaxOuter; ++a) {
         ibo[a] = a < P.n_outer ? S.o[a] * P.s_o[a] - P.p_o[a] : 0;
       }
-      const int x0 = S.q0 * P.mt * P.e0 * P.s[0] - P.p[0];
+      const int x0 = S.q0 * kMT * P.e0 * P.s[0] - P.p[0];
       const int x1 = S.q1 * P.b1 * P.s[1] - P.p[1];
       const int x2 = S.q2 * P.b2 * P.s[2] - P.p[2];
       int to[kMaxOuter];
@@ -281,9 +282,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     // ------------------------------ MMA issuer ------------------------------
-    // The whole warp runs the loop and waits; one elected lane issues the MMAs and
-    // commits (tcgen05.mma from a converged warp issues at the operand-bandwidth rate).
-    const bool leader = dev::elect_one();
+    // The whole warp runs the loop, waits and executes every MMA / commit instruction;
+    // elect.sync inside each one picks the issuing lane, so control flow never diverges.
+    const bool leader = lane == 0;
+    const uint32_t tmem_u = dev::warp_uniform(tmem);
     // Descriptors differ only in their start-address field (bits 0-13, address >> 4):
     // build the constant part once and add offsets in 16-byte units. Shared memory is
     // below 256 KB, so the field never carries into the next one.
@@ -297,7 +299,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t a_small_units = P.a_part_bytes >> 4;
     const uint32_t b_small_units = P.b_part_bytes >> 4;
     const uint32_t tile_cols = static_cast<uint32_t>(P.n_pad);
-    const uint32_t acc_cols = static_cast<uint32_t>(P.mt * P.n_pad);
+    const uint32_t acc_cols = static_cast<uint32_t>(kMT * P.n_pad);
+    // Shifted taps of a stage are walked j1 fastest with incremental addresses; the A
+    // offset steps by j1_units, or back to j1 = 0 and on to the next j0 at a j1 wrap.
+    const uint32_t j0_wrap = j0_units - static_cast<uint32_t>(P.nshift1 - 1) * j1_units;
+    const int nshift_stage = P.nshift0 * P.nshift1;
+    const int acc_mask = P.nacc - 1;  // nacc is a power of two
     int stage = 0;
     uint32_t phase = 0;
     uint32_t done = 0;
@@ -305,68 +312,68 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     for (int64_t st = blockIdx.x; st < P.supers_total && ok; st += gridDim.x, ++iter) {
       const int buf = iter & 1;
-      if (!dev::mbar_wait(&acc_empty[buf], (static_cast<uint32_t>(iter >> 1) & 1u) ^ 1u, err,
-                          kSiteMmaAcc, P.timeout_ns)) {
+      if (!dev::mbar_wait_warp(&acc_empty[buf], (static_cast<uint32_t>(iter >> 1) & 1u) ^ 1u,
+                               err, kSiteMmaAcc, P.timeout_ns)) {
         break;
       }
       dev::tc_fence_after();
-      const uint32_t dbase = tmem + static_cast<uint32_t>(buf * P.acc_stride);
-      int w = 0;  // work item (unit, shifted tap) within the super tile
+      const uint32_t dbase = tmem_u + static_cast<uint32_t>(buf * P.acc_stride);
       for (int u = 0; u < P.units && ok; ++u) {
-        const int w_unit = w;
+        const int w_unit = u * nshift_stage;  // work item (unit, shifted tap) index
         for (int cb = 0; cb < P.cblocks; ++cb) {
-          if (!dev::mbar_wait(&full[stage], phase, err, kSiteMma, P.timeout_ns)) {
+          if (!dev::mbar_wait_warp(&full[stage], phase, err, kSiteMma, P.timeout_ns)) {
             ok = false;
             break;
           }
           dev::tc_fence_after();
-          const uint32_t sa = dev::smem_u32(smem + stage * P.stage_bytes) >> 4;
-          const uint32_t sbw = sa + (P.b_off >> 4);
-          int wi = w_unit;
-          for (int j0 = 0; j0 < P.nshift0; ++j0) {
-            for (int j1 = 0; j1 < P.nshift1; ++j1, ++wi) {
-              const int acc_index = wi % P.nacc;
-              const uint32_t first = (wi < P.nacc && cb == 0) ? 1u : 0u;
-              const uint32_t b_addr =
-                  sbw + static_cast<uint32_t>(j0 * P.nshift1 + j1) * btap_units;
-              uint32_t a_addr = sa + static_cast<uint32_t>(j0) * j0_units +
-                                static_cast<uint32_t>(j1) * j1_units;
-              uint32_t d = dbase + static_cast<uint32_t>(acc_index) * acc_cols;
-              if (leader) {
-                for (int m = 0; m < P.mt; ++m, a_addr += tile_units, d += tile_cols) {
+          const uint32_t sa =
+              dev::warp_uniform(dev::smem_u32(smem + stage * P.stage_bytes) >> 4);
+          uint32_t a_tap = sa;
+          uint32_t b_tap = sa + (P.b_off >> 4);
+          int j1 = 0;
+          // The M-tile and K-step loops are unrolled at compile time: a runtime loop or
+          // per-tap division between MMAs slows the issue below the operand-feed rate.
+          for (int t = 0; t < nshift_stage; ++t) {
+            const int wi = w_unit + t;
+            const uint32_t first = (wi < P.nacc && cb == 0) ? 1u : 0u;
+            const uint32_t d0 = dbase + static_cast<uint32_t>(wi & acc_mask) * acc_cols;
 #pragma unroll
-                  for (int kk = 0; kk < kKSteps; ++kk) {
-                    const uint64_t ad = desc_hi | (a_addr + 2u * kk);
-                    const uint64_t bd = desc_hi | (b_addr + 2u * kk);
-                    const uint32_t acc = (first != 0u && kk == 0) ? 0u : 1u;
-                    if constexpr (kParts == 2) {
-                      mma<true>(d, desc_hi | (a_addr + a_small_units + 2u * kk), bd, P.idesc,
-                                acc);
-                      mma<true>(d, ad, desc_hi | (b_addr + b_small_units + 2u * kk), P.idesc,
-                                1u);
-                      mma<true>(d, ad, bd, P.idesc, 1u);
-                    } else {
-                      mma<kTF32>(d, ad, bd, P.idesc, acc);
-                    }
-                  }
+            for (int m = 0; m < kMT; ++m) {
+              const uint32_t a_addr = a_tap + static_cast<uint32_t>(m) * tile_units;
+              const uint32_t d = d0 + static_cast<uint32_t>(m) * tile_cols;
+#pragma unroll
+              for (int kk = 0; kk < kKSteps; ++kk) {
+                const uint64_t ad = desc_hi | (a_addr + 2u * kk);
+                const uint64_t bd = desc_hi | (b_tap + 2u * kk);
+                const uint32_t acc = (first != 0u && kk == 0) ? 0u : 1u;
+                if constexpr (kParts == 2) {
+                  mma<true>(d, desc_hi | (a_addr + a_small_units + 2u * kk), bd, P.idesc, acc);
+                  mma<true>(d, ad, desc_hi | (b_tap + b_small_units + 2u * kk), P.idesc, 1u);
+                  mma<true>(d, ad, bd, P.idesc, 1u);
+                } else {
+                  mma<kTF32>(d, ad, bd, P.idesc, acc);
                 }
               }
-              __syncwarp();
+            }
+            b_tap += btap_units;
+            if (++j1 == P.nshift1) {
+              j1 = 0;
+              a_tap += j0_wrap;
+            } else {
+              a_tap += j1_units;
             }
           }
-          if (leader) {
-            dev::mma_commit(&empty[stage]);
-            *progress = ++done;
-          }
+          dev::mma_commit_warp(&empty[stage]);
+          ++done;
+          if (leader) *progress = done;
           __syncwarp();
           if (++stage == P.stages) {
             stage = 0;
             phase ^= 1u;
           }
         }
-        w += P.nshift0 * P.nshift1;
       }
-      if (leader) dev::mma_commit(&acc_full[buf]);
+      dev::mma_commit_warp(&acc_full[buf]);
       __syncwarp();
     }
   } else if (warp >= 2) {
@@ -394,8 +401,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int64_t channel_base =
           (S.n * P.out_channels_total + static_cast<int64_t>(S.g) * P.n_real) * P.out_volume;
       const OutT* group_bias = bias != nullptr ? bias + static_cast<int64_t>(S.g) * P.n_real : nullptr;
-      for (int m = 0; m < P.mt; ++m) {
-        const int o0 = (S.q0 * P.mt + m) * P.e0 + i0;
+      for (int m = 0; m < kMT; ++m) {
+        const int o0 = (S.q0 * kMT + m) * P.e0 + i0;
         const bool valid = o0 < P.out[0] && o1 < P.out[1] && o2 < P.out[2];
         const int64_t sp = S.outer_lin * P.out_box_vol +
                            (static_cast<int64_t>(o0) * P.out[1] + o1) * P.out[2] + o2;
@@ -414,7 +421,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t v[16];
             __syncwarp();
             dev::tmem_load16(
-                dbase + static_cast<uint32_t>((a * P.mt + m) * P.n_pad + c * 16), v);
+                dbase + static_cast<uint32_t>((a * kMT + m) * P.n_pad + c * 16), v);
             dev::tmem_load_wait();
 #pragma unroll
             for (int i = 0; i < 16; ++i) sum[i] += __uint_as_float(v[i]);
@@ -786,12 +793,15 @@ int launch_fprop(const ConvPass& pass, const FpropPlan& plan_in, cudaStream_t st
   const int kind = pass.op == kOpF16 ? kKindF16
                    : pass.op == kOpBF16 ? kKindBF16
                    : (plan.parts == 2 ? kKind3xTF32 : kKindTF32);
-#define CND_FPROP_CASE(KIND, KSTEPS) \
-  if (kind == KIND && P.ksteps == KSTEPS) kernel = fprop_kernel<KIND, KSTEPS>;
-  CND_FPROP_CASE(kKindF16, 1) CND_FPROP_CASE(kKindF16, 2) CND_FPROP_CASE(kKindF16, 4)
-  CND_FPROP_CASE(kKindBF16, 1) CND_FPROP_CASE(kKindBF16, 2) CND_FPROP_CASE(kKindBF16, 4)
-  CND_FPROP_CASE(kKindTF32, 1) CND_FPROP_CASE(kKindTF32, 2) CND_FPROP_CASE(kKindTF32, 4)
-  CND_FPROP_CASE(kKind3xTF32, 1) CND_FPROP_CASE(kKind3xTF32, 2) CND_FPROP_CASE(kKind3xTF32, 4)
+#define CND_FPROP_CASE(KIND, KSTEPS, MT) \
+  if (kind == KIND && P.ksteps == KSTEPS && P.mt == MT) kernel = fprop_kernel<KIND, KSTEPS, MT>;
+#define CND_FPROP_MT(KIND, KSTEPS)                                                  \
+  CND_FPROP_CASE(KIND, KSTEPS, 1) CND_FPROP_CASE(KIND, KSTEPS, 2) CND_FPROP_CASE(KIND, KSTEPS, 4) \
+  CND_FPROP_CASE(KIND, KSTEPS, 8)
+#define CND_FPROP_KS(KIND) CND_FPROP_MT(KIND, 1) CND_FPROP_MT(KIND, 2) CND_FPROP_MT(KIND, 4)
+  CND_FPROP_KS(kKindF16) CND_FPROP_KS(kKindBF16) CND_FPROP_KS(kKindTF32) CND_FPROP_KS(kKind3xTF32)
+#undef CND_FPROP_KS
+#undef CND_FPROP_MT
 #undef CND_FPROP_CASE
   if (kernel == nullptr) return fail(CND_ERR_UNSUPPORTED, "no fprop kernel for this operand");
   cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,

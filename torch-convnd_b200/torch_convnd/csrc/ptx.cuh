@@ -85,6 +85,15 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, ErrorW
   }
 }
 
+// mbar_wait for a whole converged warp with one warp-uniform answer: lanes that poll
+// independently could disagree at the deadline, and a warp that must stay converged
+// (elect.sync issue) takes the failure path together.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, ErrorWord err,
+                                               unsigned int site, uint64_t timeout_ns) {
+  const bool ok = mbar_wait(bar, parity, err, site, timeout_ns);
+  return __all_sync(0xffffffffu, ok) != 0;
+}
+
 // Like mbar_wait, for long waits (an epilogue waiting for a whole main loop): the
 // deadline restarts whenever the shared counter `progress` changes, so the limit
 // bounds a stall rather than the total work. Polls with a short sleep between tries.
@@ -188,6 +197,47 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
       "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
           smem_u32(bar))
       : "memory");
+}
+
+// Warp-wide forms of the MMA and commit: every lane of a converged warp executes them
+// and elect.sync picks the single issuing lane inside the instruction sequence, so the
+// warp never branches around the MMA. Issue loops built from these run at the operand
+// feed rate; the same MMAs inside a divergent `if (lane is leader) { loop }` issue at
+// roughly half that rate.
+__device__ __forceinline__ void mma_f16_warp(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                             uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "elect.sync _|q, 0xffffffff;\n\t"
+      "@q tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_tf32_warp(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                              uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "elect.sync _|q, 0xffffffff;\n\t"
+      "@q tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_commit_warp(uint64_t* bar) {
+  asm volatile(
+      "{\n\t.reg .pred q;\n\t"
+      "elect.sync _|q, 0xffffffff;\n\t"
+      "@q tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+
+// Makes a value provably warp-uniform (lane 0's copy) for the compiler.
+__device__ __forceinline__ uint32_t warp_uniform(uint32_t v) {
+  return __shfl_sync(0xffffffffu, v, 0);
 }
 
 // Loads 16 consecutive 32-bit TMEM columns of this thread's lane.

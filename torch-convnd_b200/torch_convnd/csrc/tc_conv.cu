@@ -80,41 +80,6 @@ __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
   return reinterpret_cast<uint8_t*>((v + 1023) & ~static_cast<uintptr_t>(1023));
 }
 
-// Decodes box `bt` of group `grp` (boxes enumerate q[2] fastest, then q[1], q[0], then
-// the outer output positions, then the batch).
-__device__ void decode_box(const BoxGeom& g, int64_t bt, int grp, BoxInfo& info) {
-  info.valid = bt < g.boxes_per_group ? 1 : 0;
-  if (!info.valid) bt = 0;
-  int64_t rest = bt;
-  info.q[2] = static_cast<int32_t>(rest % g.nbox[2]);
-  rest /= g.nbox[2];
-  info.q[1] = static_cast<int32_t>(rest % g.nbox[1]);
-  rest /= g.nbox[1];
-  info.q[0] = static_cast<int32_t>(rest % g.nbox[0]);
-  rest /= g.nbox[0];
-  // rest = n * out_outer_vol + outer_lin
-  const int64_t outer_lin = rest % g.out_outer_vol;
-  const int64_t n = rest / g.out_outer_vol;
-  info.n = static_cast<int32_t>(n);
-  info.outer_lin = outer_lin;
-  int64_t o = outer_lin;
-#pragma unroll
-  for (int a = kMaxOuter - 1; a >= 0; --a) {
-    if (a < g.n_outer) {
-      const int64_t coord = o % g.out_o[a];
-      o /= g.out_o[a];
-      info.ib_o[a] = static_cast<int32_t>(coord * g.s_o[a] - g.p_o[a]);
-    } else {
-      info.ib_o[a] = 0;
-    }
-  }
-  for (int a = 0; a < 3; ++a) {
-    info.ib[a] = info.q[a] * g.b[a] * g.s[a] - g.p[a];
-  }
-  info.in_ng_base = (n * g.groups + grp) * g.in_merged_per_ng;
-  info.out_merged = (n * g.groups + grp) * g.out_outer_vol + outer_lin;
-}
-
 // Walks box indices in order (q2 fastest, then q1, q0, outer position, batch) without
 // divisions; the outer coordinates are re-derived only when the outer position changes.
 struct BoxCursor {
@@ -218,7 +183,7 @@ struct WgradMaps {
   CUtensorMap grad[3];
 };
 
-template <int kParts>
+template <int kParts, int kKSteps>
 __global__ void __launch_bounds__(kThreads, 1)
     wgrad_kernel(const __grid_constant__ WgradMaps maps,
                  const __grid_constant__ WgradKernelParams P) {
@@ -419,8 +384,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     (void)ok;
   } else if (warp == 1) {
-    // ---------------- MMA issuer (converged warp, one elected lane issues) ----------------
-    const bool leader = dev::elect_one();
+    // ---------------- MMA issuer ----------------
+    // The whole warp runs the loop and executes every MMA / commit; elect.sync inside
+    // each instruction picks the issuing lane, so control flow never diverges.
+    const bool leader = lane == 0;
+    const uint32_t tmem_u = dev::warp_uniform(tmem);
     int a_stage = 0, b_slot = 0;
     uint32_t a_phase = 0, b_phase = 0;
     // Constant descriptor parts; per MMA only the start-address field (address >> 4)
@@ -435,53 +403,49 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t b_part = P.b_part_bytes >> 4;
     bool ok = true;
     for (int64_t pt = p_begin; pt < p_end && ok; ++pt) {
-      if (!dev::mbar_wait(&b_full[b_slot], b_phase, err, kSiteWMma, P.timeout_ns)) break;
-      const uint32_t bs = dev::smem_u32(b_base + b_slot * P.b_slot_bytes) >> 4;
+      if (!dev::mbar_wait_warp(&b_full[b_slot], b_phase, err, kSiteWMma, P.timeout_ns)) break;
+      const uint32_t bs = dev::warp_uniform(dev::smem_u32(b_base + b_slot * P.b_slot_bytes) >> 4);
       const uint32_t first_tile = pt == p_begin ? 1u : 0u;
       for (int unit = 0; unit < unit_count; ++unit) {
-        if (!dev::mbar_wait(&a_full[a_stage], a_phase, err, kSiteWMma, P.timeout_ns)) {
+        if (!dev::mbar_wait_warp(&a_full[a_stage], a_phase, err, kSiteWMma, P.timeout_ns)) {
           ok = false;
           break;
         }
         dev::tc_fence_after();
-        if (leader) {
-          const uint32_t as = dev::smem_u32(a_base + a_stage * P.a_slot_bytes) >> 4;
-          for (int gi = 0; gi < P.mtpu; ++gi) {
-            const uint32_t d =
-                tmem + static_cast<uint32_t>((unit * P.mtpu + gi) * P.n_pad);
-            const uint32_t ag = as + static_cast<uint32_t>(gi) * group_units;
-            for (int ks = 0; ks < P.ksteps; ++ks) {
-              const uint32_t aoff = ag + static_cast<uint32_t>(ks) * a_step;
-              const uint32_t boff = bs + static_cast<uint32_t>(ks) * b_step;
+        const uint32_t as =
+            dev::warp_uniform(dev::smem_u32(a_base + a_stage * P.a_slot_bytes) >> 4);
+        for (int gi = 0; gi < P.mtpu; ++gi) {
+          const uint32_t d = tmem_u + static_cast<uint32_t>((unit * P.mtpu + gi) * P.n_pad);
+          const uint32_t ag = as + static_cast<uint32_t>(gi) * group_units;
+          // K steps unrolled at compile time (a runtime loop between MMAs slows issue).
 #pragma unroll
-              for (int q = 0; q < product_count<kParts>(); ++q) {
-                const uint64_t ad = a_hi | (aoff + product_a(kParts, q) * a_part);
-                const uint64_t bd = b_hi | (boff + product_b(kParts, q) * b_part);
-                const uint32_t acc = (first_tile != 0u && ks == 0 && q == 0) ? 0u : 1u;
-                dev::mma_f16(d, ad, bd, P.idesc, acc);
-              }
+          for (int ks = 0; ks < kKSteps; ++ks) {
+            const uint32_t aoff = ag + static_cast<uint32_t>(ks) * a_step;
+            const uint32_t boff = bs + static_cast<uint32_t>(ks) * b_step;
+#pragma unroll
+            for (int q = 0; q < product_count<kParts>(); ++q) {
+              const uint64_t ad = a_hi | (aoff + product_a(kParts, q) * a_part);
+              const uint64_t bd = b_hi | (boff + product_b(kParts, q) * b_part);
+              const uint32_t acc = (first_tile != 0u && ks == 0 && q == 0) ? 0u : 1u;
+              dev::mma_f16_warp(d, ad, bd, P.idesc, acc);
             }
           }
-          dev::mma_commit(&a_empty[a_stage]);
         }
-        __syncwarp();
+        dev::mma_commit_warp(&a_empty[a_stage]);
         if (++a_stage == P.a_stages) {
           a_stage = 0;
           a_phase ^= 1u;
         }
       }
-      if (leader) {
-        dev::mma_commit(&b_empty[b_slot]);
-        *progress = static_cast<uint32_t>(pt - p_begin + 1);
-      }
+      dev::mma_commit_warp(&b_empty[b_slot]);
+      if (leader) *progress = static_cast<uint32_t>(pt - p_begin + 1);
       __syncwarp();
       if (++b_slot == 2) {
         b_slot = 0;
         b_phase ^= 1u;
       }
     }
-    if (leader) dev::mma_commit(acc_bar);
-    __syncwarp();
+    dev::mma_commit_warp(acc_bar);
   } else if (warp >= 2) {
     // ---------------- epilogue: TMEM -> fp32 partial ----------------
     dev::mbar_wait_progress(acc_bar, 0, progress, err, kSiteWEpilogue, P.timeout_ns);
@@ -751,15 +715,6 @@ int sm_count() {
   return count;
 }
 
-// Bytes of one channel-block row for c_pad channels (the swizzle width), or 0 when the
-// padded channel count is not one of the supported shapes.
-int channel_block_bytes(int op, int c_pad) {
-  const int row = c_pad * element_size(op);
-  if (row == 32 || row == 64 || row == 128) return row;
-  if (row > 128 && row % 128 == 0) return 128;
-  return 0;
-}
-
 }  // namespace
 
 namespace {
@@ -979,22 +934,21 @@ int launch_wgrad_pass(const WgradPass& pass, cudaStream_t stream, uint64_t timeo
   }
   const dim3 grid(static_cast<unsigned>(P.splits), static_cast<unsigned>(plan.chunks),
                   static_cast<unsigned>(pass.groups));
+  using Kernel = void (*)(WgradMaps, WgradKernelParams);
+  Kernel kernel = nullptr;
   if (plan.parts == 3) {
-    auto kernel = wgrad_kernel<3>;
-    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         static_cast<int>(plan.smem));
-    kernel<<<grid, kThreads, plan.smem, stream>>>(maps, P);
+    kernel = P.ksteps == 8 ? wgrad_kernel<3, 8> : wgrad_kernel<3, 4>;
   } else if (plan.parts == 2) {
-    auto kernel = wgrad_kernel<2>;
-    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         static_cast<int>(plan.smem));
-    kernel<<<grid, kThreads, plan.smem, stream>>>(maps, P);
+    kernel = P.ksteps == 8 ? wgrad_kernel<2, 8> : wgrad_kernel<2, 4>;
   } else {
-    auto kernel = wgrad_kernel<1>;
-    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         static_cast<int>(plan.smem));
-    kernel<<<grid, kThreads, plan.smem, stream>>>(maps, P);
+    kernel = P.ksteps == 8 ? wgrad_kernel<1, 8> : wgrad_kernel<1, 4>;
   }
+  if (P.ksteps != 8 && P.ksteps != 4) {
+    return fail(CND_ERR_UNSUPPORTED, "weight-gradient K chunk outside the tcgen05 path");
+  }
+  cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       static_cast<int>(plan.smem));
+  kernel<<<grid, kThreads, plan.smem, stream>>>(maps, P);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     return fail(CND_ERR_CUDA, "wgrad_kernel launch failed: %s", cudaGetErrorString(e));
