@@ -770,8 +770,9 @@ bool plan_wgrad(const WgradPass& pass, int splits_hint, WgradPlan* plan) {
   bool planned = false;
   if (halo_ok) {
     // Position tile [1, b1, b2] with b2 a power of two >= 8 (8-row alignment of every
-    // tap window), least padding waste first.
-    for (int kc : {128, 64}) {
+    // tap window), least padding waste first. The longest K chunk that fits comes first:
+    // every A box then feeds more MMAs per barrier handoff and commit.
+    for (int kc : {256, 128, 64}) {
       double best_waste = 1e30;
       int best_b2 = 0;
       for (int b2 = 8; b2 <= kc; b2 *= 2) {
@@ -936,14 +937,19 @@ int launch_wgrad_pass(const WgradPass& pass, cudaStream_t stream, uint64_t timeo
                   static_cast<unsigned>(pass.groups));
   using Kernel = void (*)(WgradMaps, WgradKernelParams);
   Kernel kernel = nullptr;
+#define CND_WGRAD_PICK(PARTS)                                        \
+  kernel = P.ksteps == 16  ? wgrad_kernel<PARTS, 16>                 \
+           : P.ksteps == 8 ? wgrad_kernel<PARTS, 8>                  \
+                           : wgrad_kernel<PARTS, 4>;
   if (plan.parts == 3) {
-    kernel = P.ksteps == 8 ? wgrad_kernel<3, 8> : wgrad_kernel<3, 4>;
+    CND_WGRAD_PICK(3)
   } else if (plan.parts == 2) {
-    kernel = P.ksteps == 8 ? wgrad_kernel<2, 8> : wgrad_kernel<2, 4>;
+    CND_WGRAD_PICK(2)
   } else {
-    kernel = P.ksteps == 8 ? wgrad_kernel<1, 8> : wgrad_kernel<1, 4>;
+    CND_WGRAD_PICK(1)
   }
-  if (P.ksteps != 8 && P.ksteps != 4) {
+#undef CND_WGRAD_PICK
+  if (P.ksteps != 16 && P.ksteps != 8 && P.ksteps != 4) {
     return fail(CND_ERR_UNSUPPORTED, "weight-gradient K chunk outside the tcgen05 path");
   }
   cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,

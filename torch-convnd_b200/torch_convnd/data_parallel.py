@@ -66,9 +66,10 @@ class GradientBucketer:
 
     Parameters are grouped into buckets of at most `bucket_bytes` (counted in the
     reduction dtype; one dtype and device per bucket) in reverse registration order, the
-    order in which backward produces their gradients for a sequential network. With ``overlap=True`` each bucket's all-reduce starts from the
-    gradient hook of its last parameter; otherwise all buckets are reduced in
-    ``finish()``. Call ``finish()`` once per step after ``backward()``.
+    order in which backward produces their gradients for a sequential network. With
+    ``overlap=True`` each bucket's all-reduce starts from the gradient hook of its last
+    parameter; otherwise all buckets are reduced in ``finish()``. Call ``finish()`` once
+    per step after ``backward()``.
     """
 
     def __init__(self, parameters: Iterable[torch.nn.Parameter], group=None,
