@@ -42,6 +42,7 @@ constexpr uint32_t kSiteProducer = 0x301, kSiteMma = 0x302, kSiteEpilogue = 0x30
 struct FpropMaps {
   CUtensorMap act[2];
   CUtensorMap wt[2];
+  CUtensorMap out;  // channels-first output, dims (o2, o1, o0, outer, n*C): TMA stores
 };
 
 __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
@@ -106,7 +107,7 @@ struct OpTraits<kKindF16> {
   static constexpr bool tf32 = false;
   static constexpr int parts = 1;
   static __device__ __forceinline__ Out cast(float v) { return __float2half_rn(v); }
-  static __device__ __forceinline__ float load(const Out* p) { return __half2float(*p); }
+  static __device__ __forceinline__ float load(const Out* p) { return __half2float(__ldg(p)); }
 };
 template <>
 struct OpTraits<kKindBF16> {
@@ -114,7 +115,7 @@ struct OpTraits<kKindBF16> {
   static constexpr bool tf32 = false;
   static constexpr int parts = 1;
   static __device__ __forceinline__ Out cast(float v) { return __float2bfloat16_rn(v); }
-  static __device__ __forceinline__ float load(const Out* p) { return __bfloat162float(*p); }
+  static __device__ __forceinline__ float load(const Out* p) { return __bfloat162float(__ldg(p)); }
 };
 template <>
 struct OpTraits<kKindTF32> {
@@ -122,7 +123,7 @@ struct OpTraits<kKindTF32> {
   static constexpr bool tf32 = true;
   static constexpr int parts = 1;
   static __device__ __forceinline__ Out cast(float v) { return v; }
-  static __device__ __forceinline__ float load(const Out* p) { return *p; }
+  static __device__ __forceinline__ float load(const Out* p) { return __ldg(p); }
 };
 template <>
 struct OpTraits<kKind3xTF32> {
@@ -130,8 +131,43 @@ struct OpTraits<kKind3xTF32> {
   static constexpr bool tf32 = true;
   static constexpr int parts = 2;
   static __device__ __forceinline__ Out cast(float v) { return v; }
-  static __device__ __forceinline__ float load(const Out* p) { return *p; }
+  static __device__ __forceinline__ float load(const Out* p) { return __ldg(p); }
 };
+
+// One 16-channel chunk of an epilogue row: the sum of the `used` rotating accumulators
+// of M tile m (TMEM columns (a * kMT + m) * n_pad + c * 16) plus the bias. The bias
+// chunk is fetched before the TMEM loads, so its latency is paid once per chunk.
+template <typename Traits, int kMT>
+__device__ __forceinline__ void epilogue_chunk(uint32_t dbase, int m, int c, int n_pad, int used,
+                                               const typename Traits::Out* group_bias,
+                                               int n_real, float (&out)[16]) {
+  float b[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const int co = c * 16 + i;
+    b[i] = (group_bias != nullptr && co < n_real) ? Traits::load(group_bias + co) : 0.0f;
+  }
+  {
+    uint32_t v[16];
+    __syncwarp();
+    dev::tmem_load16(dbase + static_cast<uint32_t>(m * n_pad + c * 16), v);
+    dev::tmem_load_wait();
+#pragma unroll
+    for (int i = 0; i < 16; ++i) out[i] = __uint_as_float(v[i]);
+  }
+  for (int a = 1; a < used; ++a) {
+    uint32_t v[16];
+    __syncwarp();
+    dev::tmem_load16(dbase + static_cast<uint32_t>((a * kMT + m) * n_pad + c * 16), v);
+    dev::tmem_load_wait();
+#pragma unroll
+    for (int i = 0; i < 16; ++i) out[i] += __uint_as_float(v[i]);
+  }
+  if (group_bias != nullptr) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) out[i] += b[i];
+  }
+}
 
 template <int kOp, int kKSteps, int kMT>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -142,7 +178,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int kParts = Traits::parts;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + P.stages * P.stage_bytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + P.bar_off);
   uint64_t* empty = full + P.stages;
   uint64_t* acc_full = empty + P.stages;
   uint64_t* acc_empty = acc_full + 2;
@@ -387,6 +423,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int used = work_per_super < P.nacc ? work_per_super : P.nacc;
     const OutT* bias = static_cast<const OutT*>(P.bias);
     OutT* out = static_cast<OutT*>(P.dst);
+    const bool store_issuer = threadIdx.x == 64;  // warp 2, lane 0
+    int out_tiles = 0;
     int iter = 0;
     for (int64_t st = blockIdx.x; st < P.supers_total; st += gridDim.x, ++iter) {
       const int buf = iter & 1;
@@ -401,6 +439,37 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int64_t channel_base =
           (S.n * P.out_channels_total + static_cast<int64_t>(S.g) * P.n_real) * P.out_volume;
       const OutT* group_bias = bias != nullptr ? bias + static_cast<int64_t>(S.g) * P.n_real : nullptr;
+      if (P.tma_store) {
+        // Stage each M tile as [channel][position] and write it with one TMA store; the
+        // buffer of tile t is reused by tile t + 2 once that store has read it.
+        const int32_t nc0 = static_cast<int32_t>(S.n * P.out_channels_total +
+                                                 static_cast<int64_t>(S.g) * P.n_real);
+        for (int m = 0; m < kMT; ++m, ++out_tiles) {
+          OutT* stage_buf = reinterpret_cast<OutT*>(smem + P.out_stage_off +
+                                                    (out_tiles & 1) * P.out_tile_bytes);
+          if (store_issuer) dev::bulk_wait_group_read<1>();
+          dev::named_barrier(1, 128);
+          for (int c = 0; c < P.n_pad / 16; ++c) {
+            float value[16];
+            epilogue_chunk<Traits, kMT>(dbase, m, c, P.n_pad, used, group_bias, P.n_real, value);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const int co = c * 16 + i;
+              if (co < P.n_real) stage_buf[co * 128 + row] = Traits::cast(value[i]);
+            }
+          }
+          dev::fence_proxy_async();
+          dev::named_barrier(1, 128);
+          if (store_issuer) {
+            dev::tma_store_5d(&maps.out, stage_buf, S.q2 * P.b2, S.q1 * P.b1,
+                              (S.q0 * kMT + m) * P.e0, static_cast<int32_t>(S.outer_lin), nc0);
+            dev::bulk_commit_group();
+          }
+        }
+        dev::tc_fence_before();
+        dev::mbar_arrive(&acc_empty[buf]);
+        continue;
+      }
       for (int m = 0; m < kMT; ++m) {
         const int o0 = (S.q0 * kMT + m) * P.e0 + i0;
         const bool valid = o0 < P.out[0] && o1 < P.out[1] && o2 < P.out[2];
@@ -408,33 +477,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                            (static_cast<int64_t>(o0) * P.out[1] + o1) * P.out[2] + o2;
         OutT* dst = out + channel_base + sp;
         for (int c = 0; c < P.n_pad / 16; ++c) {
-          float sum[16];
-          {
-            uint32_t v[16];
-            __syncwarp();
-            dev::tmem_load16(dbase + static_cast<uint32_t>(m * P.n_pad + c * 16), v);
-            dev::tmem_load_wait();
-#pragma unroll
-            for (int i = 0; i < 16; ++i) sum[i] = __uint_as_float(v[i]);
-          }
-          for (int a = 1; a < used; ++a) {
-            uint32_t v[16];
-            __syncwarp();
-            dev::tmem_load16(
-                dbase + static_cast<uint32_t>((a * kMT + m) * P.n_pad + c * 16), v);
-            dev::tmem_load_wait();
-#pragma unroll
-            for (int i = 0; i < 16; ++i) sum[i] += __uint_as_float(v[i]);
-          }
+          float value[16];
+          epilogue_chunk<Traits, kMT>(dbase, m, c, P.n_pad, used, group_bias, P.n_real, value);
           if (valid) {
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
               const int co = c * 16 + i;
-              if (co < P.n_real) {
-                float value = sum[i];
-                if (group_bias != nullptr) value += Traits::load(group_bias + co);
-                dst[static_cast<int64_t>(co) * P.out_volume] = Traits::cast(value);
-              }
+              if (co < P.n_real) dst[static_cast<int64_t>(co) * P.out_volume] = Traits::cast(value[i]);
             }
           }
         }
@@ -442,6 +491,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       dev::tc_fence_before();
       dev::mbar_arrive(&acc_empty[buf]);
     }
+    // The staged stores must be complete before the CTA's shared memory goes away.
+    if (P.tma_store && store_issuer) dev::bulk_wait_group<0>();
   }
   dev::tc_fence_before();
   __syncthreads();
@@ -712,11 +763,37 @@ bool plan_fprop(const ConvPass& pass, FpropPlan* plan) {
   P.stages = static_cast<int>((200 * 1024) / P.stage_bytes);
   if (P.stages > 8) P.stages = 8;
   if (P.stages < 2) return false;
+  // Output through staged TMA stores when the channels-first rows allow 16-byte aligned
+  // boxes (innermost output extent and tile width multiples of 16 bytes) and the two
+  // staging buffers fit beside at least two stages, without giving up two CTAs per SM.
+  const size_t extra = 1024 + (2 * 8 + 4) * 8 + 64;
+  P.tma_store = 0;
+  P.out_tile_bytes = round_up(static_cast<uint32_t>(pass.n_real * 128 * es), 1024);
+  const bool store_shape = (static_cast<int64_t>(P.out[2]) * es) % 16 == 0 &&
+                           (P.b2 * es) % 16 == 0 && pass.n_real <= 256 &&
+                           pass.batch * pass.groups * pass.n_real <= kInt32Max &&
+                           P.out_outer_vol <= kInt32Max;
+  if (store_shape) {
+    const bool two = static_cast<size_t>(P.stages) * P.stage_bytes + extra <= 110 * 1024 &&
+                     pow2_columns(2 * P.nacc * P.mt * pass.n_pad) <= 256;
+    const size_t cap = two ? 110 * 1024 - extra : 216 * 1024;
+    const size_t staging = 2 * static_cast<size_t>(P.out_tile_bytes);
+    if (cap > staging) {
+      int st = static_cast<int>((cap - staging) / P.stage_bytes);
+      if (st > 8) st = 8;
+      if (st >= 2) {
+        P.stages = st;
+        P.tma_store = 1;
+      }
+    }
+  }
+  P.out_stage_off = static_cast<uint32_t>(P.stages) * P.stage_bytes;
+  P.bar_off = P.out_stage_off + (P.tma_store ? 2 * P.out_tile_bytes : 0);
   P.idesc = make_idesc(pass.op, 128, pass.n_pad);
   P.out_dtype = pass.out_dtype;
   P.out_channels_total = pass.groups * pass.n_real;
   plan->parts = parts;
-  plan->smem = static_cast<size_t>(P.stages) * P.stage_bytes + 1024 + (2 * P.stages + 4) * 8 + 64;
+  plan->smem = static_cast<size_t>(P.bar_off) + 1024 + (2 * P.stages + 4) * 8 + 64;
   // Weight packing order: one load unit's shifted taps are consecutive rows.
   plan->shift0 = P.nshift0 > 1;
   plan->shift1 = P.nshift1 > 1;
@@ -777,6 +854,27 @@ int launch_fprop(const ConvPass& pass, const FpropPlan& plan_in, cudaStream_t st
                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) {
       return fail(CND_ERR_CUDA, "cuTensorMapEncodeTiled (weights) failed with code %d",
+                  static_cast<int>(r));
+    }
+  }
+  if (P.tma_store) {
+    const cuuint64_t e = static_cast<cuuint64_t>(es);
+    cuuint64_t odims[5] = {static_cast<cuuint64_t>(P.out[2]), static_cast<cuuint64_t>(P.out[1]),
+                           static_cast<cuuint64_t>(P.out[0]),
+                           static_cast<cuuint64_t>(P.out_outer_vol),
+                           static_cast<cuuint64_t>(pass.batch * pass.groups * pass.n_real)};
+    cuuint64_t ostrides[4] = {static_cast<cuuint64_t>(P.out[2]) * e,
+                              static_cast<cuuint64_t>(P.out[1]) * P.out[2] * e,
+                              static_cast<cuuint64_t>(P.out_box_vol) * e,
+                              static_cast<cuuint64_t>(P.out_volume) * e};
+    cuuint32_t obox[5] = {static_cast<cuuint32_t>(P.b2), static_cast<cuuint32_t>(P.b1),
+                          static_cast<cuuint32_t>(P.e0), 1, static_cast<cuuint32_t>(pass.n_real)};
+    cuuint32_t oestr[5] = {1, 1, 1, 1, 1};
+    const CUresult r = encode(&maps.out, map_dtype(pass.op), 5, pass.dst, odims, ostrides, obox,
+                              oestr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                              CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+      return fail(CND_ERR_CUDA, "cuTensorMapEncodeTiled (output) failed with code %d",
                   static_cast<int>(r));
     }
   }

@@ -34,7 +34,12 @@ struct FpropParams {
   int n_pad, n_real, nacc, acc_stride;
   uint32_t a_part_bytes, b_part_bytes, b_off, stage_bytes, tx_bytes, idesc, tmem_cols;
   int stages;
-  // output (channels-first)
+  uint32_t bar_off;  // barriers after the stages (and the output staging buffers)
+  // output (channels-first); tma_store = 1 stages each M tile in shared memory as
+  // [channel][position] (two buffers of out_tile_bytes at out_stage_off) and writes it
+  // with one TMA store, else every thread stores its position's channels directly
+  int tma_store;
+  uint32_t out_stage_off, out_tile_bytes;
   void* dst;
   const void* bias;
   int out_dtype;
