@@ -135,11 +135,12 @@ struct OpTraits<kKind3xTF32> {
 };
 
 // One 16-channel chunk of an epilogue row: the sum of the `used` rotating accumulators
-// of M tile m (TMEM columns (a * kMT + m) * n_pad + c * 16) plus the bias. The bias
-// chunk is fetched before the TMEM loads, so its latency is paid once per chunk.
-template <typename Traits, int kMT>
-__device__ __forceinline__ void epilogue_chunk(uint32_t dbase, int m, int c, int n_pad, int used,
-                                               const typename Traits::Out* group_bias,
+// of an M tile (TMEM columns tile_col + a * kMT * n_pad + c * 16) plus the bias. The
+// bias chunk is fetched before the TMEM loads, so its latency is paid once per chunk.
+// kZero writes zeros back over the columns read (folded passes accumulate onto them).
+template <typename Traits, int kMT, bool kZero>
+__device__ __forceinline__ void epilogue_chunk(uint32_t dbase, int tile_col, int c, int n_pad,
+                                               int used, const typename Traits::Out* group_bias,
                                                int n_real, float (&out)[16]) {
   float b[16];
 #pragma unroll
@@ -147,19 +148,22 @@ __device__ __forceinline__ void epilogue_chunk(uint32_t dbase, int m, int c, int
     const int co = c * 16 + i;
     b[i] = (group_bias != nullptr && co < n_real) ? Traits::load(group_bias + co) : 0.0f;
   }
+  const uint32_t col = dbase + static_cast<uint32_t>(tile_col + c * 16);
   {
     uint32_t v[16];
     __syncwarp();
-    dev::tmem_load16(dbase + static_cast<uint32_t>(m * n_pad + c * 16), v);
+    dev::tmem_load16(col, v);
     dev::tmem_load_wait();
+    if constexpr (kZero) dev::tmem_zero16(col);
 #pragma unroll
     for (int i = 0; i < 16; ++i) out[i] = __uint_as_float(v[i]);
   }
   for (int a = 1; a < used; ++a) {
     uint32_t v[16];
     __syncwarp();
-    dev::tmem_load16(dbase + static_cast<uint32_t>((a * kMT + m) * n_pad + c * 16), v);
+    dev::tmem_load16(col + static_cast<uint32_t>(a * kMT * n_pad), v);
     dev::tmem_load_wait();
+    if constexpr (kZero) dev::tmem_zero16(col + static_cast<uint32_t>(a * kMT * n_pad));
 #pragma unroll
     for (int i = 0; i < 16; ++i) out[i] += __uint_as_float(v[i]);
   }
@@ -169,7 +173,7 @@ __device__ __forceinline__ void epilogue_chunk(uint32_t dbase, int m, int c, int
   }
 }
 
-template <int kOp, int kKSteps, int kMT>
+template <int kOp, int kKSteps, int kMT, int kFold>
 __global__ void __launch_bounds__(kThreads, 1)
     fprop_kernel(const __grid_constant__ FpropMaps maps, const __grid_constant__ FpropParams P) {
   using Traits = OpTraits<kOp>;
@@ -348,8 +352,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     for (int64_t st = blockIdx.x; st < P.supers_total && ok; st += gridDim.x, ++iter) {
       const int buf = iter & 1;
-      if (!dev::mbar_wait_warp(&acc_empty[buf], (static_cast<uint32_t>(iter >> 1) & 1u) ^ 1u,
-                               err, kSiteMmaAcc, P.timeout_ns)) {
+      // Folded passes wait for the epilogue's zeroing of the buffer (it arrives once at
+      // start); otherwise the first use of each buffer passes at once.
+      const uint32_t acc_parity = (static_cast<uint32_t>(iter >> 1) & 1u) ^ (kFold ? 0u : 1u);
+      if (!dev::mbar_wait_warp(&acc_empty[buf], acc_parity, err, kSiteMmaAcc, P.timeout_ns)) {
         break;
       }
       dev::tc_fence_after();
@@ -364,6 +370,31 @@ __global__ void __launch_bounds__(kThreads, 1)
           dev::tc_fence_after();
           const uint32_t sa =
               dev::warp_uniform(dev::smem_u32(smem + stage * P.stage_bytes) >> 4);
+          if constexpr (kFold > 0) {
+            // One MMA per A slice i (and a1 shift): tap blocks j0 in [lo, hi] with
+            // 0 <= i - j0 < kMT, N = (hi - lo + 1) * n_pad, D at tile i - lo's column.
+            const uint32_t sbw = sa + (P.b_off >> 4);
+            for (int j1 = 0; j1 < P.nshift1; ++j1) {
+              const uint32_t a_j1 = sa + static_cast<uint32_t>(j1) * j1_units;
+              const uint32_t b_j1 = sbw + static_cast<uint32_t>(j1 * kFold) * btap_units;
+#pragma unroll
+              for (int i = 0; i < kMT + kFold - 1; ++i) {
+                constexpr int kLast = kMT - 1;
+                const int lo = i > kLast ? i - kLast : 0;
+                const int hi = i < kFold - 1 ? i : kFold - 1;
+                const uint32_t idesc =
+                    P.idesc_base | (static_cast<uint32_t>(((hi - lo + 1) * P.n_pad) >> 3) << 17);
+                const uint32_t a_addr = a_j1 + static_cast<uint32_t>(i) * tile_units;
+                const uint32_t b_addr = b_j1 + static_cast<uint32_t>(lo) * btap_units;
+                const uint32_t d = dbase + static_cast<uint32_t>(kLast - i + lo) * tile_cols;
+#pragma unroll
+                for (int kk = 0; kk < kKSteps; ++kk) {
+                  mma<kTF32>(d, desc_hi | (a_addr + 2u * kk), desc_hi | (b_addr + 2u * kk), idesc,
+                             1u);
+                }
+              }
+            }
+          } else {
           uint32_t a_tap = sa;
           uint32_t b_tap = sa + (P.b_off >> 4);
           int j1 = 0;
@@ -399,6 +430,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               a_tap += j1_units;
             }
           }
+          }
           dev::mma_commit_warp(&empty[stage]);
           ++done;
           if (leader) *progress = done;
@@ -424,6 +456,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     const OutT* bias = static_cast<const OutT*>(P.bias);
     OutT* out = static_cast<OutT*>(P.dst);
     const bool store_issuer = threadIdx.x == 64;  // warp 2, lane 0
+    // TMEM column of M tile m's accumulator (descending when the a0 taps are folded).
+    auto tile_col = [&](int m) { return (kFold > 0 ? kMT - 1 - m : m) * P.n_pad; };
+    if constexpr (kFold > 0) {
+      // Folded MMAs all accumulate: start both accumulator buffers at zero.
+      for (int c = 0; c < 2 * P.acc_stride; c += 16) {
+        __syncwarp();
+        dev::tmem_zero16(lane_addr + static_cast<uint32_t>(c));
+      }
+      dev::tmem_store_wait();
+      dev::tc_fence_before();
+      dev::mbar_arrive(&acc_empty[0]);
+      dev::mbar_arrive(&acc_empty[1]);
+    }
     int out_tiles = 0;
     int iter = 0;
     for (int64_t st = blockIdx.x; st < P.supers_total; st += gridDim.x, ++iter) {
@@ -451,7 +496,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           dev::named_barrier(1, 128);
           for (int c = 0; c < P.n_pad / 16; ++c) {
             float value[16];
-            epilogue_chunk<Traits, kMT>(dbase, m, c, P.n_pad, used, group_bias, P.n_real, value);
+            epilogue_chunk<Traits, kMT, (kFold > 0)>(dbase, tile_col(m), c, P.n_pad, used,
+                                                     group_bias, P.n_real, value);
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
               const int co = c * 16 + i;
@@ -466,6 +512,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             dev::bulk_commit_group();
           }
         }
+        if constexpr (kFold > 0) dev::tmem_store_wait();
         dev::tc_fence_before();
         dev::mbar_arrive(&acc_empty[buf]);
         continue;
@@ -478,7 +525,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         OutT* dst = out + channel_base + sp;
         for (int c = 0; c < P.n_pad / 16; ++c) {
           float value[16];
-          epilogue_chunk<Traits, kMT>(dbase, m, c, P.n_pad, used, group_bias, P.n_real, value);
+          epilogue_chunk<Traits, kMT, (kFold > 0)>(dbase, tile_col(m), c, P.n_pad, used,
+                                                   group_bias, P.n_real, value);
           if (valid) {
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
@@ -488,6 +536,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
+      if constexpr (kFold > 0) dev::tmem_store_wait();
       dev::tc_fence_before();
       dev::mbar_arrive(&acc_empty[buf]);
     }
@@ -642,12 +691,27 @@ bool fill_geometry(const ConvPass& pass, FpropParams* P) {
 }
 
 struct Candidate {
-  int e0, b1, b2, mt, shift0, shift1;
+  int e0, b1, b2, mt, shift0, shift1, row_bytes, fold;
 };
+
+// Cycles of one M=128, K=16 (or tf32 K=8) MMA with N columns on this part: the larger of
+// the tensor-pipe time and the shared-memory operand feed (A 4 KB + B 32 B per column at
+// 128 B per clock), both measured on B200.
+double mma_cycles(int n) {
+  const double compute = n / 2.0;
+  const double feed = (4096.0 + 32.0 * n) / 128.0;
+  return compute > feed ? compute : feed;
+}
 
 // Shared-memory stage layout of a candidate; false when it does not fit.
 bool layout_candidate(const ConvPass& pass, FpropParams* P, const Candidate& c, int parts) {
-  const int row_bytes = row_bytes_for(pass.op, pass.c_pad);
+  const int row_bytes = c.row_bytes;
+  const int es = pass.op == kOpF32 ? 4 : 2;
+  P->cblk_elems = row_bytes / es;
+  P->cblocks = pass.c_pad / P->cblk_elems;
+  P->ksteps = row_bytes / 32;
+  P->layout = static_cast<int>(layout_for(row_bytes));
+  P->fold = c.fold;
   const int k0 = P->k[0], k1 = P->k[1];
   P->e0 = c.e0;
   P->b1 = c.b1;
@@ -679,16 +743,12 @@ bool plan_fprop(const ConvPass& pass, FpropPlan* plan) {
   std::memset(plan, 0, sizeof(*plan));
   FpropParams& P = plan->params;
   if (pass.n_pad < 16 || pass.n_pad > 256 || pass.n_pad % 16 != 0) return false;
-  const int row_bytes = row_bytes_for(pass.op, pass.c_pad);
-  if (row_bytes == 0) return false;
+  const int row_max = row_bytes_for(pass.op, pass.c_pad);
+  if (row_max == 0) return false;
   if (!fill_geometry(pass, &P)) return false;
   const bool tf32 = pass.op == kOpF32;
   const int parts = (tf32 && pass.split3) ? 2 : 1;
   const int es = elem_size(pass.op);
-  P.cblk_elems = row_bytes / es;
-  P.cblocks = pass.c_pad / P.cblk_elems;
-  P.ksteps = row_bytes / 32;
-  P.layout = static_cast<int>(layout_for(row_bytes));
   P.n_pad = pass.n_pad;
   P.n_real = pass.n_real;
   const int products = parts == 2 ? 3 : 1;
@@ -697,17 +757,32 @@ bool plan_fprop(const ConvPass& pass, FpropPlan* plan) {
   double best = 1e300;
   FpropParams chosen{};
   bool found = false;
-  for (int e0 = 1; e0 <= 128; e0 *= 2) {
+  for (int row_bytes = row_max; row_bytes >= 32; row_bytes /= 2) {
+   // Narrower channel blocks (more K passes) only when the full row already fills 128 B.
+   if (row_bytes != row_max &&
+       (row_max < 64 || row_bytes < row_max / 2 || (pass.c_pad * es) % row_bytes != 0)) {
+     break;
+   }
+   for (int fold = 0; fold <= 1; ++fold) {
+    // Folding the a0 taps into N needs unit-stride a0 tiles of one slice, three a0 taps,
+    // single-product bf16/fp16 MMAs and 3 * n_pad <= 256.
+    if (fold && (tf32 || P.k[0] != 3 || P.d[0] != 1 || P.s[0] != 1 || 3 * pass.n_pad > 256)) {
+      continue;
+    }
+    for (int e0 = 1; e0 <= 128; e0 *= 2) {
+    if (fold && e0 != 1) continue;
     for (int b2 = 8; b2 <= 128; b2 *= 2) {
       if (128 % (e0 * b2) != 0) continue;
       const int b1 = 128 / (e0 * b2);
       for (int mt = 1; mt <= 8; mt *= 2) {
+        if (fold && mt < 2) continue;
         for (int shift0 = 0; shift0 <= 1; ++shift0) {
           if (shift0 && (P.s[0] != 1 || P.k[0] == 1)) continue;
+          if (fold && !shift0) continue;
           for (int shift1 = 0; shift1 <= 1; ++shift1) {
             if (shift1 && (P.s[1] != 1 || P.k[1] == 1 || e0 != 1)) continue;
             FpropParams trial = P;
-            const Candidate cand{e0, b1, b2, mt, shift0, shift1};
+            const Candidate cand{e0, b1, b2, mt, shift0, shift1, row_bytes, fold};
             if (!layout_candidate(pass, &trial, cand, parts)) continue;
             int nacc = 1;
             if (tf32) {
@@ -720,15 +795,25 @@ bool plan_fprop(const ConvPass& pass, FpropPlan* plan) {
             const double waste = (tiles0 * mt * e0 / P.out[0]) *
                                  (double((P.out[1] + b1 - 1) / b1) * b1 / P.out[1]) *
                                  (double((P.out[2] + b2 - 1) / b2) * b2 / P.out[2]);
-            const double mma_steps = double(mt) * P.taps * P.cblocks * P.ksteps * products;
-            const double mma_cycles = mma_steps * (pass.n_pad / 2.0);
-            const double feed_cycles = mma_steps * (128.0 * 32 + pass.n_pad * 32.0) / 128.0;
             const int nshift = trial.nshift0 * trial.nshift1;
-            const double units = double(P.taps) / nshift * P.cblocks;
+            const double units = double(P.taps) / nshift * trial.cblocks;
+            double mma_total;
+            if (fold) {
+              // one MMA per (slice, a1 shift), N = taps of the slice that hit a tile
+              double per_pass = 0.0;
+              for (int i = 0; i < mt + 2; ++i) {
+                const int lo = i > mt - 1 ? i - (mt - 1) : 0;
+                const int hi = i < 2 ? i : 2;
+                per_pass += mma_cycles((hi - lo + 1) * pass.n_pad);
+              }
+              mma_total = units * trial.nshift1 * trial.ksteps * per_pass;
+            } else {
+              mma_total = double(mt) * P.taps * trial.cblocks * trial.ksteps * products *
+                          mma_cycles(pass.n_pad);
+            }
             const double l2_cycles = units * trial.tx_bytes / 70.0;
             const double issue_cycles = units * 250.0;
-            double cycles = mma_cycles;
-            if (feed_cycles > cycles) cycles = feed_cycles;
+            double cycles = mma_total;
             if (l2_cycles > cycles) cycles = l2_cycles;
             if (issue_cycles > cycles) cycles = issue_cycles;
             // Bound plus a small preference for less L2 traffic and fewer load units
@@ -750,6 +835,8 @@ bool plan_fprop(const ConvPass& pass, FpropPlan* plan) {
         }
       }
     }
+    }
+   }
   }
   if (!found) return false;
   P = chosen;
@@ -790,6 +877,7 @@ bool plan_fprop(const ConvPass& pass, FpropPlan* plan) {
   P.out_stage_off = static_cast<uint32_t>(P.stages) * P.stage_bytes;
   P.bar_off = P.out_stage_off + (P.tma_store ? 2 * P.out_tile_bytes : 0);
   P.idesc = make_idesc(pass.op, 128, pass.n_pad);
+  P.idesc_base = P.idesc & ~(0x3Fu << 17);
   P.out_dtype = pass.out_dtype;
   P.out_channels_total = pass.groups * pass.n_real;
   plan->parts = parts;
@@ -797,6 +885,7 @@ bool plan_fprop(const ConvPass& pass, FpropPlan* plan) {
   // Weight packing order: one load unit's shifted taps are consecutive rows.
   plan->shift0 = P.nshift0 > 1;
   plan->shift1 = P.nshift1 > 1;
+  plan->fold = P.fold;
   plan->k_box[0] = P.k[0];
   plan->k_box[1] = P.k[1];
   plan->k_box[2] = P.k[2];
@@ -891,13 +980,24 @@ int launch_fprop(const ConvPass& pass, const FpropPlan& plan_in, cudaStream_t st
   const int kind = pass.op == kOpF16 ? kKindF16
                    : pass.op == kOpBF16 ? kKindBF16
                    : (plan.parts == 2 ? kKind3xTF32 : kKindTF32);
-#define CND_FPROP_CASE(KIND, KSTEPS, MT) \
-  if (kind == KIND && P.ksteps == KSTEPS && P.mt == MT) kernel = fprop_kernel<KIND, KSTEPS, MT>;
+#define CND_FPROP_CASE(KIND, KSTEPS, MT)                                                 \
+  if (kind == KIND && P.ksteps == KSTEPS && P.mt == MT && !P.fold)                        \
+    kernel = fprop_kernel<KIND, KSTEPS, MT, 0>;
+#define CND_FPROP_FOLD(KIND, KSTEPS, MT)                                                 \
+  if (kind == KIND && P.ksteps == KSTEPS && P.mt == MT && P.fold)                         \
+    kernel = fprop_kernel<KIND, KSTEPS, MT, 3>;
 #define CND_FPROP_MT(KIND, KSTEPS)                                                  \
   CND_FPROP_CASE(KIND, KSTEPS, 1) CND_FPROP_CASE(KIND, KSTEPS, 2) CND_FPROP_CASE(KIND, KSTEPS, 4) \
   CND_FPROP_CASE(KIND, KSTEPS, 8)
+#define CND_FPROP_FOLDS(KIND, KSTEPS) \
+  CND_FPROP_FOLD(KIND, KSTEPS, 2) CND_FPROP_FOLD(KIND, KSTEPS, 4) CND_FPROP_FOLD(KIND, KSTEPS, 8)
 #define CND_FPROP_KS(KIND) CND_FPROP_MT(KIND, 1) CND_FPROP_MT(KIND, 2) CND_FPROP_MT(KIND, 4)
+#define CND_FPROP_KSF(KIND) CND_FPROP_FOLDS(KIND, 1) CND_FPROP_FOLDS(KIND, 2) CND_FPROP_FOLDS(KIND, 4)
   CND_FPROP_KS(kKindF16) CND_FPROP_KS(kKindBF16) CND_FPROP_KS(kKindTF32) CND_FPROP_KS(kKind3xTF32)
+  CND_FPROP_KSF(kKindF16) CND_FPROP_KSF(kKindBF16)
+#undef CND_FPROP_KSF
+#undef CND_FPROP_FOLDS
+#undef CND_FPROP_FOLD
 #undef CND_FPROP_KS
 #undef CND_FPROP_MT
 #undef CND_FPROP_CASE

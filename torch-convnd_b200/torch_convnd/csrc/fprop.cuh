@@ -25,6 +25,11 @@ struct FpropParams {
   // tiling
   int e0, b1, b2, mt;
   int nshift0, nshift1;  // taps of a0 / a1 served by shared-memory shifts (1 = none)
+  // fold = 1: the a0 taps of a unit run as one MMA per A slice whose N spans every tap
+  // block that lands on a tile of the super (N = blocks * n_pad); tile m's accumulator
+  // sits at column (mt - 1 - m) * n_pad, so block j0 of slice i lands on tile i - j0.
+  // Accumulators are zeroed by the epilogue and every MMA accumulates.
+  int fold;
   int h0, h1;            // halo box extents (rows) along a0 / a1
   int nsup[3];
   int64_t supers_total;
@@ -33,6 +38,7 @@ struct FpropParams {
   int cblocks, cblk_elems, ksteps, row_bytes, layout;
   int n_pad, n_real, nacc, acc_stride;
   uint32_t a_part_bytes, b_part_bytes, b_off, stage_bytes, tx_bytes, idesc, tmem_cols;
+  uint32_t idesc_base;  // idesc without its N field (folded MMAs set N per slice)
   int stages;
   uint32_t bar_off;  // barriers after the stages (and the output staging buffers)
   // output (channels-first); tma_store = 1 stages each M tile in shared memory as
@@ -53,7 +59,7 @@ struct FpropPlan {
   int parts;         // 2 for 3xTF32 (big + small operand arrays)
   size_t smem;
   // weight packing order (see PackWeightArgs::unit_order)
-  int shift0, shift1;
+  int shift0, shift1, fold;
   int k_box[3];
 };
 

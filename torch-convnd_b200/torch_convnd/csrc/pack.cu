@@ -124,13 +124,13 @@ __global__ void __launch_bounds__(256) pack_act_kernel(const Tin* __restrict__ s
 // unit = (outer taps, t0 unless shifted, t1 unless shifted, t2) row-major, and within a
 // unit the shifted taps (t0 if shift0, t1 if shift1) row-major.
 __device__ __forceinline__ int packed_row_tap(int row, int k0, int k1, int k2, int shift0,
-                                              int shift1) {
+                                              int shift1, int fold) {
   const int n1 = shift1 ? k1 : 1;
   const int n0 = shift0 ? k0 : 1;
   const int ls = row % (n0 * n1);
   int rest = row / (n0 * n1);
-  const int j1 = ls % n1;
-  const int j0 = ls / n1;
+  const int j1 = fold ? ls / n0 : ls % n1;
+  const int j0 = fold ? ls % n0 : ls / n1;
   const int t2 = rest % k2;
   rest /= k2;
   int t1 = j1, t0 = j0;
@@ -214,7 +214,8 @@ __global__ void pack_weight_kernel(const T* __restrict__ w, T* __restrict__ dst,
     r /= a.n_pad;
     const int row = static_cast<int>(r % a.taps);
     const int g = static_cast<int>(r / a.taps);
-    const int t = packed_row_tap(row, a.k_box[0], a.k_box[1], a.k_box[2], a.shift0, a.shift1);
+    const int t = packed_row_tap(row, a.k_box[0], a.k_box[1], a.k_box[2], a.shift0, a.shift1,
+                                 a.fold);
     float v = 0.0f;
     if (!a.dgrad) {
       // forward operand: B[n = output channel][k = input channel] of tap t

@@ -29,6 +29,7 @@ struct PackWeightArgs {
   int groups, cout_g, cin_g, taps, n_pad, c_pad, dtype, mode, dgrad;
   int k_box[3];
   int shift0, shift1;
+  int fold;  // 1: within a unit the a0 taps are consecutive (j0 fastest), else a1 taps
 };
 
 int pack_activations(const PackActArgs& args, cudaStream_t stream);
