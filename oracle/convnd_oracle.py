@@ -163,8 +163,9 @@ def tap_reference(x, w, b, stride, padding, dilation, groups):
 
 def sampled_forward(x, w, b, stride, padding, dilation, groups, points):
     """Exact float64 outputs at sampled (n, co, out-coordinate) points, for full-size
-    property checks where the whole oracle would take too long."""
-    x = x.detach().to(torch.float64)
+    property checks where the whole oracle would take too long (reference
+    convnd.cpp:305-343 evaluated at single output positions)."""
+    x = x.detach()
     w = w.detach().to(torch.float64)
     rank = x.ndim - 2
     cg = x.shape[1] // groups
@@ -184,7 +185,76 @@ def sampled_forward(x, w, b, stride, padding, dilation, groups, points):
                 idx.append(c)
             if not ok:
                 continue
-            column = x[(n, slice(g * cg, (g + 1) * cg), *idx)]
+            column = x[(n, slice(g * cg, (g + 1) * cg), *idx)].to(torch.float64)
             total += float((w[(co, slice(None), *tap)] * column).sum())
         values.append(total)
+    return torch.tensor(values, dtype=torch.float64)
+
+
+def sampled_dgrad(dy, w, input_spatial, stride, padding, dilation, groups, points):
+    """Exact float64 input gradients at sampled (n, ci, in-coordinate) points: the sum over
+    the output channels of ci's group and the taps whose output position
+    o = (i + p - t*d) / s is integral and in range (the fold of reference
+    convnd_cuda.cu:147-169, evaluated at single input positions)."""
+    dy = dy.detach()
+    w = w.detach().to(torch.float64)
+    rank = dy.ndim - 2
+    cg = w.shape[1]
+    og = w.shape[0] // groups
+    out = dy.shape[2:]
+    values = []
+    for n, ci, coords in points:
+        g, cl = divmod(ci, cg)
+        total = 0.0
+        for tap in itertools.product(*(range(k) for k in w.shape[2:])):
+            idx = []
+            for axis in range(rank):
+                q = coords[axis] + padding[axis] - tap[axis] * dilation[axis]
+                if q < 0 or q % stride[axis] != 0 or q // stride[axis] >= out[axis]:
+                    break
+                idx.append(q // stride[axis])
+            else:
+                grads = dy[(n, slice(g * og, (g + 1) * og), *idx)].to(torch.float64)
+                total += float((w[(slice(g * og, (g + 1) * og), cl, *tap)] * grads).sum())
+        values.append(total)
+    del input_spatial  # the input extents bound the points, not the sum
+    return torch.tensor(values, dtype=torch.float64)
+
+
+def sampled_wgrad(dy, x, kernel, stride, padding, dilation, groups, entries):
+    """Exact float64 weight gradients at sampled (co, ci_in_group, tap) entries: the sum
+    over the batch and every output position whose input tap stays inside the input
+    (reference convnd.cpp:402-406, one entry of grad_weight at a time)."""
+    dy = dy.detach()
+    x = x.detach()
+    rank = x.ndim - 2
+    cg = x.shape[1] // groups
+    og = dy.shape[1] // groups
+    out = dy.shape[2:]
+    values = []
+    for co, cl, tap in entries:
+        g = co // og
+        out_slices, in_slices = [], []
+        empty = False
+        for axis in range(rank):
+            s, p, d, size = stride[axis], padding[axis], dilation[axis], x.shape[2 + axis]
+            shift = tap[axis] * d - p  # input = o * s + shift
+            lo = 0
+            while lo < out[axis] and lo * s + shift < 0:
+                lo += 1
+            hi = out[axis]
+            while hi > lo and (hi - 1) * s + shift >= size:
+                hi -= 1
+            if hi <= lo:
+                empty = True
+                break
+            out_slices.append(slice(lo, hi))
+            in_slices.append(slice(lo * s + shift, (hi - 1) * s + shift + 1, s))
+        if empty:
+            values.append(0.0)
+            continue
+        a = dy[(slice(None), co, *out_slices)].to(torch.float64)
+        b = x[(slice(None), g * cg + cl, *in_slices)].to(torch.float64)
+        values.append(float((a * b).sum()))
+    del kernel
     return torch.tensor(values, dtype=torch.float64)

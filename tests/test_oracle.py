@@ -147,3 +147,38 @@ def test_compiled_reference_matches_golden():
     assert result.returncode == 0, result.stderr[-2000:]
     worst = float(result.stdout.strip().split("=")[-1])
     assert worst < 1e-12
+
+
+@pytest.mark.parametrize(
+    ("shape", "cout", "kernel", "stride", "padding", "dilation", "groups"),
+    [((2, 4, 7, 6, 5), 6, (3, 2, 3), (1, 2, 1), (1, 1, 2), (1, 1, 2), 2),
+     ((1, 2, 9, 8), 3, (3, 3), (2, 2), (1, 0), (1, 2), 1),
+     ((2, 3, 5, 4, 4, 3), 2, (2, 3, 1, 3), (1, 1, 2, 1), (0, 1, 0, 2), (2, 1, 1, 1), 1)],
+)
+def test_sampled_oracle_matches_full_oracle(shape, cout, kernel, stride, padding, dilation,
+                                            groups):
+    """The point samplers used by the full-size GPU checks agree with the full fp64
+    oracle at every point of small strided, dilated and grouped problems."""
+    generator = torch.Generator().manual_seed(11)
+    x = torch.randn(shape, generator=generator, dtype=torch.float64)
+    w = torch.randn((cout, shape[1] // groups, *kernel), generator=generator,
+                    dtype=torch.float64)
+    b = torch.randn(cout, generator=generator, dtype=torch.float64)
+    y = oracle.forward(x, w, b, stride, padding, dilation, groups)
+    dy = torch.randn(y.shape, generator=generator, dtype=torch.float64)
+    dx, dw, _ = oracle.backward(dy, x, w, stride, padding, dilation, groups)
+    out_points = [(n, c, idx) for n in range(shape[0]) for c in range(cout)
+                  for idx in itertools.product(*map(range, y.shape[2:]))]
+    in_points = [(n, c, idx) for n in range(shape[0]) for c in range(shape[1])
+                 for idx in itertools.product(*map(range, shape[2:]))]
+    entries = [(co, cl, t) for co in range(cout) for cl in range(shape[1] // groups)
+               for t in itertools.product(*map(range, kernel))]
+    sy = oracle.sampled_forward(x, w, b, stride, padding, dilation, groups, out_points)
+    sdx = oracle.sampled_dgrad(dy, w, shape[2:], stride, padding, dilation, groups, in_points)
+    sdw = oracle.sampled_wgrad(dy, x, kernel, stride, padding, dilation, groups, entries)
+    torch.testing.assert_close(sy, torch.stack([y[n, c][i] for n, c, i in out_points]),
+                               rtol=1e-12, atol=1e-12)
+    torch.testing.assert_close(sdx, torch.stack([dx[n, c][i] for n, c, i in in_points]),
+                               rtol=1e-12, atol=1e-12)
+    torch.testing.assert_close(sdw, torch.stack([dw[co, cl][t] for co, cl, t in entries]),
+                               rtol=1e-12, atol=1e-12)

@@ -867,6 +867,14 @@ bool plan_wgrad(const WgradPass& pass, int splits_hint, WgradPlan* plan) {
   if (splits <= 0) {
     const int64_t ctas_per_split = static_cast<int64_t>(plan->chunks) * pass.groups;
     int64_t s = (sm_count() + ctas_per_split - 1) / ctas_per_split;
+    if (parts > 1) {
+      // float32 problems: at most ~4096 positions per split. The tensor core's fp32
+      // accumulation error grows with the number of accumulation steps; the fp32
+      // partials are then summed in a fixed order by the reduction kernel.
+      const int64_t tiles_per_split = 4096 / P.kc_rows > 0 ? 4096 / P.kc_rows : 1;
+      const int64_t need = (P.ptiles + tiles_per_split - 1) / tiles_per_split;
+      if (s < need) s = need < 1024 ? need : 1024;
+    }
     if (s > P.ptiles) s = P.ptiles;
     if (s < 1) s = 1;
     splits = static_cast<int>(s);
