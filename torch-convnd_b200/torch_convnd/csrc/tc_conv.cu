@@ -292,95 +292,104 @@ __global__ void __launch_bounds__(kThreads, 1)
   dev::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0 && lane == 0) {
-    // ---------------- TMA producer ----------------
-    for (int part = 0; part < kParts; ++part) {
-      dev::prefetch_tensormap(&maps.act[part]);
-      dev::prefetch_tensormap(&maps.grad[part]);
+  if (warp == 0) {
+    // ---------------- TMA producer (whole warp) ----------------
+    // Lane 0 keeps the position-tile bookkeeping in shared memory; the loads of a tile or
+    // unit (boxes x taps x parts) are spread over the 32 lanes, which issue them in
+    // parallel. One lane alone issued only one load every several hundred cycles, too
+    // few for units made of many small per-tap tiles.
+    if (lane == 0) {
+      for (int part = 0; part < kParts; ++part) {
+        dev::prefetch_tensormap(&maps.act[part]);
+        dev::prefetch_tensormap(&maps.grad[part]);
+      }
     }
     int a_stage = 0, b_slot = 0;
     uint32_t a_phase = 0, b_phase = 0;
     bool ok = true;
     BoxCursor cursor;
     cursor_init(g, p_begin * g.nb, cursor);
+    const int b_loads = g.nb * P.b_blocks * kParts;
+    const int a_loads = P.entries_per_unit * g.nb * kParts;
     for (int64_t pt = p_begin; pt < p_end && ok; ++pt) {
       // Boxes of this position tile and, per box, which outer tap combinations stay
       // inside the input (bit c of box_mask; recomputed when the outer position moves).
-      for (int j = 0; j < g.nb; ++j) {
-        BoxInfo& B = boxes[j];
-        const bool refresh = cursor.outer_changed || g.nb > 1;
-        cursor_box(g, cursor, grp, refresh, B);
-        if (refresh) {
-          uint64_t mask = 0;
-          for (int c = 0; c < P.outer_combos; ++c) {
-            bool inside = true;
+      if (lane == 0) {
+        for (int j = 0; j < g.nb; ++j) {
+          BoxInfo& B = boxes[j];
+          const bool refresh = cursor.outer_changed || g.nb > 1;
+          cursor_box(g, cursor, grp, refresh, B);
+          if (refresh) {
+            uint64_t mask = 0;
+            for (int c = 0; c < P.outer_combos; ++c) {
+              bool inside = true;
 #pragma unroll
-            for (int a = 0; a < kMaxOuter; ++a) {
-              if (a < g.n_outer) {
-                const int coord = B.ib_o[a] + combos[c].off[a];
-                inside = inside && coord >= 0 && coord < g.in_o[a];
+              for (int a = 0; a < kMaxOuter; ++a) {
+                if (a < g.n_outer) {
+                  const int coord = B.ib_o[a] + combos[c].off[a];
+                  inside = inside && coord >= 0 && coord < g.in_o[a];
+                }
               }
+              if (inside) mask |= uint64_t{1} << c;
             }
-            if (inside) mask |= uint64_t{1} << c;
+            box_mask[j] = mask;
           }
-          box_mask[j] = mask;
+          cursor_next(g, cursor);
         }
-        cursor_next(g, cursor);
       }
       // Output-gradient tile (B operand), shared by every tap tile of this CTA.
-      if (!dev::mbar_wait(&b_empty[b_slot], b_phase ^ 1u, err, kSiteWProducer, P.timeout_ns)) {
+      if (!dev::mbar_wait_warp(&b_empty[b_slot], b_phase ^ 1u, err, kSiteWProducer,
+                               P.timeout_ns)) {
         ok = false;
         break;
       }
       uint8_t* bs = b_base + b_slot * P.b_slot_bytes;
-      dev::mbar_arrive_expect_tx(&b_full[b_slot], P.b_tx);
-      for (int j = 0; j < g.nb; ++j) {
+      if (lane == 0) dev::mbar_arrive_expect_tx(&b_full[b_slot], P.b_tx);
+      __syncwarp();
+      for (int l = lane; l < b_loads; l += 32) {
+        const int part = l % kParts;
+        const int blk = (l / kParts) % P.b_blocks;
+        const int j = l / (kParts * P.b_blocks);
         const int32_t mo = boxes[j].valid ? static_cast<int32_t>(boxes[j].out_merged) : -1;
-        const int32_t y2 = boxes[j].q[2] * g.b[2];
-        const int32_t y1 = boxes[j].q[1] * g.b[1];
-        const int32_t y0 = boxes[j].q[0] * g.b[0];
-        for (int blk = 0; blk < P.b_blocks; ++blk) {
-          uint8_t* dst = bs + blk * (P.kc_rows * 128) + j * g.box_rows * P.b_row_bytes;
-          const int32_t c0 = blk * P.b_blk_elems;
-          for (int part = 0; part < kParts; ++part) {
-            dev::tma_load_5d(dst + part * P.b_part_bytes, &maps.grad[part], &b_full[b_slot], c0,
-                             y2, y1, y0, mo);
-          }
-        }
+        uint8_t* dst = bs + blk * (P.kc_rows * 128) + j * g.box_rows * P.b_row_bytes;
+        dev::tma_load_5d(dst + part * P.b_part_bytes, &maps.grad[part], &b_full[b_slot],
+                         blk * P.b_blk_elems, boxes[j].q[2] * g.b[2], boxes[j].q[1] * g.b[1],
+                         boxes[j].q[0] * g.b[0], mo);
       }
       if (++b_slot == 2) {
         b_slot = 0;
         b_phase ^= 1u;
       }
       // Activation units, coordinates from the tap table.
-      int ti = 0;
       for (int unit = 0; unit < unit_count && ok; ++unit) {
-        if (!dev::mbar_wait(&a_empty[a_stage], a_phase ^ 1u, err, kSiteWProducer,
-                            P.timeout_ns)) {
+        if (!dev::mbar_wait_warp(&a_empty[a_stage], a_phase ^ 1u, err, kSiteWProducer,
+                                 P.timeout_ns)) {
           ok = false;
           break;
         }
         uint8_t* as = a_base + a_stage * P.a_slot_bytes;
-        dev::mbar_arrive_expect_tx(&a_full[a_stage], P.a_tx);
-        for (int jt = 0; jt < P.entries_per_unit; ++jt, ++ti) {
-          const TapEntry e = taps[ti];
-          for (int j = 0; j < g.nb; ++j) {
-            const BoxInfo& B = boxes[j];
-            const bool inside =
-                B.valid && e.outer >= 0 && ((box_mask[j] >> e.outer) & 1u);
-            const int32_t mc = inside ? static_cast<int32_t>(B.in_ng_base + e.delta) : -1;
-            uint8_t* dst = as + jt * P.a_tile_bytes + j * g.box_rows * P.a_row_bytes;
-            for (int part = 0; part < kParts; ++part) {
-              dev::tma_load_5d(dst + part * P.a_part_bytes, &maps.act[part], &a_full[a_stage], 0,
-                               B.ib[2] + e.dx2, B.ib[1] + e.dx1, B.ib[0] + e.dx0, mc);
-            }
-          }
+        if (lane == 0) dev::mbar_arrive_expect_tx(&a_full[a_stage], P.a_tx);
+        __syncwarp();
+        const int t_base = unit * P.entries_per_unit;
+        for (int l = lane; l < a_loads; l += 32) {
+          const int part = l % kParts;
+          const int j = (l / kParts) % g.nb;
+          const int jt = l / (kParts * g.nb);
+          const TapEntry e = taps[t_base + jt];
+          const BoxInfo& B = boxes[j];
+          const bool inside = B.valid && e.outer >= 0 && ((box_mask[j] >> e.outer) & 1u);
+          const int32_t mc = inside ? static_cast<int32_t>(B.in_ng_base + e.delta) : -1;
+          uint8_t* dst = as + jt * P.a_tile_bytes + j * g.box_rows * P.a_row_bytes;
+          dev::tma_load_5d(dst + part * P.a_part_bytes, &maps.act[part], &a_full[a_stage], 0,
+                           B.ib[2] + e.dx2, B.ib[1] + e.dx1, B.ib[0] + e.dx0, mc);
         }
         if (++a_stage == P.a_stages) {
           a_stage = 0;
           a_phase ^= 1u;
         }
       }
+      // Every lane has read this tile's boxes before lane 0 rewrites them.
+      __syncwarp();
     }
     (void)ok;
   } else if (warp == 1) {
