@@ -373,10 +373,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           if constexpr (kFold > 0) {
             // One MMA per A slice i (and a1 shift): tap blocks j0 in [lo, hi] with
             // 0 <= i - j0 < kMT, N = (hi - lo + 1) * n_pad, D at tile i - lo's column.
+            // Float32 passes rotate the (unit, a1 shift) groups over nacc accumulator
+            // sets, as the unfolded loop rotates taps.
             const uint32_t sbw = sa + (P.b_off >> 4);
-            for (int j1 = 0; j1 < P.nshift1; ++j1) {
+            auto fold_shift = [&](int j1) {
               const uint32_t a_j1 = sa + static_cast<uint32_t>(j1) * j1_units;
               const uint32_t b_j1 = sbw + static_cast<uint32_t>(j1 * kFold) * btap_units;
+              const int wi = u * P.nshift1 + j1;
+              const uint32_t dset = dbase + static_cast<uint32_t>(wi & acc_mask) * acc_cols;
 #pragma unroll
               for (int i = 0; i < kMT + kFold - 1; ++i) {
                 constexpr int kLast = kMT - 1;
@@ -386,13 +390,27 @@ __global__ void __launch_bounds__(kThreads, 1)
                     P.idesc_base | (static_cast<uint32_t>(((hi - lo + 1) * P.n_pad) >> 3) << 17);
                 const uint32_t a_addr = a_j1 + static_cast<uint32_t>(i) * tile_units;
                 const uint32_t b_addr = b_j1 + static_cast<uint32_t>(lo) * btap_units;
-                const uint32_t d = dbase + static_cast<uint32_t>(kLast - i + lo) * tile_cols;
+                const uint32_t d = dset + static_cast<uint32_t>(kLast - i + lo) * tile_cols;
 #pragma unroll
                 for (int kk = 0; kk < kKSteps; ++kk) {
-                  mma<kTF32>(d, desc_hi | (a_addr + 2u * kk), desc_hi | (b_addr + 2u * kk), idesc,
-                             1u);
+                  const uint64_t ad = desc_hi | (a_addr + 2u * kk);
+                  const uint64_t bd = desc_hi | (b_addr + 2u * kk);
+                  if constexpr (kParts == 2) {
+                    mma<true>(d, desc_hi | (a_addr + a_small_units + 2u * kk), bd, idesc, 1u);
+                    mma<true>(d, ad, desc_hi | (b_addr + b_small_units + 2u * kk), idesc, 1u);
+                    mma<true>(d, ad, bd, idesc, 1u);
+                  } else {
+                    mma<kTF32>(d, ad, bd, idesc, 1u);
+                  }
                 }
               }
+            };
+            if (P.nshift1 == 3) {
+              fold_shift(0);  // three a1 shifts: straight-line issue
+              fold_shift(1);
+              fold_shift(2);
+            } else {
+              for (int j1 = 0; j1 < P.nshift1; ++j1) fold_shift(j1);
             }
           } else {
           uint32_t a_tap = sa;
@@ -764,9 +782,9 @@ bool plan_fprop(const ConvPass& pass, FpropPlan* plan) {
      break;
    }
    for (int fold = 0; fold <= 1; ++fold) {
-    // Folding the a0 taps into N needs unit-stride a0 tiles of one slice, three a0 taps,
-    // single-product bf16/fp16 MMAs and 3 * n_pad <= 256.
-    if (fold && (tf32 || P.k[0] != 3 || P.d[0] != 1 || P.s[0] != 1 || 3 * pass.n_pad > 256)) {
+    // Folding the a0 taps into N needs unit-stride a0 tiles of one slice, three a0 taps
+    // and 3 * n_pad <= 256.
+    if (fold && (P.k[0] != 3 || P.d[0] != 1 || P.s[0] != 1 || 3 * pass.n_pad > 256)) {
       continue;
     }
     for (int e0 = 1; e0 <= 128; e0 *= 2) {
@@ -806,7 +824,7 @@ bool plan_fprop(const ConvPass& pass, FpropPlan* plan) {
                 const int hi = i < 2 ? i : 2;
                 per_pass += mma_cycles((hi - lo + 1) * pass.n_pad);
               }
-              mma_total = units * trial.nshift1 * trial.ksteps * per_pass;
+              mma_total = units * trial.nshift1 * trial.ksteps * products * per_pass;
             } else {
               mma_total = double(mt) * P.taps * trial.cblocks * trial.ksteps * products *
                           mma_cycles(pass.n_pad);
@@ -994,7 +1012,8 @@ int launch_fprop(const ConvPass& pass, const FpropPlan& plan_in, cudaStream_t st
 #define CND_FPROP_KS(KIND) CND_FPROP_MT(KIND, 1) CND_FPROP_MT(KIND, 2) CND_FPROP_MT(KIND, 4)
 #define CND_FPROP_KSF(KIND) CND_FPROP_FOLDS(KIND, 1) CND_FPROP_FOLDS(KIND, 2) CND_FPROP_FOLDS(KIND, 4)
   CND_FPROP_KS(kKindF16) CND_FPROP_KS(kKindBF16) CND_FPROP_KS(kKindTF32) CND_FPROP_KS(kKind3xTF32)
-  CND_FPROP_KSF(kKindF16) CND_FPROP_KSF(kKindBF16)
+  CND_FPROP_KSF(kKindF16) CND_FPROP_KSF(kKindBF16) CND_FPROP_KSF(kKindTF32)
+  CND_FPROP_KSF(kKind3xTF32)
 #undef CND_FPROP_KSF
 #undef CND_FPROP_FOLDS
 #undef CND_FPROP_FOLD
