@@ -145,58 +145,88 @@ __device__ __forceinline__ int packed_row_tap(int row, int k0, int k1, int k2, i
   return ((rest * k0 + t0) * k1 + t1) * k2 + t2;
 }
 
-// Fast path for 16-bit activations without splitting (bf16/fp16 problems): 128 positions
-// per block, 16-byte loads of 8 consecutive positions of one channel and 16-byte stores of
-// 8 consecutive channels of one position, through a [c_pad][128] shared tile.
-// Requirements (checked by the host): c_pad a multiple of 8 and <= 64, S % 8 == 0.
-constexpr int kFastPositions = 128;
+// Fast path for 16-bit activations without splitting (bf16/fp16 problems). Every thread
+// moves an 8-channel x 8-position block: eight 16-byte loads (8 positions of one channel
+// each), an 8x8 transpose of the 16-bit values in registers — output word m of position p
+// holds channels (2m, 2m+1) and is one byte permute of the two input words holding
+// positions (p & ~1, p | 1) of those channels — and eight 16-byte stores (8 channels of
+// one position each). A warp's lanes are (position group, channel group) with the
+// channel group fastest, so each store instruction writes whole position rows.
+// Requirements (checked by the host): c_pad in {8, 16, 32, 64}, S % 8 == 0, 16-byte
+// aligned tensors.
+constexpr int kFastWarps = 8;
+
+__host__ __device__ constexpr int fast_positions_per_block(int c_pad) {
+  return kFastWarps * 8 * (32 / (c_pad / 8));
+}
 
 template <typename T>
-__global__ void __launch_bounds__(256) pack_act16_kernel(const T* __restrict__ src,
-                                                         T* __restrict__ dst, int64_t S, int Cg,
-                                                         int c_pad, int G,
-                                                         float* __restrict__ chan_partial) {
-  __shared__ __align__(16) uint16_t tile[64][kFastPositions + 8];
-  const int64_t s0 = static_cast<int64_t>(blockIdx.x) * kFastPositions;
-  const int g = blockIdx.y;
-  const int64_t n = blockIdx.z;
-  const uint16_t* in = reinterpret_cast<const uint16_t*>(src) + (n * G + g) * Cg * S;
-  const int count = static_cast<int>(S - s0 < kFastPositions ? S - s0 : kFastPositions);
-  // Load: (channel, 8-position vector) pairs.
-  for (int i = threadIdx.x; i < c_pad * (kFastPositions / 8); i += blockDim.x) {
-    const int c = i >> 4;
-    const int v = i & 15;
-    uint4 value = make_uint4(0, 0, 0, 0);
-    if (c < Cg && v * 8 < count) value = *reinterpret_cast<const uint4*>(in + c * S + s0 + v * 8);
-    *reinterpret_cast<uint4*>(&tile[c][v * 8]) = value;
-  }
-  __syncthreads();
-  // Store: (position, 8-channel vector) pairs.
-  const int vectors = c_pad >> 3;
-  uint16_t* out = reinterpret_cast<uint16_t*>(dst) + ((n * G + g) * S + s0) * c_pad;
-  for (int i = threadIdx.x; i < count * vectors; i += blockDim.x) {
-    const int p = i / vectors;
-    const int k = i - p * vectors;
-    uint16_t lane[8];
+__global__ void __launch_bounds__(32 * kFastWarps)
+    pack_act16_kernel(const T* __restrict__ src, T* __restrict__ dst, int64_t S, int Cg,
+                      int c_pad, int G, float* __restrict__ chan_partial) {
+  const int cgs = c_pad >> 3;   // channel groups of 8 (1, 2, 4 or 8)
+  const int pgs = 32 / cgs;     // position groups of 8 per warp
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int cg = lane % cgs;
+  const int pg = lane / cgs;
+  const int64_t ng = static_cast<int64_t>(blockIdx.z) * G + blockIdx.y;
+  const int64_t p0 =
+      static_cast<int64_t>(blockIdx.x) * fast_positions_per_block(c_pad) + (warp * pgs + pg) * 8;
+  const bool active = p0 < S;
+  const uint16_t* in = reinterpret_cast<const uint16_t*>(src) + ng * Cg * S;
+  uint16_t* out = reinterpret_cast<uint16_t*>(dst) + ng * S * c_pad;
+  uint4 a[8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) lane[j] = tile[k * 8 + j][p];
-    uint4 value;
-    value.x = lane[0] | (static_cast<uint32_t>(lane[1]) << 16);
-    value.y = lane[2] | (static_cast<uint32_t>(lane[3]) << 16);
-    value.z = lane[4] | (static_cast<uint32_t>(lane[5]) << 16);
-    value.w = lane[6] | (static_cast<uint32_t>(lane[7]) << 16);
-    *reinterpret_cast<uint4*>(out + static_cast<int64_t>(p) * c_pad + k * 8) = value;
+  for (int ch = 0; ch < 8; ++ch) {
+    const int c = cg * 8 + ch;
+    a[ch] = make_uint4(0, 0, 0, 0);
+    if (active && c < Cg) a[ch] = __ldg(reinterpret_cast<const uint4*>(in + c * S + p0));
+  }
+  if (active) {
+#pragma unroll
+    for (int p = 0; p < 8; ++p) {
+      const uint32_t sel = (p & 1) ? 0x7632u : 0x5410u;
+      uint32_t w[4];
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+        const uint32_t* lo = reinterpret_cast<const uint32_t*>(&a[2 * m]);
+        const uint32_t* hi = reinterpret_cast<const uint32_t*>(&a[2 * m + 1]);
+        w[m] = __byte_perm(lo[p >> 1], hi[p >> 1], sel);
+      }
+      *reinterpret_cast<uint4*>(out + (p0 + p) * c_pad + cg * 8) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
   }
   if (chan_partial != nullptr) {
-    // Per-channel sum of this block's positions, in position order.
-    for (int c = threadIdx.x; c < Cg; c += blockDim.x) {
-      float sum = 0.0f;
-      for (int p = 0; p < count; ++p) {
-        T v;
-        *reinterpret_cast<uint16_t*>(&v) = tile[c][p];
-        sum += to_float(v);
+    // Per-channel sums of this block's positions: 8 positions per thread in order, then a
+    // fixed butterfly over the warp's position groups, then the warps in order.
+    __shared__ float part[kFastWarps][64];
+    float sum[8];
+#pragma unroll
+    for (int ch = 0; ch < 8; ++ch) {
+      const uint16_t* v = reinterpret_cast<const uint16_t*>(&a[ch]);
+      float t = 0.0f;
+#pragma unroll
+      for (int p = 0; p < 8; ++p) {
+        T x;
+        *reinterpret_cast<uint16_t*>(&x) = v[p];
+        t += to_float(x);
       }
-      chan_partial[((n * G + g) * gridDim.x + blockIdx.x) * Cg + c] = sum;
+      sum[ch] = t;
+    }
+    for (int off = cgs; off < 32; off <<= 1) {
+#pragma unroll
+      for (int ch = 0; ch < 8; ++ch) sum[ch] += __shfl_xor_sync(0xffffffffu, sum[ch], off);
+    }
+    if (pg == 0) {
+#pragma unroll
+      for (int ch = 0; ch < 8; ++ch) part[warp][cg * 8 + ch] = sum[ch];
+    }
+    __syncthreads();
+    for (int c = threadIdx.x; c < Cg; c += blockDim.x) {
+      float total = 0.0f;
+      for (int w = 0; w < kFastWarps; ++w) total += part[w][c];
+      chan_partial[(ng * gridDim.x + blockIdx.x) * Cg + c] = total;
     }
   }
 }
@@ -339,10 +369,11 @@ int pack_weight_typed(const PackWeightArgs& a, cudaStream_t stream) {
 
 template <typename T>
 int launch_pack_act16(const PackActArgs& a, cudaStream_t stream) {
-  const int64_t blocks = (a.spatial + kFastPositions - 1) / kFastPositions;
+  const int per_block = fast_positions_per_block(a.c_pad);
+  const int64_t blocks = (a.spatial + per_block - 1) / per_block;
   const dim3 grid(static_cast<unsigned>(blocks), static_cast<unsigned>(a.groups),
                   static_cast<unsigned>(a.batch));
-  pack_act16_kernel<T><<<grid, 256, 0, stream>>>(static_cast<const T*>(a.src),
+  pack_act16_kernel<T><<<grid, 32 * kFastWarps, 0, stream>>>(static_cast<const T*>(a.src),
                                                  static_cast<T*>(a.dst), a.spatial, a.cg,
                                                  a.c_pad, static_cast<int>(a.groups),
                                                  a.chan_partial);
@@ -351,8 +382,9 @@ int launch_pack_act16(const PackActArgs& a, cudaStream_t stream) {
 }
 
 bool pack16_fast_ok(const PackActArgs& a) {
-  return a.mode == 0 && a.c_pad % 8 == 0 && a.c_pad <= 64 && a.spatial % 8 == 0 &&
-         (a.spatial + kFastPositions - 1) / kFastPositions <= 0x7FFFFFFF && a.groups <= 65535 &&
+  return a.mode == 0 && (a.c_pad == 8 || a.c_pad == 16 || a.c_pad == 32 || a.c_pad == 64) &&
+         a.cg <= a.c_pad && a.spatial % 8 == 0 &&
+         (a.spatial + 63) / 64 <= 0x7FFFFFFF && a.groups <= 65535 &&
          a.batch <= 65535 && reinterpret_cast<uintptr_t>(a.src) % 16 == 0 &&
          reinterpret_cast<uintptr_t>(a.dst) % 16 == 0;
 }
@@ -452,7 +484,8 @@ int reduce_bias(const float* partial, int64_t batch, int groups, int blocks, int
 
 int64_t pack_blocks(const PackActArgs& args) {
   if ((args.dtype == CND_BF16 || args.dtype == CND_F16) && pack16_fast_ok(args)) {
-    return (args.spatial + kFastPositions - 1) / kFastPositions;
+    const int per_block = fast_positions_per_block(args.c_pad);
+    return (args.spatial + per_block - 1) / per_block;
   }
   return (args.spatial + kPackPositions - 1) / kPackPositions;
 }
