@@ -54,6 +54,16 @@ struct WgradKernelParams {
   uint32_t a_tile_bytes, a_part_bytes, a_slot_bytes, b_part_bytes, b_slot_bytes, a_tx, b_tx,
       idesc, tmem_cols, a_base_off, bar_off;
   int64_t ptiles;
+  // nfold = k0 > 0: the box-axis-0 taps are folded into N. Position tiles then run over
+  // input-aligned slices q (k0 - 1 more than the output slices), B is the k0-slice dY box
+  // [q - k0 + 1, q] (atom j = slice q - k0 + 1 + j = tap k0 - 1 - j), and each M tile's
+  // accumulator spans n_cols = k0 * n_pad columns.
+  int nfold, n_cols;
+  uint32_t b_lbo;  // B descriptor leading byte offset (between N atoms)
+  // B buffers with a full/empty barrier pair each: 2 whole-tile slots, or, when folded, a
+  // ring of b_ring one-slice slots (followed in memory by nfold - 1 mirror slots that
+  // repeat slots 0.., so the nfold slices of any tile are consecutive slots).
+  int b_ring;
   int outer_combos;  // product of the outer axes' kernel extents (<= 64)
   float* partial;
   unsigned int* err;
@@ -112,6 +122,37 @@ __device__ __forceinline__ void cursor_next(const BoxGeom& g, BoxCursor& c) {
   c.q[1] = 0;
   if (++c.q[0] < g.nbox[0]) return;
   c.q[0] = 0;
+  c.outer_changed = true;
+  if (++c.outer_lin < g.out_outer_vol) return;
+  c.outer_lin = 0;
+  ++c.n;
+}
+
+// Same walk with q[0] fastest (then q[2], q[1], outer position, batch): folded weight
+// gradients visit consecutive box-axis-0 slices of one (q1, q2) column in a row.
+__device__ __forceinline__ void cursor_init_q0(const BoxGeom& g, int64_t bt, BoxCursor& c) {
+  c.bt = bt;
+  int64_t rest = bt;
+  c.q[0] = static_cast<int>(rest % g.nbox[0]);
+  rest /= g.nbox[0];
+  c.q[2] = static_cast<int>(rest % g.nbox[2]);
+  rest /= g.nbox[2];
+  c.q[1] = static_cast<int>(rest % g.nbox[1]);
+  rest /= g.nbox[1];
+  c.outer_lin = rest % g.out_outer_vol;
+  c.n = rest / g.out_outer_vol;
+  c.outer_changed = true;
+}
+
+__device__ __forceinline__ void cursor_next_q0(const BoxGeom& g, BoxCursor& c) {
+  ++c.bt;
+  c.outer_changed = false;
+  if (++c.q[0] < g.nbox[0]) return;
+  c.q[0] = 0;
+  if (++c.q[2] < g.nbox[2]) return;
+  c.q[2] = 0;
+  if (++c.q[1] < g.nbox[1]) return;
+  c.q[1] = 0;
   c.outer_changed = true;
   if (++c.outer_lin < g.out_outer_vol) return;
   c.outer_lin = 0;
@@ -193,8 +234,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* a_base = smem + P.a_base_off;        // a_stages A slots
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + P.bar_off);
   uint64_t* b_full = bars;
-  uint64_t* b_empty = bars + 2;
-  uint64_t* a_full = bars + 4;
+  uint64_t* b_empty = bars + P.b_ring;
+  uint64_t* a_full = bars + 2 * P.b_ring;
   uint64_t* a_empty = a_full + P.a_stages;
   uint64_t* acc_bar = a_empty + P.a_stages;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_bar + 1);
@@ -218,7 +259,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int entry_count = unit_count * P.entries_per_unit;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < P.b_ring; ++s) {
       dev::mbar_init(&b_full[s], 1);
       dev::mbar_init(&b_empty[s], 1);
     }
@@ -257,8 +298,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (P.halo) {
         const int unit = unit_first + i;
         const int t2 = unit % g.k[2];
-        const int rest = unit / g.k[2];  // (outer, t0) row-major
-        tap = (rest * g.k[1]) * g.k[2] + t2;
+        const int rest = unit / g.k[2];  // (outer, t0) row-major; outer alone when folded
+        tap = (P.nfold ? rest * g.k[0] * g.k[1] : rest * g.k[1]) * g.k[2] + t2;
       } else {
         tap = unit_first * P.tpm + i;
       }
@@ -308,7 +349,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t a_phase = 0, b_phase = 0;
     bool ok = true;
     BoxCursor cursor;
-    cursor_init(g, p_begin * g.nb, cursor);
+    if (P.nfold) {
+      cursor_init_q0(g, p_begin * g.nb, cursor);
+    } else {
+      cursor_init(g, p_begin * g.nb, cursor);
+    }
+    // Folded dY ring: slot and phase of the next entry, and the current tile's slice
+    // index q0 (kept incrementally: no 64-bit divisions in the loop).
+    int ring_slot = 0;
+    uint32_t ring_phase = 0;
+    int q0 = P.nfold ? static_cast<int>(p_begin % g.nbox[0]) : 0;
     const int b_loads = g.nb * P.b_blocks * kParts;
     const int a_loads = P.entries_per_unit * g.nb * kParts;
     for (int64_t pt = p_begin; pt < p_end && ok; ++pt) {
@@ -334,9 +384,43 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             box_mask[j] = mask;
           }
-          cursor_next(g, cursor);
+          if (P.nfold) {
+            cursor_next_q0(g, cursor);
+          } else {
+            cursor_next(g, cursor);
+          }
         }
       }
+      __syncwarp();
+      if (P.nfold) {
+        // Folded: the tile needs dY slices q0 - nfold + 1 .. q0. A run of consecutive q0
+        // loads all of them at its first tile, then one new slice per tile.
+        const bool run_start = pt == p_begin || q0 == 0;
+        const int32_t mo = boxes[0].valid ? static_cast<int32_t>(boxes[0].out_merged) : -1;
+        for (int k = run_start ? P.nfold - 1 : 0; k >= 0 && ok; --k) {
+          const int slot = ring_slot;
+          const uint32_t par = ring_phase;
+          if (++ring_slot == P.b_ring) {
+            ring_slot = 0;
+            ring_phase ^= 1u;
+          }
+          if (!dev::mbar_wait_warp(&b_empty[slot], par ^ 1u, err, kSiteWProducer,
+                                   P.timeout_ns)) {
+            ok = false;
+            break;
+          }
+          const bool mirror = slot < P.nfold - 1;
+          if (lane == 0) dev::mbar_arrive_expect_tx(&b_full[slot], P.b_tx * (mirror ? 2u : 1u));
+          __syncwarp();
+          if (lane < (mirror ? 2 : 1)) {
+            const int dst_slot = lane == 0 ? slot : P.b_ring + slot;
+            dev::tma_load_5d(b_base + dst_slot * P.b_slot_bytes, &maps.grad[0], &b_full[slot], 0,
+                             boxes[0].q[2] * g.b[2], boxes[0].q[1] * g.b[1], q0 - k, mo);
+          }
+        }
+        if (!ok) break;
+        if (++q0 == g.nbox[0]) q0 = 0;
+      } else {
       // Output-gradient tile (B operand), shared by every tap tile of this CTA.
       if (!dev::mbar_wait_warp(&b_empty[b_slot], b_phase ^ 1u, err, kSiteWProducer,
                                P.timeout_ns)) {
@@ -359,6 +443,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (++b_slot == 2) {
         b_slot = 0;
         b_phase ^= 1u;
+      }
       }
       // Activation units, coordinates from the tap table.
       for (int unit = 0; unit < unit_count && ok; ++unit) {
@@ -404,16 +489,47 @@ __global__ void __launch_bounds__(kThreads, 1)
     // changes, and it never carries (shared memory is below 256 KB).
     const uint64_t a_hi = dev::make_smem_desc(0, P.atom_bytes, 8u * P.a_row_bytes, P.a_layout);
     const uint32_t group_units = (static_cast<uint32_t>(P.tpm) * P.atom_bytes) >> 4;
-    const uint64_t b_hi = dev::make_smem_desc(0, static_cast<uint32_t>(P.kc_rows) * 128u,
-                                              8u * P.b_row_bytes, P.b_layout);
+    const uint64_t b_hi = dev::make_smem_desc(0, P.b_lbo, 8u * P.b_row_bytes, P.b_layout);
     const uint32_t a_step = (16u * P.a_row_bytes) >> 4;  // one K step = 16 positions
     const uint32_t b_step = (16u * P.b_row_bytes) >> 4;
     const uint32_t a_part = P.a_part_bytes >> 4;
     const uint32_t b_part = P.b_part_bytes >> 4;
     bool ok = true;
+    // Folded dY ring: slot / phase of the next entry to wait for, the first (oldest)
+    // slot of the current tile and the tile's slice index, all kept incrementally.
+    int ring_slot = 0, first_slot = 0;
+    uint32_t ring_phase = 0;
+    int q0 = P.nfold ? static_cast<int>(p_begin % g.nbox[0]) : 0;
     for (int64_t pt = p_begin; pt < p_end && ok; ++pt) {
-      if (!dev::mbar_wait_warp(&b_full[b_slot], b_phase, err, kSiteWMma, P.timeout_ns)) break;
-      const uint32_t bs = dev::warp_uniform(dev::smem_u32(b_base + b_slot * P.b_slot_bytes) >> 4);
+      uint32_t bs;
+      bool run_end = false;
+      if (P.nfold) {
+        // The tile's slices are the ring entries from first_slot on; wait for the ones this
+        // tile is the first to use (all at a run's start, else the newest).
+        const bool run_start = pt == p_begin || q0 == 0;
+        run_end = pt == p_end - 1 || q0 == g.nbox[0] - 1;
+        if (++q0 == g.nbox[0]) q0 = 0;
+        if (run_start) {
+          first_slot = ring_slot;
+        } else if (++first_slot == P.b_ring) {
+          first_slot = 0;
+        }
+        for (int k = run_start ? P.nfold : 1; k > 0 && ok; --k) {
+          if (!dev::mbar_wait_warp(&b_full[ring_slot], ring_phase, err, kSiteWMma,
+                                   P.timeout_ns)) {
+            ok = false;
+          }
+          if (++ring_slot == P.b_ring) {
+            ring_slot = 0;
+            ring_phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        bs = dev::warp_uniform(dev::smem_u32(b_base + first_slot * P.b_slot_bytes) >> 4);
+      } else {
+        if (!dev::mbar_wait_warp(&b_full[b_slot], b_phase, err, kSiteWMma, P.timeout_ns)) break;
+        bs = dev::warp_uniform(dev::smem_u32(b_base + b_slot * P.b_slot_bytes) >> 4);
+      }
       const uint32_t first_tile = pt == p_begin ? 1u : 0u;
       for (int unit = 0; unit < unit_count; ++unit) {
         if (!dev::mbar_wait_warp(&a_full[a_stage], a_phase, err, kSiteWMma, P.timeout_ns)) {
@@ -424,7 +540,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t as =
             dev::warp_uniform(dev::smem_u32(a_base + a_stage * P.a_slot_bytes) >> 4);
         for (int gi = 0; gi < P.mtpu; ++gi) {
-          const uint32_t d = tmem_u + static_cast<uint32_t>((unit * P.mtpu + gi) * P.n_pad);
+          const uint32_t d = tmem_u + static_cast<uint32_t>((unit * P.mtpu + gi) * P.n_cols);
           const uint32_t ag = as + static_cast<uint32_t>(gi) * group_units;
           // K steps unrolled at compile time (a runtime loop between MMAs slows issue).
 #pragma unroll
@@ -446,13 +562,22 @@ __global__ void __launch_bounds__(kThreads, 1)
           a_phase ^= 1u;
         }
       }
-      dev::mma_commit_warp(&b_empty[b_slot]);
+      if (P.nfold) {
+        // The tile's oldest slice is no longer needed; at a run's end neither are the rest.
+        int slot = first_slot;
+        for (int k = run_end ? P.nfold : 1; k > 0; --k) {
+          dev::mma_commit_warp(&b_empty[slot]);
+          if (++slot == P.b_ring) slot = 0;
+        }
+      } else {
+        dev::mma_commit_warp(&b_empty[b_slot]);
+        if (++b_slot == 2) {
+          b_slot = 0;
+          b_phase ^= 1u;
+        }
+      }
       if (leader) *progress = static_cast<uint32_t>(pt - p_begin + 1);
       __syncwarp();
-      if (++b_slot == 2) {
-        b_slot = 0;
-        b_phase ^= 1u;
-      }
     }
     dev::mma_commit_warp(acc_bar);
   } else if (warp >= 2) {
@@ -473,28 +598,46 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int unit = unit_first + mt / P.mtpu;
         const int t1 = (mt % P.mtpu) * P.tpm + jt;
         const int t2 = unit % g.k[2];
-        const int rest = unit / g.k[2];
-        tap = (rest * g.k[1] + t1) * g.k[2] + t2;
+        const int rest = unit / g.k[2];  // (outer, t0), or outer alone when folded
+        tap = ((P.nfold ? rest * g.k[0] : rest) * g.k[1] + t1) * g.k[2] + t2;
         valid = t1 < g.k[1] && ci < P.cin_real;
       } else {
         tap = (unit_first + mt) * P.tpm + jt;
         valid = tap < g.taps && ci < P.cin_real;
       }
-      float* dst = P.partial +
-                   ((((static_cast<int64_t>(split) * g.groups + grp) * g.taps + tap) *
-                         P.cin_real +
-                     ci) *
-                    P.n_real);
-      for (int c = 0; c < P.n_pad / 16; ++c) {
+      for (int c = 0; c < P.n_cols / 16; ++c) {
+        // Column block j of a folded accumulator is tap k0 - 1 - j along box axis 0.
+        const int block = (c * 16) / P.n_pad;
+        const int co_base = c * 16 - block * P.n_pad;
+        const int tap_c = P.nfold ? tap + (P.nfold - 1 - block) * g.k[1] * g.k[2] : tap;
+        float* dst = P.partial +
+                     ((((static_cast<int64_t>(split) * g.groups + grp) * g.taps + tap_c) *
+                           P.cin_real +
+                       ci) *
+                      P.n_real);
         uint32_t v[16];
         __syncwarp();
-        dev::tmem_load16(lane_addr + static_cast<uint32_t>(mt * P.n_pad + c * 16), v);
+        dev::tmem_load16(lane_addr + static_cast<uint32_t>(mt * P.n_cols + c * 16), v);
         dev::tmem_load_wait();
         if (valid) {
+          if (empty_range) {
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int co = c * 16 + i;
-            if (co < P.n_real) dst[co] = empty_range ? 0.0f : __uint_as_float(v[i]);
+            for (int i = 0; i < 16; ++i) v[i] = 0u;
+          }
+          if ((P.n_real & 3) == 0 && co_base + 16 <= P.n_real) {
+            // 16-byte stores of four consecutive output channels (row is 16-byte aligned)
+            float4* d4 = reinterpret_cast<float4*>(dst + co_base);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              d4[i] = make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
+                                  __uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3]));
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const int co = co_base + i;
+              if (co < P.n_real) dst[co] = __uint_as_float(v[i]);
+            }
           }
         }
       }
@@ -776,12 +919,19 @@ bool plan_wgrad(const WgradPass& pass, int splits_hint, WgradPlan* plan) {
   const int mtpu = (k1 + P.tpm - 1) / P.tpm;
   const bool halo_ok = k1 >= 2 && s1 == 1 && d1 <= 16 &&
                        static_cast<double>(k1) / (mtpu * P.tpm) >= 0.6;
+  // Box axis 0 (third-to-last spatial axis): its three taps can be folded into N.
+  const int a0 = pass.rank >= 3 ? pass.rank - 3 : -1;
+  const int k0 = a0 >= 0 ? static_cast<int>(pass.k[a0]) : 1;
+  const bool fold_ok = halo_ok && k0 == 3 && a0 >= 0 && pass.s[a0] == 1 && pass.d[a0] == 1 &&
+                       parts == 1 && b_row_full <= 128 && 3 * pass.n_pad <= 256;
+  const int fold = fold_ok ? k0 : 0;
   bool planned = false;
   if (halo_ok) {
     // Position tile [1, b1, b2] with b2 a power of two >= 8 (8-row alignment of every
     // tap window), least padding waste first. The longest K chunk that fits comes first:
     // every A box then feeds more MMAs per barrier handoff and commit.
     for (int kc : {256, 128, 64}) {
+      if (fold && kc > 128) continue;  // ring slots of 256 rows leave too few A stages
       double best_waste = 1e30;
       int best_b2 = 0;
       for (int b2 = 8; b2 <= kc; b2 *= 2) {
@@ -800,7 +950,8 @@ bool plan_wgrad(const WgradPass& pass, int splits_hint, WgradPlan* plan) {
       const uint32_t rows = static_cast<uint32_t>(h1 * b2);
       const uint32_t a_part = round_up(rows * a_row, 1024);
       const uint32_t b_part = round_up(static_cast<uint32_t>(kc * b_row_full), 1024);
-      if (2 * b_part * parts + 3 * a_part * parts > 208 * 1024) continue;
+      const int b_slots = fold ? fold + 4 : 2;  // folded: smallest ring plus mirrors
+      if (b_slots * b_part * parts + 3 * a_part * parts > 208 * 1024) continue;
       const int box[3] = {1, b1, b2};
       if (!build_geom(pass.rank, pass.batch, pass.groups, pass.in, pass.out, pass.k, pass.s,
                       pass.d, pass.p, kc, &P.g, box)) {
@@ -814,6 +965,14 @@ bool plan_wgrad(const WgradPass& pass, int splits_hint, WgradPlan* plan) {
       P.atom_bytes = static_cast<uint32_t>(d1 * b2 * a_row);
       P.units_total = P.g.taps / k1;
       P.entries_per_unit = 1;
+      if (fold) {
+        // Position tiles run over the input-aligned slices q in [0, out0 + k0 - 1).
+        P.nfold = fold;
+        P.units_total = P.g.taps / (k1 * k0);
+        P.g.nbox[0] += k0 - 1;
+        P.g.boxes_per_group = P.g.outer_count * static_cast<int64_t>(P.g.nbox[0]) *
+                              P.g.nbox[1] * P.g.nbox[2];
+      }
       plan->halo_rows = h1;
       planned = true;
       break;
@@ -848,34 +1007,57 @@ bool plan_wgrad(const WgradPass& pass, int splits_hint, WgradPlan* plan) {
   P.ksteps = kc / 16;
   P.a_tile_bytes = static_cast<uint32_t>(kc * a_row);
   P.a_slot_bytes = P.a_part_bytes * parts;
+  const int slices = P.nfold ? P.nfold : 1;
   P.b_part_bytes = round_up(static_cast<uint32_t>(kc * b_row_full), 1024);
   P.b_slot_bytes = P.b_part_bytes * parts;
   P.b_tx = static_cast<uint32_t>(kc * b_row_full) * parts;
-  if (2 * P.b_slot_bytes + 2 * P.a_slot_bytes > 208 * 1024) return false;
-  int stages = static_cast<int>((208 * 1024 - 2 * P.b_slot_bytes) / P.a_slot_bytes);
+  P.n_cols = slices * pass.n_pad;
+  // N atoms: consecutive one-slice ring slots of a folded tile, else 64-channel blocks.
+  P.b_lbo = P.nfold ? P.b_slot_bytes : static_cast<uint32_t>(kc) * 128u;
+  // B memory: two tile slots, or a ring of one-slice slots plus nfold - 1 mirrors sized
+  // so that at least four A stages remain (up to 8 ring slots).
+  P.b_ring = 2;
+  uint32_t b_region = 2 * P.b_slot_bytes;
+  if (P.nfold) {
+    P.b_ring = 0;
+    for (int ring = 8; ring >= P.nfold + 1; --ring) {
+      const uint32_t region = static_cast<uint32_t>(ring + P.nfold - 1) * P.b_slot_bytes;
+      if (region + 4 * P.a_slot_bytes <= 208 * 1024) {
+        P.b_ring = ring;
+        b_region = region;
+        break;
+      }
+    }
+    if (P.b_ring == 0) return false;
+  }
+  if (b_region + 2 * P.a_slot_bytes > 208 * 1024) return false;
+  int stages = static_cast<int>((208 * 1024 - b_region) / P.a_slot_bytes);
   if (stages > 12) stages = 12;
   if (stages < 2) return false;
   P.a_stages = stages;
-  P.a_base_off = 2 * P.b_slot_bytes;
+  P.a_base_off = b_region;
   P.bar_off = P.a_base_off + stages * P.a_slot_bytes;
   int64_t combos = 1;
   for (int a = 0; a < P.g.n_outer; ++a) combos *= P.g.k_o[a];
   if (combos > kMaxOuterCombos) return false;
   P.outer_combos = static_cast<int>(combos);
   P.mt_total = P.units_total * P.mtpu;
-  const int max_units = (512 / pass.n_pad) / P.mtpu;
+  const int max_units = (512 / P.n_cols) / P.mtpu;
   if (max_units < 1) return false;
   plan->chunks = (P.units_total + max_units - 1) / max_units;
   P.units_per_cta = (P.units_total + plan->chunks - 1) / plan->chunks;
   P.mt_per_cta = P.units_per_cta * P.mtpu;
-  P.tmem_cols = tmem_columns(P.mt_per_cta * pass.n_pad);
-  P.idesc = make_idesc(pass.op, 128, pass.n_pad, true, true);
+  P.tmem_cols = tmem_columns(P.mt_per_cta * P.n_cols);
+  P.idesc = make_idesc(pass.op, 128, P.n_cols, true, true);
   plan->parts = parts;
   P.ptiles = (P.g.boxes_per_group + P.g.nb - 1) / P.g.nb;
   int splits = splits_hint;
   if (splits <= 0) {
     const int64_t ctas_per_split = static_cast<int64_t>(plan->chunks) * pass.groups;
-    int64_t s = (sm_count() + ctas_per_split - 1) / ctas_per_split;
+    // One CTA per SM: as many splits as fit one wave (a few CTAs of a second wave would
+    // double the pass time).
+    int64_t s = sm_count() / ctas_per_split;
+    if (s < 1) s = 1;
     if (parts > 1) {
       // float32 problems: at most ~4096 positions per split. The tensor core's fp32
       // accumulation error grows with the number of accumulation steps; the fp32
@@ -889,7 +1071,7 @@ bool plan_wgrad(const WgradPass& pass, int splits_hint, WgradPlan* plan) {
     splits = static_cast<int>(s);
   }
   P.splits = splits;
-  plan->smem = P.bar_off + (4 + 2 * stages + 1) * 8 + 16 +
+  plan->smem = P.bar_off + (2 * P.b_ring + 2 * stages + 1) * 8 + 16 +
                (sizeof(BoxInfo) + sizeof(uint64_t)) * kMaxBoxes +
                sizeof(OuterCombo) * kMaxOuterCombos +
                sizeof(TapEntry) * static_cast<size_t>(P.units_per_cta) * P.entries_per_unit +
