@@ -392,82 +392,133 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       __syncwarp();
+      // All TMA loads of the tile form one pool of jobs spread over the lanes: the dY
+      // loads first (folded: the new ring entries, a mirror copy for the first slots),
+      // then every unit's activation loads. Each lane waits on the barrier of its own
+      // job's slot; the first load of a slot posts the slot's expected bytes (a load may
+      // complete before that: the phase cannot finish without the posting arrival).
+      const bool run_start = P.nfold && (pt == p_begin || q0 == 0);
+      const int new_entries = P.nfold ? (run_start ? P.nfold : 1) : 0;
+      int b_jobs;
       if (P.nfold) {
-        // Folded: the tile needs dY slices q0 - nfold + 1 .. q0. A run of consecutive q0
-        // loads all of them at its first tile, then one new slice per tile.
-        const bool run_start = pt == p_begin || q0 == 0;
-        const int32_t mo = boxes[0].valid ? static_cast<int32_t>(boxes[0].out_merged) : -1;
-        for (int k = run_start ? P.nfold - 1 : 0; k >= 0 && ok; --k) {
-          const int slot = ring_slot;
-          const uint32_t par = ring_phase;
+        // entries k = 0.. hold slices q0 - new_entries + 1 + k; slots from ring_slot on
+        b_jobs = 0;
+        for (int k = 0; k < new_entries; ++k) {
+          int slot = ring_slot + k;
+          if (slot >= P.b_ring) slot -= P.b_ring;
+          b_jobs += slot < P.nfold - 1 ? 2 : 1;
+        }
+      } else {
+        b_jobs = b_loads;
+      }
+      // Rounds of jobs: each A stage appears at most once per round. Lanes of a round
+      // wait concurrently, and an mbarrier parity wait is exact only for the phase right
+      // after the last one known complete; a second use of a stage inside a round could
+      // wait two phases ahead and pass at once.
+      bool lane_ok = true;
+      for (int round_first = 0; round_first < unit_count || round_first == 0;
+           round_first += P.a_stages) {
+        const int round_units = unit_count - round_first < P.a_stages
+                                    ? unit_count - round_first
+                                    : P.a_stages;
+        const int round_b = round_first == 0 ? b_jobs : 0;
+        const int jobs = round_b + round_units * a_loads;
+        for (int l = lane; l < jobs && lane_ok; l += 32) {
+          if (l < round_b) {
+            if (P.nfold) {
+              // find entry k and copy c of job l
+              int k = 0, c = 0, rest = l, slot = ring_slot;
+              uint32_t par = ring_phase;
+              for (;;) {
+                const int copies = slot < P.nfold - 1 ? 2 : 1;
+                if (rest < copies) {
+                  c = rest;
+                  break;
+                }
+                rest -= copies;
+                ++k;
+                if (++slot == P.b_ring) {
+                  slot = 0;
+                  par ^= 1u;
+                }
+              }
+              if (!dev::mbar_wait(&b_empty[slot], par ^ 1u, err, kSiteWProducer, P.timeout_ns)) {
+                lane_ok = false;
+                break;
+              }
+              const bool mirror = slot < P.nfold - 1;
+              if (c == 0) dev::mbar_arrive_expect_tx(&b_full[slot], P.b_tx * (mirror ? 2u : 1u));
+              const int32_t mo =
+                  boxes[0].valid ? static_cast<int32_t>(boxes[0].out_merged) : -1;
+              const int dst_slot = c == 0 ? slot : P.b_ring + slot;
+              dev::tma_load_5d(b_base + dst_slot * P.b_slot_bytes, &maps.grad[0], &b_full[slot],
+                               0, boxes[0].q[2] * g.b[2], boxes[0].q[1] * g.b[1],
+                               q0 - (new_entries - 1) + k, mo);
+            } else {
+              if (!dev::mbar_wait(&b_empty[b_slot], b_phase ^ 1u, err, kSiteWProducer,
+                                  P.timeout_ns)) {
+                lane_ok = false;
+                break;
+              }
+              if (l == 0) dev::mbar_arrive_expect_tx(&b_full[b_slot], P.b_tx);
+              const int part = l % kParts;
+              const int blk = (l / kParts) % P.b_blocks;
+              const int j = l / (kParts * P.b_blocks);
+              const int32_t mo =
+                  boxes[j].valid ? static_cast<int32_t>(boxes[j].out_merged) : -1;
+              uint8_t* dst = b_base + b_slot * P.b_slot_bytes + blk * (P.kc_rows * 128) +
+                             j * g.box_rows * P.b_row_bytes;
+              dev::tma_load_5d(dst + part * P.b_part_bytes, &maps.grad[part], &b_full[b_slot],
+                               blk * P.b_blk_elems, boxes[j].q[2] * g.b[2],
+                               boxes[j].q[1] * g.b[1], boxes[j].q[0] * g.b[0], mo);
+            }
+          } else {
+            const int la = l - round_b;
+            const int unit = round_first + la / a_loads;
+            const int lu = la - (unit - round_first) * a_loads;
+            int stage = a_stage + unit;
+            uint32_t par = a_phase;
+            while (stage >= P.a_stages) {
+              stage -= P.a_stages;
+              par ^= 1u;
+            }
+            if (!dev::mbar_wait(&a_empty[stage], par ^ 1u, err, kSiteWProducer, P.timeout_ns)) {
+              lane_ok = false;
+              break;
+            }
+            if (lu == 0) dev::mbar_arrive_expect_tx(&a_full[stage], P.a_tx);
+            const int part = lu % kParts;
+            const int j = (lu / kParts) % g.nb;
+            const int jt = lu / (kParts * g.nb);
+            const TapEntry e = taps[unit * P.entries_per_unit + jt];
+            const BoxInfo& B = boxes[j];
+            const bool inside = B.valid && e.outer >= 0 && ((box_mask[j] >> e.outer) & 1u);
+            const int32_t mc = inside ? static_cast<int32_t>(B.in_ng_base + e.delta) : -1;
+            uint8_t* dst = a_base + stage * P.a_slot_bytes + jt * P.a_tile_bytes +
+                           j * g.box_rows * P.a_row_bytes;
+            dev::tma_load_5d(dst + part * P.a_part_bytes, &maps.act[part], &a_full[stage], 0,
+                             B.ib[2] + e.dx2, B.ib[1] + e.dx1, B.ib[0] + e.dx0, mc);
+          }
+        }
+        if (__all_sync(0xffffffffu, lane_ok) == 0) break;
+        if (round_first + P.a_stages >= unit_count) break;
+      }
+      ok = __all_sync(0xffffffffu, lane_ok) != 0;
+      if (!ok) break;
+      // advance the ring, the B slot and the A stages past this tile
+      if (P.nfold) {
+        for (int k = 0; k < new_entries; ++k) {
           if (++ring_slot == P.b_ring) {
             ring_slot = 0;
             ring_phase ^= 1u;
           }
-          if (!dev::mbar_wait_warp(&b_empty[slot], par ^ 1u, err, kSiteWProducer,
-                                   P.timeout_ns)) {
-            ok = false;
-            break;
-          }
-          const bool mirror = slot < P.nfold - 1;
-          if (lane == 0) dev::mbar_arrive_expect_tx(&b_full[slot], P.b_tx * (mirror ? 2u : 1u));
-          __syncwarp();
-          if (lane < (mirror ? 2 : 1)) {
-            const int dst_slot = lane == 0 ? slot : P.b_ring + slot;
-            dev::tma_load_5d(b_base + dst_slot * P.b_slot_bytes, &maps.grad[0], &b_full[slot], 0,
-                             boxes[0].q[2] * g.b[2], boxes[0].q[1] * g.b[1], q0 - k, mo);
-          }
         }
-        if (!ok) break;
         if (++q0 == g.nbox[0]) q0 = 0;
-      } else {
-      // Output-gradient tile (B operand), shared by every tap tile of this CTA.
-      if (!dev::mbar_wait_warp(&b_empty[b_slot], b_phase ^ 1u, err, kSiteWProducer,
-                               P.timeout_ns)) {
-        ok = false;
-        break;
-      }
-      uint8_t* bs = b_base + b_slot * P.b_slot_bytes;
-      if (lane == 0) dev::mbar_arrive_expect_tx(&b_full[b_slot], P.b_tx);
-      __syncwarp();
-      for (int l = lane; l < b_loads; l += 32) {
-        const int part = l % kParts;
-        const int blk = (l / kParts) % P.b_blocks;
-        const int j = l / (kParts * P.b_blocks);
-        const int32_t mo = boxes[j].valid ? static_cast<int32_t>(boxes[j].out_merged) : -1;
-        uint8_t* dst = bs + blk * (P.kc_rows * 128) + j * g.box_rows * P.b_row_bytes;
-        dev::tma_load_5d(dst + part * P.b_part_bytes, &maps.grad[part], &b_full[b_slot],
-                         blk * P.b_blk_elems, boxes[j].q[2] * g.b[2], boxes[j].q[1] * g.b[1],
-                         boxes[j].q[0] * g.b[0], mo);
-      }
-      if (++b_slot == 2) {
+      } else if (++b_slot == 2) {
         b_slot = 0;
         b_phase ^= 1u;
       }
-      }
-      // Activation units, coordinates from the tap table.
-      for (int unit = 0; unit < unit_count && ok; ++unit) {
-        if (!dev::mbar_wait_warp(&a_empty[a_stage], a_phase ^ 1u, err, kSiteWProducer,
-                                 P.timeout_ns)) {
-          ok = false;
-          break;
-        }
-        uint8_t* as = a_base + a_stage * P.a_slot_bytes;
-        if (lane == 0) dev::mbar_arrive_expect_tx(&a_full[a_stage], P.a_tx);
-        __syncwarp();
-        const int t_base = unit * P.entries_per_unit;
-        for (int l = lane; l < a_loads; l += 32) {
-          const int part = l % kParts;
-          const int j = (l / kParts) % g.nb;
-          const int jt = l / (kParts * g.nb);
-          const TapEntry e = taps[t_base + jt];
-          const BoxInfo& B = boxes[j];
-          const bool inside = B.valid && e.outer >= 0 && ((box_mask[j] >> e.outer) & 1u);
-          const int32_t mc = inside ? static_cast<int32_t>(B.in_ng_base + e.delta) : -1;
-          uint8_t* dst = as + jt * P.a_tile_bytes + j * g.box_rows * P.a_row_bytes;
-          dev::tma_load_5d(dst + part * P.a_part_bytes, &maps.act[part], &a_full[a_stage], 0,
-                           B.ib[2] + e.dx2, B.ib[1] + e.dx1, B.ib[0] + e.dx0, mc);
-        }
+      for (int u = 0; u < unit_count; ++u) {
         if (++a_stage == P.a_stages) {
           a_stage = 0;
           a_phase ^= 1u;
@@ -1014,21 +1065,14 @@ bool plan_wgrad(const WgradPass& pass, int splits_hint, WgradPlan* plan) {
   P.n_cols = slices * pass.n_pad;
   // N atoms: consecutive one-slice ring slots of a folded tile, else 64-channel blocks.
   P.b_lbo = P.nfold ? P.b_slot_bytes : static_cast<uint32_t>(kc) * 128u;
-  // B memory: two tile slots, or a ring of one-slice slots plus nfold - 1 mirrors sized
-  // so that at least four A stages remain (up to 8 ring slots).
+  // B memory: two tile slots, or a ring of nfold + 2 one-slice slots (the tile's slices
+  // plus two loaded ahead) and nfold - 1 mirrors; the A stages get the rest, since A
+  // loads are the deeper stream (several units per tile).
   P.b_ring = 2;
   uint32_t b_region = 2 * P.b_slot_bytes;
   if (P.nfold) {
-    P.b_ring = 0;
-    for (int ring = 8; ring >= P.nfold + 1; --ring) {
-      const uint32_t region = static_cast<uint32_t>(ring + P.nfold - 1) * P.b_slot_bytes;
-      if (region + 4 * P.a_slot_bytes <= 208 * 1024) {
-        P.b_ring = ring;
-        b_region = region;
-        break;
-      }
-    }
-    if (P.b_ring == 0) return false;
+    P.b_ring = P.nfold + 2;
+    b_region = static_cast<uint32_t>(P.b_ring + P.nfold - 1) * P.b_slot_bytes;
   }
   if (b_region + 2 * P.a_slot_bytes > 208 * 1024) return false;
   int stages = static_cast<int>((208 * 1024 - b_region) / P.a_slot_bytes);
