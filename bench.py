@@ -13,7 +13,9 @@ the three-layer training step over a global batch of 64 split across the ranks (
 scaling), with bucketed gradient all-reduce and an SGD update.
 `value` is whole-job TFLOP/s (all ranks' algorithmic FLOPs / max-over-ranks time).
 `e2e` is the same metric through the public module API with the step's inputs copied
-from pinned host memory and the step's result read back, inside the timed region.
+from pinned host memory and the step's result read back, inside the timed region (the
+copy of the next step's inputs runs on a side stream during the current step).
+Clock samples (nvidia-smi, 50 ms) are kept only when stamped inside the timed region.
 `roofline` reports the pass (layer x forward/dgrad/wgrad) with the largest share of the
 step against the bound its arithmetic intensity sets; `cpu_baseline` times the
 reference's native CPU implementation (compiled from its sources into oracle/_ref) on a
@@ -46,7 +48,7 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 def parse_args(argv=None):
     parser = argparse.ArgumentParser(description=__doc__.splitlines()[1])
     parser.add_argument("--gpus", type=int, default=1)
-    parser.add_argument("--steps", type=int, default=20)
+    parser.add_argument("--steps", type=int, default=300)
     parser.add_argument("--warmup", type=int, default=5)
     parser.add_argument("--impl", choices=("b200", "reference"), default="b200")
     parser.add_argument("--config", default="c2", choices=("c1", "c2", "c3", "c4", "c5"))
@@ -55,6 +57,7 @@ def parse_args(argv=None):
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--cpu-sample-images", type=int, default=1)
     parser.add_argument("--cpu-baseline-worker", action="store_true", help=argparse.SUPPRESS)
+    parser.add_argument("--time-budget", type=float, default=None, help=argparse.SUPPRESS)
     return parser.parse_args(argv)
 
 
@@ -104,9 +107,10 @@ def measured_peaks():
 
 
 class ClockSampler:
-    """Samples nvidia-smi clocks and throttle reasons while the timed region runs."""
+    """Samples nvidia-smi clocks and throttle reasons every 50 ms; `window()` marks the
+    timed region and only samples stamped inside it are summarised."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
@@ -115,12 +119,17 @@ class ClockSampler:
         self.process = None
         self.lines: list[str] = []
         self.thread = None
+        self.begin = None
+        self.end = None
+
+    def window(self, begin: float, end: float):
+        self.begin, self.end = begin, end
 
     def start(self):
         try:
             self.process = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-i", self.device_id, "-lms", "200"],
+                 "-i", self.device_id, "-lms", "50"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.process = None
@@ -142,20 +151,28 @@ class ClockSampler:
             self.process.kill()
         if self.thread is not None:
             self.thread.join(timeout=5)
+        from datetime import datetime
+
         sm, sm_max, power = [], [], []
         reasons = set()
         names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        outside = 0
         for line in self.lines:
             parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
+            if len(parts) < 10:
                 continue
             try:
-                sm.append(float(parts[1]))
-                sm_max.append(float(parts[2]))
-                power.append(float(parts[3]))
+                stamp = datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                clock, clock_max, watts = float(parts[2]), float(parts[3]), float(parts[4])
             except ValueError:
                 continue
-            for name, flag in zip(names, parts[5:9]):
+            if self.begin is not None and not self.begin - 0.06 <= stamp <= self.end + 0.06:
+                outside += 1
+                continue
+            sm.append(clock)
+            sm_max.append(clock_max)
+            power.append(watts)
+            for name, flag in zip(names, parts[6:10]):
                 if flag.lower().startswith("active"):
                     reasons.add(name)
         return {
@@ -163,6 +180,7 @@ class ClockSampler:
             "sm_max_mhz": max(sm_max) if sm_max else None,
             "power_w_max": max(power) if power else None,
             "samples": len(sm),
+            "samples_outside_timed_region": outside,
             "reasons": sorted(reasons),
         }
 
@@ -276,25 +294,34 @@ def cpu_baseline_worker(args):
             return y
     steps = max(1, args.steps)
     warmup = max(0, args.warmup)
+    budget = getattr(args, "time_budget", None) or 90.0
     for _ in range(warmup):
         step()
+    # Timed steps: all K of them, or as many as fit the wall-time budget (at least one),
+    # so the reference arm ends within minutes at any --steps.
+    timed = 0
     start = time.perf_counter()
-    for _ in range(steps):
+    while timed < steps:
         step()
-    seconds = (time.perf_counter() - start) / steps
+        timed += 1
+        if time.perf_counter() - start > budget:
+            break
+    seconds = (time.perf_counter() - start) / timed
     print(json.dumps({
         "value": flops / seconds / 1e12, "unit": "TFLOP/s", "cores": cores, "kind": kind,
         "seconds_per_step": seconds,
+        "steps_timed": timed,
         "sample": f"{images} of {full_batch} images of {name} per step, "
                   f"{args.config} dtype inputs, torch.set_num_threads({cores})",
     }))
     del keep
 
 
-def cpu_baseline(args, steps=1, warmup=0):
+def cpu_baseline(args, steps=1, warmup=0, time_budget=20.0):
     command = [sys.executable, str(Path(__file__).resolve()), "--cpu-baseline-worker",
                "--config", args.config, "--cpu-sample-images", str(args.cpu_sample_images),
-               "--steps", str(steps), "--warmup", str(warmup)]
+               "--steps", str(steps), "--warmup", str(warmup),
+               "--time-budget", str(time_budget)]
     result = subprocess.run(command, capture_output=True, text=True, timeout=900)
     if result.returncode != 0:
         return {"value": None, "unit": "TFLOP/s", "cores": os.cpu_count(), "kind": "reference",
@@ -316,7 +343,7 @@ def run_reference_arm(args):
     worker_args = argparse.Namespace(config=args.config,
                                      cpu_sample_images=args.cpu_sample_images, steps=steps,
                                      warmup=warmup)
-    result = cpu_baseline(worker_args, steps=steps, warmup=warmup)
+    result = cpu_baseline(worker_args, steps=steps, warmup=warmup, time_budget=90.0)
     import torch  # noqa: F401
 
     value = result.get("value")
@@ -331,7 +358,8 @@ def run_reference_arm(args):
         "value": value,
         "unit": "TFLOP/s",
         "n_gpus": args.gpus,
-        "steps": steps,
+        "steps": result.get("steps_timed", steps),
+        "steps_requested": steps,
         "warmup": warmup,
         "ms_per_step": None if value is None else result["seconds_per_step"] * 1e3,
         "higher_is_better": True,
@@ -355,6 +383,52 @@ def run_reference_arm(args):
 C5_WORKLOAD = ("c5: 3-layer Conv4d bf16 training step, x[64,16,32,32,16,16] -> L1 16->32 "
                "k3 s2 p1 -> GELU -> L2 32->32 k(3,3,1,1) p(2,2,0,0) d(2,2,1,1) g4 -> GELU -> "
                "L3 32->8 k1 -> MSE; fwd + bwd (no dgrad of L1) + gradient all-reduce + SGD")
+
+
+class Prefetcher:
+    """Double-buffered host-to-device input copies on a side stream: while step k runs on
+    the current stream, step k+1's pinned host inputs are copied into the other buffer.
+    Events order the copy after the last use of that buffer and the step after its copy,
+    so every step still copies its own inputs; only the overlap is new."""
+
+    def __init__(self, host_tensors, device):
+        import torch
+
+        self.host = host_tensors
+        self.bufs = [[torch.empty_like(t, device=device) for t in host_tensors] for _ in range(2)]
+        self.ready = [torch.cuda.Event() for _ in range(2)]
+        self.free = [torch.cuda.Event() for _ in range(2)]
+        self.copy_stream = torch.cuda.Stream(device=device)
+        self.index = 0
+        self.pending = False
+
+    def _issue(self, slot):
+        import torch
+
+        self.copy_stream.wait_event(self.free[slot])
+        with torch.cuda.stream(self.copy_stream):
+            for dst, src in zip(self.bufs[slot], self.host):
+                dst.copy_(src, non_blocking=True)
+            self.ready[slot].record(self.copy_stream)
+
+    def next(self):
+        """Device copies of this step's inputs (waited on by the current stream); starts
+        the copy of the following step's inputs."""
+        import torch
+
+        slot = self.index % 2
+        if not self.pending:
+            self._issue(slot)
+        torch.cuda.current_stream().wait_event(self.ready[slot])
+        self._issue(1 - slot)
+        self.pending = True
+        self.index += 1
+        return slot, self.bufs[slot]
+
+    def release(self, slot):
+        import torch
+
+        self.free[slot].record(torch.cuda.current_stream())
 
 
 class SingleOp:
@@ -424,11 +498,13 @@ class SingleOp:
         dy_host = inputs.grad.cpu().pin_memory()
         params = list(layer.parameters())
         grad_host = [torch.empty(p.shape, dtype=p.dtype, pin_memory=True) for p in params]
+        prefetch = Prefetcher([x_host, dy_host], device)
 
         def step():
-            x = x_host.to(device, non_blocking=True).requires_grad_()
-            dy = dy_host.to(device, non_blocking=True)
+            slot, (x_dev, dy) = prefetch.next()
+            x = x_dev.detach().requires_grad_()
             layer(x).backward(dy)
+            prefetch.release(slot)
             self._allreduce([p.grad for p in params])
             for host, p in zip(grad_host, params):
                 host.copy_(p.grad, non_blocking=True)
@@ -436,7 +512,9 @@ class SingleOp:
 
         h2d = sum(t.numel() * t.element_size() for t in (x_host, dy_host))
         d2h = sum(g.numel() * g.element_size() for g in grad_host)
-        return step, h2d, d2h, "torch_convnd.ConvNd forward + autograd backward"
+        return step, h2d, d2h, ("torch_convnd.ConvNd forward + autograd backward; inputs "
+                                "copied from pinned host memory each step, the next step's "
+                                "copy overlapping this step's kernels")
 
 
 class C5Step:
@@ -490,14 +568,18 @@ class C5Step:
         x_host = self.data.x.cpu().pin_memory()
         target_host = self.data.target.cpu().pin_memory()
         loss_host = torch.empty((), dtype=torch.bfloat16, pin_memory=True)
+        prefetch = Prefetcher([x_host, target_host], device)
 
         def step():
-            x = x_host.to(device, non_blocking=True)
-            target = target_host.to(device, non_blocking=True)
-            loss_host.copy_(self._train(x, target).detach(), non_blocking=True)
+            slot, (x, target) = prefetch.next()
+            loss = self._train(x, target).detach()
+            prefetch.release(slot)
+            loss_host.copy_(loss, non_blocking=True)
 
         h2d = sum(t.numel() * t.element_size() for t in (x_host, target_host))
-        return step, h2d, 2, "torch_convnd.ConvNd x3 + GELU + MSE, autograd backward, SGD"
+        return step, h2d, 2, ("torch_convnd.ConvNd x3 + GELU + MSE, autograd backward, SGD; "
+                              "inputs copied from pinned host memory each step, the next "
+                              "step's copy overlapping this step's kernels")
 
 
 # ------------------------------------------------------------------------------------
@@ -588,7 +670,9 @@ def run_b200(args):
     sampler.start()
     time.sleep(0.3)
     torch_convnd.launch_count(reset=True)
+    begin = time.time()
     ms = timed_ms(workload.step, args.steps, world, dist, device)
+    sampler.window(begin, time.time())
     clocks = sampler.stop()
     launches = torch_convnd.launch_count()
     value = workload.job_flops / (ms / 1e3) / 1e12
@@ -663,7 +747,7 @@ def run_b200(args):
 
     baseline = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        baseline = cpu_baseline(args, steps=1, warmup=0)
+        baseline = cpu_baseline(args, steps=2, warmup=1)
 
     if rank == 0:
         config = workload.config()
