@@ -968,8 +968,12 @@ bool plan_wgrad(const WgradPass& pass, int splits_hint, WgradPlan* plan) {
   const int64_t o1 = a1 >= 0 ? pass.out[a1] : 1;
   const int64_t o2 = pass.out[pass.rank - 1];
   const int mtpu = (k1 + P.tpm - 1) / P.tpm;
+  // Halo boxes cut the TMA operations per tap by k1 at the price of padding atoms; with
+  // one operand part that pays down to ~1/3 atom use (thin channels are bound by the count
+  // of small per-tap loads), with float32's three parts only above 60 %.
+  const double min_atom_use = parts == 1 ? 0.3 : 0.6;
   const bool halo_ok = k1 >= 2 && s1 == 1 && d1 <= 16 &&
-                       static_cast<double>(k1) / (mtpu * P.tpm) >= 0.6;
+                       static_cast<double>(k1) / (mtpu * P.tpm) >= min_atom_use;
   // Box axis 0 (third-to-last spatial axis): its three taps can be folded into N.
   const int a0 = pass.rank >= 3 ? pass.rank - 3 : -1;
   const int k0 = a0 >= 0 ? static_cast<int>(pass.k[a0]) : 1;
