@@ -78,6 +78,14 @@ def test_c2_plan_uses_the_folded_tma_store_path():
             assert "fold=1" in line and "tma_store=1" in line, line
 
 
+def test_thin_grouped_layer_runs_dense():
+    """c5's grouped layer (4 groups of 8 channels) runs as one dense problem with
+    block-diagonal weights; its full-size case below checks that plan."""
+    summary = _plan_summary(configs.C5_LAYERS[1])
+    assert "groups: 4 run dense" in summary, summary
+    assert "groups:" not in _plan_summary(configs.C2)
+
+
 @pytest.mark.gpu
 @pytest.mark.parametrize("name", list(CASES))
 def test_full_size_config_matches_sampled_oracle(name):

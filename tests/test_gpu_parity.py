@@ -111,6 +111,12 @@ def _sweep():
     cases.append((1, 2, 16, 16, (40,), (5,), (1,), (2,), (1,), 1))
     cases.append((7, 1, 16, 16, (3, 2, 3, 2, 3, 2, 4), (2,) * 7, (1,) * 7, (1,) * 7, (1,) * 7, 1))
     cases.append((4, 2, 8, 8, (4, 4, 4, 4), (3,) * 4, (1,) * 4, (3, 0, 2, 1), (1, 1, 1, 1), 1))
+    # thin groups, run dense with block-diagonal weights
+    cases.append((4, 2, 16, 16, (5, 6, 4, 7), (3, 3, 1, 1), (1,) * 4, (2, 2, 0, 0), (2, 2, 1, 1),
+                  4))
+    cases.append((4, 2, 32, 32, (4, 5, 4, 6), (3,) * 4, (1,) * 4, (1,) * 4, (1,) * 4, 32))
+    cases.append((5, 1, 24, 12, (4, 4, 3, 5, 4), (2, 3, 3, 2, 3), (1,) * 5, (1,) * 5, (1,) * 5, 3))
+    cases.append((4, 2, 16, 32, (7, 6, 8, 9), (3,) * 4, (2,) * 4, (1,) * 4, (1,) * 4, 2))
     return cases
 
 

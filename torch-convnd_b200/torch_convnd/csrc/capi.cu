@@ -145,6 +145,13 @@ struct Plan {
   int split3 = 0;
   int pack_mode = 0;
   int parts = 1;
+  // Channel groups of the tensor-core passes. Grouped problems whose per-group channels
+  // are thin run as one dense problem with block-diagonal weights (bd = the problem's
+  // group count): the packed rows then hold every channel once instead of each group
+  // padded to a 32-byte row, and the MMAs see all channels at once. cin_g / cout_g are
+  // the channels per pass group (all channels when bd > 1).
+  int64_t groups = 1;
+  int bd = 1;
   int64_t cin_g = 0, cout_g = 0;
   int64_t x_pad = 0, dy_pad = 0;
   bool fast_fwd = false, fast_dgrad = false, fast_wgrad = false;
@@ -186,6 +193,7 @@ Region take(size_t* cursor, size_t bytes) {
 // `forward` selects the forward plan; otherwise `mask` selects the backward passes.
 void make_plan(const cnd_problem& p, bool forward, const int32_t* mask, Plan* plan) {
   *plan = Plan();
+  plan->groups = p.groups;
   plan->cin_g = p.channels / p.groups;
   plan->cout_g = p.output_channels / p.groups;
   const bool low = p.dtype == CND_BF16 || p.dtype == CND_F16;
@@ -197,6 +205,21 @@ void make_plan(const cnd_problem& p, bool forward, const int32_t* mask, Plan* pl
   plan->pack_mode = p.dtype == CND_F32 ? (plan->split3 ? 1 : 2) : 0;
   plan->parts = plan->split3 ? 2 : 1;
   const size_t es = element_bytes(p.dtype);
+  if (p.groups > 1 && p.channels <= 64 && p.output_channels <= 64) {
+    // Dense when padding each group to its own row costs more bytes than one row of all
+    // channels (the extra block-diagonal products are cheaper than thin MMAs).
+    const bool thin =
+        p.groups * pad_channels(plan->op, plan->cin_g, 1) >
+            pad_channels(plan->op, p.channels, 1) ||
+        p.groups * pad_channels(plan->op, plan->cout_g, 16) >
+            pad_channels(plan->op, p.output_channels, 16);
+    if (thin) {
+      plan->bd = static_cast<int>(p.groups);
+      plan->groups = 1;
+      plan->cin_g = p.channels;
+      plan->cout_g = p.output_channels;
+    }
+  }
   plan->x_pad = pad_channels(plan->op, plan->cin_g, 1);
   plan->dy_pad = pad_channels(plan->op, plan->cout_g, 16);
   const int64_t taps = p.kernel_volume;
@@ -206,7 +229,7 @@ void make_plan(const cnd_problem& p, bool forward, const int32_t* mask, Plan* pl
     ConvPass& f = plan->fwd;
     f.rank = p.rank;
     f.batch = p.batch;
-    f.groups = p.groups;
+    f.groups = plan->groups;
     fill_spatial(p, f.in, f.out, f.k, f.s, f.d, f.p);
     f.c_pad = static_cast<int>(plan->x_pad);
     f.n_real = static_cast<int>(plan->cout_g);
@@ -216,8 +239,9 @@ void make_plan(const cnd_problem& p, bool forward, const int32_t* mask, Plan* pl
     f.out_dtype = p.dtype;
     plan->fast_fwd = plan->cout_g <= 256 && plan_fprop(f, &plan->fwd_plan);
     if (plan->fast_fwd) {
-      const size_t act = static_cast<size_t>(p.batch * p.groups * p.input_volume) * f.c_pad * es;
-      const size_t wts = static_cast<size_t>(p.groups * taps * f.n_pad * f.c_pad) * es;
+      const size_t act =
+          static_cast<size_t>(p.batch * plan->groups * p.input_volume) * f.c_pad * es;
+      const size_t wts = static_cast<size_t>(plan->groups * taps * f.n_pad * f.c_pad) * es;
       plan->x_cl = take(&cursor, act);
       if (plan->split3) plan->x_cl_small = take(&cursor, act);
       plan->w_fwd = take(&cursor, wts);
@@ -237,7 +261,7 @@ void make_plan(const cnd_problem& p, bool forward, const int32_t* mask, Plan* pl
     ConvPass& dg = plan->dgrad;
     dg.rank = p.rank;
     dg.batch = p.batch;
-    dg.groups = p.groups;
+    dg.groups = plan->groups;
     for (int a = 0; a < p.rank; ++a) {
       dg.in[a] = p.output[a];
       dg.out[a] = p.input[a];
@@ -265,7 +289,7 @@ void make_plan(const cnd_problem& p, bool forward, const int32_t* mask, Plan* pl
     WgradPass& wg = plan->wgrad;
     wg.rank = p.rank;
     wg.batch = p.batch;
-    wg.groups = p.groups;
+    wg.groups = plan->groups;
     fill_spatial(p, wg.in, wg.out, wg.k, wg.s, wg.d, wg.p);
     wg.c_pad = static_cast<int>(plan->wg_x_pad);
     wg.cin_real = static_cast<int>(plan->cin_g);
@@ -280,33 +304,33 @@ void make_plan(const cnd_problem& p, bool forward, const int32_t* mask, Plan* pl
   const bool need_dy = plan->fast_dgrad || (plan->fast_wgrad && !f32);
   if (need_dy) {
     const size_t bytes =
-        static_cast<size_t>(p.batch * p.groups * p.output_volume) * plan->dy_pad * es;
+        static_cast<size_t>(p.batch * plan->groups * p.output_volume) * plan->dy_pad * es;
     plan->dy_cl = take(&cursor, bytes);
     if (plan->split3) plan->dy_cl_small = take(&cursor, bytes);
   }
   if ((plan->fast_dgrad || plan->fast_wgrad) && mask[2]) {
     // Upper bound of the partial count (the generic pack uses the smallest blocks).
     const size_t blocks = static_cast<size_t>((p.output_volume + 63) / 64);
-    plan->bias_partial = take(&cursor, static_cast<size_t>(p.batch * p.groups) * blocks *
+    plan->bias_partial = take(&cursor, static_cast<size_t>(p.batch * plan->groups) * blocks *
                                            plan->cout_g * sizeof(float));
   }
   if (plan->fast_dgrad) {
     const size_t bytes =
-        static_cast<size_t>(p.groups * taps * plan->dgrad.n_pad * plan->dgrad.c_pad) * es;
+        static_cast<size_t>(plan->groups * taps * plan->dgrad.n_pad * plan->dgrad.c_pad) * es;
     plan->w_dg = take(&cursor, bytes);
     if (plan->split3) plan->w_dg_small = take(&cursor, bytes);
   }
   if (plan->fast_wgrad) {
     const size_t wes = f32 ? 2 : es;
     const size_t act =
-        static_cast<size_t>(p.batch * p.groups * p.input_volume) * plan->wg_x_pad * wes;
+        static_cast<size_t>(p.batch * plan->groups * p.input_volume) * plan->wg_x_pad * wes;
     for (int part = 0; part < plan->wg_parts; ++part) plan->wg_x[part] = take(&cursor, act);
     if (f32) {
       const size_t grad =
-          static_cast<size_t>(p.batch * p.groups * p.output_volume) * plan->wg_dy_pad * wes;
+          static_cast<size_t>(p.batch * plan->groups * p.output_volume) * plan->wg_dy_pad * wes;
       for (int part = 0; part < plan->wg_parts; ++part) plan->wg_dy[part] = take(&cursor, grad);
     }
-    plan->partial = take(&cursor, static_cast<size_t>(plan->wgrad.splits) * p.groups * taps *
+    plan->partial = take(&cursor, static_cast<size_t>(plan->wgrad.splits) * plan->groups * taps *
                                       plan->cin_g * plan->cout_g * sizeof(float));
   }
   plan->total = cursor;
@@ -356,7 +380,7 @@ int cnd_plan_summary(const cnd_problem* problem, char* buffer, size_t size) {
   const int32_t all[3] = {1, 1, 1};
   cnd::make_plan(*problem, true, nullptr, &fwd);
   cnd::make_plan(*problem, false, all, &bwd);
-  char text[1024];
+  char text[4096];
   int used = 0;
   auto describe = [&](const char* name, bool fast, const cnd::FpropPlan& plan) {
     const cnd::FpropParams& P = plan.params;
@@ -373,14 +397,20 @@ int cnd_plan_summary(const cnd_problem* problem, char* buffer, size_t size) {
                           plan.parts, static_cast<long long>(P.supers_total), P.fold,
                           P.tma_store);
   };
+  if (bwd.bd > 1) {
+    used += std::snprintf(text + used, sizeof(text) - used,
+                          "groups: %d run dense (block-diagonal weights)\n", bwd.bd);
+  }
   describe("forward", fwd.fast_fwd, fwd.fwd_plan);
   describe("dgrad", bwd.fast_dgrad, bwd.dgrad_plan);
   if (bwd.fast_wgrad) {
+    char detail[256];
+    cnd::describe_wgrad_pass(bwd.wgrad, detail, sizeof(detail));
     used += std::snprintf(text + used, sizeof(text) - used,
-                          "wgrad: tcgen05 splits=%d parts=%d x_pad=%lld dy_pad=%lld\n",
+                          "wgrad: tcgen05 splits=%d parts=%d x_pad=%lld dy_pad=%lld %s\n",
                           bwd.wgrad.splits, bwd.wgrad.parts,
                           static_cast<long long>(bwd.wg_x_pad),
-                          static_cast<long long>(bwd.wg_dy_pad));
+                          static_cast<long long>(bwd.wg_dy_pad), detail);
   } else {
     used += std::snprintf(text + used, sizeof(text) - used, "wgrad: generic CUDA cores\n");
   }
@@ -417,7 +447,7 @@ int cnd_forward(const cnd_problem* problem, const void* x, const void* w, const 
   pa.dst = at(workspace, plan.x_cl);
   pa.dst_small = at(workspace, plan.x_cl_small);
   pa.batch = p.batch;
-  pa.groups = p.groups;
+  pa.groups = plan.groups;
   pa.spatial = p.input_volume;
   pa.cg = static_cast<int>(plan.cin_g);
   pa.c_pad = static_cast<int>(plan.x_pad);
@@ -434,7 +464,8 @@ int cnd_forward(const cnd_problem* problem, const void* x, const void* w, const 
   pw.w = w;
   pw.dst = at(workspace, plan.w_fwd);
   pw.dst_small = at(workspace, plan.w_fwd_small);
-  pw.groups = static_cast<int>(p.groups);
+  pw.groups = static_cast<int>(plan.groups);
+  pw.bd = plan.bd;
   pw.cout_g = static_cast<int>(plan.cout_g);
   pw.cin_g = static_cast<int>(plan.cin_g);
   pw.taps = static_cast<int>(p.kernel_volume);
@@ -549,7 +580,7 @@ int cnd_backward(const cnd_problem* problem, const void* dy, const void* x, cons
     pa.dst = at(workspace, plan.dy_cl);
     pa.dst_small = at(workspace, plan.dy_cl_small);
     pa.batch = p.batch;
-    pa.groups = p.groups;
+    pa.groups = plan.groups;
     pa.spatial = p.output_volume;
     pa.cg = static_cast<int>(plan.cout_g);
     pa.c_pad = static_cast<int>(plan.dy_pad);
@@ -573,7 +604,7 @@ int cnd_backward(const cnd_problem* problem, const void* dy, const void* x, cons
         pa.dst_small = at(workspace, plan.wg_x[1]);
         pa.dst_third = at(workspace, plan.wg_x[2]);
         pa.batch = p.batch;
-        pa.groups = p.groups;
+        pa.groups = plan.groups;
         pa.spatial = p.input_volume;
         pa.cg = static_cast<int>(plan.cin_g);
         pa.c_pad = static_cast<int>(plan.wg_x_pad);
@@ -590,7 +621,7 @@ int cnd_backward(const cnd_problem* problem, const void* dy, const void* x, cons
         pa.dst_small = at(workspace, plan.wg_dy[1]);
         pa.dst_third = at(workspace, plan.wg_dy[2]);
         pa.batch = p.batch;
-        pa.groups = p.groups;
+        pa.groups = plan.groups;
         pa.spatial = p.output_volume;
         pa.cg = static_cast<int>(plan.cout_g);
         pa.c_pad = static_cast<int>(plan.wg_dy_pad);
@@ -616,7 +647,7 @@ int cnd_backward(const cnd_problem* problem, const void* dy, const void* x, cons
       }
       if (rc != CND_OK) return rc;
       TimedPass timed(6, stream);
-      rc = reduce_wgrad(wg.partial, wg.splits, static_cast<int>(p.groups),
+      rc = reduce_wgrad(wg.partial, wg.splits, static_cast<int>(plan.groups), plan.bd,
                         static_cast<int>(p.kernel_volume), static_cast<int>(plan.cin_g),
                         static_cast<int>(plan.cout_g), dw, p.dtype, stream);
       if (rc != CND_OK) return rc;
@@ -634,7 +665,8 @@ int cnd_backward(const cnd_problem* problem, const void* dy, const void* x, cons
       pw.w = w;
       pw.dst = at(workspace, plan.w_dg);
       pw.dst_small = at(workspace, plan.w_dg_small);
-      pw.groups = static_cast<int>(p.groups);
+      pw.groups = static_cast<int>(plan.groups);
+      pw.bd = plan.bd;
       pw.cout_g = static_cast<int>(plan.cout_g);
       pw.cin_g = static_cast<int>(plan.cin_g);
       pw.taps = static_cast<int>(p.kernel_volume);
@@ -674,7 +706,7 @@ int cnd_backward(const cnd_problem* problem, const void* dy, const void* x, cons
     TimedPass timed(bias_from_pack ? 6 : 7, stream);
     if (bias_from_pack) {
       rc = reduce_bias(static_cast<const float*>(at(workspace, plan.bias_partial)), p.batch,
-                       static_cast<int>(p.groups), blocks, static_cast<int>(plan.cout_g), db,
+                       static_cast<int>(plan.groups), blocks, static_cast<int>(plan.cout_g), db,
                        p.dtype, stream);
     } else {
       GenericCall call{GenericCall::kBias, problem, dy, nullptr, nullptr, db};

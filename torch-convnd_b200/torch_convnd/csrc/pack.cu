@@ -247,15 +247,20 @@ __global__ void pack_weight_kernel(const T* __restrict__ w, T* __restrict__ dst,
     const int t = packed_row_tap(row, a.k_box[0], a.k_box[1], a.k_box[2], a.shift0, a.shift1,
                                  a.fold);
     float v = 0.0f;
+    // Block-diagonal packing: weight row co holds input channels [gb * cin_b, +cin_b) of
+    // its group gb = co / cout_b; the other columns stay zero.
+    const int cin_b = a.cin_g / a.bd, cout_b = a.cout_g / a.bd;
     if (!a.dgrad) {
       // forward operand: B[n = output channel][k = input channel] of tap t
-      if (nn < a.cout_g && c < a.cin_g) {
-        v = to_float(w[((static_cast<int64_t>(g) * a.cout_g + nn) * a.cin_g + c) * a.taps + t]);
+      if (nn < a.cout_g && c < a.cin_g && c / cin_b == nn / cout_b) {
+        const int cw = c - (nn / cout_b) * cin_b;
+        v = to_float(w[((static_cast<int64_t>(g) * a.cout_g + nn) * cin_b + cw) * a.taps + t]);
       }
     } else {
       // dgrad operand: B[n = input channel][k = output channel] of the flipped tap
-      if (nn < a.cin_g && c < a.cout_g) {
-        v = to_float(w[((static_cast<int64_t>(g) * a.cout_g + c) * a.cin_g + nn) * a.taps +
+      if (nn < a.cin_g && c < a.cout_g && nn / cin_b == c / cout_b) {
+        const int nw = nn - (c / cout_b) * cin_b;
+        v = to_float(w[((static_cast<int64_t>(g) * a.cout_g + c) * cin_b + nw) * a.taps +
                        (a.taps - 1 - t)]);
       }
     }
@@ -290,6 +295,30 @@ __global__ void wgrad_reduce_kernel(const float* __restrict__ partial, int split
     float sum = 0.0f;
     for (int s = 0; s < splits; ++s) sum += partial[s * total + p];
     dw[((static_cast<int64_t>(g) * cout_g + co) * cin_g + ci) * taps + t] = from_float<T>(sum);
+  }
+}
+
+// Block-diagonal variant: the partials [s][t][ci][co] cover all channel pairs of a
+// problem with bd groups; dw[co][cb][t] = sum over splits of partial[s][t][gb*cin_b+cb][co]
+// with gb = co / cout_b. Threads walk (t, cb, co) with co fastest.
+template <typename T>
+__global__ void wgrad_reduce_bd_kernel(const float* __restrict__ partial, int splits, int bd,
+                                       int taps, int cin, int cout, T* __restrict__ dw) {
+  const int cin_b = cin / bd, cout_b = cout / bd;
+  const int64_t stride = static_cast<int64_t>(taps) * cin * cout;
+  const int64_t total = static_cast<int64_t>(taps) * cin_b * cout;
+  for (int64_t p = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; p < total;
+       p += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    int64_t r = p;
+    const int co = static_cast<int>(r % cout);
+    r /= cout;
+    const int cb = static_cast<int>(r % cin_b);
+    const int t = static_cast<int>(r / cin_b);
+    const int ci = (co / cout_b) * cin_b + cb;
+    const int64_t src = (static_cast<int64_t>(t) * cin + ci) * cout + co;
+    float sum = 0.0f;
+    for (int s = 0; s < splits; ++s) sum += partial[s * stride + src];
+    dw[(static_cast<int64_t>(co) * cin_b + cb) * taps + t] = from_float<T>(sum);
   }
 }
 
@@ -424,7 +453,13 @@ int pack_activations(const PackActArgs& args, cudaStream_t stream) {
   return CND_OK;
 }
 
-int pack_weights(const PackWeightArgs& args, cudaStream_t stream) {
+int pack_weights(const PackWeightArgs& in, cudaStream_t stream) {
+  PackWeightArgs args = in;
+  if (args.bd < 1) args.bd = 1;
+  if (args.cin_g % args.bd != 0 || args.cout_g % args.bd != 0) {
+    return fail(CND_ERR_INVALID, "pack_weights: %d block-diagonal groups do not divide the "
+                "channels", args.bd);
+  }
   int rc;
   if (args.dtype == CND_BF16) {
     rc = pack_weight_typed<__nv_bfloat16>(args, stream);
@@ -443,8 +478,25 @@ int pack_weights(const PackWeightArgs& args, cudaStream_t stream) {
   return CND_OK;
 }
 
-int reduce_wgrad(const float* partial, int splits, int groups, int taps, int cin_g, int cout_g,
-                 void* dw, int dtype, cudaStream_t stream) {
+int reduce_wgrad(const float* partial, int splits, int groups, int bd, int taps, int cin_g,
+                 int cout_g, void* dw, int dtype, cudaStream_t stream) {
+  if (bd > 1) {
+    const int blocks = grid_for(static_cast<int64_t>(taps) * (cin_g / bd) * cout_g, 256);
+    if (dtype == CND_BF16) {
+      wgrad_reduce_bd_kernel<<<blocks, 256, 0, stream>>>(partial, splits, bd, taps, cin_g,
+                                                         cout_g, static_cast<__nv_bfloat16*>(dw));
+    } else if (dtype == CND_F16) {
+      wgrad_reduce_bd_kernel<<<blocks, 256, 0, stream>>>(partial, splits, bd, taps, cin_g,
+                                                         cout_g, static_cast<__half*>(dw));
+    } else {
+      wgrad_reduce_bd_kernel<<<blocks, 256, 0, stream>>>(partial, splits, bd, taps, cin_g,
+                                                         cout_g, static_cast<float*>(dw));
+    }
+    count_launch();
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(CND_ERR_CUDA, "wgrad_reduce: %s", cudaGetErrorString(e));
+    return CND_OK;
+  }
   const int64_t total = static_cast<int64_t>(groups) * cout_g * cin_g * taps;
   const int blocks = grid_for(total, 256);
   if (dtype == CND_BF16) {

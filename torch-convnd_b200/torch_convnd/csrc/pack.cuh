@@ -30,12 +30,17 @@ struct PackWeightArgs {
   int k_box[3];
   int shift0, shift1;
   int fold;  // 1: within a unit the a0 taps are consecutive (j0 fastest), else a1 taps
+  // > 1: the weights of a problem with bd groups packed as one dense block-diagonal
+  // matrix (groups == 1, cout_g / cin_g = all channels; off-diagonal blocks are zero)
+  int bd;
 };
 
 int pack_activations(const PackActArgs& args, cudaStream_t stream);
 int pack_weights(const PackWeightArgs& args, cudaStream_t stream);
-int reduce_wgrad(const float* partial, int splits, int groups, int taps, int cin_g, int cout_g,
-                 void* dw, int dtype, cudaStream_t stream);
+// bd > 1: the partials are of the dense block-diagonal problem (groups == 1, cin_g /
+// cout_g = all channels); only the bd diagonal blocks are written to dw.
+int reduce_wgrad(const float* partial, int splits, int groups, int bd, int taps, int cin_g,
+                 int cout_g, void* dw, int dtype, cudaStream_t stream);
 int reduce_bias(const float* partial, int64_t batch, int groups, int blocks, int cg, void* db,
                 int dtype, cudaStream_t stream);
 // Number of position blocks (and so of bias-gradient partials per (n, g)) the activation

@@ -17,6 +17,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <cstdio>
 #include <cstring>
 #include <mutex>
 
@@ -476,6 +477,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int la = l - round_b;
             const int unit = round_first + la / a_loads;
             const int lu = la - (unit - round_first) * a_loads;
+            // Padding taps past the last one (tap tiles of the last unit) are not loaded:
+            // their accumulator rows are never read, so stale slot contents do no harm.
+            // Their jobs return before the wait: once the unit's real loads land the MMA
+            // may release the stage, and a later wait would then be one phase ahead.
+            const int unit_taps =
+                P.halo ? P.entries_per_unit
+                       : min(P.entries_per_unit, g.taps - (unit_first + unit) * P.tpm);
+            const int jt = lu / (kParts * g.nb);
+            if (jt >= unit_taps) continue;
             int stage = a_stage + unit;
             uint32_t par = a_phase;
             while (stage >= P.a_stages) {
@@ -486,10 +496,14 @@ __global__ void __launch_bounds__(kThreads, 1)
               lane_ok = false;
               break;
             }
-            if (lu == 0) dev::mbar_arrive_expect_tx(&a_full[stage], P.a_tx);
+            if (lu == 0) {
+              dev::mbar_arrive_expect_tx(
+                  &a_full[stage],
+                  P.halo ? P.a_tx
+                         : static_cast<uint32_t>(unit_taps) * (P.a_tx / P.entries_per_unit));
+            }
             const int part = lu % kParts;
             const int j = (lu / kParts) % g.nb;
-            const int jt = lu / (kParts * g.nb);
             const TapEntry e = taps[unit * P.entries_per_unit + jt];
             const BoxInfo& B = boxes[j];
             const bool inside = B.valid && e.outer >= 0 && ((box_mask[j] >> e.outer) & 1u);
@@ -1139,6 +1153,17 @@ int plan_wgrad_splits(const WgradPass& pass, int sm) {
   WgradPlan plan;
   if (!plan_wgrad(pass, 0, &plan)) return 0;
   return plan.P.splits;
+}
+
+int describe_wgrad_pass(const WgradPass& pass, char* text, size_t size) {
+  WgradPlan plan;
+  if (!plan_wgrad(pass, pass.splits, &plan)) return std::snprintf(text, size, "unplanned");
+  const WgradKernelParams& P = plan.P;
+  return std::snprintf(text, size,
+                       "halo=%d fold=%d kc=%d boxes=%dx[%d,%d,%d] taps/M=%d units=%d/%d "
+                       "chunks=%d stages=%d N=%d",
+                       P.halo, P.nfold, P.kc_rows, P.g.nb, P.g.b[0], P.g.b[1], P.g.b[2], P.tpm,
+                       P.units_per_cta, P.units_total, plan.chunks, P.a_stages, P.n_cols);
 }
 
 int launch_wgrad_pass(const WgradPass& pass, cudaStream_t stream, uint64_t timeout_ns) {

@@ -63,4 +63,7 @@ int plan_wgrad_splits(const WgradPass& pass, int sm_count);
 
 int launch_wgrad_pass(const WgradPass& pass, cudaStream_t stream, uint64_t timeout_ns);
 
+// One-line description of the pass's kernel plan (for the plan summary).
+int describe_wgrad_pass(const WgradPass& pass, char* text, size_t size);
+
 }  // namespace cnd
