@@ -56,15 +56,24 @@ struct WgradKernelParams {
       idesc, tmem_cols, a_base_off, bar_off;
   int64_t ptiles;
   // nfold = k0 > 0: the box-axis-0 taps are folded into N. Position tiles then run over
-  // input-aligned slices q (k0 - 1 more than the output slices), B is the k0-slice dY box
-  // [q - k0 + 1, q] (atom j = slice q - k0 + 1 + j = tap k0 - 1 - j), and each M tile's
-  // accumulator spans n_cols = k0 * n_pad columns.
-  int nfold, n_cols;
+  // input-aligned slices q, B is the k0-slice dY box [q - k0 + 1, q] (atom j = slice
+  // q - k0 + 1 + j = tap k0 - 1 - j), and each M tile's accumulator spans
+  // n_cols = k0 * n_pad columns. Only slices whose input slice q - p0 exists are walked
+  // (slices in the zero padding add nothing): the walk index is q - q_lo.
+  int nfold, n_cols, q_lo;
   uint32_t b_lbo;  // B descriptor leading byte offset (between N atoms)
   // B buffers with a full/empty barrier pair each: 2 whole-tile slots, or, when folded, a
   // ring of b_ring one-slice slots (followed in memory by nfold - 1 mirror slots that
   // repeat slots 0.., so the nfold slices of any tile are consecutive slots).
   int b_ring;
+  // Halo kernel: one A stage holds the boxes of every unit of a position tile, unit u at
+  // u * a_unit_bytes (its kParts parts a_part_bytes apart).
+  uint32_t a_unit_bytes;
+  // Halo kernel: the last of the `chunks` tap chunks may hold fewer units than the
+  // others; it runs over splits_last <= splits position ranges (proportionally fewer
+  // CTAs, each as busy as a full chunk's), and its CTAs write zeros into the partial slots
+  // it leaves unused.
+  int chunks, splits_last;
   int outer_combos;  // product of the outer axes' kernel extents (<= 64)
   float* partial;
   unsigned int* err;
@@ -225,6 +234,143 @@ struct WgradMaps {
   CUtensorMap grad[3];
 };
 
+// Tables of a CTA's tap entries and of the outer-axis tap combinations, filled by the
+// 128 epilogue threads (idle until the main loop ends). Non-halo: entry = one tap. Halo:
+// entry = one unit, a (outer, t0, t2) combination (outer, t2 when folded) whose k1 taps
+// along a1 share one box; its tap fields describe t1 = 0.
+__device__ __forceinline__ void wgrad_tables(const WgradKernelParams& P, int t, int unit_first,
+                                             int entry_count, OuterCombo* combos,
+                                             TapEntry* taps) {
+  const BoxGeom& g = P.g;
+  for (int c = t; c < P.outer_combos; c += 128) {
+    int rest = c;
+#pragma unroll
+    for (int a = kMaxOuter - 1; a >= 0; --a) {
+      if (a < g.n_outer) {
+        combos[c].off[a] = (rest % g.k_o[a]) * g.d_o[a];
+        rest /= g.k_o[a];
+      } else {
+        combos[c].off[a] = 0;
+      }
+    }
+  }
+  for (int i = t; i < entry_count; i += 128) {
+    int tap;
+    if (P.halo) {
+      const int unit = unit_first + i;
+      const int t2 = unit % g.k[2];
+      const int rest = unit / g.k[2];  // (outer, t0) row-major; outer alone when folded
+      tap = (P.nfold ? rest * g.k[0] * g.k[1] : rest * g.k[1]) * g.k[2] + t2;
+    } else {
+      tap = unit_first * P.tpm + i;
+    }
+    TapEntry e{0, 0, 0, 0, 0};
+    if (tap < g.taps) {
+      int rest = tap;
+      e.dx2 = (rest % g.k[2]) * g.d[2];
+      rest /= g.k[2];
+      e.dx1 = (rest % g.k[1]) * g.d[1];
+      rest /= g.k[1];
+      e.dx0 = (rest % g.k[0]) * g.d[0];
+      rest /= g.k[0];
+      e.outer = rest;  // row-major index over the outer tap axes
+      int64_t delta = 0;
+#pragma unroll
+      for (int a = kMaxOuter - 1; a >= 0; --a) {
+        if (a < g.n_outer) {
+          delta += static_cast<int64_t>(rest % g.k_o[a]) * g.d_o[a] * g.in_o_stride[a];
+          rest /= g.k_o[a];
+        }
+      }
+      e.delta = static_cast<int32_t>(delta);
+    } else {
+      e.outer = -1;  // padding slot of the last M tile: loads read zeros
+    }
+    taps[i] = e;
+  }
+}
+
+// Epilogue of a weight-gradient CTA (warps 2-5): waits for the last MMA, then writes
+// its accumulators (mt_count M tiles of n_cols columns) as one fp32 partial. A chunk run
+// over chunk_splits < P.splits position ranges also writes zeros into the slots
+// chunk_splits..P.splits-1 of its taps (CTA `split` takes every chunk_splits-th of them),
+// so that the reduction over P.splits slots finds every slot written.
+__device__ __forceinline__ void wgrad_epilogue(const WgradKernelParams& P, uint32_t tmem,
+                                               uint64_t* acc_bar, const volatile uint32_t* progress,
+                                               int split, int grp, int unit_first, int unit_count,
+                                               bool empty_range, int warp, int lane,
+                                               int chunk_splits) {
+  const BoxGeom& g = P.g;
+  const dev::ErrorWord err{P.err};
+  dev::mbar_wait_progress(acc_bar, 0, progress, err, kSiteWEpilogue, P.timeout_ns);
+  dev::tc_fence_after();
+  const int quarter = warp & 3;
+  const int row = quarter * 32 + lane;
+  const int jt = row / P.c_pad;
+  const int ci = row - jt * P.c_pad;
+  const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+  const int mt_count = unit_count * P.mtpu;
+  const int64_t slot_stride = g.groups * g.taps * static_cast<int64_t>(P.cin_real) * P.n_real;
+  for (int mt = 0; mt < mt_count; ++mt) {
+    int tap;
+    bool valid;
+    if (P.halo) {
+      const int unit = unit_first + mt / P.mtpu;
+      const int t1 = (mt % P.mtpu) * P.tpm + jt;
+      const int t2 = unit % g.k[2];
+      const int rest = unit / g.k[2];  // (outer, t0), or outer alone when folded
+      tap = ((P.nfold ? rest * g.k[0] : rest) * g.k[1] + t1) * g.k[2] + t2;
+      valid = t1 < g.k[1] && ci < P.cin_real;
+    } else {
+      tap = (unit_first + mt) * P.tpm + jt;
+      valid = tap < g.taps && ci < P.cin_real;
+    }
+    for (int c = 0; c < P.n_cols / 16; ++c) {
+      // Column block j of a folded accumulator is tap k0 - 1 - j along box axis 0.
+      const int block = (c * 16) / P.n_pad;
+      const int co_base = c * 16 - block * P.n_pad;
+      const int tap_c = P.nfold ? tap + (P.nfold - 1 - block) * g.k[1] * g.k[2] : tap;
+      float* dst = P.partial +
+                   ((((static_cast<int64_t>(split) * g.groups + grp) * g.taps + tap_c) *
+                         P.cin_real +
+                     ci) *
+                    P.n_real);
+      uint32_t v[16];
+      __syncwarp();
+      dev::tmem_load16(lane_addr + static_cast<uint32_t>(mt * P.n_cols + c * 16), v);
+      dev::tmem_load_wait();
+      if (valid) {
+        if (empty_range) {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) v[i] = 0u;
+        }
+        if ((P.n_real & 3) == 0 && co_base + 16 <= P.n_real) {
+          // 16-byte stores of four consecutive output channels (row is 16-byte aligned)
+          float4* d4 = reinterpret_cast<float4*>(dst + co_base);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            d4[i] = make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
+                                __uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3]));
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int co = co_base + i;
+            if (co < P.n_real) dst[co] = __uint_as_float(v[i]);
+          }
+        }
+        for (int slot = chunk_splits + split; slot < P.splits; slot += chunk_splits) {
+          float* zdst = dst + static_cast<int64_t>(slot - split) * slot_stride;
+          for (int i = 0; i < 16; ++i) {
+            const int co = co_base + i;
+            if (co < P.n_real) zdst[co] = 0.0f;
+          }
+        }
+      }
+    }
+  }
+}
+
 template <int kParts, int kKSteps>
 __global__ void __launch_bounds__(kThreads, 1)
     wgrad_kernel(const __grid_constant__ WgradMaps maps,
@@ -276,59 +422,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
     dev::tmem_alloc(tmem_slot, P.tmem_cols);
   }
-  // Tables of this CTA's taps and of the outer-axis tap combinations (epilogue warps,
-  // which are idle until the main loop ends).
-  if (warp >= 2) {
-    const int t = threadIdx.x - 64;
-    for (int c = t; c < P.outer_combos; c += 128) {
-      int rest = c;
-#pragma unroll
-      for (int a = kMaxOuter - 1; a >= 0; --a) {
-        if (a < g.n_outer) {
-          combos[c].off[a] = (rest % g.k_o[a]) * g.d_o[a];
-          rest /= g.k_o[a];
-        } else {
-          combos[c].off[a] = 0;
-        }
-      }
-    }
-    for (int i = t; i < entry_count; i += 128) {
-      // Non-halo: entry = one tap. Halo: entry = one unit, i.e. a (outer, t0, t2)
-      // combination whose k1 taps along a1 share one box (t1 = 0 here).
-      int tap;
-      if (P.halo) {
-        const int unit = unit_first + i;
-        const int t2 = unit % g.k[2];
-        const int rest = unit / g.k[2];  // (outer, t0) row-major; outer alone when folded
-        tap = (P.nfold ? rest * g.k[0] * g.k[1] : rest * g.k[1]) * g.k[2] + t2;
-      } else {
-        tap = unit_first * P.tpm + i;
-      }
-      TapEntry e{0, 0, 0, 0, 0};
-      if (tap < g.taps) {
-        int rest = tap;
-        e.dx2 = (rest % g.k[2]) * g.d[2];
-        rest /= g.k[2];
-        e.dx1 = (rest % g.k[1]) * g.d[1];
-        rest /= g.k[1];
-        e.dx0 = (rest % g.k[0]) * g.d[0];
-        rest /= g.k[0];
-        e.outer = rest;  // row-major index over the outer tap axes
-        int64_t delta = 0;
-#pragma unroll
-        for (int a = kMaxOuter - 1; a >= 0; --a) {
-          if (a < g.n_outer) {
-            delta += static_cast<int64_t>(rest % g.k_o[a]) * g.d_o[a] * g.in_o_stride[a];
-            rest /= g.k_o[a];
-          }
-        }
-        e.delta = static_cast<int32_t>(delta);
-      } else {
-        e.outer = -1;  // padding slot of the last M tile: loads read zeros
-      }
-      taps[i] = e;
-    }
-  }
+  if (warp >= 2) wgrad_tables(P, threadIdx.x - 64, unit_first, entry_count, combos, taps);
   dev::tc_fence_before();
   __syncthreads();
   dev::tc_fence_after();
@@ -454,7 +548,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               const int dst_slot = c == 0 ? slot : P.b_ring + slot;
               dev::tma_load_5d(b_base + dst_slot * P.b_slot_bytes, &maps.grad[0], &b_full[slot],
                                0, boxes[0].q[2] * g.b[2], boxes[0].q[1] * g.b[1],
-                               q0 - (new_entries - 1) + k, mo);
+                               P.q_lo + q0 - (new_entries - 1) + k, mo);
             } else {
               if (!dev::mbar_wait(&b_empty[b_slot], b_phase ^ 1u, err, kSiteWProducer,
                                   P.timeout_ns)) {
@@ -646,67 +740,332 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     dev::mma_commit_warp(acc_bar);
   } else if (warp >= 2) {
-    // ---------------- epilogue: TMEM -> fp32 partial ----------------
-    dev::mbar_wait_progress(acc_bar, 0, progress, err, kSiteWEpilogue, P.timeout_ns);
+    wgrad_epilogue(P, tmem, acc_bar, progress, split, grp, unit_first, unit_count,
+                   p_begin >= p_end, warp, lane, P.splits);
+  }
+  dev::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
     dev::tc_fence_after();
-    const int quarter = warp & 3;
-    const int row = quarter * 32 + lane;
-    const int jt = row / P.c_pad;
-    const int ci = row - jt * P.c_pad;
-    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
-    const bool empty_range = p_begin >= p_end;
-    const int mt_count = unit_count * P.mtpu;
-    for (int mt = 0; mt < mt_count; ++mt) {
-      int tap;
-      bool valid;
-      if (P.halo) {
-        const int unit = unit_first + mt / P.mtpu;
-        const int t1 = (mt % P.mtpu) * P.tpm + jt;
-        const int t2 = unit % g.k[2];
-        const int rest = unit / g.k[2];  // (outer, t0), or outer alone when folded
-        tap = ((P.nfold ? rest * g.k[0] : rest) * g.k[1] + t1) * g.k[2] + t2;
-        valid = t1 < g.k[1] && ci < P.cin_real;
-      } else {
-        tap = (unit_first + mt) * P.tpm + jt;
-        valid = tap < g.taps && ci < P.cin_real;
+    dev::tmem_dealloc(tmem, P.tmem_cols);
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// Weight-gradient kernel for halo plans (one box per tile, one A box per unit). Same
+// decomposition, MMAs and epilogue as wgrad_kernel, with a leaner pipeline:
+//  * one A stage per position tile holding every unit's box, so the MMA warp takes one
+//    barrier handoff per tile instead of one per unit;
+//  * the producer keeps all per-tile state in registers: lane 0 walks the boxes and
+//    broadcasts each box with warp shuffles, lane u holds unit u's tap entry. Loads from
+//    shared memory are slow while the tensor core streams operands from it, and a
+//    producer that read its tables from there fell behind the MMAs.
+template <int kParts, int kKSteps>
+__global__ void __launch_bounds__(kThreads, 1)
+    wgrad_halo_kernel(const __grid_constant__ WgradMaps maps,
+                      const __grid_constant__ WgradKernelParams P) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  uint8_t* b_base = smem;
+  uint8_t* a_base = smem + P.a_base_off;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + P.bar_off);
+  uint64_t* b_full = bars;
+  uint64_t* b_empty = bars + P.b_ring;
+  uint64_t* a_full = bars + 2 * P.b_ring;
+  uint64_t* a_empty = a_full + P.a_stages;
+  uint64_t* acc_bar = a_empty + P.a_stages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_bar + 1);
+  volatile uint32_t* progress = tmem_slot + 1;
+  OuterCombo* combos = reinterpret_cast<OuterCombo*>(tmem_slot + 4);
+  TapEntry* taps = reinterpret_cast<TapEntry*>(combos + kMaxOuterCombos);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  // Grid x: `splits` CTAs for each full chunk, then splits_last for the last chunk.
+  const int full_ctas = (P.chunks - 1) * P.splits;
+  const int bx = static_cast<int>(blockIdx.x);
+  const bool last = bx >= full_ctas;
+  const int chunk = last ? P.chunks - 1 : bx / P.splits;
+  const int split = last ? bx - full_ctas : bx - chunk * P.splits;
+  const int chunk_splits = last ? P.splits_last : P.splits;
+  const int grp = blockIdx.z;
+  const BoxGeom& g = P.g;
+  const dev::ErrorWord err{P.err};
+  const int unit_first = chunk * P.units_per_cta;
+  const int unit_count = max(0, min(P.units_per_cta, P.units_total - unit_first));
+  // Position-tile range of this CTA (empty for a CTA without units).
+  const int64_t p_begin = P.ptiles * split / chunk_splits;
+  const int64_t p_end = unit_count > 0 ? P.ptiles * (split + 1) / chunk_splits : p_begin;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < P.b_ring; ++s) {
+      dev::mbar_init(&b_full[s], 1);
+      dev::mbar_init(&b_empty[s], 1);
+    }
+    for (int s = 0; s < P.a_stages; ++s) {
+      dev::mbar_init(&a_full[s], 1);
+      dev::mbar_init(&a_empty[s], 1);
+    }
+    dev::mbar_init(acc_bar, 1);
+    *progress = 0;
+    dev::fence_barrier_init();
+  }
+  if (warp == 0) {
+    __syncwarp();
+    dev::tmem_alloc(tmem_slot, P.tmem_cols);
+  }
+  if (warp >= 2) wgrad_tables(P, threadIdx.x - 64, unit_first, unit_count, combos, taps);
+  dev::tc_fence_before();
+  __syncthreads();
+  dev::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer (whole warp, register state) ----------------
+    if (lane == 0) {
+      for (int part = 0; part < kParts; ++part) {
+        dev::prefetch_tensormap(&maps.act[part]);
+        dev::prefetch_tensormap(&maps.grad[part]);
       }
-      for (int c = 0; c < P.n_cols / 16; ++c) {
-        // Column block j of a folded accumulator is tap k0 - 1 - j along box axis 0.
-        const int block = (c * 16) / P.n_pad;
-        const int co_base = c * 16 - block * P.n_pad;
-        const int tap_c = P.nfold ? tap + (P.nfold - 1 - block) * g.k[1] * g.k[2] : tap;
-        float* dst = P.partial +
-                     ((((static_cast<int64_t>(split) * g.groups + grp) * g.taps + tap_c) *
-                           P.cin_real +
-                       ci) *
-                      P.n_real);
-        uint32_t v[16];
-        __syncwarp();
-        dev::tmem_load16(lane_addr + static_cast<uint32_t>(mt * P.n_cols + c * 16), v);
-        dev::tmem_load_wait();
-        if (valid) {
-          if (empty_range) {
+    }
+    TapEntry mine{0, 0, 0, -1, 0};
+    if (lane < unit_count) mine = taps[lane];
+    int a_stage = 0, b_slot = 0;
+    uint32_t a_phase = 0, b_phase = 0;
+    bool ok = true;
+    BoxCursor cursor;
+    if (P.nfold) {
+      cursor_init_q0(g, p_begin, cursor);
+    } else {
+      cursor_init(g, p_begin, cursor);
+    }
+    BoxInfo box;  // lane 0's walk; broadcast per tile
+    box.n = 0;
+    box.outer_lin = 0;
+    box.in_ng_base = 0;
+    box.out_merged = 0;
+    uint64_t mask = 0;
+    int ring_slot = 0;
+    uint32_t ring_phase = 0;
+    int q0 = P.nfold ? static_cast<int>(p_begin % g.nbox[0]) : 0;
+    const uint32_t stage_tx = P.a_tx * static_cast<uint32_t>(unit_count);
+    const int b_loads = P.b_blocks * kParts;
+    for (int64_t pt = p_begin; pt < p_end && ok; ++pt) {
+      if (lane == 0) {
+        const bool refresh = cursor.outer_changed;
+        cursor_box(g, cursor, grp, refresh, box);
+        if (refresh) {
+          // outer tap combinations that stay inside the input (rare: once per outer step)
+          mask = 0;
+          for (int c = 0; c < P.outer_combos; ++c) {
+            bool inside = true;
 #pragma unroll
-            for (int i = 0; i < 16; ++i) v[i] = 0u;
-          }
-          if ((P.n_real & 3) == 0 && co_base + 16 <= P.n_real) {
-            // 16-byte stores of four consecutive output channels (row is 16-byte aligned)
-            float4* d4 = reinterpret_cast<float4*>(dst + co_base);
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              d4[i] = make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
-                                  __uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3]));
+            for (int a = 0; a < kMaxOuter; ++a) {
+              if (a < g.n_outer) {
+                const int coord = box.ib_o[a] + combos[c].off[a];
+                inside = inside && coord >= 0 && coord < g.in_o[a];
+              }
             }
-          } else {
+            if (inside) mask |= uint64_t{1} << c;
+          }
+        }
+        if (P.nfold) {
+          cursor_next_q0(g, cursor);
+        } else {
+          cursor_next(g, cursor);
+        }
+      }
+      const unsigned full = 0xffffffffu;
+      const int valid = __shfl_sync(full, box.valid, 0);
+      const int ib0 = __shfl_sync(full, box.ib[0], 0);
+      const int ib1 = __shfl_sync(full, box.ib[1], 0);
+      const int ib2 = __shfl_sync(full, box.ib[2], 0);
+      const int bq0 = __shfl_sync(full, box.q[0], 0);
+      const int bq1 = __shfl_sync(full, box.q[1], 0);
+      const int bq2 = __shfl_sync(full, box.q[2], 0);
+      const int64_t in_base = __shfl_sync(full, box.in_ng_base, 0);
+      const int32_t out_m = __shfl_sync(full, static_cast<int32_t>(box.out_merged), 0);
+      const uint64_t msk = __shfl_sync(full, mask, 0);
+      bool lane_ok = true;
+      // A: every unit's box into this tile's stage, lane u loading unit u.
+      if (lane < unit_count) {
+        if (!dev::mbar_wait(&a_empty[a_stage], a_phase ^ 1u, err, kSiteWProducer,
+                            P.timeout_ns)) {
+          lane_ok = false;
+        } else {
+          if (lane == 0) dev::mbar_arrive_expect_tx(&a_full[a_stage], stage_tx);
+          const bool inside = valid && mine.outer >= 0 && ((msk >> mine.outer) & 1u);
+          const int32_t mc = inside ? static_cast<int32_t>(in_base + mine.delta) : -1;
+          uint8_t* dst = a_base + a_stage * P.a_slot_bytes + lane * P.a_unit_bytes;
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              const int co = co_base + i;
-              if (co < P.n_real) dst[co] = __uint_as_float(v[i]);
+          for (int part = 0; part < kParts; ++part) {
+            dev::tma_load_5d(dst + part * P.a_part_bytes, &maps.act[part], &a_full[a_stage], 0,
+                             ib2 + mine.dx2, ib1 + mine.dx1, ib0 + mine.dx0, mc);
+          }
+        }
+      }
+      // B: folded — the new ring entries (a mirror copy for the first nfold - 1 slots);
+      // otherwise the tile's dY box into one of two slots.
+      const bool run_start = P.nfold && (pt == p_begin || q0 == 0);
+      const int new_entries = P.nfold ? (run_start ? P.nfold : 1) : 0;
+      if (P.nfold) {
+        // job index of this lane: entries in ring order, mirrored slots twice
+        int l = 0, k = 0, c = -1, slot = ring_slot;
+        uint32_t par = ring_phase;
+        for (int e = 0; e < new_entries; ++e) {
+          const int copies = slot < P.nfold - 1 ? 2 : 1;
+          if (lane >= l && lane < l + copies) {
+            k = e;
+            c = lane - l;
+            break;
+          }
+          l += copies;
+          if (++slot == P.b_ring) {
+            slot = 0;
+            par ^= 1u;
+          }
+        }
+        if (c >= 0 && lane_ok) {
+          if (!dev::mbar_wait(&b_empty[slot], par ^ 1u, err, kSiteWProducer, P.timeout_ns)) {
+            lane_ok = false;
+          } else {
+            const bool mirror = slot < P.nfold - 1;
+            if (c == 0) dev::mbar_arrive_expect_tx(&b_full[slot], P.b_tx * (mirror ? 2u : 1u));
+            const int dst_slot = c == 0 ? slot : P.b_ring + slot;
+            dev::tma_load_5d(b_base + dst_slot * P.b_slot_bytes, &maps.grad[0], &b_full[slot], 0,
+                             bq2 * g.b[2], bq1 * g.b[1], P.q_lo + q0 - (new_entries - 1) + k,
+                             valid ? out_m : -1);
+          }
+        }
+      } else if (lane < b_loads && lane_ok) {
+        if (!dev::mbar_wait(&b_empty[b_slot], b_phase ^ 1u, err, kSiteWProducer,
+                            P.timeout_ns)) {
+          lane_ok = false;
+        } else {
+          if (lane == 0) dev::mbar_arrive_expect_tx(&b_full[b_slot], P.b_tx);
+          const int part = lane % kParts;
+          const int blk = lane / kParts;
+          uint8_t* dst = b_base + b_slot * P.b_slot_bytes + blk * (P.kc_rows * 128);
+          dev::tma_load_5d(dst + part * P.b_part_bytes, &maps.grad[part], &b_full[b_slot],
+                           blk * P.b_blk_elems, bq2 * g.b[2], bq1 * g.b[1], bq0 * g.b[0],
+                           valid ? out_m : -1);
+        }
+      }
+      ok = __all_sync(0xffffffffu, lane_ok) != 0;
+      if (!ok) break;
+      if (P.nfold) {
+        for (int e = 0; e < new_entries; ++e) {
+          if (++ring_slot == P.b_ring) {
+            ring_slot = 0;
+            ring_phase ^= 1u;
+          }
+        }
+        if (++q0 == g.nbox[0]) q0 = 0;
+      } else if (++b_slot == 2) {
+        b_slot = 0;
+        b_phase ^= 1u;
+      }
+      if (++a_stage == P.a_stages) {
+        a_stage = 0;
+        a_phase ^= 1u;
+      }
+    }
+    (void)ok;
+  } else if (warp == 1) {
+    // ---------------- MMA issuer (converged warp, elect.sync inside each MMA) ----------------
+    const bool leader = lane == 0;
+    const uint32_t tmem_u = dev::warp_uniform(tmem);
+    int a_stage = 0, b_slot = 0;
+    uint32_t a_phase = 0, b_phase = 0;
+    const uint64_t a_hi = dev::make_smem_desc(0, P.atom_bytes, 8u * P.a_row_bytes, P.a_layout);
+    const uint32_t group_units = (static_cast<uint32_t>(P.tpm) * P.atom_bytes) >> 4;
+    const uint64_t b_hi = dev::make_smem_desc(0, P.b_lbo, 8u * P.b_row_bytes, P.b_layout);
+    const uint32_t a_step = (16u * P.a_row_bytes) >> 4;
+    const uint32_t b_step = (16u * P.b_row_bytes) >> 4;
+    const uint32_t a_part = P.a_part_bytes >> 4;
+    const uint32_t b_part = P.b_part_bytes >> 4;
+    const uint32_t unit_units = P.a_unit_bytes >> 4;
+    bool ok = true;
+    int ring_slot = 0, first_slot = 0;
+    uint32_t ring_phase = 0;
+    int q0 = P.nfold ? static_cast<int>(p_begin % g.nbox[0]) : 0;
+    for (int64_t pt = p_begin; pt < p_end && ok; ++pt) {
+      uint32_t bs;
+      bool run_end = false;
+      if (P.nfold) {
+        const bool run_start = pt == p_begin || q0 == 0;
+        run_end = pt == p_end - 1 || q0 == g.nbox[0] - 1;
+        if (++q0 == g.nbox[0]) q0 = 0;
+        if (run_start) {
+          first_slot = ring_slot;
+        } else if (++first_slot == P.b_ring) {
+          first_slot = 0;
+        }
+        for (int k = run_start ? P.nfold : 1; k > 0 && ok; --k) {
+          if (!dev::mbar_wait_warp(&b_full[ring_slot], ring_phase, err, kSiteWMma,
+                                   P.timeout_ns)) {
+            ok = false;
+          }
+          if (++ring_slot == P.b_ring) {
+            ring_slot = 0;
+            ring_phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        bs = dev::warp_uniform(dev::smem_u32(b_base + first_slot * P.b_slot_bytes) >> 4);
+      } else {
+        if (!dev::mbar_wait_warp(&b_full[b_slot], b_phase, err, kSiteWMma, P.timeout_ns)) break;
+        bs = dev::warp_uniform(dev::smem_u32(b_base + b_slot * P.b_slot_bytes) >> 4);
+      }
+      if (!dev::mbar_wait_warp(&a_full[a_stage], a_phase, err, kSiteWMma, P.timeout_ns)) break;
+      dev::tc_fence_after();
+      const uint32_t first_tile = pt == p_begin ? 1u : 0u;
+      const uint32_t as =
+          dev::warp_uniform(dev::smem_u32(a_base + a_stage * P.a_slot_bytes) >> 4);
+      for (int unit = 0; unit < unit_count; ++unit) {
+        for (int gi = 0; gi < P.mtpu; ++gi) {
+          const uint32_t d = tmem_u + static_cast<uint32_t>((unit * P.mtpu + gi) * P.n_cols);
+          const uint32_t ag = as + static_cast<uint32_t>(unit) * unit_units +
+                              static_cast<uint32_t>(gi) * group_units;
+#pragma unroll
+          for (int ks = 0; ks < kKSteps; ++ks) {
+            const uint32_t aoff = ag + static_cast<uint32_t>(ks) * a_step;
+            const uint32_t boff = bs + static_cast<uint32_t>(ks) * b_step;
+#pragma unroll
+            for (int q = 0; q < product_count<kParts>(); ++q) {
+              const uint64_t ad = a_hi | (aoff + product_a(kParts, q) * a_part);
+              const uint64_t bd = b_hi | (boff + product_b(kParts, q) * b_part);
+              const uint32_t acc = (first_tile != 0u && ks == 0 && q == 0) ? 0u : 1u;
+              dev::mma_f16_warp(d, ad, bd, P.idesc, acc);
             }
           }
         }
       }
+      dev::mma_commit_warp(&a_empty[a_stage]);
+      if (++a_stage == P.a_stages) {
+        a_stage = 0;
+        a_phase ^= 1u;
+      }
+      if (P.nfold) {
+        int slot = first_slot;
+        for (int k = run_end ? P.nfold : 1; k > 0; --k) {
+          dev::mma_commit_warp(&b_empty[slot]);
+          if (++slot == P.b_ring) slot = 0;
+        }
+      } else {
+        dev::mma_commit_warp(&b_empty[b_slot]);
+        if (++b_slot == 2) {
+          b_slot = 0;
+          b_phase ^= 1u;
+        }
+      }
+      if (leader) *progress = static_cast<uint32_t>(pt - p_begin + 1);
+      __syncwarp();
     }
+    dev::mma_commit_warp(acc_bar);
+  } else if (warp >= 2) {
+    wgrad_epilogue(P, tmem, acc_bar, progress, split, grp, unit_first, unit_count,
+                   p_begin >= p_end, warp, lane, chunk_splits);
   }
   dev::tc_fence_before();
   __syncthreads();
@@ -1035,10 +1394,18 @@ bool plan_wgrad(const WgradPass& pass, int splits_hint, WgradPlan* plan) {
       P.units_total = P.g.taps / k1;
       P.entries_per_unit = 1;
       if (fold) {
-        // Position tiles run over the input-aligned slices q in [0, out0 + k0 - 1).
+        // Position tiles run over the input-aligned slices q in [q_lo, q_hi): those of
+        // [0, out0 + k0 - 1) whose input slice q - p0 lies inside the input. The box
+        // origin of walk index i is then input slice i - (p0 - q_lo).
+        const int p0 = P.g.p[0];
+        const int q_lo = std::max(0, p0);
+        const int q_hi = std::min(P.g.out[0] + k0 - 1, p0 + P.g.in[0]);
+        if (q_hi <= q_lo) continue;
         P.nfold = fold;
+        P.q_lo = q_lo;
         P.units_total = P.g.taps / (k1 * k0);
-        P.g.nbox[0] += k0 - 1;
+        P.g.nbox[0] = q_hi - q_lo;
+        P.g.p[0] = p0 - q_lo;
         P.g.boxes_per_group = P.g.outer_count * static_cast<int64_t>(P.g.nbox[0]) *
                               P.g.nbox[1] * P.g.nbox[2];
       }
@@ -1083,22 +1450,6 @@ bool plan_wgrad(const WgradPass& pass, int splits_hint, WgradPlan* plan) {
   P.n_cols = slices * pass.n_pad;
   // N atoms: consecutive one-slice ring slots of a folded tile, else 64-channel blocks.
   P.b_lbo = P.nfold ? P.b_slot_bytes : static_cast<uint32_t>(kc) * 128u;
-  // B memory: two tile slots, or a ring of nfold + 2 one-slice slots (the tile's slices
-  // plus two loaded ahead) and nfold - 1 mirrors; the A stages get the rest, since A
-  // loads are the deeper stream (several units per tile).
-  P.b_ring = 2;
-  uint32_t b_region = 2 * P.b_slot_bytes;
-  if (P.nfold) {
-    P.b_ring = P.nfold + 2;
-    b_region = static_cast<uint32_t>(P.b_ring + P.nfold - 1) * P.b_slot_bytes;
-  }
-  if (b_region + 2 * P.a_slot_bytes > 208 * 1024) return false;
-  int stages = static_cast<int>((208 * 1024 - b_region) / P.a_slot_bytes);
-  if (stages > 12) stages = 12;
-  if (stages < 2) return false;
-  P.a_stages = stages;
-  P.a_base_off = b_region;
-  P.bar_off = P.a_base_off + stages * P.a_slot_bytes;
   int64_t combos = 1;
   for (int a = 0; a < P.g.n_outer; ++a) combos *= P.g.k_o[a];
   if (combos > kMaxOuterCombos) return false;
@@ -1108,6 +1459,52 @@ bool plan_wgrad(const WgradPass& pass, int splits_hint, WgradPlan* plan) {
   if (max_units < 1) return false;
   plan->chunks = (P.units_total + max_units - 1) / max_units;
   P.units_per_cta = (P.units_total + plan->chunks - 1) / plan->chunks;
+  constexpr uint32_t kSmemBudget = 208 * 1024;
+  if (P.halo) {
+    // One A stage per position tile holding every unit's box (wgrad_halo_kernel). B: two
+    // tile slots, or a ring of nfold + extra one-slice slots (the tile's slices plus
+    // `extra` loaded ahead) followed by nfold - 1 mirror slots. Prefer a ring three
+    // slices ahead with at least three A stages; fewer units per CTA when even two
+    // stages do not fit.
+    P.a_unit_bytes = P.a_part_bytes * parts;
+    if (P.units_per_cta > 32) {  // one producer lane per unit
+      P.units_per_cta = 32;
+      plan->chunks = (P.units_total + 31) / 32;
+    }
+    bool fitted = false;
+    for (;;) {
+      P.a_slot_bytes = P.a_unit_bytes * static_cast<uint32_t>(P.units_per_cta);
+      for (int extra = 3; extra >= 2 && !fitted; --extra) {
+        const int ring = P.nfold ? P.nfold + extra : 2;
+        const uint32_t b_region =
+            static_cast<uint32_t>(P.nfold ? ring + P.nfold - 1 : 2) * P.b_slot_bytes;
+        if (b_region >= kSmemBudget) continue;
+        int stages = static_cast<int>((kSmemBudget - b_region) / P.a_slot_bytes);
+        if (stages > 8) stages = 8;
+        if (stages < (extra == 3 && P.nfold ? 3 : 2)) continue;
+        P.b_ring = ring;
+        P.a_stages = stages;
+        P.a_base_off = b_region;
+        fitted = true;
+      }
+      if (fitted || P.units_per_cta == 1) break;
+      --P.units_per_cta;
+      plan->chunks = (P.units_total + P.units_per_cta - 1) / P.units_per_cta;
+    }
+    if (!fitted) return false;
+  } else {
+    // B memory: two tile slots; the A stages (one unit of tpm tap tiles each) get the
+    // rest, since A loads are the deeper stream (several units per tile).
+    P.b_ring = 2;
+    const uint32_t b_region = 2 * P.b_slot_bytes;
+    if (b_region + 2 * P.a_slot_bytes > kSmemBudget) return false;
+    int stages = static_cast<int>((kSmemBudget - b_region) / P.a_slot_bytes);
+    if (stages > 12) stages = 12;
+    if (stages < 2) return false;
+    P.a_stages = stages;
+    P.a_base_off = b_region;
+  }
+  P.bar_off = P.a_base_off + static_cast<uint32_t>(P.a_stages) * P.a_slot_bytes;
   P.mt_per_cta = P.units_per_cta * P.mtpu;
   P.tmem_cols = tmem_columns(P.mt_per_cta * P.n_cols);
   P.idesc = make_idesc(pass.op, 128, P.n_cols, true, true);
@@ -1128,13 +1525,36 @@ bool plan_wgrad(const WgradPass& pass, int splits_hint, WgradPlan* plan) {
       const int64_t need = (P.ptiles + tiles_per_split - 1) / tiles_per_split;
       if (s < need) s = need < 1024 ? need : 1024;
     }
+    if (P.halo && plan->chunks > 1 && parts == 1) {
+      // The last chunk's CTAs get proportionally fewer splits, the full chunks more:
+      // the largest s with (chunks - 1) * s + last(s) CTAs per group in one wave.
+      const int last_units = P.units_total - (plan->chunks - 1) * P.units_per_cta;
+      for (int64_t t = 4 * s; t > s; --t) {
+        int64_t last = (t * last_units + P.units_per_cta / 2) / P.units_per_cta;
+        if (last < 1) last = 1;
+        if (((plan->chunks - 1) * t + last) * pass.groups <= sm_count()) {
+          s = t;
+          break;
+        }
+      }
+    }
     if (s > P.ptiles) s = P.ptiles;
     if (s < 1) s = 1;
     splits = static_cast<int>(s);
   }
   P.splits = splits;
-  plan->smem = P.bar_off + (2 * P.b_ring + 2 * stages + 1) * 8 + 16 +
-               (sizeof(BoxInfo) + sizeof(uint64_t)) * kMaxBoxes +
+  P.chunks = plan->chunks;
+  P.splits_last = splits;
+  if (P.halo) {
+    const int last_units = P.units_total - (plan->chunks - 1) * P.units_per_cta;
+    int64_t last = (static_cast<int64_t>(splits) * last_units + P.units_per_cta / 2) /
+                   P.units_per_cta;
+    if (last < 1) last = 1;
+    if (last > splits) last = splits;
+    P.splits_last = static_cast<int>(last);
+  }
+  plan->smem = P.bar_off + (2 * P.b_ring + 2 * P.a_stages + 1) * 8 + 16 +
+               (P.halo ? 0 : (sizeof(BoxInfo) + sizeof(uint64_t)) * kMaxBoxes) +
                sizeof(OuterCombo) * kMaxOuterCombos +
                sizeof(TapEntry) * static_cast<size_t>(P.units_per_cta) * P.entries_per_unit +
                1024;
@@ -1161,9 +1581,10 @@ int describe_wgrad_pass(const WgradPass& pass, char* text, size_t size) {
   const WgradKernelParams& P = plan.P;
   return std::snprintf(text, size,
                        "halo=%d fold=%d kc=%d boxes=%dx[%d,%d,%d] taps/M=%d units=%d/%d "
-                       "chunks=%d stages=%d N=%d",
+                       "chunks=%d stages=%d ring=%d N=%d",
                        P.halo, P.nfold, P.kc_rows, P.g.nb, P.g.b[0], P.g.b[1], P.g.b[2], P.tpm,
-                       P.units_per_cta, P.units_total, plan.chunks, P.a_stages, P.n_cols);
+                       P.units_per_cta, P.units_total, plan.chunks, P.a_stages, P.b_ring,
+                       P.n_cols);
 }
 
 int launch_wgrad_pass(const WgradPass& pass, cudaStream_t stream, uint64_t timeout_ns) {
@@ -1205,14 +1626,25 @@ int launch_wgrad_pass(const WgradPass& pass, cudaStream_t stream, uint64_t timeo
                         merged_out, P.b_blk_elems, box, ones);
     if (rc != CND_OK) return rc;
   }
-  const dim3 grid(static_cast<unsigned>(P.splits), static_cast<unsigned>(plan.chunks),
-                  static_cast<unsigned>(pass.groups));
+  // Halo kernel: x enumerates the (chunk, split) CTAs of a group.
+  const dim3 grid = P.halo ? dim3(static_cast<unsigned>((plan.chunks - 1) * P.splits +
+                                                        P.splits_last),
+                                  1u, static_cast<unsigned>(pass.groups))
+                           : dim3(static_cast<unsigned>(P.splits),
+                                  static_cast<unsigned>(plan.chunks),
+                                  static_cast<unsigned>(pass.groups));
   using Kernel = void (*)(WgradMaps, WgradKernelParams);
   Kernel kernel = nullptr;
-#define CND_WGRAD_PICK(PARTS)                                        \
-  kernel = P.ksteps == 16  ? wgrad_kernel<PARTS, 16>                 \
-           : P.ksteps == 8 ? wgrad_kernel<PARTS, 8>                  \
-                           : wgrad_kernel<PARTS, 4>;
+#define CND_WGRAD_PICK(PARTS)                                                         \
+  if (P.halo) {                                                                      \
+    kernel = P.ksteps == 16  ? wgrad_halo_kernel<PARTS, 16>                          \
+             : P.ksteps == 8 ? wgrad_halo_kernel<PARTS, 8>                           \
+                             : wgrad_halo_kernel<PARTS, 4>;                          \
+  } else {                                                                           \
+    kernel = P.ksteps == 16  ? wgrad_kernel<PARTS, 16>                               \
+             : P.ksteps == 8 ? wgrad_kernel<PARTS, 8>                                \
+                             : wgrad_kernel<PARTS, 4>;                               \
+  }
   if (plan.parts == 3) {
     CND_WGRAD_PICK(3)
   } else if (plan.parts == 2) {
