@@ -769,7 +769,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* b_base = smem;
   uint8_t* a_base = smem + P.a_base_off;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + P.bar_off);
-  uint64_t* b_full = bars;
+  // Every load of a position tile (its A boxes and its new dY slices) signals the tile's
+  // a_full barrier: the MMA warp waits once per tile. b_empty[slot] frees a dY slot.
   uint64_t* b_empty = bars + P.b_ring;
   uint64_t* a_full = bars + 2 * P.b_ring;
   uint64_t* a_empty = a_full + P.a_stages;
@@ -798,10 +799,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int64_t p_end = unit_count > 0 ? P.ptiles * (split + 1) / chunk_splits : p_begin;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < P.b_ring; ++s) {
-      dev::mbar_init(&b_full[s], 1);
-      dev::mbar_init(&b_empty[s], 1);
-    }
+    for (int s = 0; s < P.b_ring; ++s) dev::mbar_init(&b_empty[s], 1);
     for (int s = 0; s < P.a_stages; ++s) {
       dev::mbar_init(&a_full[s], 1);
       dev::mbar_init(&a_empty[s], 1);
@@ -887,13 +885,27 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int32_t out_m = __shfl_sync(full, static_cast<int32_t>(box.out_merged), 0);
       const uint64_t msk = __shfl_sync(full, mask, 0);
       bool lane_ok = true;
-      // A: every unit's box into this tile's stage, lane u loading unit u.
+      const bool run_start = P.nfold && (pt == p_begin || q0 == 0);
+      const int new_entries = P.nfold ? (run_start ? P.nfold : 1) : 0;
+      // Bytes of this tile's dY loads (folded: new ring entries, mirrored slots twice).
+      uint32_t b_bytes = P.b_tx;
+      if (P.nfold) {
+        int copies = 0, slot = ring_slot;
+        for (int e = 0; e < new_entries; ++e) {
+          copies += slot < P.nfold - 1 ? 2 : 1;
+          if (++slot == P.b_ring) slot = 0;
+        }
+        b_bytes = P.b_tx * static_cast<uint32_t>(copies);
+      }
+      // A: every unit's box into this tile's stage, lane u loading unit u. Lane 0 posts
+      // the stage's bytes, dY included (a load may land before the posting; the phase
+      // cannot complete without the posting arrival).
       if (lane < unit_count) {
         if (!dev::mbar_wait(&a_empty[a_stage], a_phase ^ 1u, err, kSiteWProducer,
                             P.timeout_ns)) {
           lane_ok = false;
         } else {
-          if (lane == 0) dev::mbar_arrive_expect_tx(&a_full[a_stage], stage_tx);
+          if (lane == 0) dev::mbar_arrive_expect_tx(&a_full[a_stage], stage_tx + b_bytes);
           const bool inside = valid && mine.outer >= 0 && ((msk >> mine.outer) & 1u);
           const int32_t mc = inside ? static_cast<int32_t>(in_base + mine.delta) : -1;
           uint8_t* dst = a_base + a_stage * P.a_slot_bytes + lane * P.a_unit_bytes;
@@ -906,8 +918,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // B: folded — the new ring entries (a mirror copy for the first nfold - 1 slots);
       // otherwise the tile's dY box into one of two slots.
-      const bool run_start = P.nfold && (pt == p_begin || q0 == 0);
-      const int new_entries = P.nfold ? (run_start ? P.nfold : 1) : 0;
       if (P.nfold) {
         // job index of this lane: entries in ring order, mirrored slots twice
         int l = 0, k = 0, c = -1, slot = ring_slot;
@@ -929,10 +939,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!dev::mbar_wait(&b_empty[slot], par ^ 1u, err, kSiteWProducer, P.timeout_ns)) {
             lane_ok = false;
           } else {
-            const bool mirror = slot < P.nfold - 1;
-            if (c == 0) dev::mbar_arrive_expect_tx(&b_full[slot], P.b_tx * (mirror ? 2u : 1u));
             const int dst_slot = c == 0 ? slot : P.b_ring + slot;
-            dev::tma_load_5d(b_base + dst_slot * P.b_slot_bytes, &maps.grad[0], &b_full[slot], 0,
+            dev::tma_load_5d(b_base + dst_slot * P.b_slot_bytes, &maps.grad[0], &a_full[a_stage], 0,
                              bq2 * g.b[2], bq1 * g.b[1], P.q_lo + q0 - (new_entries - 1) + k,
                              valid ? out_m : -1);
           }
@@ -942,11 +950,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                             P.timeout_ns)) {
           lane_ok = false;
         } else {
-          if (lane == 0) dev::mbar_arrive_expect_tx(&b_full[b_slot], P.b_tx);
           const int part = lane % kParts;
           const int blk = lane / kParts;
           uint8_t* dst = b_base + b_slot * P.b_slot_bytes + blk * (P.kc_rows * 128);
-          dev::tma_load_5d(dst + part * P.b_part_bytes, &maps.grad[part], &b_full[b_slot],
+          dev::tma_load_5d(dst + part * P.b_part_bytes, &maps.grad[part], &a_full[a_stage],
                            blk * P.b_blk_elems, bq2 * g.b[2], bq1 * g.b[1], bq0 * g.b[0],
                            valid ? out_m : -1);
         }
@@ -970,13 +977,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         a_phase ^= 1u;
       }
     }
-    (void)ok;
+    if (!ok) {
+      // A wait expired: give loads already issued time to land (they take microseconds)
+      // before the CTA's shared memory goes away.
+      const uint64_t start = dev::global_timer_ns();
+      while (dev::global_timer_ns() - start < 200000u) __nanosleep(1000);
+    }
   } else if (warp == 1) {
     // ---------------- MMA issuer (converged warp, elect.sync inside each MMA) ----------------
     const bool leader = lane == 0;
     const uint32_t tmem_u = dev::warp_uniform(tmem);
     int a_stage = 0, b_slot = 0;
-    uint32_t a_phase = 0, b_phase = 0;
+    uint32_t a_phase = 0;
     const uint64_t a_hi = dev::make_smem_desc(0, P.atom_bytes, 8u * P.a_row_bytes, P.a_layout);
     const uint32_t group_units = (static_cast<uint32_t>(P.tpm) * P.atom_bytes) >> 4;
     const uint64_t b_hi = dev::make_smem_desc(0, P.b_lbo, 8u * P.b_row_bytes, P.b_layout);
@@ -987,7 +999,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t unit_units = P.a_unit_bytes >> 4;
     bool ok = true;
     int ring_slot = 0, first_slot = 0;
-    uint32_t ring_phase = 0;
     int q0 = P.nfold ? static_cast<int>(p_begin % g.nbox[0]) : 0;
     for (int64_t pt = p_begin; pt < p_end && ok; ++pt) {
       uint32_t bs;
@@ -1001,20 +1012,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         } else if (++first_slot == P.b_ring) {
           first_slot = 0;
         }
-        for (int k = run_start ? P.nfold : 1; k > 0 && ok; --k) {
-          if (!dev::mbar_wait_warp(&b_full[ring_slot], ring_phase, err, kSiteWMma,
-                                   P.timeout_ns)) {
-            ok = false;
-          }
-          if (++ring_slot == P.b_ring) {
-            ring_slot = 0;
-            ring_phase ^= 1u;
-          }
+        if (run_start) {
+          ring_slot += P.nfold;
+          if (ring_slot >= P.b_ring) ring_slot -= P.b_ring;
+        } else if (++ring_slot == P.b_ring) {
+          ring_slot = 0;
         }
-        if (!ok) break;
         bs = dev::warp_uniform(dev::smem_u32(b_base + first_slot * P.b_slot_bytes) >> 4);
       } else {
-        if (!dev::mbar_wait_warp(&b_full[b_slot], b_phase, err, kSiteWMma, P.timeout_ns)) break;
         bs = dev::warp_uniform(dev::smem_u32(b_base + b_slot * P.b_slot_bytes) >> 4);
       }
       if (!dev::mbar_wait_warp(&a_full[a_stage], a_phase, err, kSiteWMma, P.timeout_ns)) break;
@@ -1054,12 +1059,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       } else {
         dev::mma_commit_warp(&b_empty[b_slot]);
-        if (++b_slot == 2) {
-          b_slot = 0;
-          b_phase ^= 1u;
-        }
+        if (++b_slot == 2) b_slot = 0;
       }
-      if (leader) *progress = static_cast<uint32_t>(pt - p_begin + 1);
+      // progress (read by the epilogue's bounded wait) every 8 tiles
+      if (((pt - p_begin) & 7) == 7 && leader) *progress = static_cast<uint32_t>(pt - p_begin + 1);
       __syncwarp();
     }
     dev::mma_commit_warp(acc_bar);
@@ -1303,6 +1306,22 @@ struct WgradPlan {
   int halo_rows;  // box rows along a1 in halo mode
 };
 
+// Splits of the last tap chunk when the full chunks run `splits`: a CTA's time is about
+// (kTileCost + units) x its position tiles, in units of one unit's MMAs per tile, where
+// kTileCost is the fixed per-tile cost (dY slices, barrier handoffs, commits; measured
+// on B200 at 1.2-2 units' worth). The last chunk's CTAs get as many tiles as keep them
+// as busy as a full chunk's.
+int64_t last_chunk_splits(const WgradKernelParams& P, int64_t splits) {
+  constexpr double kTileCost = 1.5;
+  const int last_units = P.units_total - (P.chunks - 1) * P.units_per_cta;
+  if (P.chunks <= 1 || last_units >= P.units_per_cta) return splits;
+  const double ratio = (kTileCost + last_units) / (kTileCost + P.units_per_cta);
+  int64_t last = static_cast<int64_t>(static_cast<double>(splits) * ratio + 0.5);
+  if (last < 1) last = 1;
+  if (last > splits) last = splits;
+  return last;
+}
+
 bool plan_wgrad(const WgradPass& pass, int splits_hint, WgradPlan* plan) {
   WgradKernelParams& P = plan->P;
   std::memset(&P, 0, sizeof(P));
@@ -1510,6 +1529,7 @@ bool plan_wgrad(const WgradPass& pass, int splits_hint, WgradPlan* plan) {
   P.idesc = make_idesc(pass.op, 128, P.n_cols, true, true);
   plan->parts = parts;
   P.ptiles = (P.g.boxes_per_group + P.g.nb - 1) / P.g.nb;
+  P.chunks = plan->chunks;
   int splits = splits_hint;
   if (splits <= 0) {
     const int64_t ctas_per_split = static_cast<int64_t>(plan->chunks) * pass.groups;
@@ -1526,13 +1546,10 @@ bool plan_wgrad(const WgradPass& pass, int splits_hint, WgradPlan* plan) {
       if (s < need) s = need < 1024 ? need : 1024;
     }
     if (P.halo && plan->chunks > 1 && parts == 1) {
-      // The last chunk's CTAs get proportionally fewer splits, the full chunks more:
-      // the largest s with (chunks - 1) * s + last(s) CTAs per group in one wave.
-      const int last_units = P.units_total - (plan->chunks - 1) * P.units_per_cta;
+      // The last chunk's CTAs get fewer splits, the full chunks more: the largest s with
+      // (chunks - 1) * s + last(s) CTAs per group in one wave.
       for (int64_t t = 4 * s; t > s; --t) {
-        int64_t last = (t * last_units + P.units_per_cta / 2) / P.units_per_cta;
-        if (last < 1) last = 1;
-        if (((plan->chunks - 1) * t + last) * pass.groups <= sm_count()) {
+        if (((plan->chunks - 1) * t + last_chunk_splits(P, t)) * pass.groups <= sm_count()) {
           s = t;
           break;
         }
@@ -1545,14 +1562,7 @@ bool plan_wgrad(const WgradPass& pass, int splits_hint, WgradPlan* plan) {
   P.splits = splits;
   P.chunks = plan->chunks;
   P.splits_last = splits;
-  if (P.halo) {
-    const int last_units = P.units_total - (plan->chunks - 1) * P.units_per_cta;
-    int64_t last = (static_cast<int64_t>(splits) * last_units + P.units_per_cta / 2) /
-                   P.units_per_cta;
-    if (last < 1) last = 1;
-    if (last > splits) last = splits;
-    P.splits_last = static_cast<int>(last);
-  }
+  if (P.halo) P.splits_last = static_cast<int>(last_chunk_splits(P, splits));
   plan->smem = P.bar_off + (2 * P.b_ring + 2 * P.a_stages + 1) * 8 + 16 +
                (P.halo ? 0 : (sizeof(BoxInfo) + sizeof(uint64_t)) * kMaxBoxes) +
                sizeof(OuterCombo) * kMaxOuterCombos +
