@@ -776,9 +776,11 @@ bool plan_fprop(const ConvPass& pass, FpropPlan* plan) {
   FpropParams chosen{};
   bool found = false;
   for (int row_bytes = row_max; row_bytes >= 32; row_bytes /= 2) {
-   // Narrower channel blocks (more K passes) only when the full row already fills 128 B.
+   // Narrower channel blocks (more K passes, down to a quarter row) only when the full
+   // row already fills 128 B: they make room for more M tiles per super tile (c2 dgrad:
+   // 8 tiles of 32-byte blocks, fewer narrow edge MMAs of the a0 fold).
    if (row_bytes != row_max &&
-       (row_max < 64 || row_bytes < row_max / 2 || (pass.c_pad * es) % row_bytes != 0)) {
+       (row_max < 64 || row_bytes < row_max / 4 || (pass.c_pad * es) % row_bytes != 0)) {
      break;
    }
    for (int fold = 0; fold <= 1; ++fold) {
