@@ -818,9 +818,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   dev::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0) {
-    // ---------------- TMA producer (whole warp, register state) ----------------
-    if (lane == 0) {
+  if (warp == 0 || warp == 2) {
+    // ---------------- TMA producers (whole warps, register state) ----------------
+    // Warp 0 loads the activation boxes of every tile and posts each stage's bytes;
+    // warp 2 (an epilogue warp, idle until the main loop ends) loads the dY slices. Both
+    // walk the same tiles and wait for a stage to be free before loading into it, and all
+    // loads of a tile signal its a_full barrier.
+    const bool a_role = warp == 0;
+    if (lane == 0 && a_role) {
       for (int part = 0; part < kParts; ++part) {
         dev::prefetch_tensormap(&maps.act[part]);
         dev::prefetch_tensormap(&maps.grad[part]);
@@ -852,7 +857,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) {
         const bool refresh = cursor.outer_changed;
         cursor_box(g, cursor, grp, refresh, box);
-        if (refresh) {
+        if (refresh && a_role) {
           // outer tap combinations that stay inside the input (rare: once per outer step)
           mask = 0;
           for (int c = 0; c < P.outer_combos; ++c) {
@@ -900,7 +905,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // A: every unit's box into this tile's stage, lane u loading unit u. Lane 0 posts
       // the stage's bytes, dY included (a load may land before the posting; the phase
       // cannot complete without the posting arrival).
-      if (lane < unit_count) {
+      if (a_role && lane < unit_count) {
         if (!dev::mbar_wait(&a_empty[a_stage], a_phase ^ 1u, err, kSiteWProducer,
                             P.timeout_ns)) {
           lane_ok = false;
@@ -918,7 +923,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // B: folded — the new ring entries (a mirror copy for the first nfold - 1 slots);
       // otherwise the tile's dY box into one of two slots.
-      if (P.nfold) {
+      if (a_role) {
+        // the dY loads belong to warp 2
+      } else if (P.nfold) {
         // job index of this lane: entries in ring order, mirrored slots twice
         int l = 0, k = 0, c = -1, slot = ring_slot;
         uint32_t par = ring_phase;
@@ -936,7 +943,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         if (c >= 0 && lane_ok) {
-          if (!dev::mbar_wait(&b_empty[slot], par ^ 1u, err, kSiteWProducer, P.timeout_ns)) {
+          if (!dev::mbar_wait(&a_empty[a_stage], a_phase ^ 1u, err, kSiteWProducer,
+                              P.timeout_ns) ||
+              !dev::mbar_wait(&b_empty[slot], par ^ 1u, err, kSiteWProducer, P.timeout_ns)) {
             lane_ok = false;
           } else {
             const int dst_slot = c == 0 ? slot : P.b_ring + slot;
@@ -946,7 +955,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       } else if (lane < b_loads && lane_ok) {
-        if (!dev::mbar_wait(&b_empty[b_slot], b_phase ^ 1u, err, kSiteWProducer,
+        if (!dev::mbar_wait(&a_empty[a_stage], a_phase ^ 1u, err, kSiteWProducer,
+                            P.timeout_ns) ||
+            !dev::mbar_wait(&b_empty[b_slot], b_phase ^ 1u, err, kSiteWProducer,
                             P.timeout_ns)) {
           lane_ok = false;
         } else {
@@ -983,7 +994,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t start = dev::global_timer_ns();
       while (dev::global_timer_ns() - start < 200000u) __nanosleep(1000);
     }
-  } else if (warp == 1) {
+  }
+  if (warp == 1) {
     // ---------------- MMA issuer (converged warp, elect.sync inside each MMA) ----------------
     const bool leader = lane == 0;
     const uint32_t tmem_u = dev::warp_uniform(tmem);
