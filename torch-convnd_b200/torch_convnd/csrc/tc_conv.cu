@@ -949,9 +949,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             lane_ok = false;
           } else {
             const int dst_slot = c == 0 ? slot : P.b_ring + slot;
-            dev::tma_load_5d(b_base + dst_slot * P.b_slot_bytes, &maps.grad[0], &a_full[a_stage], 0,
-                             bq2 * g.b[2], bq1 * g.b[1], P.q_lo + q0 - (new_entries - 1) + k,
-                             valid ? out_m : -1);
+#pragma unroll
+            for (int part = 0; part < kParts; ++part) {
+              dev::tma_load_5d(b_base + dst_slot * P.b_slot_bytes + part * P.b_part_bytes,
+                               &maps.grad[part], &a_full[a_stage], 0, bq2 * g.b[2],
+                               bq1 * g.b[1], P.q_lo + q0 - (new_entries - 1) + k,
+                               valid ? out_m : -1);
+            }
           }
         }
       } else if (lane < b_loads && lane_ok) {
@@ -1372,37 +1376,50 @@ bool plan_wgrad(const WgradPass& pass, int splits_hint, WgradPlan* plan) {
   const int64_t o1 = a1 >= 0 ? pass.out[a1] : 1;
   const int64_t o2 = pass.out[pass.rank - 1];
   const int mtpu = (k1 + P.tpm - 1) / P.tpm;
-  // Halo boxes cut the TMA operations per tap by k1 at the price of padding atoms; with
-  // one operand part that pays down to ~1/3 atom use (thin channels are bound by the count
-  // of small per-tap loads), with float32's three parts only above 60 %.
-  const double min_atom_use = parts == 1 ? 0.3 : 0.6;
-  const bool halo_ok = k1 >= 2 && s1 == 1 && d1 <= 16 &&
-                       static_cast<double>(k1) / (mtpu * P.tpm) >= min_atom_use;
   // Box axis 0 (third-to-last spatial axis): its three taps can be folded into N.
   const int a0 = pass.rank >= 3 ? pass.rank - 3 : -1;
   const int k0 = a0 >= 0 ? static_cast<int>(pass.k[a0]) : 1;
-  const bool fold_ok = halo_ok && k0 == 3 && a0 >= 0 && pass.s[a0] == 1 && pass.d[a0] == 1 &&
-                       parts == 1 && b_row_full <= 128 && 3 * pass.n_pad <= 256;
+  const bool foldable = k0 == 3 && a0 >= 0 && pass.s[a0] == 1 && pass.d[a0] == 1 &&
+                        b_row_full <= 128 && 3 * pass.n_pad <= 256;
+  // Halo boxes cut the TMA operations per tap by k1 at the price of padding atoms. That
+  // pays down to ~1/3 atom use with one operand part, or with the a0 fold (thin channels
+  // are bound by the count of small per-tap loads); float32's three unfolded parts need
+  // 60 %.
+  const double min_atom_use = parts == 1 || foldable ? 0.3 : 0.6;
+  const bool halo_ok = k1 >= 2 && s1 == 1 && d1 <= 16 &&
+                       static_cast<double>(k1) / (mtpu * P.tpm) >= min_atom_use;
+  const bool fold_ok = halo_ok && foldable;
   const int fold = fold_ok ? k0 : 0;
   bool planned = false;
   if (halo_ok) {
     // Position tile [1, b1, b2] with b2 a power of two >= 8 (8-row alignment of every
-    // tap window), least padding waste first. The longest K chunk that fits comes first:
-    // every A box then feeds more MMAs per barrier handoff and commit.
-    for (int kc : {256, 128, 64}) {
-      if (fold && kc > 128) continue;  // ring slots of 256 rows leave too few A stages
+    // tap window), least padding waste first. The longest K chunk that fits comes first
+    // (every A box then feeds more MMAs per barrier handoff, and its halo rows spread over
+    // more positions) unless a shorter one wastes over a third less: measured on B200,
+    // c4's 8-wide axes run best on 64-row tiles (half the padding of 128), c3's 12-wide
+    // axes on 128-row ones (a quarter more padding than 64 but half the halo bytes).
+    auto tile_waste = [&](int kc, int* b2_out) {
       double best_waste = 1e30;
-      int best_b2 = 0;
       for (int b2 = 8; b2 <= kc; b2 *= 2) {
         const int b1 = kc / b2;
         const double waste = double((o1 + b1 - 1) / b1 * b1) / o1 *
                              double((o2 + b2 - 1) / b2 * b2) / o2;
         if (waste < best_waste - 1e-9) {
           best_waste = waste;
-          best_b2 = b2;
+          *b2_out = b2;
         }
       }
-      const int b2 = best_b2;
+      return best_waste;
+    };
+    double least_waste = 1e30;
+    for (int kc : {256, 128, 64}) {
+      int b2 = 0;
+      if (!(fold && kc > 128)) least_waste = std::min(least_waste, tile_waste(kc, &b2));
+    }
+    for (int kc : {256, 128, 64}) {
+      if (fold && kc > 128) continue;  // ring slots of 256 rows leave too few A stages
+      int b2 = 0;
+      if (tile_waste(kc, &b2) > 1.35 * least_waste) continue;
       const int b1 = kc / b2;
       const int h1 = b1 + (mtpu * P.tpm - 1) * static_cast<int>(d1);
       if (h1 > 256) continue;
