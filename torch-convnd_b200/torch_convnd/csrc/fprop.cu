@@ -794,8 +794,11 @@ bool plan_fprop(const ConvPass& pass, FpropPlan* plan) {
     for (int b2 = 8; b2 <= 128; b2 *= 2) {
       if (128 % (e0 * b2) != 0) continue;
       const int b1 = 128 / (e0 * b2);
-      for (int mt = 1; mt <= 8; mt *= 2) {
+      for (int mt : {1, 2, 4, 6, 8, 12}) {
         if (fold && mt < 2) continue;
+        // 6 and 12 tiles per super tile (12-wide a0 axes without padding slices) are
+        // instantiated for the folded 16-bit kernels only.
+        if ((mt == 6 || mt == 12) && (!fold || tf32)) continue;
         for (int shift0 = 0; shift0 <= 1; ++shift0) {
           if (shift0 && (P.s[0] != 1 || P.k[0] == 1)) continue;
           if (fold && !shift0) continue;
@@ -1011,12 +1014,18 @@ int launch_fprop(const ConvPass& pass, const FpropPlan& plan_in, cudaStream_t st
   CND_FPROP_CASE(KIND, KSTEPS, 8)
 #define CND_FPROP_FOLDS(KIND, KSTEPS) \
   CND_FPROP_FOLD(KIND, KSTEPS, 2) CND_FPROP_FOLD(KIND, KSTEPS, 4) CND_FPROP_FOLD(KIND, KSTEPS, 8)
+#define CND_FPROP_FOLDS16(KIND, KSTEPS) \
+  CND_FPROP_FOLDS(KIND, KSTEPS) CND_FPROP_FOLD(KIND, KSTEPS, 6) CND_FPROP_FOLD(KIND, KSTEPS, 12)
 #define CND_FPROP_KS(KIND) CND_FPROP_MT(KIND, 1) CND_FPROP_MT(KIND, 2) CND_FPROP_MT(KIND, 4)
 #define CND_FPROP_KSF(KIND) CND_FPROP_FOLDS(KIND, 1) CND_FPROP_FOLDS(KIND, 2) CND_FPROP_FOLDS(KIND, 4)
+#define CND_FPROP_KSF16(KIND) \
+  CND_FPROP_FOLDS16(KIND, 1) CND_FPROP_FOLDS16(KIND, 2) CND_FPROP_FOLDS16(KIND, 4)
   CND_FPROP_KS(kKindF16) CND_FPROP_KS(kKindBF16) CND_FPROP_KS(kKindTF32) CND_FPROP_KS(kKind3xTF32)
-  CND_FPROP_KSF(kKindF16) CND_FPROP_KSF(kKindBF16) CND_FPROP_KSF(kKindTF32)
+  CND_FPROP_KSF16(kKindF16) CND_FPROP_KSF16(kKindBF16) CND_FPROP_KSF(kKindTF32)
   CND_FPROP_KSF(kKind3xTF32)
+#undef CND_FPROP_KSF16
 #undef CND_FPROP_KSF
+#undef CND_FPROP_FOLDS16
 #undef CND_FPROP_FOLDS
 #undef CND_FPROP_FOLD
 #undef CND_FPROP_KS
