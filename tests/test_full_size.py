@@ -78,6 +78,23 @@ def test_c2_plan_uses_the_folded_tma_store_path():
             assert "fold=1" in line and "tma_store=1" in line, line
 
 
+def test_six_tile_case_uses_six_tile_super_tiles():
+    """The small GPU parity case SIX_TILE_CASE plans 6-tile folded super tiles for its
+    forward and dgrad (as c3's forward does), so the GPU test checks those kernels."""
+    from types import SimpleNamespace
+
+    from test_gpu_parity import SIX_TILE_CASE
+
+    rank, batch, cin, cout, spatial, kernel, stride, padding, dilation, groups = SIX_TILE_CASE
+    cfg = SimpleNamespace(rank=rank, batch=batch, in_channels=cin, out_channels=cout,
+                          spatial=spatial, kernel=kernel, stride=stride, padding=padding,
+                          dilation=dilation, groups=groups, dtype=torch.bfloat16)
+    summary = _plan_summary(cfg)
+    for line in summary.splitlines():
+        if line.startswith(("forward", "dgrad")):
+            assert "x6 " in line and "fold=1" in line, line
+
+
 def test_thin_grouped_layer_runs_dense():
     """c5's grouped layer (4 groups of 8 channels) runs as one dense problem with
     block-diagonal weights; its full-size case below checks that plan."""

@@ -141,6 +141,29 @@ def test_geometry_sweep_against_oracle(case, dtype):
     assert_matches(db, db_ref, dtype, "db")
 
 
+# 12 slices along box axis 0 and enough work per slice for 6-tile folded super tiles
+# (the c3 forward plan); tests/test_full_size.py pins that plan on the CPU.
+SIX_TILE_CASE = (4, 4, 16, 32, (10, 12, 12, 12), (3,) * 4, (1,) * 4, (1,) * 4, (1,) * 4, 1)
+
+
+def test_six_tile_folded_super_tiles_match_oracle():
+    rank, batch, cin, cout, spatial, kernel, stride, padding, dilation, groups = SIX_TILE_CASE
+    generator = torch.Generator().manual_seed(66)
+    x = torch.randn((batch, cin, *spatial), generator=generator).bfloat16()
+    w = (torch.randn((cout, cin, *kernel), generator=generator) * 0.1).bfloat16()
+    b = torch.randn(cout, generator=generator).bfloat16()
+    y_ref = oracle.forward(x, w, b, stride, padding, dilation, groups)
+    dy = torch.randn(y_ref.shape, generator=generator).bfloat16()
+    dx_ref, dw_ref, db_ref = oracle.backward(dy, x, w, stride, padding, dilation, groups)
+    y, dx, dw, db = _run(x.cuda(), w.cuda(), b.cuda(), dy.cuda(), stride, padding, dilation,
+                         groups)
+    torch.cuda.synchronize()
+    torch_convnd.device_status()
+    for got, ref, what in ((y, y_ref, "y"), (dx, dx_ref, "dx"), (dw, dw_ref, "dw"),
+                           (db, db_ref, "db")):
+        assert_matches(got, ref, torch.bfloat16, what)
+
+
 @pytest.mark.parametrize("rank", [4, 5, 6, 7, 8])
 def test_float64_ranks_match_tap_reference(rank):
     """Reference tests/test_convnd.py:98-116 on the generic CUDA-core kernels."""

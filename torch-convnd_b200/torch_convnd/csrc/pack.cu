@@ -293,6 +293,9 @@ __global__ void wgrad_reduce_kernel(const float* __restrict__ partial, int split
     const int t = static_cast<int>(r % taps);
     const int g = static_cast<int>(r / taps);
     float sum = 0.0f;
+    // unrolled so the loads of several splits are in flight at once; the sum keeps
+    // split order
+#pragma unroll 8
     for (int s = 0; s < splits; ++s) sum += partial[s * total + p];
     dw[((static_cast<int64_t>(g) * cout_g + co) * cin_g + ci) * taps + t] = from_float<T>(sum);
   }
