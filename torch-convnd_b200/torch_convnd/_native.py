@@ -87,9 +87,12 @@ def core() -> ctypes.CDLL:
 def set_fp32_precision(mode: str) -> str:
     """Choose how float32 convolutions use the tensor cores; returns the previous mode.
 
-    ``"3xtf32"`` (default): three TF32 products per multiply-add recover about fp32
-    accuracy. ``"tf32"``: one TF32 product (the reference's bmm under
-    ``allow_tf32=True``). ``"ieee"``: exact fp32 on the CUDA cores.
+    ``"3xtf32"`` (default): error-compensated split products well inside fp32's
+    tolerance — three TF32 products (big/small parts) per multiply-add, or, where it
+    halves the MMAs (input-gradient passes over 16 or more gradient channels), three
+    products of bfloat16 hi/lo parts; the weight gradient always uses bfloat16 hi/lo
+    parts. ``"tf32"``: one TF32 product for the forward and input gradient (the
+    reference's bmm under ``allow_tf32=True``). ``"ieee"``: exact fp32 on the CUDA cores.
     """
     if mode not in FP32_MODES:
         raise ValueError(f"Invalid fp32 precision {mode!r}; expected one of {sorted(FP32_MODES)}")

@@ -155,6 +155,10 @@ struct Plan {
   int64_t cin_g = 0, cout_g = 0;
   int64_t x_pad = 0, dy_pad = 0;
   bool fast_fwd = false, fast_dgrad = false, fast_wgrad = false;
+  // float32 dgrad on bfloat16 hi + lo operand parts (three kind::f16 products) instead
+  // of 3xTF32, when that halves the K steps (dy channels a multiple of 16). Its packed dy
+  // is the weight gradient's (wg_dy).
+  bool dgrad_bf16 = false;
   ConvPass fwd{}, dgrad{};
   FpropPlan fwd_plan{}, dgrad_plan{};
   WgradPass wgrad{};
@@ -276,8 +280,24 @@ void make_plan(const cnd_problem& p, bool forward, const int32_t* mask, Plan* pl
     dg.op = plan->op;
     dg.split3 = plan->split3;
     dg.out_dtype = p.dtype;
-    plan->fast_dgrad =
-        !strided && !wide_pad && plan->cin_g <= 256 && plan_fprop(dg, &plan->dgrad_plan);
+    const bool dgrad_ok = !strided && !wide_pad && plan->cin_g <= 256;
+    // One bf16 K step covers 16 dy channels, one TF32 step 8: the bf16 parts win when
+    // they need fewer K steps (dy channels >= 16); below that they would only lose
+    // precision.
+    const int64_t bf16_pad = pad_channels(kOpBF16, plan->cout_g, 16);
+    if (dgrad_ok && plan->split3 && bf16_pad / 16 < plan->dy_pad / 8) {
+      ConvPass bf = dg;
+      bf.op = kOpBF16;
+      bf.c_pad = static_cast<int>(bf16_pad);
+      if (plan_fprop(bf, &plan->dgrad_plan)) {
+        dg = bf;
+        plan->dgrad_bf16 = true;
+        plan->fast_dgrad = true;
+      }
+    }
+    if (!plan->dgrad_bf16) {
+      plan->fast_dgrad = dgrad_ok && plan_fprop(dg, &plan->dgrad_plan);
+    }
   }
   const bool f32 = p.dtype == CND_F32;
   plan->wg_op = f32 ? kOpBF16 : plan->op;
@@ -304,7 +324,7 @@ void make_plan(const cnd_problem& p, bool forward, const int32_t* mask, Plan* pl
     if (plan->fast_wgrad) wg.splits = plan_wgrad_splits(wg, 0);
     if (wg.splits <= 0) plan->fast_wgrad = false;
   }
-  const bool need_dy = plan->fast_dgrad || (plan->fast_wgrad && !f32);
+  const bool need_dy = (plan->fast_dgrad && !plan->dgrad_bf16) || (plan->fast_wgrad && !f32);
   if (need_dy) {
     const size_t bytes =
         static_cast<size_t>(p.batch * plan->groups * p.output_volume) * plan->dy_pad * es;
@@ -328,13 +348,14 @@ void make_plan(const cnd_problem& p, bool forward, const int32_t* mask, Plan* pl
     const size_t act =
         static_cast<size_t>(p.batch * plan->groups * p.input_volume) * plan->wg_x_pad * wes;
     for (int part = 0; part < plan->wg_parts; ++part) plan->wg_x[part] = take(&cursor, act);
-    if (f32) {
-      const size_t grad =
-          static_cast<size_t>(p.batch * plan->groups * p.output_volume) * plan->wg_dy_pad * wes;
-      for (int part = 0; part < plan->wg_parts; ++part) plan->wg_dy[part] = take(&cursor, grad);
-    }
     plan->partial = take(&cursor, static_cast<size_t>(plan->wgrad.splits) * plan->groups * taps *
                                       plan->cin_g * plan->cout_g * sizeof(float));
+  }
+  if (f32 && (plan->fast_wgrad || plan->dgrad_bf16)) {
+    // dy as bfloat16 hi + lo parts, read by the weight gradient and a bf16-part dgrad
+    const size_t grad =
+        static_cast<size_t>(p.batch * plan->groups * p.output_volume) * plan->wg_dy_pad * 2;
+    for (int part = 0; part < 2; ++part) plan->wg_dy[part] = take(&cursor, grad);
   }
   plan->total = cursor;
 }
@@ -596,6 +617,28 @@ int cnd_backward(const cnd_problem* problem, const void* dy, const void* x, cons
     rc = pack_activations(pa, stream);
     if (rc != CND_OK) return rc;
   }
+  if (plan.wg_dy[0].bytes > 0) {
+    // float32 dy as bfloat16 hi + lo parts (weight gradient, bf16-part dgrad)
+    PackActArgs pa{};
+    pa.src = dy;
+    pa.dst = at(workspace, plan.wg_dy[0]);
+    pa.dst_small = at(workspace, plan.wg_dy[1]);
+    pa.batch = p.batch;
+    pa.groups = plan.groups;
+    pa.spatial = p.output_volume;
+    pa.cg = static_cast<int>(plan.cout_g);
+    pa.c_pad = static_cast<int>(plan.wg_dy_pad);
+    pa.dtype = p.dtype;
+    pa.mode = plan.wg_mode;
+    if (output_mask[2] && !bias_from_pack) {
+      pa.chan_partial = bias_partial;
+      bias_from_pack = true;
+      blocks = static_cast<int>(pack_blocks(pa));
+    }
+    TimedPass timed(4, stream);
+    rc = pack_activations(pa, stream);
+    if (rc != CND_OK) return rc;
+  }
   // ---- weight gradient ----
   if (output_mask[1]) {
     if (plan.fast_wgrad) {
@@ -618,26 +661,6 @@ int cnd_backward(const cnd_problem* problem, const void* dy, const void* x, cons
         if (rc != CND_OK) return rc;
       }
       if (f32) {
-        PackActArgs pa{};
-        pa.src = dy;
-        pa.dst = at(workspace, plan.wg_dy[0]);
-        pa.dst_small = at(workspace, plan.wg_dy[1]);
-        pa.dst_third = at(workspace, plan.wg_dy[2]);
-        pa.batch = p.batch;
-        pa.groups = plan.groups;
-        pa.spatial = p.output_volume;
-        pa.cg = static_cast<int>(plan.cout_g);
-        pa.c_pad = static_cast<int>(plan.wg_dy_pad);
-        pa.dtype = p.dtype;
-        pa.mode = plan.wg_mode;
-        if (output_mask[2] && !bias_from_pack) {
-          pa.chan_partial = bias_partial;
-          bias_from_pack = true;
-          blocks = static_cast<int>(pack_blocks(pa));
-        }
-        TimedPass timed(4, stream);
-        rc = pack_activations(pa, stream);
-        if (rc != CND_OK) return rc;
         for (int part = 0; part < 3; ++part) wg.grad[part] = at(workspace, plan.wg_dy[part]);
       } else {
         wg.grad[0] = at(workspace, plan.dy_cl);
@@ -676,7 +699,7 @@ int cnd_backward(const cnd_problem* problem, const void* dy, const void* x, cons
       pw.n_pad = plan.dgrad.n_pad;
       pw.c_pad = plan.dgrad.c_pad;
       pw.dtype = p.dtype;
-      pw.mode = plan.pack_mode;
+      pw.mode = plan.dgrad_bf16 ? 4 : plan.pack_mode;
       pw.dgrad = 1;
       pw.shift0 = plan.dgrad_plan.shift0;
       pw.shift1 = plan.dgrad_plan.shift1;
@@ -688,8 +711,8 @@ int cnd_backward(const cnd_problem* problem, const void* dy, const void* x, cons
       }
       if (rc != CND_OK) return rc;
       ConvPass pass = plan.dgrad;
-      pass.act = at(workspace, plan.dy_cl);
-      pass.act_small = at(workspace, plan.dy_cl_small);
+      pass.act = at(workspace, plan.dgrad_bf16 ? plan.wg_dy[0] : plan.dy_cl);
+      pass.act_small = at(workspace, plan.dgrad_bf16 ? plan.wg_dy[1] : plan.dy_cl_small);
       pass.wt = pw.dst;
       pass.wt_small = pw.dst_small;
       pass.dst = dx;

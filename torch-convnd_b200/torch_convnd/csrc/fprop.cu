@@ -96,8 +96,10 @@ __device__ __forceinline__ void mma(uint32_t d, uint64_t a, uint64_t b, uint32_t
 }
 
 // Operand kinds of the kernel instantiations: the element type of activations, weights
-// and output, and whether float32 runs as one or three TF32 products.
-enum KernelOp { kKindF16 = 0, kKindBF16 = 1, kKindTF32 = 2, kKind3xTF32 = 3 };
+// and output, and whether float32 runs as one or three TF32 products, or as three
+// products of bfloat16 hi / lo parts (kind::f16, about 16 significant bits per operand;
+// one K = 16 MMA covers what takes two K = 8 TF32 MMAs).
+enum KernelOp { kKindF16 = 0, kKindBF16 = 1, kKindTF32 = 2, kKind3xTF32 = 3, kKind2xBF16 = 4 };
 
 template <int kOp>
 struct OpTraits;
@@ -129,6 +131,14 @@ template <>
 struct OpTraits<kKind3xTF32> {
   using Out = float;
   static constexpr bool tf32 = true;
+  static constexpr int parts = 2;
+  static __device__ __forceinline__ Out cast(float v) { return v; }
+  static __device__ __forceinline__ float load(const Out* p) { return __ldg(p); }
+};
+template <>
+struct OpTraits<kKind2xBF16> {
+  using Out = float;
+  static constexpr bool tf32 = false;
   static constexpr int parts = 2;
   static __device__ __forceinline__ Out cast(float v) { return v; }
   static __device__ __forceinline__ float load(const Out* p) { return __ldg(p); }
@@ -396,9 +406,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                   const uint64_t ad = desc_hi | (a_addr + 2u * kk);
                   const uint64_t bd = desc_hi | (b_addr + 2u * kk);
                   if constexpr (kParts == 2) {
-                    mma<true>(d, desc_hi | (a_addr + a_small_units + 2u * kk), bd, idesc, 1u);
-                    mma<true>(d, ad, desc_hi | (b_addr + b_small_units + 2u * kk), idesc, 1u);
-                    mma<true>(d, ad, bd, idesc, 1u);
+                    mma<kTF32>(d, desc_hi | (a_addr + a_small_units + 2u * kk), bd, idesc, 1u);
+                    mma<kTF32>(d, ad, desc_hi | (b_addr + b_small_units + 2u * kk), idesc, 1u);
+                    mma<kTF32>(d, ad, bd, idesc, 1u);
                   } else {
                     mma<kTF32>(d, ad, bd, idesc, 1u);
                   }
@@ -432,9 +442,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const uint64_t bd = desc_hi | (b_tap + 2u * kk);
                 const uint32_t acc = (first != 0u && kk == 0) ? 0u : 1u;
                 if constexpr (kParts == 2) {
-                  mma<true>(d, desc_hi | (a_addr + a_small_units + 2u * kk), bd, P.idesc, acc);
-                  mma<true>(d, ad, desc_hi | (b_tap + b_small_units + 2u * kk), P.idesc, 1u);
-                  mma<true>(d, ad, bd, P.idesc, 1u);
+                  mma<kTF32>(d, desc_hi | (a_addr + a_small_units + 2u * kk), bd, P.idesc, acc);
+                  mma<kTF32>(d, ad, desc_hi | (b_tap + b_small_units + 2u * kk), P.idesc, 1u);
+                  mma<kTF32>(d, ad, bd, P.idesc, 1u);
                 } else {
                   mma<kTF32>(d, ad, bd, P.idesc, acc);
                 }
@@ -765,8 +775,10 @@ bool plan_fprop(const ConvPass& pass, FpropPlan* plan) {
   if (row_max == 0) return false;
   if (!fill_geometry(pass, &P)) return false;
   const bool tf32 = pass.op == kOpF32;
-  const int parts = (tf32 && pass.split3) ? 2 : 1;
+  // split3: float32 operands as two parts (TF32 big + small, or bf16 hi + lo)
+  const int parts = pass.split3 ? 2 : 1;
   const int es = elem_size(pass.op);
+  const int out_es = pass.out_dtype == CND_F32 ? 4 : 2;  // the output's element size
   P.n_pad = pass.n_pad;
   P.n_real = pass.n_real;
   const int products = parts == 2 ? 3 : 1;
@@ -798,7 +810,7 @@ bool plan_fprop(const ConvPass& pass, FpropPlan* plan) {
         if (fold && mt < 2) continue;
         // 6 and 12 tiles per super tile (12-wide a0 axes without padding slices) are
         // instantiated for the folded 16-bit kernels only.
-        if ((mt == 6 || mt == 12) && (!fold || tf32)) continue;
+        if ((mt == 6 || mt == 12) && (!fold || parts > 1)) continue;
         for (int shift0 = 0; shift0 <= 1; ++shift0) {
           if (shift0 && (P.s[0] != 1 || P.k[0] == 1)) continue;
           if (fold && !shift0) continue;
@@ -808,7 +820,7 @@ bool plan_fprop(const ConvPass& pass, FpropPlan* plan) {
             const Candidate cand{e0, b1, b2, mt, shift0, shift1, row_bytes, fold};
             if (!layout_candidate(pass, &trial, cand, parts)) continue;
             int nacc = 1;
-            if (tf32) {
+            if (parts > 1 || tf32) {
               nacc = 8;
               while (nacc > 1 && 2 * nacc * mt * pass.n_pad > 512) nacc /= 2;
             }
@@ -878,9 +890,9 @@ bool plan_fprop(const ConvPass& pass, FpropPlan* plan) {
   // staging buffers fit beside at least two stages, without giving up two CTAs per SM.
   const size_t extra = 1024 + (2 * 8 + 4) * 8 + 64;
   P.tma_store = 0;
-  P.out_tile_bytes = round_up(static_cast<uint32_t>(pass.n_real * 128 * es), 1024);
-  const bool store_shape = (static_cast<int64_t>(P.out[2]) * es) % 16 == 0 &&
-                           (P.b2 * es) % 16 == 0 && pass.n_real <= 256 &&
+  P.out_tile_bytes = round_up(static_cast<uint32_t>(pass.n_real * 128 * out_es), 1024);
+  const bool store_shape = (static_cast<int64_t>(P.out[2]) * out_es) % 16 == 0 &&
+                           (P.b2 * out_es) % 16 == 0 && pass.n_real <= 256 &&
                            pass.batch * pass.groups * pass.n_real <= kInt32Max &&
                            P.out_outer_vol <= kInt32Max;
   if (store_shape) {
@@ -970,7 +982,13 @@ int launch_fprop(const ConvPass& pass, const FpropPlan& plan_in, cudaStream_t st
     }
   }
   if (P.tma_store) {
-    const cuuint64_t e = static_cast<cuuint64_t>(es);
+    // the output's own element type (float32 problems may run bf16-part operands)
+    const cuuint64_t e = pass.out_dtype == CND_F32 ? 4u : 2u;
+    const CUtensorMapDataType out_type = pass.out_dtype == CND_F32
+                                             ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                             : (pass.out_dtype == CND_BF16
+                                                    ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                    : CU_TENSOR_MAP_DATA_TYPE_FLOAT16);
     cuuint64_t odims[5] = {static_cast<cuuint64_t>(P.out[2]), static_cast<cuuint64_t>(P.out[1]),
                            static_cast<cuuint64_t>(P.out[0]),
                            static_cast<cuuint64_t>(P.out_outer_vol),
@@ -982,7 +1000,7 @@ int launch_fprop(const ConvPass& pass, const FpropPlan& plan_in, cudaStream_t st
     cuuint32_t obox[5] = {static_cast<cuuint32_t>(P.b2), static_cast<cuuint32_t>(P.b1),
                           static_cast<cuuint32_t>(P.e0), 1, static_cast<cuuint32_t>(pass.n_real)};
     cuuint32_t oestr[5] = {1, 1, 1, 1, 1};
-    const CUresult r = encode(&maps.out, map_dtype(pass.op), 5, pass.dst, odims, ostrides, obox,
+    const CUresult r = encode(&maps.out, out_type, 5, pass.dst, odims, ostrides, obox,
                               oestr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
                               CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) {
@@ -1001,7 +1019,7 @@ int launch_fprop(const ConvPass& pass, const FpropPlan& plan_in, cudaStream_t st
   using Kernel = void (*)(FpropMaps, FpropParams);
   Kernel kernel = nullptr;
   const int kind = pass.op == kOpF16 ? kKindF16
-                   : pass.op == kOpBF16 ? kKindBF16
+                   : pass.op == kOpBF16 ? (plan.parts == 2 ? kKind2xBF16 : kKindBF16)
                    : (plan.parts == 2 ? kKind3xTF32 : kKindTF32);
 #define CND_FPROP_CASE(KIND, KSTEPS, MT)                                                 \
   if (kind == KIND && P.ksteps == KSTEPS && P.mt == MT && !P.fold)                        \
@@ -1021,8 +1039,9 @@ int launch_fprop(const ConvPass& pass, const FpropPlan& plan_in, cudaStream_t st
 #define CND_FPROP_KSF16(KIND) \
   CND_FPROP_FOLDS16(KIND, 1) CND_FPROP_FOLDS16(KIND, 2) CND_FPROP_FOLDS16(KIND, 4)
   CND_FPROP_KS(kKindF16) CND_FPROP_KS(kKindBF16) CND_FPROP_KS(kKindTF32) CND_FPROP_KS(kKind3xTF32)
+  CND_FPROP_KS(kKind2xBF16)
   CND_FPROP_KSF16(kKindF16) CND_FPROP_KSF16(kKindBF16) CND_FPROP_KSF(kKindTF32)
-  CND_FPROP_KSF(kKind3xTF32)
+  CND_FPROP_KSF(kKind3xTF32) CND_FPROP_KSF(kKind2xBF16)
 #undef CND_FPROP_KSF16
 #undef CND_FPROP_KSF
 #undef CND_FPROP_FOLDS16

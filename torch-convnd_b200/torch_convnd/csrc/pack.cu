@@ -231,9 +231,9 @@ __global__ void __launch_bounds__(32 * kFastWarps)
   }
 }
 
-template <typename T, int kMode>
-__global__ void pack_weight_kernel(const T* __restrict__ w, T* __restrict__ dst,
-                                   T* __restrict__ dst_small, PackWeightArgs a) {
+template <typename T, typename Tout, int kMode>
+__global__ void pack_weight_kernel(const T* __restrict__ w, Tout* __restrict__ dst,
+                                   Tout* __restrict__ dst_small, PackWeightArgs a) {
   const int64_t total = static_cast<int64_t>(a.groups) * a.taps * a.n_pad * a.c_pad;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -264,15 +264,7 @@ __global__ void pack_weight_kernel(const T* __restrict__ w, T* __restrict__ dst,
                        (a.taps - 1 - t)]);
       }
     }
-    if constexpr (kMode == 1) {
-      const float big = tf32_round(v);
-      dst[i] = from_float<T>(big);
-      dst_small[i] = from_float<T>(tf32_round(v - big));
-    } else if constexpr (kMode == 2) {
-      dst[i] = from_float<T>(tf32_round(v));
-    } else {
-      dst[i] = from_float<T>(v);
-    }
+    split_value<Tout, kMode>(v, dst, dst_small, nullptr, i);
   }
 }
 
@@ -387,11 +379,15 @@ int pack_weight_typed(const PackWeightArgs& a, cudaStream_t stream) {
   T* dst = static_cast<T*>(a.dst);
   T* dst_small = static_cast<T*>(a.dst_small);
   if (a.mode == 1) {
-    pack_weight_kernel<T, 1><<<blocks, 256, 0, stream>>>(w, dst, dst_small, a);
+    pack_weight_kernel<T, T, 1><<<blocks, 256, 0, stream>>>(w, dst, dst_small, a);
   } else if (a.mode == 2) {
-    pack_weight_kernel<T, 2><<<blocks, 256, 0, stream>>>(w, dst, dst_small, a);
+    pack_weight_kernel<T, T, 2><<<blocks, 256, 0, stream>>>(w, dst, dst_small, a);
+  } else if (a.mode == 4) {
+    // float32 weights as bfloat16 hi + lo parts
+    pack_weight_kernel<T, __nv_bfloat16, 4><<<blocks, 256, 0, stream>>>(
+        w, static_cast<__nv_bfloat16*>(a.dst), static_cast<__nv_bfloat16*>(a.dst_small), a);
   } else {
-    pack_weight_kernel<T, 0><<<blocks, 256, 0, stream>>>(w, dst, dst_small, a);
+    pack_weight_kernel<T, T, 0><<<blocks, 256, 0, stream>>>(w, dst, dst_small, a);
   }
   count_launch();
   return CND_OK;

@@ -19,7 +19,8 @@ struct PackActArgs {
   float* chan_partial;  // optional [batch][groups][pack_blocks(spatial)][cg]
 };
 
-// Weights [groups*cout_g][cin_g][taps] -> [groups][taps][n_pad][c_pad], rows in the
+// Weights [groups*cout_g][cin_g][taps] -> [groups][taps][n_pad][c_pad] (mode as for
+// activations; mode 4 writes float32 weights as bfloat16 hi + lo parts), rows in the
 // convolution pass's load-unit order (k_box = kernel extents of the three box axes,
 // shift0/shift1 = whether the a0 / a1 taps of a unit are served by shared-memory shifts).
 struct PackWeightArgs {
