@@ -1393,14 +1393,17 @@ bool plan_wgrad(const WgradPass& pass, int splits_hint, WgradPlan* plan) {
   bool planned = false;
   if (halo_ok) {
     // Position tile [1, b1, b2] with b2 a power of two >= 8 (8-row alignment of every
-    // tap window), least padding waste first. The longest K chunk that fits comes first
-    // (every A box then feeds more MMAs per barrier handoff, and its halo rows spread over
-    // more positions) unless a shorter one wastes over a third less: measured on B200,
-    // c4's 8-wide axes run best on 64-row tiles (half the padding of 128), c3's 12-wide
-    // axes on 128-row ones (a quarter more padding than 64 but half the halo bytes).
+    // tap window; the K chunk b1 * b2 itself need not be a power of two), least padding
+    // waste first. Among K chunks within 30 % of the least waste, the longest that fits
+    // comes first (every A box then feeds more MMAs per barrier handoff), skipping tiles
+    // with more halo rows than rows of their own. Measured on B200: c4's 8-wide axes run
+    // best on 64-row tiles [1, 8, 8], c3's 12-wide axes on 192-row tiles [1, 12, 16]
+    // (128 rows pad them 1.78x, 64 rows [1, 4, 16] carry 7 halo rows per 4).
+    const int halo_extra = (mtpu * P.tpm - 1) * static_cast<int>(d1);
     auto tile_waste = [&](int kc, int* b2_out) {
       double best_waste = 1e30;
       for (int b2 = 8; b2 <= kc; b2 *= 2) {
+        if (kc % b2 != 0) continue;
         const int b1 = kc / b2;
         const double waste = double((o1 + b1 - 1) / b1 * b1) / o1 *
                              double((o2 + b2 - 1) / b2 * b2) / o2;
@@ -1411,17 +1414,29 @@ bool plan_wgrad(const WgradPass& pass, int splits_hint, WgradPlan* plan) {
       }
       return best_waste;
     };
+    constexpr int kChunks[] = {256, 192, 128, 64};
+    auto preferred = [&](int kc) {
+      int b2 = 0;
+      tile_waste(kc, &b2);
+      return b2 > 0 && halo_extra <= kc / b2;
+    };
     double least_waste = 1e30;
-    for (int kc : {256, 128, 64}) {
+    for (int kc : kChunks) {
       int b2 = 0;
-      if (!(fold && kc > 128)) least_waste = std::min(least_waste, tile_waste(kc, &b2));
+      if (!(fold && kc > 192) && preferred(kc)) {
+        least_waste = std::min(least_waste, tile_waste(kc, &b2));
+      }
     }
-    for (int kc : {256, 128, 64}) {
-      if (fold && kc > 128) continue;  // ring slots of 256 rows leave too few A stages
+    // First the preferred chunks, then (if none fits) any chunk, longest first.
+    for (int round = 0; round < 2 && !planned; ++round)
+    for (int kc : kChunks) {
+      if (fold && kc > 192) continue;  // ring slots of 256 rows leave too few A stages
       int b2 = 0;
-      if (tile_waste(kc, &b2) > 1.35 * least_waste) continue;
+      const double waste = tile_waste(kc, &b2);
+      if (b2 == 0) continue;
+      if (round == 0 && (!preferred(kc) || waste > 1.3 * least_waste)) continue;
       const int b1 = kc / b2;
-      const int h1 = b1 + (mtpu * P.tpm - 1) * static_cast<int>(d1);
+      const int h1 = b1 + halo_extra;
       if (h1 > 256) continue;
       const uint32_t rows = static_cast<uint32_t>(h1 * b2);
       const uint32_t a_part = round_up(rows * a_row, 1024);
@@ -1676,9 +1691,10 @@ int launch_wgrad_pass(const WgradPass& pass, cudaStream_t stream, uint64_t timeo
   Kernel kernel = nullptr;
 #define CND_WGRAD_PICK(PARTS)                                                         \
   if (P.halo) {                                                                      \
-    kernel = P.ksteps == 16  ? wgrad_halo_kernel<PARTS, 16>                          \
-             : P.ksteps == 8 ? wgrad_halo_kernel<PARTS, 8>                           \
-                             : wgrad_halo_kernel<PARTS, 4>;                          \
+    kernel = P.ksteps == 16   ? wgrad_halo_kernel<PARTS, 16>                         \
+             : P.ksteps == 12 ? wgrad_halo_kernel<PARTS, 12>                         \
+             : P.ksteps == 8  ? wgrad_halo_kernel<PARTS, 8>                          \
+                              : wgrad_halo_kernel<PARTS, 4>;                         \
   } else {                                                                           \
     kernel = P.ksteps == 16  ? wgrad_kernel<PARTS, 16>                               \
              : P.ksteps == 8 ? wgrad_kernel<PARTS, 8>                                \
@@ -1692,7 +1708,7 @@ int launch_wgrad_pass(const WgradPass& pass, cudaStream_t stream, uint64_t timeo
     CND_WGRAD_PICK(1)
   }
 #undef CND_WGRAD_PICK
-  if (P.ksteps != 16 && P.ksteps != 8 && P.ksteps != 4) {
+  if (P.ksteps != 16 && P.ksteps != 8 && P.ksteps != 4 && !(P.halo && P.ksteps == 12)) {
     return fail(CND_ERR_UNSUPPORTED, "weight-gradient K chunk outside the tcgen05 path");
   }
   cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
