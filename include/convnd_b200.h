@@ -59,10 +59,15 @@ typedef enum cnd_dtype {
 } cnd_dtype;
 
 /* How float32 problems use the tensor cores.
- *   CND_FP32_3XTF32: each fp32 operand is split into a TF32 "big" part and a TF32
- *                    remainder; three kind::tf32 MMAs recover ~fp32 accuracy (default).
- *   CND_FP32_TF32:   one kind::tf32 MMA per product (what cuBLAS does under
- *                    allow_tf32=True in the reference's bmm calls, convnd.cpp:334).
+ *   CND_FP32_3XTF32: error-compensated split products (default): each fp32 operand is
+ *                    split into a TF32 "big" part and a TF32 remainder and three
+ *                    kind::tf32 MMAs form each product; input-gradient passes over 16
+ *                    or more gradient channels, and every weight gradient, split into
+ *                    bfloat16 hi + lo parts instead (three kind::f16 MMAs, ~16
+ *                    significant bits per operand, inside fp32's rtol 1e-3 bar).
+ *   CND_FP32_TF32:   one kind::tf32 MMA per forward / input-gradient product (what
+ *                    cuBLAS does under allow_tf32=True in the reference's bmm calls,
+ *                    convnd.cpp:334); weight gradients as above.
  *   CND_FP32_SIMT:   exact fp32 CUDA-core path (no tensor cores). */
 typedef enum cnd_fp32_mode {
   CND_FP32_3XTF32 = 0,
