@@ -204,7 +204,8 @@ __device__ __forceinline__ void cursor_box(const BoxGeom& g, const BoxCursor& c,
 }
 
 // ---------------------------------------------------------------------------------------
-// Weight-gradient kernel. Grid (split, tap chunk, group). Each CTA accumulates
+// Weight-gradient kernel for per-tap plans (each tap tile its own TMA box; halo plans run
+// wgrad_halo_kernel below). Grid (split, tap chunk, group). Each CTA accumulates
 // mt_per_cta tiles of 128 (tap, channel) rows x n_pad output channels in TMEM over its
 // range of position tiles, then writes one fp32 partial.
 //
@@ -444,16 +445,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t a_phase = 0, b_phase = 0;
     bool ok = true;
     BoxCursor cursor;
-    if (P.nfold) {
-      cursor_init_q0(g, p_begin * g.nb, cursor);
-    } else {
-      cursor_init(g, p_begin * g.nb, cursor);
-    }
-    // Folded dY ring: slot and phase of the next entry, and the current tile's slice
-    // index q0 (kept incrementally: no 64-bit divisions in the loop).
-    int ring_slot = 0;
-    uint32_t ring_phase = 0;
-    int q0 = P.nfold ? static_cast<int>(p_begin % g.nbox[0]) : 0;
+    cursor_init(g, p_begin * g.nb, cursor);
     const int b_loads = g.nb * P.b_blocks * kParts;
     const int a_loads = P.entries_per_unit * g.nb * kParts;
     for (int64_t pt = p_begin; pt < p_end && ok; ++pt) {
@@ -479,33 +471,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             box_mask[j] = mask;
           }
-          if (P.nfold) {
-            cursor_next_q0(g, cursor);
-          } else {
-            cursor_next(g, cursor);
-          }
+          cursor_next(g, cursor);
         }
       }
       __syncwarp();
       // All TMA loads of the tile form one pool of jobs spread over the lanes: the dY
-      // loads first (folded: the new ring entries, a mirror copy for the first slots),
-      // then every unit's activation loads. Each lane waits on the barrier of its own
-      // job's slot; the first load of a slot posts the slot's expected bytes (a load may
-      // complete before that: the phase cannot finish without the posting arrival).
-      const bool run_start = P.nfold && (pt == p_begin || q0 == 0);
-      const int new_entries = P.nfold ? (run_start ? P.nfold : 1) : 0;
-      int b_jobs;
-      if (P.nfold) {
-        // entries k = 0.. hold slices q0 - new_entries + 1 + k; slots from ring_slot on
-        b_jobs = 0;
-        for (int k = 0; k < new_entries; ++k) {
-          int slot = ring_slot + k;
-          if (slot >= P.b_ring) slot -= P.b_ring;
-          b_jobs += slot < P.nfold - 1 ? 2 : 1;
-        }
-      } else {
-        b_jobs = b_loads;
-      }
+      // loads first, then every unit's activation loads. Each lane waits on the barrier of
+      // its own job's slot; the first load of a slot posts the slot's expected bytes (a
+      // load may complete before that: the phase cannot finish without the posting
+      // arrival).
       // Rounds of jobs: each A stage appears at most once per round. Lanes of a round
       // wait concurrently, and an mbarrier parity wait is exact only for the phase right
       // after the last one known complete; a second use of a stage inside a round could
@@ -516,57 +490,25 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int round_units = unit_count - round_first < P.a_stages
                                     ? unit_count - round_first
                                     : P.a_stages;
-        const int round_b = round_first == 0 ? b_jobs : 0;
+        const int round_b = round_first == 0 ? b_loads : 0;
         const int jobs = round_b + round_units * a_loads;
         for (int l = lane; l < jobs && lane_ok; l += 32) {
           if (l < round_b) {
-            if (P.nfold) {
-              // find entry k and copy c of job l
-              int k = 0, c = 0, rest = l, slot = ring_slot;
-              uint32_t par = ring_phase;
-              for (;;) {
-                const int copies = slot < P.nfold - 1 ? 2 : 1;
-                if (rest < copies) {
-                  c = rest;
-                  break;
-                }
-                rest -= copies;
-                ++k;
-                if (++slot == P.b_ring) {
-                  slot = 0;
-                  par ^= 1u;
-                }
-              }
-              if (!dev::mbar_wait(&b_empty[slot], par ^ 1u, err, kSiteWProducer, P.timeout_ns)) {
-                lane_ok = false;
-                break;
-              }
-              const bool mirror = slot < P.nfold - 1;
-              if (c == 0) dev::mbar_arrive_expect_tx(&b_full[slot], P.b_tx * (mirror ? 2u : 1u));
-              const int32_t mo =
-                  boxes[0].valid ? static_cast<int32_t>(boxes[0].out_merged) : -1;
-              const int dst_slot = c == 0 ? slot : P.b_ring + slot;
-              dev::tma_load_5d(b_base + dst_slot * P.b_slot_bytes, &maps.grad[0], &b_full[slot],
-                               0, boxes[0].q[2] * g.b[2], boxes[0].q[1] * g.b[1],
-                               P.q_lo + q0 - (new_entries - 1) + k, mo);
-            } else {
-              if (!dev::mbar_wait(&b_empty[b_slot], b_phase ^ 1u, err, kSiteWProducer,
-                                  P.timeout_ns)) {
-                lane_ok = false;
-                break;
-              }
-              if (l == 0) dev::mbar_arrive_expect_tx(&b_full[b_slot], P.b_tx);
-              const int part = l % kParts;
-              const int blk = (l / kParts) % P.b_blocks;
-              const int j = l / (kParts * P.b_blocks);
-              const int32_t mo =
-                  boxes[j].valid ? static_cast<int32_t>(boxes[j].out_merged) : -1;
-              uint8_t* dst = b_base + b_slot * P.b_slot_bytes + blk * (P.kc_rows * 128) +
-                             j * g.box_rows * P.b_row_bytes;
-              dev::tma_load_5d(dst + part * P.b_part_bytes, &maps.grad[part], &b_full[b_slot],
-                               blk * P.b_blk_elems, boxes[j].q[2] * g.b[2],
-                               boxes[j].q[1] * g.b[1], boxes[j].q[0] * g.b[0], mo);
+            if (!dev::mbar_wait(&b_empty[b_slot], b_phase ^ 1u, err, kSiteWProducer,
+                                P.timeout_ns)) {
+              lane_ok = false;
+              break;
             }
+            if (l == 0) dev::mbar_arrive_expect_tx(&b_full[b_slot], P.b_tx);
+            const int part = l % kParts;
+            const int blk = (l / kParts) % P.b_blocks;
+            const int j = l / (kParts * P.b_blocks);
+            const int32_t mo = boxes[j].valid ? static_cast<int32_t>(boxes[j].out_merged) : -1;
+            uint8_t* dst = b_base + b_slot * P.b_slot_bytes + blk * (P.kc_rows * 128) +
+                           j * g.box_rows * P.b_row_bytes;
+            dev::tma_load_5d(dst + part * P.b_part_bytes, &maps.grad[part], &b_full[b_slot],
+                             blk * P.b_blk_elems, boxes[j].q[2] * g.b[2],
+                             boxes[j].q[1] * g.b[1], boxes[j].q[0] * g.b[0], mo);
           } else {
             const int la = l - round_b;
             const int unit = round_first + la / a_loads;
@@ -575,9 +517,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             // their accumulator rows are never read, so stale slot contents do no harm.
             // Their jobs return before the wait: once the unit's real loads land the MMA
             // may release the stage, and a later wait would then be one phase ahead.
-            const int unit_taps =
-                P.halo ? P.entries_per_unit
-                       : min(P.entries_per_unit, g.taps - (unit_first + unit) * P.tpm);
+            const int unit_taps = min(P.entries_per_unit, g.taps - (unit_first + unit) * P.tpm);
             const int jt = lu / (kParts * g.nb);
             if (jt >= unit_taps) continue;
             int stage = a_stage + unit;
@@ -592,9 +532,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             if (lu == 0) {
               dev::mbar_arrive_expect_tx(
-                  &a_full[stage],
-                  P.halo ? P.a_tx
-                         : static_cast<uint32_t>(unit_taps) * (P.a_tx / P.entries_per_unit));
+                  &a_full[stage], static_cast<uint32_t>(unit_taps) * (P.a_tx / P.entries_per_unit));
             }
             const int part = lu % kParts;
             const int j = (lu / kParts) % g.nb;
@@ -613,16 +551,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       ok = __all_sync(0xffffffffu, lane_ok) != 0;
       if (!ok) break;
-      // advance the ring, the B slot and the A stages past this tile
-      if (P.nfold) {
-        for (int k = 0; k < new_entries; ++k) {
-          if (++ring_slot == P.b_ring) {
-            ring_slot = 0;
-            ring_phase ^= 1u;
-          }
-        }
-        if (++q0 == g.nbox[0]) q0 = 0;
-      } else if (++b_slot == 2) {
+      // advance the B slot and the A stages past this tile
+      if (++b_slot == 2) {
         b_slot = 0;
         b_phase ^= 1u;
       }
@@ -654,41 +584,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t a_part = P.a_part_bytes >> 4;
     const uint32_t b_part = P.b_part_bytes >> 4;
     bool ok = true;
-    // Folded dY ring: slot / phase of the next entry to wait for, the first (oldest)
-    // slot of the current tile and the tile's slice index, all kept incrementally.
-    int ring_slot = 0, first_slot = 0;
-    uint32_t ring_phase = 0;
-    int q0 = P.nfold ? static_cast<int>(p_begin % g.nbox[0]) : 0;
     for (int64_t pt = p_begin; pt < p_end && ok; ++pt) {
-      uint32_t bs;
-      bool run_end = false;
-      if (P.nfold) {
-        // The tile's slices are the ring entries from first_slot on; wait for the ones this
-        // tile is the first to use (all at a run's start, else the newest).
-        const bool run_start = pt == p_begin || q0 == 0;
-        run_end = pt == p_end - 1 || q0 == g.nbox[0] - 1;
-        if (++q0 == g.nbox[0]) q0 = 0;
-        if (run_start) {
-          first_slot = ring_slot;
-        } else if (++first_slot == P.b_ring) {
-          first_slot = 0;
-        }
-        for (int k = run_start ? P.nfold : 1; k > 0 && ok; --k) {
-          if (!dev::mbar_wait_warp(&b_full[ring_slot], ring_phase, err, kSiteWMma,
-                                   P.timeout_ns)) {
-            ok = false;
-          }
-          if (++ring_slot == P.b_ring) {
-            ring_slot = 0;
-            ring_phase ^= 1u;
-          }
-        }
-        if (!ok) break;
-        bs = dev::warp_uniform(dev::smem_u32(b_base + first_slot * P.b_slot_bytes) >> 4);
-      } else {
-        if (!dev::mbar_wait_warp(&b_full[b_slot], b_phase, err, kSiteWMma, P.timeout_ns)) break;
-        bs = dev::warp_uniform(dev::smem_u32(b_base + b_slot * P.b_slot_bytes) >> 4);
-      }
+      if (!dev::mbar_wait_warp(&b_full[b_slot], b_phase, err, kSiteWMma, P.timeout_ns)) break;
+      const uint32_t bs =
+          dev::warp_uniform(dev::smem_u32(b_base + b_slot * P.b_slot_bytes) >> 4);
       const uint32_t first_tile = pt == p_begin ? 1u : 0u;
       for (int unit = 0; unit < unit_count; ++unit) {
         if (!dev::mbar_wait_warp(&a_full[a_stage], a_phase, err, kSiteWMma, P.timeout_ns)) {
@@ -721,19 +620,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           a_phase ^= 1u;
         }
       }
-      if (P.nfold) {
-        // The tile's oldest slice is no longer needed; at a run's end neither are the rest.
-        int slot = first_slot;
-        for (int k = run_end ? P.nfold : 1; k > 0; --k) {
-          dev::mma_commit_warp(&b_empty[slot]);
-          if (++slot == P.b_ring) slot = 0;
-        }
-      } else {
-        dev::mma_commit_warp(&b_empty[b_slot]);
-        if (++b_slot == 2) {
-          b_slot = 0;
-          b_phase ^= 1u;
-        }
+      dev::mma_commit_warp(&b_empty[b_slot]);
+      if (++b_slot == 2) {
+        b_slot = 0;
+        b_phase ^= 1u;
       }
       if (leader) *progress = static_cast<uint32_t>(pt - p_begin + 1);
       __syncwarp();
