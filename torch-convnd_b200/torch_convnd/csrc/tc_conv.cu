@@ -1214,11 +1214,12 @@ struct WgradPlan {
 
 // Splits of the last tap chunk when the full chunks run `splits`: a CTA's time is about
 // (kTileCost + units) x its position tiles, in units of one unit's MMAs per tile, where
-// kTileCost is the fixed per-tile cost (dY slices, barrier handoffs, commits; measured
-// on B200 at 1.2-2 units' worth). The last chunk's CTAs get as many tiles as keep them
-// as busy as a full chunk's.
+// kTileCost is the fixed per-tile cost (dY slices, barrier handoffs, commits). The last
+// chunk's CTAs get as many tiles as keep them as busy as a full chunk's. 2.2 was the
+// fastest of 1.0 / 1.5 / 2.2 measured on B200 (c2 wgrad call 0.463 / 0.449 / 0.435 ms,
+// c3 unchanged or slower below it).
 int64_t last_chunk_splits(const WgradKernelParams& P, int64_t splits) {
-  constexpr double kTileCost = 1.5;
+  constexpr double kTileCost = 2.2;
   const int last_units = P.units_total - (P.chunks - 1) * P.units_per_cta;
   if (P.chunks <= 1 || last_units >= P.units_per_cta) return splits;
   const double ratio = (kTileCost + last_units) / (kTileCost + P.units_per_cta);
