@@ -17,9 +17,13 @@ from pinned host memory and the step's result read back, inside the timed region
 copy of the next step's inputs runs on a side stream during the current step).
 Clock samples (nvidia-smi, 50 ms) are kept only when stamped inside the timed region.
 `roofline` reports the pass (layer x forward/dgrad/wgrad) with the largest share of the
-step against the bound its arithmetic intensity sets; `cpu_baseline` times the
-reference's native CPU implementation (compiled from its sources into oracle/_ref) on a
-bounded sample of the same workload.
+step against the bound its arithmetic intensity sets: the measured burst bf16 tensor peak
+(halved for float32, the dense TF32 rate; the passes run in millisecond windows at full
+clock) or the measured HBM copy bandwidth; `step_roofline` compares the whole step with
+the sum over its passes of those bounds. `configs` holds the same measurement block for
+the other BASELINE configurations (c3, c4 and c5 by default), run in the same process
+after the headline. `cpu_baseline` times the reference's native CPU implementation
+(compiled from its sources into oracle/_ref) on a bounded sample of the same workload.
 """
 
 from __future__ import annotations
@@ -53,6 +57,8 @@ def parse_args(argv=None):
     parser.add_argument("--impl", choices=("b200", "reference"), default="b200")
     parser.add_argument("--config", default="c2", choices=("c1", "c2", "c3", "c4", "c5"))
     parser.add_argument("--fp32-precision", default="3xtf32", choices=("3xtf32", "tf32", "ieee"))
+    parser.add_argument("--extra-configs", default="c3,c4,c5",
+                        help="other configurations measured in the same run ('' for none)")
     parser.add_argument("--no-e2e", action="store_true")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--cpu-sample-images", type=int, default=1)
@@ -451,25 +457,43 @@ class SingleOp:
         self.dtype = dtype_name(cfg.dtype)
         self.op = torch.ops.torch_convnd
 
-    def _allreduce(self, grads):
+    def _allreduce_start(self, grads):
+        """Starts the mean all-reduce of `grads` in one fp32 bucket (NCCL runs it on its
+        own stream, after the work queued so far on the current stream)."""
         import torch
 
-        if self.world == 1:
-            return
         bucket = torch.cat([g.reshape(-1).float() for g in grads])
-        self.dist.all_reduce(bucket)
         bucket.div_(self.world)
+        return bucket, self.dist.all_reduce(bucket, async_op=True)
+
+    def _allreduce_finish(self, grads, bucket, work):
+        work.wait()
         offset = 0
         for g in grads:
             g.copy_(bucket[offset: offset + g.numel()].view_as(g))
             offset += g.numel()
 
+    def _allreduce(self, grads):
+        if self.world == 1:
+            return
+        self._allreduce_finish(grads, *self._allreduce_start(grads))
+
     def step(self):
         i = self.inputs
         y = self.op.conv_nd.default(i.x, i.weight, i.bias, *self.geo)
-        dx, dw, db = self.op.conv_nd_backward.default(i.grad, i.x, i.weight, *self.geo,
-                                                      [True, True, i.bias is not None])
-        self._allreduce([g for g in (dw, db) if g is not None])
+        has_bias = i.bias is not None
+        if self.world == 1:
+            self.op.conv_nd_backward.default(i.grad, i.x, i.weight, *self.geo,
+                                             [True, True, has_bias])
+            return y
+        # Weight and bias gradients first; their all-reduce runs under the dgrad pass.
+        _, dw, db = self.op.conv_nd_backward.default(i.grad, i.x, i.weight, *self.geo,
+                                                     [False, True, has_bias])
+        grads = [g for g in (dw, db) if g is not None]
+        pending = self._allreduce_start(grads)
+        self.op.conv_nd_backward.default(i.grad, i.x, i.weight, *self.geo,
+                                         [True, False, False])
+        self._allreduce_finish(grads, *pending)
         return y
 
     def config(self):
@@ -528,7 +552,7 @@ class C5Step:
         import torch
 
         import torch_convnd
-        from torch_convnd.data_parallel import GradientBucketer
+        from torch_convnd.data_parallel import GradientBucketer, layer_groups, shard_fraction
 
         configs = load_configs()
         self.world, self.device, self.rank = world, device, rank
@@ -538,7 +562,10 @@ class C5Step:
         self.job_flops = configs.C5_STEP_FLOPS
         self.dtype = "bf16"
         self.net = configs.c5_network(torch_convnd.ConvNd, self.data.parameters, device)
-        self.bucketer = GradientBucketer(self.net.parameters())
+        # one bucket per layer, so L3's and L2's all-reduces run under L1's weight gradient
+        self.bucketer = GradientBucketer(layer_groups(self.net),
+                                         batch_fraction=shard_fraction(configs.C5_BATCH, rank,
+                                                                       world))
         self.optimizer = torch.optim.SGD(self.net.parameters(), lr=1e-4)
         self.mse = torch.nn.functional.mse_loss
 
@@ -643,22 +670,25 @@ def attribute_passes(timings, layers, steps):
     return per_layer
 
 
-def run_b200(args):
+def roofline_terms(layer, peaks):
+    """(flop-bound seconds, byte-bound seconds, tensor peak TF/s) of one pass of `layer`:
+    the conv's algorithmic FLOPs against the measured burst tensor peak (halved for float32:
+    the dense TF32 rate) and its minimum HBM bytes against the measured copy bandwidth."""
     import torch
-    import torch.distributed as dist
 
-    rank = int(os.environ.get("RANK", "0"))
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    device = torch.device("cuda", local)
-    if world > 1:
-        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=device)
+    peak_t = peaks["tensor"] / (2 if layer.dtype == torch.float32 else 1)
+    return (layer.forward_flops / (peak_t * 1e12), pass_bytes(layer) / (peaks["hbm"] * 1e9),
+            peak_t)
+
+
+def measure(workload, args, world, dist, device, peaks):
+    """Times `workload.step` (warm-up, then args.steps steps between barriers and
+    synchronizes, max over ranks), then times each library pass with CUDA events on its
+    launching stream over a few more steps. Returns the measurement block."""
+    import torch
 
     import torch_convnd
 
-    torch_convnd.set_fp32_precision(args.fp32_precision)
-    workload = (C5Step if args.config == "c5" else SingleOp)(args, device, rank, world, dist)
     warmup = max(args.warmup, 3)
     for _ in range(warmup):
         workload.step()
@@ -666,7 +696,7 @@ def run_b200(args):
     torch_convnd.device_status()
     props = torch.cuda.get_device_properties(device)
     uuid = getattr(props, "uuid", None)
-    sampler = ClockSampler(f"GPU-{uuid}" if uuid is not None else str(local))
+    sampler = ClockSampler(f"GPU-{uuid}" if uuid is not None else str(device.index))
     sampler.start()
     time.sleep(0.3)
     torch_convnd.launch_count(reset=True)
@@ -695,22 +725,20 @@ def run_b200(args):
         entry["avg_ms"] = entry["total_ms"] / entry["launches"]
         entry["share_of_step"] = entry.pop("total_ms") / timing_steps / ms
 
-    peaks, source = measured_peaks()
-    hbm = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
-    tensor_peak = float(peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"]))
     passes = {}
     by_name = {l.name: l for l in workload.layers}
+    target_ms = 0.0
     for (kind, name), values in attribute_passes(timings, workload.layers, timing_steps).items():
         layer = by_name[name]
         avg = sum(values) / len(values)
-        peak_t = tensor_peak / (2 if layer.dtype == torch.float32 else 1)
-        t_flop = layer.forward_flops / (peak_t * 1e12)
-        t_byte = pass_bytes(layer) / (hbm * 1e9)
+        t_flop, t_byte, _ = roofline_terms(layer, peaks)
+        target_ms += max(t_flop, t_byte) * 1e3 * len(values) / timing_steps
         passes[f"{name} {kind}"] = {
             "layer": name, "kind": kind, "launches": len(values), "avg_ms": avg,
             "tflops": layer.forward_flops / (avg / 1e3) / 1e12,
             "gbs": pass_bytes(layer) / (avg / 1e3) / 1e9,
             "bound": "tensor" if t_flop >= t_byte else "hbm",
+            "roofline_ms": max(t_flop, t_byte) * 1e3,
             "share_of_step": sum(values) / timing_steps / ms,
         }
     roofline = None
@@ -719,20 +747,58 @@ def run_b200(args):
         info = passes[key]
         layer = by_name[info["layer"]]
         traffic = traffic_from_profiles(layer.name, info["kind"])
+        _, _, peak_t = roofline_terms(layer, peaks)
         if info["bound"] == "tensor":
-            peak = tensor_peak / (2 if layer.dtype == torch.float32 else 1)
-            note = f"{source} cuBLAS bf16 sustained" + (
-                " / 2 (dense TF32 rate)" if layer.dtype == torch.float32 else "")
-            achieved, unit = info["tflops"], "TFLOP/s"
+            fp32 = layer.dtype == torch.float32
+            note = (f"{peaks['source']} cuBLAS bf16 burst (the passes run in short windows at "
+                    "full clock)" + (" / 2: the dense TF32 rate" if fp32 else ""))
+            peak, achieved, unit = peak_t, info["tflops"], "TFLOP/s"
             algorithmic = f"{layer.forward_flops / 1e9:.1f} GFLOP per launch"
         else:
-            peak, note = hbm, f"{source} HBM copy bandwidth"
+            peak, note = peaks["hbm"], f"{peaks['source']} HBM copy bandwidth"
             achieved, unit = info["gbs"], "GB/s"
             algorithmic = f"{pass_bytes(layer) / 1e6:.1f} MB per launch"
         roofline = {"kernel": f"{key} pass (tcgen05)", "bound": info["bound"],
                     "achieved": achieved, "peak": peak, "unit": unit,
                     "frac": achieved / peak, "peak_source": note,
                     "algorithmic": algorithmic, "traffic": traffic}
+        if info["bound"] == "tensor":
+            sustained = peaks["tensor_sustained"] / (2 if layer.dtype == torch.float32 else 1)
+            roofline["frac_of_sustained"] = achieved / sustained
+    # The whole step against the sum over its passes of max(FLOPs / peak, bytes / HBM).
+    step_roofline = {"target_ms": target_ms, "frac": target_ms / ms if ms else None,
+                     "note": "sum over the step's passes of max(FLOPs / tensor peak, "
+                             "minimum bytes / HBM bandwidth); frac = target / measured"}
+    return {"ms_per_step": ms, "value": value, "value_per_gpu": value / world,
+            "passes": passes, "kernels": kernels, "roofline": roofline,
+            "step_roofline": step_roofline, "gpu_launches": launches, "clocks": clocks,
+            "warmup": warmup}
+
+
+def run_b200(args):
+    import torch
+    import torch.distributed as dist
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=device)
+
+    import torch_convnd
+
+    torch_convnd.set_fp32_precision(args.fp32_precision)
+    data, source = measured_peaks()
+    peaks = {"source": source,
+             "hbm": float(data.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])),
+             "tensor": float(data.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"])),
+             "tensor_sustained": float(data.get("bf16_tflops_sustained",
+                                                FALLBACK_PEAKS["bf16_tflops_sustained"]))}
+    workload = (C5Step if args.config == "c5" else SingleOp)(args, device, rank, world, dist)
+    block = measure(workload, args, world, dist, device, peaks)
+    ms, value = block["ms_per_step"], block["value"]
 
     e2e = None
     if not args.no_e2e:
@@ -744,38 +810,62 @@ def run_b200(args):
         e2e = {"value": workload.job_flops / (e2e_ms / 1e3) / 1e12, "unit": "TFLOP/s",
                "ms_per_step": e2e_ms, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                "api": api}
+    config = workload.config()
+    if workload.dtype == "fp32":
+        config["fp32_precision"] = args.fp32_precision
+    headline_dtype, headline_scaling = workload.dtype, workload.scaling
+    del workload
+    torch.cuda.empty_cache()
+
+    # The other BASELINE configurations, measured the same way in the same run (every
+    # rank runs each in the same order, so their collectives line up).
+    extra = {}
+    names = [] if args.extra_configs in ("", "none") else args.extra_configs.split(",")
+    for name in names:
+        if name == args.config:
+            continue
+        sub = argparse.Namespace(**vars(args))
+        sub.config = name
+        other = (C5Step if name == "c5" else SingleOp)(sub, device, rank, world, dist)
+        result = measure(other, sub, world, dist, device, peaks)
+        result.update({"metric_unit": "TFLOP/s", "dtype": other.dtype,
+                       "scaling": other.scaling, "config": other.config()})
+        if other.dtype == "fp32":
+            result["config"]["fp32_precision"] = args.fp32_precision
+        extra[name] = result
+        del other
+        torch.cuda.empty_cache()
 
     baseline = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         baseline = cpu_baseline(args, steps=2, warmup=1)
 
     if rank == 0:
-        config = workload.config()
-        if workload.dtype == "fp32":
-            config["fp32_precision"] = args.fp32_precision
         line = {
             "metric": METRIC,
             "value": value,
             "unit": "TFLOP/s",
             "n_gpus": world,
             "steps": args.steps,
-            "warmup": warmup,
+            "warmup": block["warmup"],
             "ms_per_step": ms,
             "higher_is_better": True,
-            "scaling": workload.scaling,
+            "scaling": headline_scaling,
             "vs_baseline": None,
-            "dtype": workload.dtype,
+            "dtype": headline_dtype,
             "data": "synthetic (seeded N(0,1) activations and gradients, kaiming-uniform "
                     "weights, uniform bias; the reference config's shapes)",
             "config": config,
-            "value_per_gpu": value / world,
-            "roofline": roofline,
-            "passes": passes,
-            "kernels": kernels,
+            "value_per_gpu": block["value_per_gpu"],
+            "roofline": block["roofline"],
+            "step_roofline": block["step_roofline"],
+            "passes": block["passes"],
+            "kernels": block["kernels"],
             "cpu_baseline": baseline,
             "e2e": e2e,
-            "gpu_launches": launches,
-            "clocks": clocks,
+            "gpu_launches": block["gpu_launches"],
+            "clocks": block["clocks"],
+            "configs": extra,
         }
         print(json.dumps(line))
     if world > 1:

@@ -8,7 +8,8 @@ the installed torch (headers and libraries), the same one the reference JIT-buil
 against. No reference source is copied into this repository; the output goes to
 oracle/_ref/ (git-ignored, but carried to the GPU box with the tree).
 
-Usage: python oracle/build_ref.py [REFERENCE_ROOT]   (default /root/reference)
+Usage: python oracle/build_ref.py REFERENCE_ROOT
+(or set CONVND_REFERENCE_ROOT; without either, only an existing build is used).
 """
 
 from __future__ import annotations
@@ -21,9 +22,16 @@ HERE = Path(__file__).resolve().parent
 OUTPUT = HERE / "_ref" / "libtorch_convnd_ref_cpu.so"
 
 
-def build(reference_root: str = "/root/reference", verbose: bool = False) -> Path | None:
-    source = Path(reference_root) / "src" / "torch_convnd" / "csrc" / "convnd.cpp"
-    if not source.exists():
+def build(reference_root: str | None = None, verbose: bool = False) -> Path | None:
+    """Compile the reference's CPU operators from `reference_root` (default: the
+    CONVND_REFERENCE_ROOT environment variable). Returns the library, or None when
+    there is neither a source tree nor an earlier build."""
+    import os
+
+    reference_root = reference_root or os.environ.get("CONVND_REFERENCE_ROOT")
+    source = (Path(reference_root) / "src" / "torch_convnd" / "csrc" / "convnd.cpp"
+              if reference_root else None)
+    if source is None or not source.exists():
         return OUTPUT if OUTPUT.exists() else None
     import torch
     from torch.utils import cpp_extension
@@ -68,5 +76,4 @@ def load(path: Path = OUTPUT):
 
 
 if __name__ == "__main__":
-    root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
-    print(build(root, verbose=True))
+    print(build(sys.argv[1] if len(sys.argv) > 1 else None, verbose=True))

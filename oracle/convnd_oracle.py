@@ -19,7 +19,12 @@ Two independent float64 restatements of what the reference computes:
 
 * ``tap_reference`` restates the reference tests' independent check
   (tests/test_convnd.py:38-67): one channel contraction per tap over padded, strided,
-  dilated slices. No index map is shared with the first restatement.
+  dilated slices. No index map is shared with the first restatement. ``tap_dgrad`` and
+  ``tap_wgrad`` are its adjoints, tap by tap (the input gradient scatters each tap's
+  contraction back into the same padded slices; the weight gradient contracts each tap's
+  slice with dY), the derivatives autograd takes of the reference tests' formula. These
+  three run on whatever device their tensors are on, so full-size checks can run them
+  in float64 on the GPU that is being tested (as checker only).
 
 Both are pinned against golden vectors produced by the reference itself
 (tests/golden/make_golden.py runs the reference's backend='torch' in float64).
@@ -159,6 +164,51 @@ def tap_reference(x, w, b, stride, padding, dilation, groups):
     if b is not None:
         result = result + b.detach().to(torch.float64).reshape(1, -1, *((1,) * rank))
     return result
+
+
+def _tap_slices(tap, dilation, out, stride):
+    return tuple(slice(t * d, t * d + size * s, s)
+                 for t, d, size, s in zip(tap, dilation, out, stride, strict=True))
+
+
+def tap_dgrad(dy, w, input_spatial, stride, padding, dilation, groups):
+    """float64 input gradient, tap by tap: the adjoint of ``tap_reference`` (each tap's
+    W^T . dY added into the padded input slice that the tap reads; padding cropped)."""
+    dy = dy.detach().to(torch.float64)
+    w = w.detach().to(torch.float64)
+    batch, cout = dy.shape[:2]
+    out = tuple(dy.shape[2:])
+    cg = w.shape[1]
+    padded_shape = tuple(size + 2 * p for size, p in zip(input_spatial, padding, strict=True))
+    grad = torch.zeros((batch, groups * cg, *padded_shape), dtype=torch.float64,
+                       device=dy.device)
+    flat_dy = dy.reshape(batch, groups, cout // groups, -1)
+    for tap in itertools.product(*(range(k) for k in w.shape[2:])):
+        coefficient = w[(slice(None), slice(None), *tap)].reshape(groups, cout // groups, cg)
+        term = torch.einsum("goc,bgop->bgcp", coefficient, flat_dy)
+        region = grad[(slice(None), slice(None), *_tap_slices(tap, dilation, out, stride))]
+        region += term.reshape(batch, groups * cg, *out)
+    crop = tuple(slice(p, p + size) for p, size in zip(padding, input_spatial, strict=True))
+    return grad[(slice(None), slice(None), *crop)].contiguous()
+
+
+def tap_wgrad(dy, x, kernel, stride, padding, dilation, groups):
+    """float64 weight gradient, tap by tap: each tap's padded input slice contracted
+    with dY over the batch and the output positions."""
+    dy = dy.detach().to(torch.float64)
+    x = x.detach().to(torch.float64)
+    batch, cin = x.shape[:2]
+    cout = dy.shape[1]
+    out = tuple(dy.shape[2:])
+    padded = torch.nn.functional.pad(x, tuple(v for p in reversed(padding) for v in (p, p)))
+    flat_dy = dy.reshape(batch, groups, cout // groups, -1)
+    grad = torch.empty((cout, cin // groups, *kernel), dtype=torch.float64, device=dy.device)
+    for tap in itertools.product(*(range(k) for k in kernel)):
+        patch = padded[(slice(None), slice(None), *_tap_slices(tap, dilation, out, stride))]
+        patch = patch.reshape(batch, groups, cin // groups, -1)
+        term = torch.einsum("bgop,bgcp->goc", flat_dy, patch)
+        grad[(slice(None), slice(None), *tap)] = term.reshape(cout, cin // groups)
+    return grad
 
 
 def sampled_forward(x, w, b, stride, padding, dilation, groups, points):

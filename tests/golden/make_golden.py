@@ -1,8 +1,8 @@
 """Generate the golden fixtures from the reference implementation itself.
 
-Run in the build container, where the reference is importable, as
+Run in a checkout where the reference's source tree is available, as
 
-    PYTHONPATH=/root/reference/src python tests/golden/make_golden.py
+    PYTHONPATH=<reference root>/src python tests/golden/make_golden.py
 
 It imports the reference package (torch-convnd 0.5.0), runs its portable backend
 (``backend='torch'``) in float64 on the seeded inputs of each case — the oracle BASELINE

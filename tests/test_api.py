@@ -58,6 +58,34 @@ def test_invalid_geometry_messages(kwargs, message):
                 **kwargs)
 
 
+def test_backward_checks_the_workspace_budget():
+    """The backward operator applies the reference's patch-budget rule too
+    (convnd.cpp:357-375): 4-byte elements for 16-bit inputs, and only when dx or dW is
+    requested."""
+    x, w = torch.randn(1, 2, 3, 3, 3, 3), torch.randn(4, 2, 2, 2, 2, 2)
+    dy = torch.randn(1, 4, 2, 2, 2, 2)
+    op = torch.ops.torch_convnd.conv_nd_backward
+    geometry = ([1] * 4, [0] * 4, [1] * 4, 1)
+    # one position's patch column: 2 channels * 16 taps * 4 bytes = 128 bytes
+    with pytest.raises(RuntimeError, match="requires at least 128"):
+        op(dy, x, w, *geometry, 127, [True, True, True])
+    with pytest.raises(RuntimeError, match="requires at least 128"):
+        op(dy.bfloat16(), x.bfloat16(), w.bfloat16(), *geometry, 127, [False, True, False])
+    # enough budget: validation passes and the CPU kernel refuses to run
+    with pytest.raises(RuntimeError, match="CUDA devices only"):
+        op(dy, x, w, *geometry, 128, [True, True, True])
+    # a bias-only request needs no patch budget in float32
+    with pytest.raises(RuntimeError, match="CUDA devices only"):
+        op(dy, x, w, *geometry, 1, [False, False, True])
+
+
+def test_module_backend_torch_is_refused_like_the_function():
+    """ConvNd(backend='torch') raises when called, as conv_nd(backend='torch') does."""
+    layer = Conv4d(2, 4, 2, backend="torch")
+    with pytest.raises(ValueError, match="not part of the B200 build"):
+        layer(torch.randn(1, 2, 3, 3, 3, 3))
+
+
 def test_dtype_bias_and_kernel_errors():
     """Reference tests/test_convnd.py:278-290."""
     x, w = torch.randn(1, 2, 3, 3, 3, 3), torch.randn(4, 2, 2, 2, 2, 2)

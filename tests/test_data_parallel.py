@@ -83,18 +83,21 @@ def oracle_network(seed):
                          nn.GELU(), OracleConv(**LAYERS[2]))
 
 
-def batch(dtype=torch.float64):
-    generator = torch.Generator().manual_seed(7)
-    x = torch.randn(BATCH, LAYERS[0]["cin"], *SPATIAL, generator=generator)
+def batch(dtype=torch.float64, rows=BATCH, seed=7):
+    generator = torch.Generator().manual_seed(seed)
+    x = torch.randn(rows, LAYERS[0]["cin"], *SPATIAL, generator=generator)
     out = oracle.output_shape(SPATIAL, LAYERS[0]["kernel"], LAYERS[0]["stride"],
                               LAYERS[0]["padding"], LAYERS[0]["dilation"])
-    target = torch.randn(BATCH, LAYERS[2]["cout"], *out, generator=generator)
+    target = torch.randn(rows, LAYERS[2]["cout"], *out, generator=generator)
     return x.to(dtype), target.to(dtype)
 
 
-def full_batch_gradients(network):
-    x, target = batch()
-    nn.functional.mse_loss(network(x), target).backward()
+def full_batch_gradients(network, rows=BATCH, micro_batches=(7,)):
+    """Gradients of the mean loss over the whole batch, summed over micro-batches."""
+    network.zero_grad(set_to_none=True)
+    for seed in micro_batches:
+        x, target = batch(rows=rows, seed=seed)
+        nn.functional.mse_loss(network(x), target).backward()
     return {name: p.grad.clone() for name, p in network.named_parameters()}
 
 
@@ -176,6 +179,76 @@ def test_two_gloo_ranks_match_one_process_on_the_whole_batch(tmp_path):
             torch.testing.assert_close(params[name], p.detach(), rtol=0, atol=0)
             torch.testing.assert_close(grads[name], expected[name], rtol=1e-12, atol=1e-12,
                                        msg=f"{name} overlap={overlap} bucket={bucket_bytes}")
+
+
+def test_layer_groups_make_one_bucket_per_layer():
+    network = oracle_network(0)
+    bucketer = data_parallel.GradientBucketer(data_parallel.layer_groups(network))
+    # reverse layer order, weight and bias of a layer together
+    assert bucketer.bucket_sizes == [16 + 2, 144 + 8, 2592 + 8]
+
+
+def test_second_backward_without_no_sync_is_an_error():
+    """A second backward before finish() would drop a micro-batch; it raises instead."""
+    network = oracle_network(0)
+    bucketer = data_parallel.GradientBucketer(data_parallel.layer_groups(network))
+    bucketer.overlap = True  # single process: exercise the hook bookkeeping directly
+    for group in data_parallel.layer_groups(network):
+        for p in group:
+            bucketer._handles.append(p.register_post_accumulate_grad_hook(bucketer._ready))
+    bucketer._launch = lambda bucket: None
+    x, target = batch()
+    nn.functional.mse_loss(network(x), target).backward()
+    with pytest.raises(RuntimeError, match="no_sync"):
+        nn.functional.mse_loss(network(x), target).backward()
+    network.zero_grad(set_to_none=True)
+    bucketer.finish()
+    with bucketer.no_sync():
+        nn.functional.mse_loss(network(x), target).backward()
+    nn.functional.mse_loss(network(x), target).backward()  # the step's last micro-batch
+    bucketer.remove_hooks()
+
+
+def _train_uneven(rank, world, rows, store, path):
+    dist.init_process_group("gloo", init_method=store, rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=120))
+    try:
+        network = oracle_network(seed=0)
+        fraction = data_parallel.shard_fraction(rows, rank, world)
+        bucketer = data_parallel.GradientBucketer(data_parallel.layer_groups(network),
+                                                  batch_fraction=fraction)
+        network.zero_grad(set_to_none=True)
+        # two micro-batches: the first accumulates only, the second starts the reduction
+        for index, seed in enumerate((7, 8)):
+            x, target = batch(rows=rows, seed=seed)
+            x = data_parallel.shard(x, rank, world)
+            target = data_parallel.shard(target, rank, world)
+            loss = nn.functional.mse_loss(network(x), target)
+            if index == 0:
+                with bucketer.no_sync():
+                    loss.backward()
+            else:
+                loss.backward()
+        bucketer.finish()
+        bucketer.remove_hooks()
+        if rank == 0:
+            torch.save({n: p.grad.clone() for n, p in network.named_parameters()}, path)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not gloo_available(), reason="torch.distributed has no usable Gloo device")
+def test_three_gloo_ranks_uneven_shards_and_accumulation(tmp_path):
+    """Batch 5 over 3 ranks (shards 2, 2, 1) with two accumulated micro-batches equals
+    one process's gradient of the two whole-batch mean losses."""
+    rows, world = 5, 3
+    path = tmp_path / "grads.pt"
+    mp.spawn(_train_uneven, args=(world, rows, (tmp_path / "store").as_uri(), str(path)),
+             nprocs=world, join=True)
+    grads = torch.load(path)
+    expected = full_batch_gradients(oracle_network(seed=0), rows=rows, micro_batches=(7, 8))
+    for name, value in expected.items():
+        torch.testing.assert_close(grads[name], value, rtol=1e-12, atol=1e-12, msg=name)
 
 
 # ------------------------------------------------------------------------------------

@@ -15,7 +15,7 @@ import torch
 
 import torch_convnd
 from oracle import convnd_oracle as oracle
-from tolerances import assert_matches
+from tolerances import assert_conv_matches, assert_matches, conv_magnitudes
 from torch_convnd import _native, conv_nd
 
 pytestmark = pytest.mark.gpu
@@ -53,11 +53,11 @@ def test_golden_case(name, golden):
     torch.cuda.synchronize()
     torch_convnd.device_status()
     assert y.dtype == dtype
-    assert_matches(y, record["y"], dtype, f"{name} y")
-    assert_matches(dx, record["dx"], dtype, f"{name} dx")
-    assert_matches(dw, record["dw"], dtype, f"{name} dw")
-    if record["db"] is not None:
-        assert_matches(db, record["db"], dtype, f"{name} db")
+    magnitudes = None
+    if dtype == torch.float32:
+        magnitudes = conv_magnitudes(record["x"], record["weight"], record["grad"],
+                                     c["stride"], c["padding"], c["dilation"], c["groups"])
+    assert_conv_matches({"y": y, "dx": dx, "dw": dw, "db": db}, record, dtype, name, magnitudes)
 
 
 def _problem_mask(x, w, stride, padding, dilation, groups):
@@ -135,10 +135,12 @@ def test_geometry_sweep_against_oracle(case, dtype):
                          groups)
     torch.cuda.synchronize()
     torch_convnd.device_status()
-    assert_matches(y, y_ref, dtype, "y")
-    assert_matches(dx, dx_ref, dtype, "dx")
-    assert_matches(dw, dw_ref, dtype, "dw")
-    assert_matches(db, db_ref, dtype, "db")
+    magnitudes = None
+    if dtype == torch.float32:
+        magnitudes = conv_magnitudes(x, w, dy, stride, padding, dilation, groups)
+    assert_conv_matches({"y": y, "dx": dx, "dw": dw, "db": db},
+                        {"y": y_ref, "dx": dx_ref, "dw": dw_ref, "db": db_ref}, dtype, "sweep",
+                        magnitudes)
 
 
 # 12 slices along box axis 0 and enough work per slice for 6-tile folded super tiles

@@ -46,6 +46,20 @@ def test_tap_reference_matches_reference_golden(name, golden):
     torch.testing.assert_close(y, record["y"], rtol=1e-10, atol=1e-10)
 
 
+@pytest.mark.parametrize("name", ["c1", "c4r", "c5l1r", "c5l2r", "tiled4d", "full5d",
+                                  "strided_bf16"])
+def test_tap_adjoints_match_reference_golden(name, golden):
+    """tap_dgrad / tap_wgrad (used by the full-size GPU checks) reproduce the reference's
+    own input and weight gradients."""
+    record = golden(name)
+    stride, padding, dilation, groups = _geometry(record)
+    x, w, dy = record["x"], record["weight"], record["grad"]
+    dx = oracle.tap_dgrad(dy, w, tuple(x.shape[2:]), stride, padding, dilation, groups)
+    torch.testing.assert_close(dx, record["dx"], rtol=1e-10, atol=1e-10)
+    dw = oracle.tap_wgrad(dy, x, tuple(w.shape[2:]), stride, padding, dilation, groups)
+    torch.testing.assert_close(dw, record["dw"], rtol=1e-10, atol=1e-10)
+
+
 def _geometries():
     """Deterministic sweep in the spirit of the reference's Hypothesis geometry test
     (tests/test_correctness_properties.py:14-91): ranks 1-5, groups 1-2, kernel 1-3,

@@ -96,6 +96,18 @@ void check_grad_output(const at::Tensor& grad_output, const at::Tensor& input,
               "grad_output must match the convolution output shape, device and dtype");
 }
 
+// The reference's backward validates the patch budget with 4-byte elements for 16-bit
+// inputs (their gradients accumulate in fp32; on CUDA always, convnd.cpp:357-362), and
+// with the element size for fp32/fp64 when dx or dW is requested on a non-empty batch
+// (convnd.cpp:375, after the early return at :391-393).
+void check_backward_budget(const at::Tensor& input, const cnd_problem& problem,
+                           int64_t workspace_bytes, const std::array<bool, 3>& output_mask) {
+  const bool low = input.scalar_type() == at::kHalf || input.scalar_type() == at::kBFloat16;
+  if (!low && ((!output_mask[0] && !output_mask[1]) || input.size(0) == 0)) return;
+  const int64_t element = input.element_size() > 4 ? input.element_size() : 4;
+  check_status(cnd_check_workspace_budget(&problem, element, workspace_bytes));
+}
+
 at::Tensor workspace_tensor(size_t bytes, const at::Tensor& like) {
   return at::empty({static_cast<int64_t>(bytes > 0 ? bytes : 1)},
                    like.options().dtype(at::kByte));
@@ -131,7 +143,7 @@ conv_nd_backward_cuda(const at::Tensor& grad_output, const at::Tensor& input,
                       std::array<bool, 3> output_mask) {
   cnd_problem problem = make_problem(input, weight, stride, padding, dilation, groups);
   check_grad_output(grad_output, input, problem);
-  (void)workspace_bytes;
+  check_backward_budget(input, problem, workspace_bytes, output_mask);
   const c10::cuda::CUDAGuard guard(input.device());
   std::optional<at::Tensor> grad_input, grad_weight, grad_bias;
   if (output_mask[0]) grad_input = at::empty(input.sizes(), input.options());
@@ -179,8 +191,12 @@ conv_nd_backward_cpu(const at::Tensor& grad_output, const at::Tensor& input,
                      std::array<bool, 3> output_mask) {
   cnd_problem problem = make_problem(input, weight, stride, padding, dilation, groups);
   check_grad_output(grad_output, input, problem);
-  (void)workspace_bytes;
-  (void)output_mask;
+  // The reference's CPU path promotes 16-bit inputs to fp32 and then applies the fp32
+  // rule (convnd.cpp:363-366).
+  if ((output_mask[0] || output_mask[1]) && input.size(0) > 0) {
+    const int64_t element = input.element_size() > 4 ? input.element_size() : 4;
+    check_status(cnd_check_workspace_budget(&problem, element, workspace_bytes));
+  }
   refuse_cpu();
 }
 

@@ -13,8 +13,14 @@ of the global-batch mean loss. The reference checks exactly this property with
 * a bucket's all-reduce is started from a post-accumulate-grad hook as soon as every
   parameter in it has its gradient, so the collective of a late layer (the first to
   finish backward) overlaps the backward kernels of the layers before it;
-* ``finish()`` waits for the collectives, divides by the world size and writes the
-  averaged values back into ``param.grad``.
+* ``finish()`` waits for the collectives and writes the averaged values back into
+  ``param.grad``. Each rank's gradient is weighted by its share of the global batch
+  (``batch_fraction``; 1/world for even shards) before the sum, so uneven shards, where
+  the first ``batch % world`` ranks hold one extra row, still give the gradient of the
+  global-batch mean loss;
+* gradient accumulation over several backward passes per step uses ``no_sync()`` for
+  all but the last micro-batch; a second backward outside it before ``finish()`` is an
+  error rather than a silently dropped micro-batch.
 
 With NCCL the all-reduce runs on NCCL's own stream, ordered after the work queued on
 the current stream when it is issued; with Gloo (CPU tests) it runs synchronously.
@@ -22,7 +28,8 @@ the current stream when it is issued; with Gloo (CPU tests) it runs synchronousl
 
 from __future__ import annotations
 
-from collections.abc import Iterable, Sequence
+import contextlib
+from collections.abc import Sequence
 
 import torch
 import torch.distributed as dist
@@ -47,6 +54,24 @@ def shard(tensor: torch.Tensor, rank: int, world: int) -> torch.Tensor:
     return tensor[start:stop]
 
 
+def shard_fraction(batch: int, rank: int, world: int) -> float:
+    """`rank`'s share of a batch split by ``shard_bounds``: the weight of its mean-loss
+    gradient in the gradient of the global-batch mean loss."""
+    start, stop = shard_bounds(batch, rank, world)
+    return (stop - start) / batch
+
+
+def layer_groups(module: torch.nn.Module) -> list[list[torch.nn.Parameter]]:
+    """Parameters grouped by the submodule that owns them directly, in registration order:
+    one group per layer, whose gradients one backward call produces together."""
+    groups = []
+    for sub in module.modules():
+        params = [p for p in sub.parameters(recurse=False) if p.requires_grad]
+        if params:
+            groups.append(params)
+    return groups
+
+
 def _reduce_dtype(dtype: torch.dtype) -> torch.dtype:
     return torch.promote_types(dtype, torch.float32)
 
@@ -64,32 +89,50 @@ class _Bucket:
 class GradientBucketer:
     """Averages parameter gradients across the ranks of a process group.
 
-    Parameters are grouped into buckets of at most `bucket_bytes` (counted in the
-    reduction dtype; one dtype and device per bucket) in reverse registration order, the
-    order in which backward produces their gradients for a sequential network. With
+    `parameters` is an iterable of parameters, or of parameter groups (lists, e.g. from
+    ``layer_groups(module)``; a group is never split across buckets). Groups are taken in
+    reverse order, the order in which backward produces their gradients for a sequential
+    network, and consecutive groups are merged while a bucket stays within `bucket_bytes`
+    (counted in the reduction dtype; one dtype and device per bucket). The default of 0
+    gives one bucket per group: per layer for ``layer_groups``, so the all-reduce of a
+    late layer starts as soon as its weight and bias gradients exist. With
     ``overlap=True`` each bucket's all-reduce starts from the gradient hook of its last
-    parameter; otherwise all buckets are reduced in ``finish()``. Call ``finish()`` once
-    per step after ``backward()``.
+    parameter; otherwise all buckets are reduced in ``finish()``.
+
+    `batch_fraction` is this rank's share of the global batch (``shard_fraction``); each
+    rank's gradients are scaled by it and summed. None means 1/world (even shards).
+    Call ``finish()`` once per step after the last ``backward()``.
     """
 
-    def __init__(self, parameters: Iterable[torch.nn.Parameter], group=None,
-                 bucket_bytes: int = 4 << 20, overlap: bool = True):
-        params = [p for p in parameters if p.requires_grad]
-        if not params:
+    def __init__(self, parameters, group=None, bucket_bytes: int = 0, overlap: bool = True,
+                 batch_fraction: float | None = None):
+        groups = []
+        for item in parameters:
+            members = list(item) if isinstance(item, (list, tuple)) else [item]
+            members = [p for p in members if p.requires_grad]
+            if members:
+                groups.append(members)
+        if not groups:
             raise ValueError("no parameters require a gradient")
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.overlap = overlap and self.world > 1
+        self.scale = 1.0 / self.world if batch_fraction is None else float(batch_fraction)
+        self._sync = True
         self.buckets: list[_Bucket] = []
         current: list[torch.nn.Parameter] = []
         size = 0
-        for p in reversed(params):
-            nbytes = p.numel() * _reduce_dtype(p.dtype).itemsize
-            if current and (size + nbytes > bucket_bytes or p.dtype != current[0].dtype
-                            or p.device != current[0].device):
+        for members in reversed(groups):
+            members = list(reversed(members))
+            nbytes = sum(p.numel() * _reduce_dtype(p.dtype).itemsize for p in members)
+            kind = (members[0].dtype, members[0].device)
+            if any((p.dtype, p.device) != kind for p in members):
+                raise ValueError("a parameter group mixes dtypes or devices")
+            if current and (size + nbytes > bucket_bytes
+                            or kind != (current[0].dtype, current[0].device)):
                 self.buckets.append(_Bucket(current))
                 current, size = [], 0
-            current.append(p)
+            current.extend(members)
             size += nbytes
         self.buckets.append(_Bucket(current))
         self._owner = {}
@@ -102,7 +145,13 @@ class GradientBucketer:
 
     # -- hooks -------------------------------------------------------------------------
     def _ready(self, param: torch.nn.Parameter) -> None:
+        if not self._sync:
+            return
         bucket = self._owner[id(param)]
+        if bucket.pending <= 0:
+            raise RuntimeError(
+                "GradientBucketer: backward() ran again before finish(); run the "
+                "micro-batches that only accumulate gradients under no_sync()")
         bucket.pending -= 1
         if bucket.pending == 0:
             self._launch(bucket)
@@ -117,12 +166,26 @@ class GradientBucketer:
                 bucket.flat[offset:offset + n].copy_(p.grad.reshape(-1))
             offset += n
         if self.world > 1:
+            bucket.flat.mul_(self.scale)
             bucket.work = dist.all_reduce(bucket.flat, group=self.group, async_op=True)
 
     # -- per step ----------------------------------------------------------------------
+    @contextlib.contextmanager
+    def no_sync(self):
+        """Backward passes inside only accumulate into ``param.grad``; the reduction
+        starts with the first backward after the block (the step's last micro-batch)."""
+        previous = self._sync
+        self._sync = False
+        try:
+            yield
+        finally:
+            self._sync = previous
+
     def finish(self) -> None:
         """Completes every bucket's reduction and writes the averaged gradients back."""
         if self.world == 1:
+            for bucket in self.buckets:
+                bucket.pending = len(bucket.params)
             return
         for bucket in self.buckets:
             if bucket.work is None and (not self.overlap or bucket.pending > 0):
@@ -130,7 +193,6 @@ class GradientBucketer:
             if bucket.work is not None:
                 bucket.work.wait()
                 bucket.work = None
-            bucket.flat.div_(self.world)
             offset = 0
             for p in bucket.params:
                 n = p.numel()

@@ -106,7 +106,7 @@ class ConvNd(nn.Module):
             self.groups,
             padding_mode=self.padding_mode,
             workspace_bytes=self.workspace_bytes,
-            backend="native" if self.backend == "torch" else self.backend,
+            backend=self.backend,
         )
 
     def extra_repr(self) -> str:
