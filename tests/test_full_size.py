@@ -84,6 +84,23 @@ def test_six_tile_case_uses_six_tile_super_tiles():
             assert "x6 " in line and "fold=1" in line, line
 
 
+def test_pointwise_axes_are_merged_and_unit_axes_dropped():
+    """c5's k = (3,3,1,1) layer plans its forward and dgrad on [16,16,64] (the two
+    pointwise axes merged); a problem with extent-1 kernel-1 axes plans without them
+    (the reference's without_unit_axes, csrc/convnd.h:32-48)."""
+    from types import SimpleNamespace
+
+    summary = _plan_summary(configs.C5_LAYERS[1])
+    for line in summary.splitlines():
+        if line.startswith(("forward", "dgrad")):
+            assert "axes [16,16,64]" in line, line
+    unit = SimpleNamespace(rank=5, batch=2, in_channels=16, out_channels=32,
+                           spatial=(1, 6, 1, 7, 5), kernel=(1, 3, 1, 3, 1), stride=(1,) * 5,
+                           padding=(0, 1, 0, 1, 0), dilation=(1,) * 5, groups=1,
+                           dtype=torch.bfloat16)
+    assert "forward: axes [6,7,5]" in _plan_summary(unit)
+
+
 def test_thin_grouped_layer_runs_dense():
     """c5's grouped layer (4 groups of 8 channels) runs as one dense problem with
     block-diagonal weights; its full-size case below checks that plan."""

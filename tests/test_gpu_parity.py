@@ -117,6 +117,13 @@ def _sweep():
     cases.append((4, 2, 32, 32, (4, 5, 4, 6), (3,) * 4, (1,) * 4, (1,) * 4, (1,) * 4, 32))
     cases.append((5, 1, 24, 12, (4, 4, 3, 5, 4), (2, 3, 3, 2, 3), (1,) * 5, (1,) * 5, (1,) * 5, 3))
     cases.append((4, 2, 16, 32, (7, 6, 8, 9), (3,) * 4, (2,) * 4, (1,) * 4, (1,) * 4, 2))
+    # unit axes (extent 1, kernel 1, no padding) dropped as the reference's
+    # without_unit_axes does, and runs of pointwise axes merged into one
+    cases.append((5, 2, 16, 32, (1, 6, 1, 7, 5), (1, 3, 1, 3, 1), (1,) * 5, (0, 1, 0, 1, 0),
+                  (1,) * 5, 1))
+    cases.append((4, 2, 32, 32, (9, 10, 4, 6), (3, 3, 1, 1), (1,) * 4, (2, 2, 0, 0),
+                  (2, 2, 1, 1), 4))
+    cases.append((6, 1, 16, 16, (1, 1, 1, 1, 1, 1), (1,) * 6, (1,) * 6, (0,) * 6, (1,) * 6, 1))
     return cases
 
 

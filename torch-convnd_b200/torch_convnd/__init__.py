@@ -18,6 +18,7 @@ from ._native import (
 from ._operators import ensure_native_definitions
 from .functional import conv_nd
 from .modules import Conv1d, Conv2d, Conv3d, Conv4d, ConvNd
+from .onnx import export_onnx
 
 __version__ = "0.5.0+b200.1"
 
@@ -35,6 +36,7 @@ __all__ = [
     "conv_nd",
     "device_status",
     "ensure_native_definitions",
+    "export_onnx",
     "launch_count",
     "load_native",
     "native_unavailable_reason",

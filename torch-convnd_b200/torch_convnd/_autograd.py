@@ -1,7 +1,7 @@
-"""Fake (meta) kernels and derivative formulas of the torch_convnd operators.
+"""Fake (meta) kernels, derivative formulas and batching rule of the torch_convnd operators.
 
 Registered from Python like the reference's ``_autograd.py`` (fake kernels :8-26,
-autograd :29-46, double backward :49-90): the forward saves (input, weight) and its
+autograd :29-46, double backward :49-90, vmap :93-149): the forward saves (input, weight) and its
 backward calls ``conv_nd_backward`` with ``output_mask = [needs dx, needs dW, has bias
 and needs db]``, so frozen inputs cost no work (a c5-style first layer whose input is
 data runs forward + wgrad only).
@@ -96,6 +96,43 @@ def _backward_backward(ctx, gg_input, gg_weight, gg_bias):
     return d_grad_output, d_input, d_weight, None, None, None, None, None, None
 
 
+def _vmap_conv_nd(info, in_dims, input, weight, bias, stride, padding, dilation, groups,
+                  workspace_bytes):
+    """Batching rule of conv_nd (the reference registers one too, _autograd.py:93-134).
+
+    The mapped dimension folds into the operator's own dimensions, so a vmapped call is
+    one native launch: into the batch when only the input is mapped; into the groups when
+    the weight (or the bias) is mapped: input [V, N, C, ...] -> [N, V*C, ...], weight
+    [V, Cout, C/g, ...] -> [V*Cout, C/g, ...], groups g -> V*g, output [N, V*Cout, ...]
+    -> [V, N, Cout, ...].
+    """
+    size = info.batch_size
+    x_dim, w_dim, b_dim = in_dims[:3]
+    if w_dim is None and b_dim is None:
+        mapped = input.movedim(x_dim, 0)
+        output = torch.ops.torch_convnd.conv_nd.default(
+            mapped.flatten(0, 1), weight, bias, stride, padding, dilation, groups,
+            workspace_bytes)
+        return output.unflatten(0, (size, mapped.shape[1])), 0
+    x = input.movedim(x_dim, 0) if x_dim is not None else input.expand(size, *input.shape)
+    w = weight.movedim(w_dim, 0) if w_dim is not None else weight.expand(size, *weight.shape)
+    batch, channels = x.shape[1], x.shape[2]
+    cout = w.shape[1]
+    if size == 0:
+        spatial = [_output_extent(s, k, st, p, d) for s, k, st, p, d in
+                   zip(x.shape[3:], w.shape[3:], stride, padding, dilation, strict=True)]
+        return x.new_empty((0, batch, cout, *spatial)), 0
+    folded_x = x.movedim(0, 1).reshape(batch, size * channels, *x.shape[3:])
+    folded_w = w.reshape(size * cout, *w.shape[2:])
+    folded_b = None
+    if bias is not None:
+        b = bias.movedim(b_dim, 0) if b_dim is not None else bias.expand(size, *bias.shape)
+        folded_b = b.reshape(size * cout)
+    output = torch.ops.torch_convnd.conv_nd.default(
+        folded_x, folded_w, folded_b, stride, padding, dilation, groups * size, workspace_bytes)
+    return output.unflatten(1, (size, cout)).movedim(1, 0), 0
+
+
 def register_training() -> None:
     torch.library.register_fake("torch_convnd::conv_nd")(_fake_forward)
     torch.library.register_fake("torch_convnd::conv_nd_backward")(_fake_backward)
@@ -107,3 +144,4 @@ def register_training() -> None:
         _backward_backward,
         setup_context=_setup_backward_context,
     )
+    torch.library.register_vmap("torch_convnd::conv_nd", _vmap_conv_nd)

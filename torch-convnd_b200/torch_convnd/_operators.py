@@ -1,7 +1,8 @@
 """Schema definitions of the torch_convnd operators.
 
-The two schemas are the reference's operator contract, character for character
-(``src/torch_convnd/_operators.py:47-56``), because they are the drop-in boundary: code
+The schemas are the reference's operator contract, character for character
+(``src/torch_convnd/_operators.py:47-56``; ``compatible_conv_nd``, the entry point of
+scripted graphs, ``_dispatch.py:176-180``), because they are the drop-in boundary: code
 and compiled graphs that call ``torch.ops.torch_convnd.conv_nd`` keep working. The CUDA,
 AutocastCUDA and CPU kernels come from the native shim (``_lib/_C.so``); until it is
 loaded, a CompositeExplicitAutograd kernel loads it on the first real call.
@@ -25,6 +26,28 @@ CONV_ND_BACKWARD_SCHEMA = (
     "int[] padding, int[] dilation, int groups, int workspace_bytes, "
     "bool[3] output_mask) -> (Tensor?, Tensor?, Tensor?)"
 )
+
+
+COMPATIBLE_CONV_ND_SCHEMA = (
+    "compatible_conv_nd(Tensor input, Tensor weight, Tensor? bias, int[] stride, "
+    "int[] padding, int[] dilation, int groups, int workspace_bytes, str backend) -> Tensor"
+)
+
+
+def _compatible_conv_nd(input, weight, bias, stride, padding, dilation, groups, workspace_bytes,
+                        backend):
+    """The entry point of scripted graphs (reference _dispatch.py:160-181): a composite
+    over conv_nd, so autograd, autocast and vmap reach the native operator's own rules.
+    `backend` follows conv_nd's policy: 'auto' and 'native' run the B200 kernels and the
+    portable 'torch' decomposition is refused."""
+    if backend not in ("auto", "native"):
+        if backend == "torch":
+            raise ValueError(
+                "backend='torch' (the reference's portable decomposition) is not part of "
+                "the B200 build; use backend='native' or 'auto'")
+        raise ValueError(f"Invalid backend {backend!r}; expected 'auto', 'native' or 'torch'")
+    return torch.ops.torch_convnd.conv_nd.default(
+        input, weight, bias, stride, padding, dilation, groups, workspace_bytes)
 
 
 def _first_call_forward(input, weight, bias, stride, padding, dilation, groups, workspace_bytes):
@@ -58,6 +81,8 @@ def ensure_native_definitions() -> None:
         library.define(CONV_ND_BACKWARD_SCHEMA)
         library.impl("conv_nd", _first_call_forward, "CompositeExplicitAutograd")
         library.impl("conv_nd_backward", _first_call_backward, "CompositeExplicitAutograd")
+        library.define(COMPATIBLE_CONV_ND_SCHEMA)
+        library.impl("compatible_conv_nd", _compatible_conv_nd, "CompositeImplicitAutograd")
         from ._autograd import register_training
 
         register_training()

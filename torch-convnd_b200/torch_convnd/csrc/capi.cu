@@ -173,16 +173,99 @@ struct Plan {
   size_t total = 0;
 };
 
-void fill_spatial(const cnd_problem& p, int64_t* in, int64_t* out, int64_t* k, int64_t* s,
-                  int64_t* d, int64_t* pad) {
-  for (int a = 0; a < p.rank; ++a) {
-    in[a] = p.input[a];
-    out[a] = p.output[a];
-    k[a] = p.kernel[a];
-    s[a] = p.stride[a];
-    d[a] = p.dilation[a];
-    pad[a] = p.padding[a];
+// Spatial geometry of the tensor-core passes after axis reduction.
+struct Axes {
+  int rank = 0;
+  int64_t in[CND_MAX_RANK], out[CND_MAX_RANK], k[CND_MAX_RANK], s[CND_MAX_RANK],
+      d[CND_MAX_RANK], p[CND_MAX_RANK];
+  void push(int64_t in_, int64_t out_, int64_t k_, int64_t s_, int64_t d_, int64_t p_) {
+    in[rank] = in_;
+    out[rank] = out_;
+    k[rank] = k_;
+    s[rank] = s_;
+    d[rank] = d_;
+    p[rank] = p_;
+    ++rank;
   }
+};
+
+// The reference's without_unit_axes (src/torch_convnd/csrc/convnd.h:32-48): an axis with
+// one sample, a one-tap kernel and no padding puts every element at coordinate 0, so it
+// is dropped from the index arithmetic (one axis is always kept). Memory layouts and
+// volumes are unchanged: the packed operands and the outputs do not depend on it.
+Axes without_unit_axes(const cnd_problem& p) {
+  Axes a;
+  for (int axis = 0; axis < p.rank; ++axis) {
+    const bool unit = p.input[axis] == 1 && p.kernel[axis] == 1 && p.padding[axis] == 0;
+    if (unit && (a.rank > 0 || axis + 1 < p.rank)) continue;
+    a.push(p.input[axis], p.output[axis], p.kernel[axis], p.stride[axis], p.dilation[axis],
+           p.padding[axis]);
+  }
+  return a;
+}
+
+// Adjacent pointwise axes (kernel 1, stride 1, padding 0: the output coordinate equals the
+// input coordinate and every tap sits at offset 0) address memory exactly like one axis of
+// their product extent, so each run of them becomes one axis. The planners see a longer
+// innermost extent (c5's k = (3,3,1,1) layer: [16,16,64] instead of [16,16,8,8]).
+Axes merge_pointwise(const Axes& a) {
+  Axes m;
+  bool last_pointwise = false;
+  for (int axis = 0; axis < a.rank; ++axis) {
+    const bool pointwise = a.k[axis] == 1 && a.s[axis] == 1 && a.p[axis] == 0;
+    if (pointwise && last_pointwise) {
+      m.in[m.rank - 1] *= a.in[axis];
+      m.out[m.rank - 1] *= a.out[axis];
+      continue;
+    }
+    m.push(a.in[axis], a.out[axis], a.k[axis], a.s[axis], pointwise ? 1 : a.d[axis],
+           a.p[axis]);
+    last_pointwise = pointwise;
+  }
+  return m;
+}
+
+void fill_spatial(const Axes& ax, int64_t* in, int64_t* out, int64_t* k, int64_t* s,
+                  int64_t* d, int64_t* pad) {
+  for (int a = 0; a < ax.rank; ++a) {
+    in[a] = ax.in[a];
+    out[a] = ax.out[a];
+    k[a] = ax.k[a];
+    s[a] = ax.s[a];
+    d[a] = ax.d[a];
+    pad[a] = ax.p[a];
+  }
+}
+
+// Plans a forward-type pass over each axis variant that fits the kernels and keeps the
+// one the cost model scores best.
+bool plan_best(ConvPass* pass, FpropPlan* plan, const Axes* const* variants, int count,
+               bool dgrad) {
+  bool found = false;
+  double best = 0.0;
+  for (int v = 0; v < count; ++v) {
+    const Axes& ax = *variants[v];
+    if (ax.rank > kMaxFastRank) continue;
+    ConvPass trial = *pass;
+    trial.rank = ax.rank;
+    for (int a = 0; a < ax.rank; ++a) {
+      trial.in[a] = dgrad ? ax.out[a] : ax.in[a];
+      trial.out[a] = dgrad ? ax.in[a] : ax.out[a];
+      trial.k[a] = ax.k[a];
+      trial.s[a] = dgrad ? 1 : ax.s[a];
+      trial.d[a] = ax.d[a];
+      trial.p[a] = dgrad ? ax.d[a] * (ax.k[a] - 1) - ax.p[a] : ax.p[a];
+    }
+    FpropPlan candidate;
+    if (!plan_fprop(trial, &candidate)) continue;
+    if (!found || candidate.score < best) {
+      found = true;
+      best = candidate.score;
+      *pass = trial;
+      *plan = candidate;
+    }
+  }
+  return found;
 }
 
 Region take(size_t* cursor, size_t bytes) {
@@ -197,12 +280,16 @@ Region take(size_t* cursor, size_t bytes) {
 // `forward` selects the forward plan; otherwise `mask` selects the backward passes.
 void make_plan(const cnd_problem& p, bool forward, const int32_t* mask, Plan* plan) {
   *plan = Plan();
+  const Axes reduced = without_unit_axes(p);
+  const Axes merged = merge_pointwise(reduced);
+  const Axes* variants[2] = {&reduced, &merged};
+  const int nvariants = merged.rank < reduced.rank ? 2 : 1;
   plan->groups = p.groups;
   plan->cin_g = p.channels / p.groups;
   plan->cout_g = p.output_channels / p.groups;
   const bool low = p.dtype == CND_BF16 || p.dtype == CND_F16;
   const bool f32_tensor = p.dtype == CND_F32 && p.fp32_mode != CND_FP32_SIMT;
-  plan->tensor_cores = (low || f32_tensor) && p.rank <= kMaxFastRank && p.batch > 0;
+  plan->tensor_cores = (low || f32_tensor) && merged.rank <= kMaxFastRank && p.batch > 0;
   if (!plan->tensor_cores) return;
   plan->op = operand_type(p.dtype);
   plan->split3 = (p.dtype == CND_F32 && p.fp32_mode == CND_FP32_3XTF32) ? 1 : 0;
@@ -231,17 +318,16 @@ void make_plan(const cnd_problem& p, bool forward, const int32_t* mask, Plan* pl
 
   if (forward) {
     ConvPass& f = plan->fwd;
-    f.rank = p.rank;
     f.batch = p.batch;
     f.groups = plan->groups;
-    fill_spatial(p, f.in, f.out, f.k, f.s, f.d, f.p);
     f.c_pad = static_cast<int>(plan->x_pad);
     f.n_real = static_cast<int>(plan->cout_g);
     f.n_pad = static_cast<int>(round16(plan->cout_g));
     f.op = plan->op;
     f.split3 = plan->split3;
     f.out_dtype = p.dtype;
-    plan->fast_fwd = plan->cout_g <= 256 && plan_fprop(f, &plan->fwd_plan);
+    plan->fast_fwd =
+        plan->cout_g <= 256 && plan_best(&f, &plan->fwd_plan, variants, nvariants, false);
     if (plan->fast_fwd) {
       const size_t act =
           static_cast<size_t>(p.batch * plan->groups * p.input_volume) * f.c_pad * es;
@@ -263,17 +349,8 @@ void make_plan(const cnd_problem& p, bool forward, const int32_t* mask, Plan* pl
   }
   if (mask[0]) {
     ConvPass& dg = plan->dgrad;
-    dg.rank = p.rank;
     dg.batch = p.batch;
     dg.groups = plan->groups;
-    for (int a = 0; a < p.rank; ++a) {
-      dg.in[a] = p.output[a];
-      dg.out[a] = p.input[a];
-      dg.k[a] = p.kernel[a];
-      dg.s[a] = 1;
-      dg.d[a] = p.dilation[a];
-      dg.p[a] = p.dilation[a] * (p.kernel[a] - 1) - p.padding[a];
-    }
     dg.c_pad = static_cast<int>(plan->dy_pad);
     dg.n_real = static_cast<int>(plan->cin_g);
     dg.n_pad = static_cast<int>(round16(plan->cin_g));
@@ -289,14 +366,14 @@ void make_plan(const cnd_problem& p, bool forward, const int32_t* mask, Plan* pl
       ConvPass bf = dg;
       bf.op = kOpBF16;
       bf.c_pad = static_cast<int>(bf16_pad);
-      if (plan_fprop(bf, &plan->dgrad_plan)) {
+      if (plan_best(&bf, &plan->dgrad_plan, variants, nvariants, true)) {
         dg = bf;
         plan->dgrad_bf16 = true;
         plan->fast_dgrad = true;
       }
     }
     if (!plan->dgrad_bf16) {
-      plan->fast_dgrad = dgrad_ok && plan_fprop(dg, &plan->dgrad_plan);
+      plan->fast_dgrad = dgrad_ok && plan_best(&dg, &plan->dgrad_plan, variants, nvariants, true);
     }
   }
   const bool f32 = p.dtype == CND_F32;
@@ -310,10 +387,10 @@ void make_plan(const cnd_problem& p, bool forward, const int32_t* mask, Plan* pl
   plan->wg_dy_pad = f32 ? pad_channels(kOpBF16, plan->cout_g, 16) : plan->dy_pad;
   if (mask[1]) {
     WgradPass& wg = plan->wgrad;
-    wg.rank = p.rank;
+    wg.rank = reduced.rank;
     wg.batch = p.batch;
     wg.groups = plan->groups;
-    fill_spatial(p, wg.in, wg.out, wg.k, wg.s, wg.d, wg.p);
+    fill_spatial(reduced, wg.in, wg.out, wg.k, wg.s, wg.d, wg.p);
     wg.c_pad = static_cast<int>(plan->wg_x_pad);
     wg.cin_real = static_cast<int>(plan->cin_g);
     wg.n_pad = static_cast<int>(plan->wg_dy_pad);
@@ -406,17 +483,23 @@ int cnd_plan_summary(const cnd_problem* problem, char* buffer, size_t size) {
   cnd::make_plan(*problem, false, all, &bwd);
   char text[4096];
   int used = 0;
-  auto describe = [&](const char* name, bool fast, const cnd::FpropPlan& plan) {
+  auto describe = [&](const char* name, bool fast, const cnd::FpropPlan& plan,
+                      const cnd::ConvPass& pass) {
     const cnd::FpropParams& P = plan.params;
     if (!fast) {
       used += std::snprintf(text + used, sizeof(text) - used, "%s: generic CUDA cores\n", name);
       return;
     }
+    used += std::snprintf(text + used, sizeof(text) - used, "%s: axes [", name);
+    for (int a = 0; a < pass.rank; ++a) {
+      used += std::snprintf(text + used, sizeof(text) - used, a ? ",%lld" : "%lld",
+                            static_cast<long long>(pass.out[a]));
+    }
     used += std::snprintf(text + used, sizeof(text) - used,
-                          "%s: tcgen05 tile [%d,%d,%d] x%d halo(a0=%d,a1=%d) box %dx%dx%d "
+                          "] tcgen05 tile [%d,%d,%d] x%d halo(a0=%d,a1=%d) box %dx%dx%d "
                           "units=%d cblocks=%d N=%d stages=%d stage_bytes=%u nacc=%d parts=%d "
                           "supers=%lld fold=%d tma_store=%d\n",
-                          name, P.e0, P.b1, P.b2, P.mt, P.nshift0, P.nshift1, P.h0, P.h1, P.b2,
+                          P.e0, P.b1, P.b2, P.mt, P.nshift0, P.nshift1, P.h0, P.h1, P.b2,
                           P.units, P.cblocks, P.n_pad, P.stages, P.stage_bytes, P.nacc,
                           plan.parts, static_cast<long long>(P.supers_total), P.fold,
                           P.tma_store);
@@ -425,8 +508,8 @@ int cnd_plan_summary(const cnd_problem* problem, char* buffer, size_t size) {
     used += std::snprintf(text + used, sizeof(text) - used,
                           "groups: %d run dense (block-diagonal weights)\n", bwd.bd);
   }
-  describe("forward", fwd.fast_fwd, fwd.fwd_plan);
-  describe("dgrad", bwd.fast_dgrad, bwd.dgrad_plan);
+  describe("forward", fwd.fast_fwd, fwd.fwd_plan, fwd.fwd);
+  describe("dgrad", bwd.fast_dgrad, bwd.dgrad_plan, bwd.dgrad);
   if (bwd.fast_wgrad) {
     char detail[256];
     cnd::describe_wgrad_pass(bwd.wgrad, detail, sizeof(detail));

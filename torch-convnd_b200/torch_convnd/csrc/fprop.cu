@@ -874,6 +874,7 @@ bool plan_fprop(const ConvPass& pass, FpropPlan* plan) {
    }
   }
   if (!found) return false;
+  plan->score = best;
   P = chosen;
   P.units = P.taps / (P.nshift0 * P.nshift1);
   P.nsup[0] = (P.out[0] + P.mt * P.e0 - 1) / (P.mt * P.e0);

@@ -57,6 +57,7 @@ struct FpropParams {
 struct FpropPlan {
   FpropParams params;
   int parts;         // 2 for 3xTF32 (big + small operand arrays)
+  double score;      // the cost model's estimated cycles per output position (lower wins)
   size_t smem;
   // weight packing order (see PackWeightArgs::unit_order)
   int shift0, shift1, fold;

@@ -109,6 +109,13 @@ class ConvNd(nn.Module):
             backend=self.backend,
         )
 
+    def __prepare_scriptable__(self):
+        """torch.jit.script hook: script the TorchScript form, which calls the native
+        operator through torch_convnd::compatible_conv_nd (reference modules.py:137-155)."""
+        from ._script import ScriptableConvNd
+
+        return ScriptableConvNd(self)
+
     def extra_repr(self) -> str:
         return (
             f"{self.in_channels}, {self.out_channels}, kernel_size={self.kernel_size}, "
