@@ -37,7 +37,7 @@ class Problem(ctypes.Structure):
 
 def _library():
     library = _native.core()
-    library.cnd_backward.argtypes = [ctypes.c_void_p] * 8 + [ctypes.c_void_p, ctypes.c_void_p,
+    library.cnd_backward.argtypes = [ctypes.c_void_p] * 8 + [ctypes.c_void_p,
                                                              ctypes.c_size_t, ctypes.c_void_p]
     library.cnd_backward.restype = ctypes.c_int
     library.cnd_backward_workspace_size.argtypes = [ctypes.c_void_p, ctypes.c_void_p]
