@@ -59,6 +59,9 @@ def parse_args(argv=None):
     parser.add_argument("--fp32-precision", default="3xtf32", choices=("3xtf32", "tf32", "ieee"))
     parser.add_argument("--extra-configs", default="c3,c4,c5",
                         help="other configurations measured in the same run ('' for none)")
+    parser.add_argument("--c5-layout", default="channels-last",
+                        choices=("channels-last", "channels-first"),
+                        help="activation layout of the c5 training step")
     parser.add_argument("--no-e2e", action="store_true")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--cpu-sample-images", type=int, default=1)
@@ -557,6 +560,13 @@ class C5Step:
         configs = load_configs()
         self.world, self.device, self.rank = world, device, rank
         self.data = configs.make_c5_inputs(device=device, rank=rank, world=world)
+        # Activations channels-last end to end: the batch (and its target) arrive in that
+        # layout, as from a channels-last data loader; every layer then reads its input
+        # in place and writes its output channels-last (no layout pass between layers).
+        self.layout = args.c5_layout
+        if self.layout == "channels-last":
+            self.data.x = torch_convnd.channels_last(self.data.x)
+            self.data.target = torch_convnd.channels_last(self.data.target)
         shard = self.data.x.shape[0]
         self.layers = [layer.with_batch(shard) for layer in configs.C5_LAYERS]
         self.job_flops = configs.C5_STEP_FLOPS
@@ -584,6 +594,7 @@ class C5Step:
         configs = load_configs()
         return {"workload": C5_WORKLOAD, "global_batch": configs.C5_BATCH,
                 "per_gpu_batch": self.layers[0].batch, "parallelism": f"dp{self.world}",
+                "activation_layout": self.layout,
                 "step_gflop_per_gpu": sum(l.step_flops for l in self.layers) / 1e9,
                 "gradient_buckets": len(self.bucketer.buckets),
                 "l2": "inputs larger than L2 (x alone is 537 MB at batch 64)"}
@@ -594,6 +605,11 @@ class C5Step:
         device = self.device
         x_host = self.data.x.cpu().pin_memory()
         target_host = self.data.target.cpu().pin_memory()
+        if self.layout == "channels-last":
+            import torch_convnd
+
+            x_host = torch_convnd.channels_last(self.data.x.cpu()).pin_memory()
+            target_host = torch_convnd.channels_last(self.data.target.cpu()).pin_memory()
         loss_host = torch.empty((), dtype=torch.bfloat16, pin_memory=True)
         prefetch = Prefetcher([x_host, target_host], device)
 

@@ -14,8 +14,9 @@
  * (schemas: src/torch_convnd/_operators.py:47-56; C++ kernels: convnd.cpp:305-415).
  * This header carries the same contract through plain pointers and sizes, so that any
  * host (the bundled PyTorch shim, ctypes, cgo, JNI) can drive the kernels. No torch types
- * appear here. All tensors are dense, contiguous, channels-first ([N, C, d0, d1, ...]) in
- * device memory, exactly as the reference's operators see them after `.contiguous()`.
+ * appear here. All tensors are dense and in device memory; activations are channels-first
+ * ([N, C, d0, d1, ...]), exactly as the reference's operators see them after
+ * `.contiguous()`, unless cnd_problem.layout marks them channels-last.
  *
  * Error convention: every entry point returns CND_OK (0) or a negative status; the
  * message of the last failure on the calling thread is returned by cnd_last_error().
@@ -75,13 +76,27 @@ typedef enum cnd_fp32_mode {
   CND_FP32_SIMT = 2
 } cnd_fp32_mode;
 
+/* Memory layouts of the activation tensors (cnd_problem.layout, a bit set). By default
+ * every activation is dense channels-first [N, C, d0, d1, ...] (what the reference's
+ * operators see after `.contiguous()`). A set bit makes that tensor dense channels-last,
+ * [N, d0, d1, ..., C] in memory (PyTorch's channels_last strides of the same logical
+ * shape), which the tensor-core passes read without a layout pass when its channel rows
+ * already have the kernels' width (16-bit, 16/32/64 or a multiple of 64 channels, one
+ * group or thin groups run dense) and write directly:
+ *   CND_LAYOUT_X_CL: x (forward, backward) and dx (backward);
+ *   CND_LAYOUT_Y_CL: y (forward) and dy (backward).
+ * Weights, biases and their gradients have no layout choice. */
+#define CND_LAYOUT_X_CL 1
+#define CND_LAYOUT_Y_CL 2
+
 /* Convolution problem. Mirrors the reference's `Geometry` record (csrc/convnd.h:13-27)
- * plus batch size and dtype. Filled and validated by cnd_problem_init. */
+ * plus batch size, dtype and activation layouts. Filled and validated by
+ * cnd_problem_init (which sets layout to 0, channels-first). */
 typedef struct cnd_problem {
   int32_t rank;           /* spatial rank, 1..62 */
   int32_t dtype;          /* cnd_dtype */
   int32_t fp32_mode;      /* cnd_fp32_mode, only read for CND_F32 */
-  int32_t reserved;
+  int32_t layout;         /* CND_LAYOUT_* bits; 0 = every activation channels-first */
   int64_t batch;
   int64_t channels;        /* input channels (all groups) */
   int64_t output_channels; /* output channels (all groups) */

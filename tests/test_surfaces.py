@@ -58,6 +58,18 @@ def test_module_scripts_to_the_compatible_operator():
     assert scripted.weight.data_ptr() == layer.weight.data_ptr()
 
 
+def test_onnx_export_needs_the_onnx_package():
+    """Without the optional onnx package the exporter says what to install (the
+    reference's export_onnx does the same, onnx.py:143-150)."""
+    try:
+        import onnx  # noqa: F401
+    except ImportError:
+        with pytest.raises(ImportError, match="onnx"):
+            torch_convnd.export_onnx(Conv4d(2, 2, 1), (torch.randn(1, 2, 2, 2, 2, 2),), None)
+    else:
+        pytest.skip("onnx is installed; the GPU test exports a model")
+
+
 # ------------------------------------------------------------------------------------
 # GPU: numbers against the eager operator
 # ------------------------------------------------------------------------------------

@@ -8,6 +8,7 @@ never compiles anything.
 """
 
 from ._geometry import DEFAULT_WORKSPACE_BYTES
+from ._layout import channels_last, is_channels_last
 from ._native import (
     device_status,
     launch_count,
@@ -33,10 +34,12 @@ __all__ = [
     "Conv3d",
     "Conv4d",
     "ConvNd",
+    "channels_last",
     "conv_nd",
     "device_status",
     "ensure_native_definitions",
     "export_onnx",
+    "is_channels_last",
     "launch_count",
     "load_native",
     "native_unavailable_reason",

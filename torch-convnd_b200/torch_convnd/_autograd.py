@@ -11,6 +11,8 @@ from __future__ import annotations
 
 import torch
 
+from ._layout import empty_activation, is_channels_last
+
 
 def _output_extent(size, kernel, step, pad, dil):
     return (size + 2 * pad - dil * (kernel - 1) - 1) // step + 1
@@ -22,14 +24,16 @@ def _fake_forward(input, weight, bias, stride, padding, dilation, groups, worksp
         input.shape[2:], weight.shape[2:], stride, padding, dilation, strict=True
     ):
         shape.append(_output_extent(size, kernel, step, pad, dil))
-    return input.new_empty(shape)
+    # a channels-last input gives a channels-last output (the shim's layout rule)
+    return empty_activation(shape, is_channels_last(input), input)
 
 
 def _fake_backward(
     grad_output, input, weight, stride, padding, dilation, groups, workspace_bytes, output_mask
 ):
     contiguous = torch.contiguous_format
-    grad_input = torch.empty_like(input, memory_format=contiguous) if output_mask[0] else None
+    grad_input = (empty_activation(list(input.shape), is_channels_last(input), input)
+                  if output_mask[0] else None)
     grad_weight = torch.empty_like(weight, memory_format=contiguous) if output_mask[1] else None
     grad_bias = input.new_empty(weight.shape[0]) if output_mask[2] else None
     return grad_input, grad_weight, grad_bias

@@ -154,6 +154,10 @@ struct Plan {
   int bd = 1;
   int64_t cin_g = 0, cout_g = 0;
   int64_t x_pad = 0, dy_pad = 0;
+  // Channels-last activations (cnd_problem.layout) whose rows already are the packed
+  // operand rows (16-bit, one pass group, channel count equal to the padded width) are
+  // read in place: no layout pass and no workspace copy.
+  bool x_cl = false, y_cl = false, x_direct = false, dy_direct = false;
   bool fast_fwd = false, fast_dgrad = false, fast_wgrad = false;
   // float32 dgrad on bfloat16 hi + lo operand parts (three kind::f16 products) instead
   // of 3xTF32, when that halves the K steps (dy channels a multiple of 16). Its packed dy
@@ -162,13 +166,13 @@ struct Plan {
   ConvPass fwd{}, dgrad{};
   FpropPlan fwd_plan{}, dgrad_plan{};
   WgradPass wgrad{};
-  // weight-gradient operands: 16-bit problems reuse x_cl / dy_cl; float32 problems pack
+  // weight-gradient operands: 16-bit problems reuse the packed x / dy; float32 problems pack
   // x and dy again as 3 (3xtf32 mode) or 2 (tf32 mode) bfloat16 terms.
   int wg_op = 0, wg_parts = 1, wg_mode = 0;
   int64_t wg_x_pad = 0, wg_dy_pad = 0;
   // workspace
-  Region x_cl, x_cl_small, w_fwd, w_fwd_small, dy_cl, dy_cl_small, w_dg, w_dg_small, partial,
-      bias_partial;
+  Region x_pack, x_pack_small, w_fwd, w_fwd_small, dy_pack, dy_pack_small, w_dg, w_dg_small,
+      partial, bias_partial;
   Region wg_x[3], wg_dy[3];
   size_t total = 0;
 };
@@ -313,6 +317,11 @@ void make_plan(const cnd_problem& p, bool forward, const int32_t* mask, Plan* pl
   }
   plan->x_pad = pad_channels(plan->op, plan->cin_g, 1);
   plan->dy_pad = pad_channels(plan->op, plan->cout_g, 16);
+  plan->x_cl = (p.layout & CND_LAYOUT_X_CL) != 0;
+  plan->y_cl = (p.layout & CND_LAYOUT_Y_CL) != 0;
+  plan->x_direct = plan->x_cl && low && plan->groups == 1 && p.channels == plan->x_pad;
+  plan->dy_direct =
+      plan->y_cl && low && plan->groups == 1 && p.output_channels == plan->dy_pad;
   const int64_t taps = p.kernel_volume;
   size_t cursor = 0;
 
@@ -326,14 +335,15 @@ void make_plan(const cnd_problem& p, bool forward, const int32_t* mask, Plan* pl
     f.op = plan->op;
     f.split3 = plan->split3;
     f.out_dtype = p.dtype;
+    f.out_cl = plan->y_cl ? 1 : 0;
     plan->fast_fwd =
         plan->cout_g <= 256 && plan_best(&f, &plan->fwd_plan, variants, nvariants, false);
     if (plan->fast_fwd) {
       const size_t act =
           static_cast<size_t>(p.batch * plan->groups * p.input_volume) * f.c_pad * es;
       const size_t wts = static_cast<size_t>(plan->groups * taps * f.n_pad * f.c_pad) * es;
-      plan->x_cl = take(&cursor, act);
-      if (plan->split3) plan->x_cl_small = take(&cursor, act);
+      if (!plan->x_direct) plan->x_pack = take(&cursor, act);
+      if (plan->split3) plan->x_pack_small = take(&cursor, act);
       plan->w_fwd = take(&cursor, wts);
       if (plan->split3) plan->w_fwd_small = take(&cursor, wts);
     }
@@ -357,6 +367,7 @@ void make_plan(const cnd_problem& p, bool forward, const int32_t* mask, Plan* pl
     dg.op = plan->op;
     dg.split3 = plan->split3;
     dg.out_dtype = p.dtype;
+    dg.out_cl = plan->x_cl ? 1 : 0;
     const bool dgrad_ok = !strided && !wide_pad && plan->cin_g <= 256;
     // One bf16 K step covers 16 dy channels, one TF32 step 8: the bf16 parts win when
     // they need fewer K steps (dy channels >= 16); below that they would only lose
@@ -402,11 +413,11 @@ void make_plan(const cnd_problem& p, bool forward, const int32_t* mask, Plan* pl
     if (wg.splits <= 0) plan->fast_wgrad = false;
   }
   const bool need_dy = (plan->fast_dgrad && !plan->dgrad_bf16) || (plan->fast_wgrad && !f32);
-  if (need_dy) {
+  if (need_dy && !plan->dy_direct) {
     const size_t bytes =
         static_cast<size_t>(p.batch * plan->groups * p.output_volume) * plan->dy_pad * es;
-    plan->dy_cl = take(&cursor, bytes);
-    if (plan->split3) plan->dy_cl_small = take(&cursor, bytes);
+    plan->dy_pack = take(&cursor, bytes);
+    if (plan->split3) plan->dy_pack_small = take(&cursor, bytes);
   }
   if ((plan->fast_dgrad || plan->fast_wgrad) && mask[2]) {
     // Upper bound of the partial count (the generic pack uses the smallest blocks).
@@ -424,7 +435,9 @@ void make_plan(const cnd_problem& p, bool forward, const int32_t* mask, Plan* pl
     const size_t wes = f32 ? 2 : es;
     const size_t act =
         static_cast<size_t>(p.batch * plan->groups * p.input_volume) * plan->wg_x_pad * wes;
-    for (int part = 0; part < plan->wg_parts; ++part) plan->wg_x[part] = take(&cursor, act);
+    if (f32 || !plan->x_direct) {
+      for (int part = 0; part < plan->wg_parts; ++part) plan->wg_x[part] = take(&cursor, act);
+    }
     plan->partial = take(&cursor, static_cast<size_t>(plan->wgrad.splits) * plan->groups * taps *
                                       plan->cin_g * plan->cout_g * sizeof(float));
   }
@@ -551,8 +564,8 @@ int cnd_forward(const cnd_problem* problem, const void* x, const void* w, const 
   }
   PackActArgs pa{};
   pa.src = x;
-  pa.dst = at(workspace, plan.x_cl);
-  pa.dst_small = at(workspace, plan.x_cl_small);
+  pa.dst = at(workspace, plan.x_pack);
+  pa.dst_small = at(workspace, plan.x_pack_small);
   pa.batch = p.batch;
   pa.groups = plan.groups;
   pa.spatial = p.input_volume;
@@ -561,8 +574,11 @@ int cnd_forward(const cnd_problem* problem, const void* x, const void* w, const 
   pa.dtype = p.dtype;
   pa.mode = plan.pack_mode;
   pa.chan_partial = nullptr;
-  int rc;
-  {
+  pa.src_cl = plan.x_cl ? 1 : 0;
+  int rc = CND_OK;
+  if (plan.x_direct) {
+    pa.dst = const_cast<void*>(x);  // channels-last x is the packed operand itself
+  } else {
     TimedPass timed(4, stream);
     rc = pack_activations(pa, stream);
   }
@@ -681,11 +697,14 @@ int cnd_backward(const cnd_problem* problem, const void* dy, const void* x, cons
   int blocks = 0;  // bias-gradient partials per (n, g), set by the pack that makes them
   float* bias_partial = static_cast<float*>(at(workspace, plan.bias_partial));
   bool bias_from_pack = false;
-  if (plan.dy_cl.bytes > 0) {
+  const void* dy_operand = plan.dy_direct ? dy : at(workspace, plan.dy_pack);
+  if (plan.dy_pack.bytes > 0 || (plan.dy_direct && output_mask[2] && bias_partial != nullptr)) {
+    // dy to the packed layout, with the bias-gradient partials of the same read; when dy
+    // is read in place this pass only sums its channels.
     PackActArgs pa{};
     pa.src = dy;
-    pa.dst = at(workspace, plan.dy_cl);
-    pa.dst_small = at(workspace, plan.dy_cl_small);
+    pa.dst = at(workspace, plan.dy_pack);
+    pa.dst_small = at(workspace, plan.dy_pack_small);
     pa.batch = p.batch;
     pa.groups = plan.groups;
     pa.spatial = p.output_volume;
@@ -693,10 +712,11 @@ int cnd_backward(const cnd_problem* problem, const void* dy, const void* x, cons
     pa.c_pad = static_cast<int>(plan.dy_pad);
     pa.dtype = p.dtype;
     pa.mode = plan.pack_mode;
+    pa.src_cl = plan.y_cl ? 1 : 0;
     pa.chan_partial = output_mask[2] ? bias_partial : nullptr;
     bias_from_pack = output_mask[2] != 0;
     if (bias_from_pack) blocks = static_cast<int>(pack_blocks(pa));
-    TimedPass timed(4, stream);
+    TimedPass timed(plan.dy_direct ? 6 : 4, stream);
     rc = pack_activations(pa, stream);
     if (rc != CND_OK) return rc;
   }
@@ -713,6 +733,7 @@ int cnd_backward(const cnd_problem* problem, const void* dy, const void* x, cons
     pa.c_pad = static_cast<int>(plan.wg_dy_pad);
     pa.dtype = p.dtype;
     pa.mode = plan.wg_mode;
+    pa.src_cl = plan.y_cl ? 1 : 0;
     if (output_mask[2] && !bias_from_pack) {
       pa.chan_partial = bias_partial;
       bias_from_pack = true;
@@ -726,7 +747,7 @@ int cnd_backward(const cnd_problem* problem, const void* dy, const void* x, cons
   if (output_mask[1]) {
     if (plan.fast_wgrad) {
       WgradPass wg = plan.wgrad;
-      {
+      if (plan.wg_x[0].bytes > 0) {
         PackActArgs pa{};
         pa.src = x;
         pa.dst = at(workspace, plan.wg_x[0]);
@@ -739,6 +760,7 @@ int cnd_backward(const cnd_problem* problem, const void* dy, const void* x, cons
         pa.c_pad = static_cast<int>(plan.wg_x_pad);
         pa.dtype = p.dtype;
         pa.mode = plan.wg_mode;
+        pa.src_cl = plan.x_cl ? 1 : 0;
         TimedPass timed(4, stream);
         rc = pack_activations(pa, stream);
         if (rc != CND_OK) return rc;
@@ -746,9 +768,10 @@ int cnd_backward(const cnd_problem* problem, const void* dy, const void* x, cons
       if (f32) {
         for (int part = 0; part < 3; ++part) wg.grad[part] = at(workspace, plan.wg_dy[part]);
       } else {
-        wg.grad[0] = at(workspace, plan.dy_cl);
+        wg.grad[0] = dy_operand;
       }
       for (int part = 0; part < 3; ++part) wg.act[part] = at(workspace, plan.wg_x[part]);
+      if (plan.wg_x[0].bytes == 0) wg.act[0] = x;  // channels-last x read in place
       wg.partial = static_cast<float*>(at(workspace, plan.partial));
       {
         TimedPass timed(3, stream);
@@ -794,8 +817,8 @@ int cnd_backward(const cnd_problem* problem, const void* dy, const void* x, cons
       }
       if (rc != CND_OK) return rc;
       ConvPass pass = plan.dgrad;
-      pass.act = at(workspace, plan.dgrad_bf16 ? plan.wg_dy[0] : plan.dy_cl);
-      pass.act_small = at(workspace, plan.dgrad_bf16 ? plan.wg_dy[1] : plan.dy_cl_small);
+      pass.act = plan.dgrad_bf16 ? at(workspace, plan.wg_dy[0]) : dy_operand;
+      pass.act_small = at(workspace, plan.dgrad_bf16 ? plan.wg_dy[1] : plan.dy_pack_small);
       pass.wt = pw.dst;
       pass.wt_small = pw.dst_small;
       pass.dst = dx;

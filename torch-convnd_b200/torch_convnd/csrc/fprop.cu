@@ -144,6 +144,22 @@ struct OpTraits<kKind2xBF16> {
   static __device__ __forceinline__ float load(const Out* p) { return __ldg(p); }
 };
 
+// Rounding of an fp32 epilogue value to the output type.
+template <typename T>
+struct OpCast;
+template <>
+struct OpCast<float> {
+  static __device__ __forceinline__ float cast(float v) { return v; }
+};
+template <>
+struct OpCast<__nv_bfloat16> {
+  static __device__ __forceinline__ __nv_bfloat16 cast(float v) { return __float2bfloat16_rn(v); }
+};
+template <>
+struct OpCast<__half> {
+  static __device__ __forceinline__ __half cast(float v) { return __float2half_rn(v); }
+};
+
 // One 16-channel chunk of an epilogue row: the sum of the `used` rotating accumulators
 // of an M tile (TMEM columns tile_col + a * kMT * n_pad + c * 16) plus the bias. The
 // bias chunk is fetched before the TMEM loads, so its latency is paid once per chunk.
@@ -181,6 +197,24 @@ __device__ __forceinline__ void epilogue_chunk(uint32_t dbase, int tile_col, int
 #pragma unroll
     for (int i = 0; i < 16; ++i) out[i] += b[i];
   }
+}
+
+// Stores `count` (<= 16 used) consecutive channels of one channels-last output row, as
+// 16-byte vectors when the run is whole and aligned.
+template <typename OutT>
+__device__ __forceinline__ void store_run16(OutT* dst, const float (&value)[16], int count) {
+  constexpr int kPer = 16 / sizeof(OutT);  // elements per 16-byte vector
+  if (count >= 16 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+#pragma unroll
+    for (int v = 0; v < 16 / kPer; ++v) {
+      alignas(16) OutT packed[kPer];
+#pragma unroll
+      for (int i = 0; i < kPer; ++i) packed[i] = OpCast<OutT>::cast(value[v * kPer + i]);
+      *reinterpret_cast<uint4*>(dst + v * kPer) = *reinterpret_cast<const uint4*>(packed);
+    }
+    return;
+  }
+  for (int i = 0; i < 16 && i < count; ++i) dst[i] = OpCast<OutT>::cast(value[i]);
 }
 
 template <int kOp, int kKSteps, int kMT, int kFold>
@@ -545,6 +579,27 @@ __global__ void __launch_bounds__(kThreads, 1)
         dev::mbar_arrive(&acc_empty[buf]);
         continue;
       }
+      if (P.out_cl) {
+        // Channels-last rows: this thread's position holds n_real consecutive channels.
+        for (int m = 0; m < kMT; ++m) {
+          const int o0 = (S.q0 * kMT + m) * P.e0 + i0;
+          const bool valid = o0 < P.out[0] && o1 < P.out[1] && o2 < P.out[2];
+          const int64_t sp = S.outer_lin * P.out_box_vol +
+                             (static_cast<int64_t>(o0) * P.out[1] + o1) * P.out[2] + o2;
+          OutT* dst = out + (S.n * P.out_volume + sp) * P.out_channels_total +
+                      static_cast<int64_t>(S.g) * P.n_real;
+          for (int c = 0; c < P.n_pad / 16; ++c) {
+            float value[16];
+            epilogue_chunk<Traits, kMT, (kFold > 0)>(dbase, tile_col(m), c, P.n_pad, used,
+                                                     group_bias, P.n_real, value);
+            if (valid) store_run16<OutT>(dst + c * 16, value, P.n_real - c * 16);
+          }
+        }
+        if constexpr (kFold > 0) dev::tmem_store_wait();
+        dev::tc_fence_before();
+        dev::mbar_arrive(&acc_empty[buf]);
+        continue;
+      }
       for (int m = 0; m < kMT; ++m) {
         const int o0 = (S.q0 * kMT + m) * P.e0 + i0;
         const bool valid = o0 < P.out[0] && o1 < P.out[1] && o2 < P.out[2];
@@ -892,7 +947,8 @@ bool plan_fprop(const ConvPass& pass, FpropPlan* plan) {
   const size_t extra = 1024 + (2 * 8 + 4) * 8 + 64;
   P.tma_store = 0;
   P.out_tile_bytes = round_up(static_cast<uint32_t>(pass.n_real * 128 * out_es), 1024);
-  const bool store_shape = (static_cast<int64_t>(P.out[2]) * out_es) % 16 == 0 &&
+  P.out_cl = pass.out_cl;
+  const bool store_shape = !pass.out_cl && (static_cast<int64_t>(P.out[2]) * out_es) % 16 == 0 &&
                            (P.b2 * out_es) % 16 == 0 && pass.n_real <= 256 &&
                            pass.batch * pass.groups * pass.n_real <= kInt32Max &&
                            P.out_outer_vol <= kInt32Max;

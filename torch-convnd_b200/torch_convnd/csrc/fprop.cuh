@@ -45,6 +45,9 @@ struct FpropParams {
   // [channel][position] (two buffers of out_tile_bytes at out_stage_off) and writes it
   // with one TMA store, else every thread stores its position's channels directly
   int tma_store;
+  // out_cl = 1: the output is channels-last [N][positions][G * n_real]; each epilogue
+  // thread writes its position's channels as one contiguous run (no TMA store)
+  int out_cl;
   uint32_t out_stage_off, out_tile_bytes;
   void* dst;
   const void* bias;

@@ -2,7 +2,8 @@
 // groups and dtype (fp16/bf16/fp32 accumulate in fp32, fp64 in fp64), with 64-bit index
 // arithmetic. They run the passes the tcgen05 kernels do not cover (fp64, strided dgrad,
 // padding larger than the dilated kernel, very wide channel groups) and every pass when
-// the caller asks for exact fp32 (CND_FP32_SIMT).
+// the caller asks for exact fp32 (CND_FP32_SIMT). Activations may be channels-first or
+// channels-last (cnd_problem.layout).
 //
 // Index maps follow the reference's column_input_offset / input_column_offset
 // (src/torch_convnd/csrc/convnd.h:57-104): input coordinate = out*stride - pad +
@@ -56,6 +57,14 @@ __device__ __forceinline__ void st<__half, float>(__half* p, int64_t i, float v)
   p[i] = __float2half_rn(v);
 }
 
+// Element index of activation (n, c, position) of a tensor with `channels` channels and
+// `volume` positions per image: channels-first [N][C][S], or channels-last [N][S][C] when
+// `cl` (the CND_LAYOUT_* bit of that tensor).
+__device__ __forceinline__ int64_t act_at(int64_t n, int64_t c, int64_t position,
+                                          int64_t channels, int64_t volume, bool cl) {
+  return cl ? (n * volume + position) * channels + c : (n * channels + c) * volume + position;
+}
+
 // Forward: one thread per output element (n, co, position).
 template <typename T>
 __global__ void generic_forward_kernel(const T* __restrict__ x, const T* __restrict__ w,
@@ -66,6 +75,7 @@ __global__ void generic_forward_kernel(const T* __restrict__ x, const T* __restr
   const int64_t cin_g = P.channels / P.groups;
   const int64_t cout_g = P.output_channels / P.groups;
   const int64_t total = P.batch * P.output_channels * P.output_volume;
+  const bool x_cl = (P.layout & CND_LAYOUT_X_CL) != 0, y_cl = (P.layout & CND_LAYOUT_Y_CL) != 0;
   for (int64_t index = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
        index < total; index += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int64_t position = index % P.output_volume;
@@ -91,14 +101,14 @@ __global__ void generic_forward_kernel(const T* __restrict__ x, const T* __restr
         multiplier *= P.input[axis];
       }
       if (!inside) continue;
-      const int64_t x_base = (n * P.channels + g * cin_g) * P.input_volume + offset;
       const int64_t w_base = (co * cin_g) * P.kernel_volume + tap;
       for (int64_t ci = 0; ci < cin_g; ++ci) {
-        sum += ld(x, x_base + ci * P.input_volume) * ld(w, w_base + ci * P.kernel_volume);
+        sum += ld(x, act_at(n, g * cin_g + ci, offset, P.channels, P.input_volume, x_cl)) *
+               ld(w, w_base + ci * P.kernel_volume);
       }
     }
     if (b != nullptr) sum += ld(b, co);
-    st(y, index, sum);
+    st(y, act_at(n, co, position, P.output_channels, P.output_volume, y_cl), sum);
   }
 }
 
@@ -112,6 +122,7 @@ __global__ void generic_dgrad_kernel(const T* __restrict__ dy, const T* __restri
   const int64_t cin_g = P.channels / P.groups;
   const int64_t cout_g = P.output_channels / P.groups;
   const int64_t total = P.batch * P.channels * P.input_volume;
+  const bool x_cl = (P.layout & CND_LAYOUT_X_CL) != 0, y_cl = (P.layout & CND_LAYOUT_Y_CL) != 0;
   for (int64_t index = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
        index < total; index += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int64_t position = index % P.input_volume;
@@ -144,11 +155,11 @@ __global__ void generic_dgrad_kernel(const T* __restrict__ dy, const T* __restri
       if (!reached) continue;
       for (int64_t col = 0; col < cout_g; ++col) {
         const int64_t co = g * cout_g + col;
-        sum += ld(dy, (n * P.output_channels + co) * P.output_volume + offset) *
+        sum += ld(dy, act_at(n, co, offset, P.output_channels, P.output_volume, y_cl)) *
                ld(w, (co * cin_g + ci_local) * P.kernel_volume + tap);
       }
     }
-    st(dx, index, sum);
+    st(dx, act_at(n, ci, position, P.channels, P.input_volume, x_cl), sum);
   }
 }
 
@@ -165,6 +176,7 @@ __global__ void __launch_bounds__(256) generic_wgrad_kernel(const T* __restrict_
   const int64_t cin_g = P.channels / P.groups;
   const int64_t cout_g = P.output_channels / P.groups;
   const int64_t total = P.output_channels * cin_g * P.kernel_volume;
+  const bool x_cl = (P.layout & CND_LAYOUT_X_CL) != 0, y_cl = (P.layout & CND_LAYOUT_Y_CL) != 0;
   for (int64_t element = blockIdx.x; element < total; element += gridDim.x) {
     const int64_t tap = element % P.kernel_volume;
     const int64_t ci_local = (element / P.kernel_volume) % cin_g;
@@ -192,8 +204,8 @@ __global__ void __launch_bounds__(256) generic_wgrad_kernel(const T* __restrict_
         multiplier *= P.input[axis];
       }
       if (!inside) continue;
-      sum += ld(dy, (n * P.output_channels + co) * P.output_volume + position) *
-             ld(x, (n * P.channels + ci) * P.input_volume + offset);
+      sum += ld(dy, act_at(n, co, position, P.output_channels, P.output_volume, y_cl)) *
+             ld(x, act_at(n, ci, offset, P.channels, P.input_volume, x_cl));
     }
     partial[threadIdx.x] = sum;
     __syncthreads();
@@ -213,13 +225,14 @@ __global__ void __launch_bounds__(256) generic_bias_kernel(const T* __restrict__
                                                            const cnd_problem P) {
   using A = typename Acc<T>::type;
   __shared__ A partial[256];
+  const bool y_cl = (P.layout & CND_LAYOUT_Y_CL) != 0;
   for (int64_t co = blockIdx.x; co < P.output_channels; co += gridDim.x) {
     A sum = 0;
     const int64_t work = P.batch * P.output_volume;
     for (int64_t item = threadIdx.x; item < work; item += blockDim.x) {
       const int64_t position = item % P.output_volume;
       const int64_t n = item / P.output_volume;
-      sum += ld(dy, (n * P.output_channels + co) * P.output_volume + position);
+      sum += ld(dy, act_at(n, co, position, P.output_channels, P.output_volume, y_cl));
     }
     partial[threadIdx.x] = sum;
     __syncthreads();

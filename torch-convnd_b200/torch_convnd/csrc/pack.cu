@@ -80,9 +80,10 @@ __device__ __forceinline__ void split_value(float v, T* out0, T* out1, T* out2, 
   }
 }
 
-// One block: 64 positions x all channels of one (n, g). Loads coalesced along positions,
-// stores coalesced along channels.
-template <typename Tin, typename Tout, int kMode>
+// One block: 64 positions x all channels of one (n, g). Loads coalesced along positions
+// (channels-first source) or along channels (channels-last source, kSrcCL), stores
+// coalesced along channels; with no destination only the channel sums are produced.
+template <typename Tin, typename Tout, int kMode, bool kSrcCL>
 __global__ void __launch_bounds__(256) pack_act_kernel(const Tin* __restrict__ src,
                                                        Tout* __restrict__ dst0,
                                                        Tout* __restrict__ dst1,
@@ -94,21 +95,35 @@ __global__ void __launch_bounds__(256) pack_act_kernel(const Tin* __restrict__ s
   const int g = blockIdx.y;
   const int64_t n = blockIdx.z;
   const int width = kPackPositions + 1;
-  const Tin* in = src + (n * G + g) * static_cast<int64_t>(Cg) * S;
-  for (int i = threadIdx.x; i < c_pad * kPackPositions; i += blockDim.x) {
-    const int c = i / kPackPositions;
-    const int s = i - c * kPackPositions;
-    float v = 0.0f;
-    if (c < Cg && s0 + s < S) v = to_float(in[static_cast<int64_t>(c) * S + s0 + s]);
-    tile[c * width + s] = v;
+  if constexpr (kSrcCL) {
+    const int64_t row = static_cast<int64_t>(G) * Cg;
+    const Tin* in = src + (n * S + s0) * row + static_cast<int64_t>(g) * Cg;
+    for (int i = threadIdx.x; i < c_pad * kPackPositions; i += blockDim.x) {
+      const int s = i / c_pad;
+      const int c = i - s * c_pad;
+      float v = 0.0f;
+      if (c < Cg && s0 + s < S) v = to_float(in[s * row + c]);
+      tile[c * width + s] = v;
+    }
+  } else {
+    const Tin* in = src + (n * G + g) * static_cast<int64_t>(Cg) * S;
+    for (int i = threadIdx.x; i < c_pad * kPackPositions; i += blockDim.x) {
+      const int c = i / kPackPositions;
+      const int s = i - c * kPackPositions;
+      float v = 0.0f;
+      if (c < Cg && s0 + s < S) v = to_float(in[static_cast<int64_t>(c) * S + s0 + s]);
+      tile[c * width + s] = v;
+    }
   }
   __syncthreads();
   const int64_t base = ((n * G + g) * S + s0) * c_pad;
   const int count = static_cast<int>(S - s0 < kPackPositions ? S - s0 : kPackPositions);
-  for (int i = threadIdx.x; i < count * c_pad; i += blockDim.x) {
-    const int s = i / c_pad;
-    const int c = i - s * c_pad;
-    split_value<Tout, kMode>(tile[c * width + s], dst0, dst1, dst2, base + i);
+  if (dst0 != nullptr) {
+    for (int i = threadIdx.x; i < count * c_pad; i += blockDim.x) {
+      const int s = i / c_pad;
+      const int c = i - s * c_pad;
+      split_value<Tout, kMode>(tile[c * width + s], dst0, dst1, dst2, base + i);
+    }
   }
   if (chan_partial != nullptr) {
     // Per-channel sum of this block's positions, in position order.
@@ -350,8 +365,8 @@ int grid_for(int64_t total, int threads) {
   return static_cast<int>(blocks);
 }
 
-template <typename Tin, typename Tout, int kMode>
-int launch_pack_act(const PackActArgs& a, cudaStream_t stream) {
+template <typename Tin, typename Tout, int kMode, bool kSrcCL>
+int launch_pack_act_impl(const PackActArgs& a, cudaStream_t stream) {
   const int64_t blocks = (a.spatial + kPackPositions - 1) / kPackPositions;
   if (blocks > 0x7FFFFFFF || a.groups > 65535 || a.batch > 65535) {
     return fail(CND_ERR_UNSUPPORTED, "pack_act: grid too large");
@@ -360,7 +375,7 @@ int launch_pack_act(const PackActArgs& a, cudaStream_t stream) {
                   static_cast<unsigned>(a.batch));
   const size_t smem = static_cast<size_t>(a.c_pad) * (kPackPositions + 1) * sizeof(float);
   if (smem > 200 * 1024) return fail(CND_ERR_UNSUPPORTED, "pack_act: too many channels");
-  auto kernel = pack_act_kernel<Tin, Tout, kMode>;
+  auto kernel = pack_act_kernel<Tin, Tout, kMode, kSrcCL>;
   cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        static_cast<int>(smem));
   kernel<<<grid, 256, smem, stream>>>(static_cast<const Tin*>(a.src), static_cast<Tout*>(a.dst),
@@ -369,6 +384,12 @@ int launch_pack_act(const PackActArgs& a, cudaStream_t stream) {
                                       static_cast<int>(a.groups), a.chan_partial);
   count_launch();
   return CND_OK;
+}
+
+template <typename Tin, typename Tout, int kMode>
+int launch_pack_act(const PackActArgs& a, cudaStream_t stream) {
+  if (a.src_cl) return launch_pack_act_impl<Tin, Tout, kMode, true>(a, stream);
+  return launch_pack_act_impl<Tin, Tout, kMode, false>(a, stream);
 }
 
 template <typename T>
@@ -410,7 +431,7 @@ int launch_pack_act16(const PackActArgs& a, cudaStream_t stream) {
 }
 
 bool pack16_fast_ok(const PackActArgs& a) {
-  return a.mode == 0 && (a.c_pad == 8 || a.c_pad == 16 || a.c_pad == 32 || a.c_pad == 64) &&
+  return a.mode == 0 && !a.src_cl && a.dst != nullptr && (a.c_pad == 8 || a.c_pad == 16 || a.c_pad == 32 || a.c_pad == 64) &&
          a.cg <= a.c_pad && a.spatial % 8 == 0 &&
          (a.spatial + 63) / 64 <= 0x7FFFFFFF && a.groups <= 65535 &&
          a.batch <= 65535 && reinterpret_cast<uintptr_t>(a.src) % 16 == 0 &&

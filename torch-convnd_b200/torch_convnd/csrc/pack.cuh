@@ -10,13 +10,16 @@ namespace cnd {
 // mode: 0 = copy, 1 = TF32 big + small (3xTF32), 2 = round to TF32, 3 = fp32 -> bf16
 // hi + mid + lo, 4 = fp32 -> bf16 hi + lo (modes 3/4 write bfloat16 parts).
 struct PackActArgs {
-  const void* src;      // channels-first [batch][groups*cg][spatial]
-  void* dst;            // channels-last [batch][groups][spatial][c_pad]
+  const void* src;      // channels-first [batch][groups*cg][spatial], or channels-last
+                        // [batch][spatial][groups*cg] when src_cl
+  void* dst;            // channels-last [batch][groups][spatial][c_pad]; null: only the
+                        // channel partial sums are produced
   void* dst_small;      // second part (modes 1, 3, 4)
   void* dst_third;      // third part (mode 3)
   int64_t batch, groups, spatial;
   int cg, c_pad, dtype, mode;
   float* chan_partial;  // optional [batch][groups][pack_blocks(spatial)][cg]
+  int src_cl;           // 1: the source is channels-last
 };
 
 // Weights [groups*cout_g][cin_g][taps] -> [groups][taps][n_pad][c_pad] (mode as for

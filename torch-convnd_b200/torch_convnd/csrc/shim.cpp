@@ -108,6 +108,33 @@ void check_backward_budget(const at::Tensor& input, const cnd_problem& problem,
   check_status(cnd_check_workspace_budget(&problem, element, workspace_bytes));
 }
 
+// Dense channels-last activation: [N, C, d0..] stored as [N, d0.., C] (PyTorch's
+// channels_last strides for any rank). A tensor that is also contiguous counts as
+// channels-first. The kernels read it in place, so its data must be 16-byte aligned.
+bool is_channels_last(const at::Tensor& t) {
+  if (t.dim() < 3 || t.is_contiguous()) return false;
+  if (reinterpret_cast<uintptr_t>(t.const_data_ptr()) % 16 != 0) return false;
+  int64_t expected = 1;
+  if (t.size(1) != 1 && t.stride(1) != expected) return false;
+  expected *= t.size(1);
+  for (int64_t a = t.dim() - 1; a >= 2; --a) {
+    if (t.size(a) != 1 && t.stride(a) != expected) return false;
+    expected *= t.size(a);
+  }
+  return t.size(0) == 1 || t.stride(0) == expected;
+}
+
+// New dense tensor of logical shape `shape` ([N, C, spatial...]), channels-last if `cl`.
+at::Tensor empty_activation(std::vector<int64_t> shape, bool cl, const at::TensorOptions& options) {
+  if (!cl) return at::empty(shape, options);
+  std::vector<int64_t> stored = {shape[0]};
+  stored.insert(stored.end(), shape.begin() + 2, shape.end());
+  stored.push_back(shape[1]);
+  std::vector<int64_t> order = {0, static_cast<int64_t>(shape.size()) - 1};
+  for (int64_t a = 1; a + 1 < static_cast<int64_t>(shape.size()); ++a) order.push_back(a);
+  return at::empty(stored, options).permute(order);
+}
+
 at::Tensor workspace_tensor(size_t bytes, const at::Tensor& like) {
   return at::empty({static_cast<int64_t>(bytes > 0 ? bytes : 1)},
                    like.options().dtype(at::kByte));
@@ -121,11 +148,15 @@ at::Tensor conv_nd_cuda(const at::Tensor& input, const at::Tensor& weight,
   check_bias(bias, input, problem);
   check_status(cnd_check_workspace_budget(&problem, input.element_size(), workspace_bytes));
   const c10::cuda::CUDAGuard guard(input.device());
-  const at::Tensor x = input.contiguous();
+  // A channels-last input is read in place and gives a channels-last output (PyTorch's
+  // memory-format propagation); any other layout is made contiguous, as the reference does.
+  const bool cl = is_channels_last(input);
+  const at::Tensor x = cl ? input : input.contiguous();
+  if (cl) problem.layout = CND_LAYOUT_X_CL | CND_LAYOUT_Y_CL;
   const at::Tensor w = weight.contiguous();
   at::Tensor b;
   if (bias.has_value()) b = bias->contiguous();
-  at::Tensor output = at::empty(output_shape(input, problem), input.options());
+  at::Tensor output = empty_activation(output_shape(input, problem), cl, input.options());
   if (input.size(0) == 0) return output;
   const size_t bytes = cnd_forward_workspace_size(&problem);
   at::Tensor workspace = workspace_tensor(bytes, input);
@@ -146,14 +177,17 @@ conv_nd_backward_cuda(const at::Tensor& grad_output, const at::Tensor& input,
   check_backward_budget(input, problem, workspace_bytes, output_mask);
   const c10::cuda::CUDAGuard guard(input.device());
   std::optional<at::Tensor> grad_input, grad_weight, grad_bias;
-  if (output_mask[0]) grad_input = at::empty(input.sizes(), input.options());
+  const bool x_cl = is_channels_last(input);
+  const bool dy_cl = is_channels_last(grad_output);
+  problem.layout = (x_cl ? CND_LAYOUT_X_CL : 0) | (dy_cl ? CND_LAYOUT_Y_CL : 0);
+  if (output_mask[0]) grad_input = empty_activation(input.sizes().vec(), x_cl, input.options());
   if (output_mask[1]) grad_weight = at::empty(weight.sizes(), weight.options());
   if (output_mask[2]) grad_bias = at::empty({problem.output_channels}, input.options());
   if (!output_mask[0] && !output_mask[1] && !output_mask[2]) {
     return {grad_input, grad_weight, grad_bias};
   }
-  const at::Tensor dy = grad_output.contiguous();
-  const at::Tensor x = input.contiguous();
+  const at::Tensor dy = dy_cl ? grad_output : grad_output.contiguous();
+  const at::Tensor x = x_cl ? input : input.contiguous();
   const at::Tensor w = weight.contiguous();
   const int32_t mask[3] = {output_mask[0], output_mask[1], output_mask[2]};
   const size_t bytes = cnd_backward_workspace_size(&problem, mask);

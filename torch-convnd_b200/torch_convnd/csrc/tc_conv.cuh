@@ -29,9 +29,11 @@ struct ConvPass {
   const void* act_small;
   const void* wt;   // packed [G][taps][n_pad][c_pad]
   const void* wt_small;
-  void* dst;        // channels-first [N][G*n_real][out...] of out_dtype
+  void* dst;        // channels-first [N][G*n_real][out...] of out_dtype (channels-last
+                    // [N][out...][G*n_real] when out_cl)
   const void* bias; // [G*n_real] of out_dtype, or null
   int out_dtype;    // cnd_dtype
+  int out_cl;
 };
 
 // Weight-gradient pass: dW[g][tap][ci][co] partials of
