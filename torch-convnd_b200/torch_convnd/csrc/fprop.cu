@@ -204,17 +204,20 @@ __device__ __forceinline__ void epilogue_chunk(uint32_t dbase, int tile_col, int
 template <typename OutT>
 __device__ __forceinline__ void store_run16(OutT* dst, const float (&value)[16], int count) {
   constexpr int kPer = 16 / sizeof(OutT);  // elements per 16-byte vector
-  if (count >= 16 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+  int done = 0;
+  if ((reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
 #pragma unroll
     for (int v = 0; v < 16 / kPer; ++v) {
-      alignas(16) OutT packed[kPer];
+      if ((v + 1) * kPer <= count) {
+        alignas(16) OutT packed[kPer];
 #pragma unroll
-      for (int i = 0; i < kPer; ++i) packed[i] = OpCast<OutT>::cast(value[v * kPer + i]);
-      *reinterpret_cast<uint4*>(dst + v * kPer) = *reinterpret_cast<const uint4*>(packed);
+        for (int i = 0; i < kPer; ++i) packed[i] = OpCast<OutT>::cast(value[v * kPer + i]);
+        *reinterpret_cast<uint4*>(dst + v * kPer) = *reinterpret_cast<const uint4*>(packed);
+        done = (v + 1) * kPer;
+      }
     }
-    return;
   }
-  for (int i = 0; i < 16 && i < count; ++i) dst[i] = OpCast<OutT>::cast(value[i]);
+  for (int i = done; i < 16 && i < count; ++i) dst[i] = OpCast<OutT>::cast(value[i]);
 }
 
 template <int kOp, int kKSteps, int kMT, int kFold>
@@ -546,6 +549,54 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int64_t channel_base =
           (S.n * P.out_channels_total + static_cast<int64_t>(S.g) * P.n_real) * P.out_volume;
       const OutT* group_bias = bias != nullptr ? bias + static_cast<int64_t>(S.g) * P.n_real : nullptr;
+      if (P.tma_store && P.out_cl) {
+        // Channels-last rows: stage the tile as [position][channel] (swizzled 16-byte
+        // chunks, so a warp's row stores spread over the banks) and write each column
+        // chunk with one TMA store; buffers alternate as below.
+        const uint32_t span = P.out_span;
+        const uint32_t mask = span == 128 ? 7u : (span == 64 ? 3u : (span == 32 ? 1u : 0u));
+        const int row_bytes = P.n_real * static_cast<int>(sizeof(OutT));
+        const int32_t merged = static_cast<int32_t>(S.n * P.out_outer_vol + S.outer_lin);
+        for (int m = 0; m < kMT; ++m, ++out_tiles) {
+          uint8_t* stage = smem + P.out_stage_off + (out_tiles & 1) * P.out_tile_bytes;
+          if (store_issuer) dev::bulk_wait_group_read<1>();
+          dev::named_barrier(1, 128);
+          for (int c = 0; c < P.n_pad / 16; ++c) {
+            float value[16];
+            epilogue_chunk<Traits, kMT, (kFold > 0)>(dbase, tile_col(m), c, P.n_pad, used,
+                                                     group_bias, P.n_real, value);
+            alignas(16) OutT packed[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) packed[i] = Traits::cast(value[i]);
+#pragma unroll
+            for (int v = 0; v < static_cast<int>(sizeof(OutT)); ++v) {  // 16-byte vectors
+              const int off = c * 16 * static_cast<int>(sizeof(OutT)) + v * 16;
+              if (off < row_bytes) {
+                const uint32_t chunk = static_cast<uint32_t>(off) / span;
+                uint32_t addr = chunk * 128u * span + static_cast<uint32_t>(row) * span +
+                                static_cast<uint32_t>(off) % span;
+                addr ^= ((addr >> 7) & mask) << 4;
+                *reinterpret_cast<uint4*>(stage + addr) =
+                    reinterpret_cast<const uint4*>(packed)[v];
+              }
+            }
+          }
+          dev::fence_proxy_async();
+          dev::named_barrier(1, 128);
+          if (store_issuer) {
+            for (int k = 0; k * static_cast<int>(span) < row_bytes; ++k) {
+              dev::tma_store_5d(&maps.out, stage + k * 128 * span,
+                                S.g * P.n_real + k * static_cast<int>(span / sizeof(OutT)),
+                                S.q2 * P.b2, S.q1 * P.b1, (S.q0 * kMT + m) * P.e0, merged);
+            }
+            dev::bulk_commit_group();
+          }
+        }
+        if constexpr (kFold > 0) dev::tmem_store_wait();
+        dev::tc_fence_before();
+        dev::mbar_arrive(&acc_empty[buf]);
+        continue;
+      }
       if (P.tma_store) {
         // Stage each M tile as [channel][position] and write it with one TMA store; the
         // buffer of tile t is reused by tile t + 2 once that store has read it.
@@ -948,10 +999,25 @@ bool plan_fprop(const ConvPass& pass, FpropPlan* plan) {
   P.tma_store = 0;
   P.out_tile_bytes = round_up(static_cast<uint32_t>(pass.n_real * 128 * out_es), 1024);
   P.out_cl = pass.out_cl;
-  const bool store_shape = !pass.out_cl && (static_cast<int64_t>(P.out[2]) * out_es) % 16 == 0 &&
-                           (P.b2 * out_es) % 16 == 0 && pass.n_real <= 256 &&
-                           pass.batch * pass.groups * pass.n_real <= kInt32Max &&
-                           P.out_outer_vol <= kInt32Max;
+  // Channels-last rows go through TMA stores when one position's channels form 16 bytes
+  // or a swizzle width (32 / 64 / 128 bytes), or whole 128-byte chunks.
+  const int cl_row = pass.n_real * out_es;
+  P.out_span = 0;
+  if (pass.out_cl) {
+    if (cl_row == 16 || cl_row == 32 || cl_row == 64 || cl_row == 128) {
+      P.out_span = static_cast<uint32_t>(cl_row);
+    } else if (cl_row % 128 == 0) {
+      P.out_span = 128;
+    }
+  }
+  const bool store_shape =
+      pass.out_cl
+          ? (P.out_span > 0 && pass.n_real <= 256 &&
+             pass.batch * P.out_outer_vol <= kInt32Max &&
+             (pass.groups * pass.n_real * out_es) % 16 == 0)
+          : ((static_cast<int64_t>(P.out[2]) * out_es) % 16 == 0 && (P.b2 * out_es) % 16 == 0 &&
+             pass.n_real <= 256 && pass.batch * pass.groups * pass.n_real <= kInt32Max &&
+             P.out_outer_vol <= kInt32Max);
   if (store_shape) {
     const bool two = static_cast<size_t>(P.stages) * P.stage_bytes + extra <= 110 * 1024 &&
                      pow2_columns(2 * P.nacc * P.mt * pass.n_pad) <= 256;
@@ -1038,7 +1104,38 @@ int launch_fprop(const ConvPass& pass, const FpropPlan& plan_in, cudaStream_t st
                   static_cast<int>(r));
     }
   }
-  if (P.tma_store) {
+  if (P.tma_store && P.out_cl) {
+    // channels-last output: dims (channels, o2, o1, o0, batch x outer positions)
+    const cuuint64_t e = pass.out_dtype == CND_F32 ? 4u : 2u;
+    const CUtensorMapDataType out_type = pass.out_dtype == CND_F32
+                                             ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                             : (pass.out_dtype == CND_BF16
+                                                    ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                    : CU_TENSOR_MAP_DATA_TYPE_FLOAT16);
+    const cuuint64_t row = static_cast<cuuint64_t>(pass.groups * pass.n_real) * e;
+    cuuint64_t odims[5] = {static_cast<cuuint64_t>(pass.groups * pass.n_real),
+                           static_cast<cuuint64_t>(P.out[2]), static_cast<cuuint64_t>(P.out[1]),
+                           static_cast<cuuint64_t>(P.out[0]),
+                           static_cast<cuuint64_t>(pass.batch * P.out_outer_vol)};
+    cuuint64_t ostrides[4] = {row * P.out[2], row * P.out[2] * P.out[1],
+                              row * static_cast<cuuint64_t>(P.out_box_vol),
+                              row * static_cast<cuuint64_t>(P.out_box_vol) * P.out_outer_vol};
+    cuuint32_t obox[5] = {static_cast<cuuint32_t>(P.out_span / e), static_cast<cuuint32_t>(P.b2),
+                          static_cast<cuuint32_t>(P.b1), static_cast<cuuint32_t>(P.e0), 1};
+    cuuint32_t oestr[5] = {1, 1, 1, 1, 1};
+    const CUtensorMapSwizzle swizzle =
+        P.out_span == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+        : P.out_span == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+        : P.out_span == 32 ? CU_TENSOR_MAP_SWIZZLE_32B
+                           : CU_TENSOR_MAP_SWIZZLE_NONE;
+    const CUresult r = encode(&maps.out, out_type, 5, pass.dst, odims, ostrides, obox, oestr,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+                              CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+      return fail(CND_ERR_CUDA, "cuTensorMapEncodeTiled (channels-last output) failed with code %d",
+                  static_cast<int>(r));
+    }
+  } else if (P.tma_store) {
     // the output's own element type (float32 problems may run bf16-part operands)
     const cuuint64_t e = pass.out_dtype == CND_F32 ? 4u : 2u;
     const CUtensorMapDataType out_type = pass.out_dtype == CND_F32

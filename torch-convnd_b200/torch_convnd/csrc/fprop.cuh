@@ -45,9 +45,12 @@ struct FpropParams {
   // [channel][position] (two buffers of out_tile_bytes at out_stage_off) and writes it
   // with one TMA store, else every thread stores its position's channels directly
   int tma_store;
-  // out_cl = 1: the output is channels-last [N][positions][G * n_real]; each epilogue
-  // thread writes its position's channels as one contiguous run (no TMA store)
+  // out_cl = 1: the output is channels-last [N][positions][G * n_real]. With tma_store
+  // each M tile is staged as [position][channel] rows in column chunks of out_span bytes
+  // (16, or 32 / 64 / 128 with the TMA swizzle of that width) and written by one TMA
+  // store per chunk; otherwise each thread stores its position's channels directly.
   int out_cl;
+  uint32_t out_span;
   uint32_t out_stage_off, out_tile_bytes;
   void* dst;
   const void* bias;

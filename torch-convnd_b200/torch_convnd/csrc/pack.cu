@@ -246,6 +246,47 @@ __global__ void __launch_bounds__(32 * kFastWarps)
   }
 }
 
+// Per-channel sums of a 16-bit channels-last activation [N][S][C] (C a multiple of 8,
+// at most 256): the bias-gradient partials when dy is read in place. Block (b, n) covers
+// positions [b * kSumRows, +kSumRows) of image n; thread t reads 16-byte vectors (8
+// channels) of rows t / vpr, t / vpr + per_pass, ... in order, then the threads holding
+// the same channel group are added in thread order: a fixed summation order.
+constexpr int kSumRows = 512;
+
+template <typename T>
+__global__ void __launch_bounds__(256) channel_sum_cl16_kernel(const T* __restrict__ src,
+                                                               int64_t S, int C,
+                                                               float* __restrict__ partial) {
+  __shared__ float part[256][8];
+  const int vpr = C >> 3;  // 16-byte vectors per row
+  const int per_pass = 256 / vpr;
+  const int t = threadIdx.x;
+  const int v = t % vpr;
+  const int r0 = t / vpr;
+  float sum[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  const int64_t row_base = static_cast<int64_t>(blockIdx.x) * kSumRows;
+  const int64_t image = blockIdx.z;
+  if (r0 < per_pass) {
+    for (int r = r0; r < kSumRows; r += per_pass) {
+      const int64_t pos = row_base + r;
+      if (pos >= S) break;
+      const uint4 word = __ldg(reinterpret_cast<const uint4*>(src + (image * S + pos) * C) + v);
+      const T* x = reinterpret_cast<const T*>(&word);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) sum[i] += to_float(x[i]);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) part[t][i] = sum[i];
+  __syncthreads();
+  for (int c = t; c < C; c += blockDim.x) {
+    const int group = c >> 3;
+    float total = 0.0f;
+    for (int r = 0; r < per_pass; ++r) total += part[r * vpr + group][c & 7];
+    partial[(image * gridDim.x + blockIdx.x) * C + c] = total;
+  }
+}
+
 template <typename T, typename Tout, int kMode>
 __global__ void pack_weight_kernel(const T* __restrict__ w, Tout* __restrict__ dst,
                                    Tout* __restrict__ dst_small, PackWeightArgs a) {
@@ -438,9 +479,14 @@ bool pack16_fast_ok(const PackActArgs& a) {
          reinterpret_cast<uintptr_t>(a.dst) % 16 == 0;
 }
 
+bool channel_sums_fast_ok(const PackActArgs& a);
+int channel_sums(const PackActArgs& a, cudaStream_t stream);
+
 int pack_activations(const PackActArgs& args, cudaStream_t stream) {
   int rc;
-  if ((args.dtype == CND_BF16 || args.dtype == CND_F16) && pack16_fast_ok(args)) {
+  if (channel_sums_fast_ok(args)) {
+    return channel_sums(args, stream);
+  } else if ((args.dtype == CND_BF16 || args.dtype == CND_F16) && pack16_fast_ok(args)) {
     rc = args.dtype == CND_BF16 ? launch_pack_act16<__nv_bfloat16>(args, stream)
                                 : launch_pack_act16<__half>(args, stream);
   } else if (args.dtype == CND_BF16) {
@@ -554,7 +600,32 @@ int reduce_bias(const float* partial, int64_t batch, int groups, int blocks, int
   return CND_OK;
 }
 
+bool channel_sums_fast_ok(const PackActArgs& a) {
+  const int64_t channels = a.groups * a.cg;
+  return a.src_cl && a.dst == nullptr && (a.dtype == CND_BF16 || a.dtype == CND_F16) &&
+         channels % 8 == 0 && channels <= 256 && 256 % (channels / 8) == 0 &&
+         a.batch <= 65535 && reinterpret_cast<uintptr_t>(a.src) % 16 == 0;
+}
+
+int channel_sums(const PackActArgs& a, cudaStream_t stream) {
+  const int channels = static_cast<int>(a.groups * a.cg);
+  const int64_t blocks = (a.spatial + kSumRows - 1) / kSumRows;
+  const dim3 grid(static_cast<unsigned>(blocks), 1, static_cast<unsigned>(a.batch));
+  if (a.dtype == CND_BF16) {
+    channel_sum_cl16_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(
+        static_cast<const __nv_bfloat16*>(a.src), a.spatial, channels, a.chan_partial);
+  } else {
+    channel_sum_cl16_kernel<__half><<<grid, 256, 0, stream>>>(
+        static_cast<const __half*>(a.src), a.spatial, channels, a.chan_partial);
+  }
+  count_launch();
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(CND_ERR_CUDA, "channel_sum launch: %s", cudaGetErrorString(e));
+  return CND_OK;
+}
+
 int64_t pack_blocks(const PackActArgs& args) {
+  if (channel_sums_fast_ok(args)) return (args.spatial + kSumRows - 1) / kSumRows;
   if ((args.dtype == CND_BF16 || args.dtype == CND_F16) && pack16_fast_ok(args)) {
     const int per_block = fast_positions_per_block(args.c_pad);
     return (args.spatial + per_block - 1) / per_block;
