@@ -1117,9 +1117,18 @@ int launch_fprop(const ConvPass& pass, const FpropPlan& plan_in, cudaStream_t st
                            static_cast<cuuint64_t>(P.out[2]), static_cast<cuuint64_t>(P.out[1]),
                            static_cast<cuuint64_t>(P.out[0]),
                            static_cast<cuuint64_t>(pass.batch * P.out_outer_vol)};
-    cuuint64_t ostrides[4] = {row * P.out[2], row * P.out[2] * P.out[1],
-                              row * static_cast<cuuint64_t>(P.out_box_vol),
-                              row * static_cast<cuuint64_t>(P.out_box_vol) * P.out_outer_vol};
+    // byte strides of dims 1..4 (o2, o1, o0, merged); dim 0 (channels) is contiguous
+    cuuint64_t ostrides[4] = {row, row * P.out[2], row * P.out[2] * P.out[1],
+                              row * static_cast<cuuint64_t>(P.out_box_vol)};
+    // The map must stay inside the output tensor: its furthest element is the last one.
+    cuuint64_t last = (odims[0] - 1) * e;
+    for (int d = 1; d < 5; ++d) last += (odims[d] - 1) * ostrides[d - 1];
+    const cuuint64_t bytes = static_cast<cuuint64_t>(pass.batch) * P.out_volume * row;
+    if (last + e != bytes) {
+      return fail(CND_ERR_INVALID, "channels-last output map spans %llu bytes, tensor has %llu",
+                  static_cast<unsigned long long>(last + e),
+                  static_cast<unsigned long long>(bytes));
+    }
     cuuint32_t obox[5] = {static_cast<cuuint32_t>(P.out_span / e), static_cast<cuuint32_t>(P.b2),
                           static_cast<cuuint32_t>(P.b1), static_cast<cuuint32_t>(P.e0), 1};
     cuuint32_t oestr[5] = {1, 1, 1, 1, 1};
@@ -1151,6 +1160,12 @@ int launch_fprop(const ConvPass& pass, const FpropPlan& plan_in, cudaStream_t st
                               static_cast<cuuint64_t>(P.out[1]) * P.out[2] * e,
                               static_cast<cuuint64_t>(P.out_box_vol) * e,
                               static_cast<cuuint64_t>(P.out_volume) * e};
+    cuuint64_t last = (odims[0] - 1) * e;
+    for (int d = 1; d < 5; ++d) last += (odims[d] - 1) * ostrides[d - 1];
+    if (last + e != static_cast<cuuint64_t>(pass.batch * pass.groups * pass.n_real) *
+                        static_cast<cuuint64_t>(P.out_volume) * e) {
+      return fail(CND_ERR_INVALID, "output map does not cover the output tensor exactly");
+    }
     cuuint32_t obox[5] = {static_cast<cuuint32_t>(P.b2), static_cast<cuuint32_t>(P.b1),
                           static_cast<cuuint32_t>(P.e0), 1, static_cast<cuuint32_t>(pass.n_real)};
     cuuint32_t oestr[5] = {1, 1, 1, 1, 1};
