@@ -69,7 +69,8 @@ def test_c2_plan_uses_the_folded_tma_store_path():
 
 def test_six_tile_case_uses_six_tile_super_tiles():
     """The small GPU parity case SIX_TILE_CASE plans 6-tile folded super tiles for its
-    forward and dgrad (as c3's forward does), so the GPU test checks those kernels."""
+    forward (as c3's forward does) and the a2 fold for its dgrad (as c3's dgrad does), so
+    the GPU test checks those kernels."""
     from types import SimpleNamespace
 
     from test_gpu_parity import SIX_TILE_CASE
@@ -80,8 +81,10 @@ def test_six_tile_case_uses_six_tile_super_tiles():
                           dilation=dilation, groups=groups, dtype=torch.bfloat16)
     summary = _plan_summary(cfg)
     for line in summary.splitlines():
-        if line.startswith(("forward", "dgrad")):
+        if line.startswith("forward"):
             assert "x6 " in line and "fold=1" in line, line
+        if line.startswith("dgrad"):  # 16 channels: the a2 taps fold into N as well
+            assert "fold=1" in line and "k2f=3" in line, line
 
 
 def test_pointwise_axes_are_merged_and_unit_axes_dropped():
@@ -99,6 +102,15 @@ def test_pointwise_axes_are_merged_and_unit_axes_dropped():
                            padding=(0, 1, 0, 1, 0), dilation=(1,) * 5, groups=1,
                            dtype=torch.bfloat16)
     assert "forward: axes [6,7,5]" in _plan_summary(unit)
+
+
+def test_thin_passes_fold_the_a2_taps():
+    """Passes over 16 padded output channels (c3's dgrad, c4's forward and dgrad) fold the
+    a2 taps into N with the a0 taps (k2f=3), so the full-size cases check that epilogue."""
+    for cfg, passes in ((configs.C3, ("dgrad",)), (configs.C4, ("forward", "dgrad"))):
+        for line in _plan_summary(cfg).splitlines():
+            if line.startswith(passes):
+                assert "k2f=3" in line, line
 
 
 def test_thin_grouped_layer_runs_dense():

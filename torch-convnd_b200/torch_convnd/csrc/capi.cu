@@ -511,11 +511,11 @@ int cnd_plan_summary(const cnd_problem* problem, char* buffer, size_t size) {
     used += std::snprintf(text + used, sizeof(text) - used,
                           "] tcgen05 tile [%d,%d,%d] x%d halo(a0=%d,a1=%d) box %dx%dx%d "
                           "units=%d cblocks=%d N=%d stages=%d stage_bytes=%u nacc=%d parts=%d "
-                          "supers=%lld fold=%d tma_store=%d\n",
+                          "supers=%lld fold=%d k2f=%d tma_store=%d\n",
                           P.e0, P.b1, P.b2, P.mt, P.nshift0, P.nshift1, P.h0, P.h1, P.b2,
                           P.units, P.cblocks, P.n_pad, P.stages, P.stage_bytes, P.nacc,
                           plan.parts, static_cast<long long>(P.supers_total), P.fold,
-                          P.tma_store);
+                          P.k2f, P.tma_store);
   };
   if (bwd.bd > 1) {
     used += std::snprintf(text + used, sizeof(text) - used,
@@ -600,6 +600,7 @@ int cnd_forward(const cnd_problem* problem, const void* x, const void* w, const 
   pw.shift0 = plan.fwd_plan.shift0;
   pw.shift1 = plan.fwd_plan.shift1;
   pw.fold = plan.fwd_plan.fold;
+  pw.fold2 = plan.fwd_plan.fold2;
   for (int a = 0; a < 3; ++a) pw.k_box[a] = plan.fwd_plan.k_box[a];
   {
     TimedPass timed(5, stream);
@@ -810,6 +811,7 @@ int cnd_backward(const cnd_problem* problem, const void* dy, const void* x, cons
       pw.shift0 = plan.dgrad_plan.shift0;
       pw.shift1 = plan.dgrad_plan.shift1;
       pw.fold = plan.dgrad_plan.fold;
+      pw.fold2 = plan.dgrad_plan.fold2;
       for (int a = 0; a < 3; ++a) pw.k_box[a] = plan.dgrad_plan.k_box[a];
       {
         TimedPass timed(5, stream);

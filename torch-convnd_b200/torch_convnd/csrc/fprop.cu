@@ -167,6 +167,53 @@ struct OpCast<__half> {
 template <typename Traits, int kMT, bool kZero>
 __device__ __forceinline__ void epilogue_chunk(uint32_t dbase, int tile_col, int c, int n_pad,
                                                int used, const typename Traits::Out* group_bias,
+                                               int n_real, float (&out)[16]);
+
+// epilogue_chunk for passes with the a2 taps folded into N (k2f > 1): the M tile's
+// columns hold k2f blocks of n_pad, block j for a2 tap j at the tile row of its input
+// position. Output row r of a line (b2 rows, a power of two <= 32, aligned within the
+// warp) is the sum over j of block j at row r + j * d2: one shuffle per block. Rows whose
+// line position is at or past b2o come out as garbage and are not stored.
+template <typename Traits, int kMT>
+__device__ __forceinline__ void epilogue_chunk_k2(uint32_t dbase, int tile_col, int c,
+                                                  const FpropParams& P, int used,
+                                                  const typename Traits::Out* group_bias,
+                                                  float (&out)[16]) {
+  float b[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const int co = c * 16 + i;
+    b[i] = (group_bias != nullptr && co < P.n_real) ? Traits::load(group_bias + co) : 0.0f;
+    out[i] = 0.0f;
+  }
+  for (int j = 0; j < P.k2f; ++j) {
+    float v[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = 0.0f;
+    const uint32_t col = dbase + static_cast<uint32_t>(tile_col + j * P.n_pad + c * 16);
+    for (int a = 0; a < used; ++a) {
+      uint32_t raw[16];
+      const uint32_t addr = col + static_cast<uint32_t>(a * kMT * P.n_blk);
+      __syncwarp();
+      dev::tmem_load16(addr, raw);
+      dev::tmem_load_wait();
+      dev::tmem_zero16(addr);  // folded passes accumulate onto zeroed columns
+#pragma unroll
+      for (int i = 0; i < 16; ++i) v[i] += __uint_as_float(raw[i]);
+    }
+    const int shift = j * P.d[2];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) out[i] += __shfl_down_sync(0xffffffffu, v[i], shift, P.b2);
+  }
+  if (group_bias != nullptr) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) out[i] += b[i];
+  }
+}
+
+template <typename Traits, int kMT, bool kZero>
+__device__ __forceinline__ void epilogue_chunk(uint32_t dbase, int tile_col, int c, int n_pad,
+                                               int used, const typename Traits::Out* group_bias,
                                                int n_real, float (&out)[16]) {
   float b[16];
 #pragma unroll
@@ -262,6 +309,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = *tmem_slot;
   const int nshift = P.nshift0 * P.nshift1;
   const int work_per_super = P.units * nshift;
+  const int unit_rows = nshift * P.k2f;  // packed weight rows (taps) of one load unit
+  const int k2_units = P.k2f > 1 ? 1 : P.k[2];  // a2 taps walked as separate units
 
   if (warp == 0 && lane == 0) {
     // ------------------------------ TMA producer ------------------------------
@@ -284,7 +333,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const int x0 = S.q0 * kMT * P.e0 * P.s[0] - P.p[0];
       const int x1 = S.q1 * P.b1 * P.s[1] - P.p[1];
-      const int x2 = S.q2 * P.b2 * P.s[2] - P.p[2];
+      const int x2 = S.q2 * P.b2o * P.s[2] - P.p[2];
       int to[kMaxOuter];
 #pragma unroll
       for (int a = 0; a < kMaxOuter; ++a) to[a] = 0;
@@ -305,7 +354,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int32_t c0 = x0 + (P.nshift0 > 1 ? 0 : t0 * P.d[0]);
         const int32_t c1 = x1 + (P.nshift1 > 1 ? 0 : t1 * P.d[1]);
         const int32_t c2 = x2 + t2 * P.d[2];
-        const int32_t w_row = w_base + u * nshift;
+        const int32_t w_row = w_base + u * unit_rows;
         for (int cb = 0; cb < P.cblocks; ++cb) {
           if (!dev::mbar_wait(&empty[stage], phase ^ 1u, err, kSiteProducer, P.timeout_ns)) {
             ok = false;
@@ -327,8 +376,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             phase ^= 1u;
           }
         }
-        // Next unit: t2 fastest, then the unshifted a1 / a0 taps, then the outer taps.
-        if (++t2 == P.k[2]) {
+        // Next unit: t2 fastest (unless folded), then the unshifted a1 / a0 taps, then the
+        // outer taps.
+        if (++t2 == k2_units) {
           t2 = 0;
           bool carry = true;
           if (P.nshift1 == 1) {
@@ -382,11 +432,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tile_units = static_cast<uint32_t>(P.e0 * P.h1 * P.b2) * row_units;
     const uint32_t j0_units = static_cast<uint32_t>(P.d[0] * P.h1 * P.b2) * row_units;
     const uint32_t j1_units = static_cast<uint32_t>(P.d[1] * P.b2) * row_units;
-    const uint32_t btap_units = static_cast<uint32_t>(P.n_pad) * row_units;
+    // B rows and TMEM columns of one tap block: n_pad, or k2f * n_pad with the a2 fold.
+    const uint32_t btap_units = static_cast<uint32_t>(P.n_blk) * row_units;
     const uint32_t a_small_units = P.a_part_bytes >> 4;
     const uint32_t b_small_units = P.b_part_bytes >> 4;
-    const uint32_t tile_cols = static_cast<uint32_t>(P.n_pad);
-    const uint32_t acc_cols = static_cast<uint32_t>(kMT * P.n_pad);
+    const uint32_t tile_cols = static_cast<uint32_t>(P.n_blk);
+    const uint32_t acc_cols = static_cast<uint32_t>(kMT * P.n_blk);
     // Shifted taps of a stage are walked j1 fastest with incremental addresses; the A
     // offset steps by j1_units, or back to j1 = 0 and on to the next j0 at a j1 wrap.
     const uint32_t j0_wrap = j0_units - static_cast<uint32_t>(P.nshift1 - 1) * j1_units;
@@ -434,7 +485,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int lo = i > kLast ? i - kLast : 0;
                 const int hi = i < kFold - 1 ? i : kFold - 1;
                 const uint32_t idesc =
-                    P.idesc_base | (static_cast<uint32_t>(((hi - lo + 1) * P.n_pad) >> 3) << 17);
+                    P.idesc_base | (static_cast<uint32_t>(((hi - lo + 1) * P.n_blk) >> 3) << 17);
                 const uint32_t a_addr = a_j1 + static_cast<uint32_t>(i) * tile_units;
                 const uint32_t b_addr = b_j1 + static_cast<uint32_t>(lo) * btap_units;
                 const uint32_t d = dset + static_cast<uint32_t>(kLast - i + lo) * tile_cols;
@@ -516,13 +567,27 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int i2 = row % P.b2;
     const int i1 = (row / P.b2) % P.b1;
     const int i0 = row / (P.b2 * P.b1);
+    // Output rows of a tile: the first b2o of every line (all of them unless the a2 taps
+    // are folded); prow is a row's place among them, the staging order of TMA stores.
+    const bool line_ok = i2 < P.b2o;
+    const int prow = (i0 * P.b1 + i1) * P.b2o + i2;
+    const int tile_rows = P.e0 * P.b1 * P.b2o;
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
     const int used = work_per_super < P.nacc ? work_per_super : P.nacc;
     const OutT* bias = static_cast<const OutT*>(P.bias);
     OutT* out = static_cast<OutT*>(P.dst);
     const bool store_issuer = threadIdx.x == 64;  // warp 2, lane 0
     // TMEM column of M tile m's accumulator (descending when the a0 taps are folded).
-    auto tile_col = [&](int m) { return (kFold > 0 ? kMT - 1 - m : m) * P.n_pad; };
+    auto tile_col = [&](int m) { return (kFold > 0 ? kMT - 1 - m : m) * P.n_blk; };
+    // One 16-channel chunk of this thread's output row of M tile m.
+    auto chunk = [&](uint32_t dbase, int m, int c, const OutT* group_bias, float (&value)[16]) {
+      if (P.k2f > 1) {
+        epilogue_chunk_k2<Traits, kMT>(dbase, tile_col(m), c, P, used, group_bias, value);
+      } else {
+        epilogue_chunk<Traits, kMT, (kFold > 0)>(dbase, tile_col(m), c, P.n_pad, used,
+                                                 group_bias, P.n_real, value);
+      }
+    };
     if constexpr (kFold > 0) {
       // Folded MMAs all accumulate: start both accumulator buffers at zero.
       for (int c = 0; c < 2 * P.acc_stride; c += 16) {
@@ -545,7 +610,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       decode_super(P, st, S);
       const uint32_t dbase = lane_addr + static_cast<uint32_t>(buf * P.acc_stride);
       const int o1 = S.q1 * P.b1 + i1;
-      const int o2 = S.q2 * P.b2 + i2;
+      const int o2 = S.q2 * P.b2o + i2;
       const int64_t channel_base =
           (S.n * P.out_channels_total + static_cast<int64_t>(S.g) * P.n_real) * P.out_volume;
       const OutT* group_bias = bias != nullptr ? bias + static_cast<int64_t>(S.g) * P.n_real : nullptr;
@@ -563,17 +628,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           dev::named_barrier(1, 128);
           for (int c = 0; c < P.n_pad / 16; ++c) {
             float value[16];
-            epilogue_chunk<Traits, kMT, (kFold > 0)>(dbase, tile_col(m), c, P.n_pad, used,
-                                                     group_bias, P.n_real, value);
+            chunk(dbase, m, c, group_bias, value);
             alignas(16) OutT packed[16];
 #pragma unroll
             for (int i = 0; i < 16; ++i) packed[i] = Traits::cast(value[i]);
 #pragma unroll
             for (int v = 0; v < static_cast<int>(sizeof(OutT)); ++v) {  // 16-byte vectors
               const int off = c * 16 * static_cast<int>(sizeof(OutT)) + v * 16;
-              if (off < row_bytes) {
-                const uint32_t chunk = static_cast<uint32_t>(off) / span;
-                uint32_t addr = chunk * 128u * span + static_cast<uint32_t>(row) * span +
+              if (off < row_bytes && line_ok) {
+                const uint32_t part = static_cast<uint32_t>(off) / span;
+                uint32_t addr = part * 128u * span + static_cast<uint32_t>(prow) * span +
                                 static_cast<uint32_t>(off) % span;
                 addr ^= ((addr >> 7) & mask) << 4;
                 *reinterpret_cast<uint4*>(stage + addr) =
@@ -587,7 +651,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int k = 0; k * static_cast<int>(span) < row_bytes; ++k) {
               dev::tma_store_5d(&maps.out, stage + k * 128 * span,
                                 S.g * P.n_real + k * static_cast<int>(span / sizeof(OutT)),
-                                S.q2 * P.b2, S.q1 * P.b1, (S.q0 * kMT + m) * P.e0, merged);
+                                S.q2 * P.b2o, S.q1 * P.b1, (S.q0 * kMT + m) * P.e0, merged);
             }
             dev::bulk_commit_group();
           }
@@ -609,18 +673,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           dev::named_barrier(1, 128);
           for (int c = 0; c < P.n_pad / 16; ++c) {
             float value[16];
-            epilogue_chunk<Traits, kMT, (kFold > 0)>(dbase, tile_col(m), c, P.n_pad, used,
-                                                     group_bias, P.n_real, value);
+            chunk(dbase, m, c, group_bias, value);
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
               const int co = c * 16 + i;
-              if (co < P.n_real) stage_buf[co * 128 + row] = Traits::cast(value[i]);
+              if (co < P.n_real && line_ok) stage_buf[co * tile_rows + prow] = Traits::cast(value[i]);
             }
           }
           dev::fence_proxy_async();
           dev::named_barrier(1, 128);
           if (store_issuer) {
-            dev::tma_store_5d(&maps.out, stage_buf, S.q2 * P.b2, S.q1 * P.b1,
+            dev::tma_store_5d(&maps.out, stage_buf, S.q2 * P.b2o, S.q1 * P.b1,
                               (S.q0 * kMT + m) * P.e0, static_cast<int32_t>(S.outer_lin), nc0);
             dev::bulk_commit_group();
           }
@@ -634,15 +697,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         // Channels-last rows: this thread's position holds n_real consecutive channels.
         for (int m = 0; m < kMT; ++m) {
           const int o0 = (S.q0 * kMT + m) * P.e0 + i0;
-          const bool valid = o0 < P.out[0] && o1 < P.out[1] && o2 < P.out[2];
+          const bool valid = line_ok && o0 < P.out[0] && o1 < P.out[1] && o2 < P.out[2];
           const int64_t sp = S.outer_lin * P.out_box_vol +
                              (static_cast<int64_t>(o0) * P.out[1] + o1) * P.out[2] + o2;
           OutT* dst = out + (S.n * P.out_volume + sp) * P.out_channels_total +
                       static_cast<int64_t>(S.g) * P.n_real;
           for (int c = 0; c < P.n_pad / 16; ++c) {
             float value[16];
-            epilogue_chunk<Traits, kMT, (kFold > 0)>(dbase, tile_col(m), c, P.n_pad, used,
-                                                     group_bias, P.n_real, value);
+            chunk(dbase, m, c, group_bias, value);
             if (valid) store_run16<OutT>(dst + c * 16, value, P.n_real - c * 16);
           }
         }
@@ -653,14 +715,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       for (int m = 0; m < kMT; ++m) {
         const int o0 = (S.q0 * kMT + m) * P.e0 + i0;
-        const bool valid = o0 < P.out[0] && o1 < P.out[1] && o2 < P.out[2];
+        const bool valid = line_ok && o0 < P.out[0] && o1 < P.out[1] && o2 < P.out[2];
         const int64_t sp = S.outer_lin * P.out_box_vol +
                            (static_cast<int64_t>(o0) * P.out[1] + o1) * P.out[2] + o2;
         OutT* dst = out + channel_base + sp;
         for (int c = 0; c < P.n_pad / 16; ++c) {
           float value[16];
-          epilogue_chunk<Traits, kMT, (kFold > 0)>(dbase, tile_col(m), c, P.n_pad, used,
-                                                   group_bias, P.n_real, value);
+          chunk(dbase, m, c, group_bias, value);
           if (valid) {
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
@@ -825,7 +886,7 @@ bool fill_geometry(const ConvPass& pass, FpropParams* P) {
 }
 
 struct Candidate {
-  int e0, b1, b2, mt, shift0, shift1, row_bytes, fold;
+  int e0, b1, b2, mt, shift0, shift1, row_bytes, fold, k2f;
 };
 
 // Cycles of one M=128, K=16 (or tf32 K=8) MMA with N columns on this part: the larger of
@@ -851,6 +912,15 @@ bool layout_candidate(const ConvPass& pass, FpropParams* P, const Candidate& c, 
   P->b1 = c.b1;
   P->b2 = c.b2;
   P->mt = c.mt;
+  P->k2f = c.k2f;
+  P->b2o = c.b2;
+  if (c.k2f > 1) {
+    // a line of b2 input-aligned rows completes b2 - (k2 - 1) * d2 outputs; one line
+    // covers a short axis whole
+    P->b2o = c.b2 - (c.k2f - 1) * P->d[2];
+    if (P->b2o > P->out[2]) P->b2o = P->out[2];
+  }
+  P->n_blk = c.k2f * pass.n_pad;
   P->nshift0 = c.shift0 ? k0 : 1;
   P->nshift1 = c.shift1 ? k1 : 1;
   P->h0 = c.mt * c.e0 + (c.shift0 ? (k0 - 1) * P->d[0] : 0);
@@ -863,7 +933,7 @@ bool layout_candidate(const ConvPass& pass, FpropParams* P, const Candidate& c, 
   const uint32_t rows = static_cast<uint32_t>(P->h0 * P->h1 * c.b2);
   P->row_bytes = row_bytes;
   P->a_part_bytes = round_up(rows * row_bytes, 1024);
-  const int nshift = P->nshift0 * P->nshift1;
+  const int nshift = P->nshift0 * P->nshift1 * c.k2f;  // weight rows (taps) per unit
   P->b_part_bytes = round_up(static_cast<uint32_t>(nshift * pass.n_pad * row_bytes), 1024);
   P->b_off = P->a_part_bytes * parts;
   P->stage_bytes = P->b_off + P->b_part_bytes * parts;
@@ -901,16 +971,20 @@ bool plan_fprop(const ConvPass& pass, FpropPlan* plan) {
        (row_max < 64 || row_bytes < row_max / 4 || (pass.c_pad * es) % row_bytes != 0)) {
      break;
    }
-   for (int fold = 0; fold <= 1; ++fold) {
+   for (int fold = 0; fold <= 2; ++fold) {
     // Folding the a0 taps into N needs unit-stride a0 tiles of one slice, three a0 taps
-    // and 3 * n_pad <= 256.
+    // and 3 * n_pad <= 256. fold = 2 folds the a2 taps as well (k2f = k2): unit-stride a2,
+    // 3 * k2 * n_pad <= 256, lines of 16 or 32 rows.
     if (fold && (P.k[0] != 3 || P.d[0] != 1 || P.s[0] != 1 || 3 * pass.n_pad > 256)) {
       continue;
     }
+    const int k2f = fold == 2 ? P.k[2] : 1;
+    if (fold == 2 && (P.k[2] < 2 || P.s[2] != 1 || 3 * k2f * pass.n_pad > 256)) continue;
     for (int e0 = 1; e0 <= 128; e0 *= 2) {
     if (fold && e0 != 1) continue;
     for (int b2 = 8; b2 <= 128; b2 *= 2) {
       if (128 % (e0 * b2) != 0) continue;
+      if (fold == 2 && (b2 < 16 || b2 > 32 || b2 - (k2f - 1) * P.d[2] < 1)) continue;
       const int b1 = 128 / (e0 * b2);
       for (int mt : {1, 2, 4, 6, 8, 12}) {
         if (fold && mt < 2) continue;
@@ -923,20 +997,25 @@ bool plan_fprop(const ConvPass& pass, FpropPlan* plan) {
           for (int shift1 = 0; shift1 <= 1; ++shift1) {
             if (shift1 && (P.s[1] != 1 || P.k[1] == 1 || e0 != 1)) continue;
             FpropParams trial = P;
-            const Candidate cand{e0, b1, b2, mt, shift0, shift1, row_bytes, fold};
+            const Candidate cand{e0, b1, b2, mt, shift0, shift1, row_bytes, fold ? 1 : 0, k2f};
             if (!layout_candidate(pass, &trial, cand, parts)) continue;
+            const int n_blk = k2f * pass.n_pad;
             int nacc = 1;
             if (parts > 1 || tf32) {
               nacc = 8;
-              while (nacc > 1 && 2 * nacc * mt * pass.n_pad > 512) nacc /= 2;
+              while (nacc > 1 && 2 * nacc * mt * n_blk > 512) nacc /= 2;
+              // split-product (float32) passes keep at least two rotating accumulators:
+              // one accumulator over a whole unit walk grows the accumulation error
+              if (nacc < 2) continue;
             }
-            if (2 * nacc * mt * pass.n_pad > 512) continue;
+            if (2 * nacc * mt * n_blk > 512) continue;
             // Estimated cycles per useful output position.
+            const int b2o = trial.b2o;
             const double tiles0 = (P.out[0] + mt * e0 - 1) / (mt * e0);
             const double waste = (tiles0 * mt * e0 / P.out[0]) *
                                  (double((P.out[1] + b1 - 1) / b1) * b1 / P.out[1]) *
-                                 (double((P.out[2] + b2 - 1) / b2) * b2 / P.out[2]);
-            const int nshift = trial.nshift0 * trial.nshift1;
+                                 (double((P.out[2] + b2o - 1) / b2o) * b2 / P.out[2]);
+            const int nshift = trial.nshift0 * trial.nshift1 * k2f;
             const double units = double(P.taps) / nshift * trial.cblocks;
             double mma_total;
             if (fold) {
@@ -945,7 +1024,7 @@ bool plan_fprop(const ConvPass& pass, FpropPlan* plan) {
               for (int i = 0; i < mt + 2; ++i) {
                 const int lo = i > mt - 1 ? i - (mt - 1) : 0;
                 const int hi = i < 2 ? i : 2;
-                per_pass += mma_cycles((hi - lo + 1) * pass.n_pad);
+                per_pass += mma_cycles((hi - lo + 1) * n_blk);
               }
               mma_total = units * trial.nshift1 * trial.ksteps * products * per_pass;
             } else {
@@ -963,7 +1042,7 @@ bool plan_fprop(const ConvPass& pass, FpropPlan* plan) {
                 (cycles + 0.15 * l2_cycles + 0.05 * issue_cycles) * waste / (mt * 128.0);
             // Enough super tiles to fill the machine.
             const double supers = double(outer_count) * tiles0 *
-                                  ((P.out[1] + b1 - 1) / b1) * ((P.out[2] + b2 - 1) / b2);
+                                  ((P.out[1] + b1 - 1) / b1) * ((P.out[2] + b2o - 1) / b2o);
             const double fill = supers >= device_sms() ? 1.0 : device_sms() / supers;
             const double score = per_position * fill;
             if (score < best) {
@@ -982,12 +1061,12 @@ bool plan_fprop(const ConvPass& pass, FpropPlan* plan) {
   if (!found) return false;
   plan->score = best;
   P = chosen;
-  P.units = P.taps / (P.nshift0 * P.nshift1);
+  P.units = P.taps / (P.nshift0 * P.nshift1 * P.k2f);
   P.nsup[0] = (P.out[0] + P.mt * P.e0 - 1) / (P.mt * P.e0);
   P.nsup[1] = (P.out[1] + P.b1 - 1) / P.b1;
-  P.nsup[2] = (P.out[2] + P.b2 - 1) / P.b2;
+  P.nsup[2] = (P.out[2] + P.b2o - 1) / P.b2o;
   P.supers_total = outer_count * P.nsup[0] * P.nsup[1] * P.nsup[2];
-  P.acc_stride = P.nacc * P.mt * pass.n_pad;
+  P.acc_stride = P.nacc * P.mt * P.n_blk;
   P.tmem_cols = pow2_columns(2 * P.acc_stride);
   P.stages = static_cast<int>((200 * 1024) / P.stage_bytes);
   if (P.stages > 8) P.stages = 8;
@@ -1015,12 +1094,12 @@ bool plan_fprop(const ConvPass& pass, FpropPlan* plan) {
           ? (P.out_span > 0 && pass.n_real <= 256 &&
              pass.batch * P.out_outer_vol <= kInt32Max &&
              (pass.groups * pass.n_real * out_es) % 16 == 0)
-          : ((static_cast<int64_t>(P.out[2]) * out_es) % 16 == 0 && (P.b2 * out_es) % 16 == 0 &&
+          : ((static_cast<int64_t>(P.out[2]) * out_es) % 16 == 0 && (P.b2o * out_es) % 16 == 0 &&
              pass.n_real <= 256 && pass.batch * pass.groups * pass.n_real <= kInt32Max &&
              P.out_outer_vol <= kInt32Max);
   if (store_shape) {
     const bool two = static_cast<size_t>(P.stages) * P.stage_bytes + extra <= 110 * 1024 &&
-                     pow2_columns(2 * P.nacc * P.mt * pass.n_pad) <= 256;
+                     pow2_columns(2 * P.nacc * P.mt * P.n_blk) <= 256;
     const size_t cap = two ? 110 * 1024 - extra : 216 * 1024;
     const size_t staging = 2 * static_cast<size_t>(P.out_tile_bytes);
     if (cap > staging) {
@@ -1044,6 +1123,7 @@ bool plan_fprop(const ConvPass& pass, FpropPlan* plan) {
   plan->shift0 = P.nshift0 > 1;
   plan->shift1 = P.nshift1 > 1;
   plan->fold = P.fold;
+  plan->fold2 = P.k2f;
   plan->k_box[0] = P.k[0];
   plan->k_box[1] = P.k[1];
   plan->k_box[2] = P.k[2];
@@ -1089,7 +1169,7 @@ int launch_fprop(const ConvPass& pass, const FpropPlan& plan_in, cudaStream_t st
       return fail(CND_ERR_CUDA, "cuTensorMapEncodeTiled (activations) failed with code %d",
                   static_cast<int>(r));
     }
-    const int nshift = P.nshift0 * P.nshift1;
+    const int nshift = P.nshift0 * P.nshift1 * P.k2f;
     cuuint64_t wdims[3] = {static_cast<cuuint64_t>(pass.c_pad), static_cast<cuuint64_t>(pass.n_pad),
                            static_cast<cuuint64_t>(pass.groups * P.taps)};
     cuuint64_t wstrides[2] = {c, c * pass.n_pad};
@@ -1129,7 +1209,7 @@ int launch_fprop(const ConvPass& pass, const FpropPlan& plan_in, cudaStream_t st
                   static_cast<unsigned long long>(last + e),
                   static_cast<unsigned long long>(bytes));
     }
-    cuuint32_t obox[5] = {static_cast<cuuint32_t>(P.out_span / e), static_cast<cuuint32_t>(P.b2),
+    cuuint32_t obox[5] = {static_cast<cuuint32_t>(P.out_span / e), static_cast<cuuint32_t>(P.b2o),
                           static_cast<cuuint32_t>(P.b1), static_cast<cuuint32_t>(P.e0), 1};
     cuuint32_t oestr[5] = {1, 1, 1, 1, 1};
     const CUtensorMapSwizzle swizzle =
@@ -1166,7 +1246,7 @@ int launch_fprop(const ConvPass& pass, const FpropPlan& plan_in, cudaStream_t st
                         static_cast<cuuint64_t>(P.out_volume) * e) {
       return fail(CND_ERR_INVALID, "output map does not cover the output tensor exactly");
     }
-    cuuint32_t obox[5] = {static_cast<cuuint32_t>(P.b2), static_cast<cuuint32_t>(P.b1),
+    cuuint32_t obox[5] = {static_cast<cuuint32_t>(P.b2o), static_cast<cuuint32_t>(P.b1),
                           static_cast<cuuint32_t>(P.e0), 1, static_cast<cuuint32_t>(pass.n_real)};
     cuuint32_t oestr[5] = {1, 1, 1, 1, 1};
     const CUresult r = encode(&maps.out, out_type, 5, pass.dst, odims, ostrides, obox,

@@ -30,6 +30,13 @@ struct FpropParams {
   // sits at column (mt - 1 - m) * n_pad, so block j0 of slice i lands on tile i - j0.
   // Accumulators are zeroed by the epilogue and every MMA accumulates.
   int fold;
+  // k2f = k2 (3): the a2 taps of a unit are folded into N as well. A tile row then is an
+  // input-aligned position of a line of b2 rows and the MMA for a2 tap j2 writes the
+  // column block j2 of that row; output position r of a line is the sum over j2 of block
+  // j2 at row r + j2 (one warp-shuffle per tap in the epilogue, lines never cross a warp
+  // boundary), so a line of b2 rows yields b2o = b2 - k2 + 1 outputs. k2f = 1 otherwise
+  // (b2o = b2). n_blk = k2f * n_pad TMEM columns per M tile.
+  int k2f, b2o, n_blk;
   int h0, h1;            // halo box extents (rows) along a0 / a1
   int nsup[3];
   int64_t supers_total;
@@ -66,7 +73,7 @@ struct FpropPlan {
   double score;      // the cost model's estimated cycles per output position (lower wins)
   size_t smem;
   // weight packing order (see PackWeightArgs::unit_order)
-  int shift0, shift1, fold;
+  int shift0, shift1, fold, fold2;
   int k_box[3];
 };
 

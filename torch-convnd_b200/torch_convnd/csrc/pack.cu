@@ -136,18 +136,25 @@ __global__ void __launch_bounds__(256) pack_act_kernel(const Tin* __restrict__ s
 }
 
 // Original tap index of row `row` of the packed weights. Rows are grouped by load unit:
-// unit = (outer taps, t0 unless shifted, t1 unless shifted, t2) row-major, and within a
-// unit the shifted taps (t0 if shift0, t1 if shift1) row-major.
+// unit = (outer taps, t0 unless shifted, t1 unless shifted, t2 unless folded) row-major,
+// and within a unit the shifted taps (t0 if shift0, t1 if shift1) row-major, or with the
+// a0 fold j1-major and j0 within; with the a2 fold (fold2 = k2) j2 is innermost.
 __device__ __forceinline__ int packed_row_tap(int row, int k0, int k1, int k2, int shift0,
-                                              int shift1, int fold) {
+                                              int shift1, int fold, int fold2) {
   const int n1 = shift1 ? k1 : 1;
   const int n0 = shift0 ? k0 : 1;
-  const int ls = row % (n0 * n1);
-  int rest = row / (n0 * n1);
+  const int n2 = fold2 > 1 ? k2 : 1;
+  const int inner = row % (n0 * n1 * n2);
+  int rest = row / (n0 * n1 * n2);
+  const int ls = inner / n2;
+  const int j2 = inner % n2;
   const int j1 = fold ? ls / n0 : ls % n1;
   const int j0 = fold ? ls % n0 : ls / n1;
-  const int t2 = rest % k2;
-  rest /= k2;
+  int t2 = j2;
+  if (n2 == 1) {
+    t2 = rest % k2;
+    rest /= k2;
+  }
   int t1 = j1, t0 = j0;
   if (!shift1) {
     t1 = rest % k1;
@@ -301,7 +308,7 @@ __global__ void pack_weight_kernel(const T* __restrict__ w, Tout* __restrict__ d
     const int row = static_cast<int>(r % a.taps);
     const int g = static_cast<int>(r / a.taps);
     const int t = packed_row_tap(row, a.k_box[0], a.k_box[1], a.k_box[2], a.shift0, a.shift1,
-                                 a.fold);
+                                 a.fold, a.fold2);
     float v = 0.0f;
     // Block-diagonal packing: weight row co holds input channels [gb * cin_b, +cin_b) of
     // its group gb = co / cout_b; the other columns stay zero.

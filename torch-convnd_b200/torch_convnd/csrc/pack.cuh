@@ -34,6 +34,9 @@ struct PackWeightArgs {
   int k_box[3];
   int shift0, shift1;
   int fold;  // 1: within a unit the a0 taps are consecutive (j0 fastest), else a1 taps
+  // > 1: the k2 taps of box axis a2 are inside every unit too, fastest of all (each
+  // (j1, j0) block of the B operand is [j2][n]: the a2 taps folded into the MMA N)
+  int fold2;
   // > 1: the weights of a problem with bd groups packed as one dense block-diagonal
   // matrix (groups == 1, cout_g / cin_g = all channels; off-diagonal blocks are zero)
   int bd;
