@@ -1004,9 +1004,10 @@ bool plan_fprop(const ConvPass& pass, FpropPlan* plan) {
             if (parts > 1 || tf32) {
               nacc = 8;
               while (nacc > 1 && 2 * nacc * mt * n_blk > 512) nacc /= 2;
-              // split-product (float32) passes keep at least two rotating accumulators:
-              // one accumulator over a whole unit walk grows the accumulation error
-              if (nacc < 2) continue;
+              // split-product (float32) passes keep at least two rotating accumulators
+              // (one accumulator over a whole unit walk grows the accumulation error);
+              // with the a2 fold the k2f column blocks already split every chain
+              if (nacc < 2 && k2f < 2) continue;
             }
             if (2 * nacc * mt * n_blk > 512) continue;
             // Estimated cycles per useful output position.
