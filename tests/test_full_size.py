@@ -113,6 +113,14 @@ def test_thin_passes_fold_the_a2_taps():
                 assert "k2f=3" in line, line
 
 
+def test_strided_dgrad_runs_as_phase_sub_convolutions():
+    """A stride-2 Conv4d (c5's first layer with an input gradient) plans its dgrad as the
+    16 residue classes of dx positions, each a stride-1 tcgen05 pass."""
+    summary = _plan_summary(configs.C5_LAYERS[0])
+    assert "dgrad: 16 phase sub-convolutions" in summary, summary
+    assert "generic" not in summary, summary
+
+
 def test_thin_grouped_layer_runs_dense():
     """c5's grouped layer (4 groups of 8 channels) runs as one dense problem with
     block-diagonal weights; its full-size case below checks that plan."""

@@ -84,11 +84,13 @@ def _problem_mask(x, w, stride, padding, dilation, groups):
 
 @pytest.mark.parametrize(
     ("name", "expected"),
-    [("c2r", 7), ("c3r", 7), ("c4r", 7), ("c5l1r", 5), ("c5l2r", 7), ("c5l3r", 7), ("c1", 7)],
+    [("c2r", 7), ("c3r", 7), ("c4r", 7), ("c5l1r", 7), ("c5l2r", 7), ("c5l3r", 7), ("c1", 7),
+     ("strided_bf16", 7)],
 )
 def test_configs_run_on_tensor_cores(name, expected, golden):
-    """The BASELINE configurations take the tcgen05 path for every pass they need
-    (c5's first layer is strided: its dgrad is never requested in training)."""
+    """The BASELINE configurations take the tcgen05 path for every pass, strided input
+    gradients included (phase sub-convolutions; c5's first layer never requests one in
+    training, but a strided layer with an input gradient no longer leaves the fast path)."""
     record = golden(name)
     c = record["config"]
     mask = _problem_mask(record["x"], record["weight"], c["stride"], c["padding"], c["dilation"],
@@ -124,6 +126,14 @@ def _sweep():
     cases.append((4, 2, 32, 32, (9, 10, 4, 6), (3, 3, 1, 1), (1,) * 4, (2, 2, 0, 0),
                   (2, 2, 1, 1), 4))
     cases.append((6, 1, 16, 16, (1, 1, 1, 1, 1, 1), (1,) * 6, (1,) * 6, (0,) * 6, (1,) * 6, 1))
+    # strided input gradients as phase sub-convolutions: mixed strides and paddings,
+    # dilation sharing a factor with the stride, and a kernel-1 stride-2 axis whose odd
+    # positions receive no tap (zeroed residue classes)
+    cases.append((4, 1, 16, 32, (7, 8, 6, 9), (3,) * 4, (2, 1, 2, 1), (0, 1, 2, 1),
+                  (1, 1, 1, 2), 1))
+    cases.append((3, 2, 16, 16, (9, 10, 11), (3, 2, 1), (2, 3, 2), (1, 0, 0), (2, 1, 1), 1))
+    cases.append((4, 2, 32, 16, (8, 7, 9, 6), (3, 3, 2, 3), (2, 2, 1, 1), (1, 1, 0, 1),
+                  (1, 1, 1, 1), 2))
     return cases
 
 

@@ -165,6 +165,16 @@ struct Plan {
   bool dgrad_bf16 = false;
   ConvPass fwd{}, dgrad{};
   FpropPlan fwd_plan{}, dgrad_plan{};
+  // Strided dgrad as phase sub-convolutions (one per residue class of dx positions modulo
+  // the strides): nphase > 0 replaces the single dgrad pass; phase_empty: some residue
+  // class has no tap, so dx is zeroed before the phases write theirs.
+  static constexpr int kMaxPhases = 16;
+  int nphase = 0;
+  bool phase_empty = false;
+  ConvPass phase[kMaxPhases]{};
+  FpropPlan phase_plan[kMaxPhases]{};
+  PackWeightArgs phase_taps[kMaxPhases]{};
+  Region w_phase[kMaxPhases], w_phase_small[kMaxPhases];
   WgradPass wgrad{};
   // weight-gradient operands: 16-bit problems reuse the packed x / dy; float32 problems pack
   // x and dy again as 3 (3xtf32 mode) or 2 (tf32 mode) bfloat16 terms.
@@ -280,6 +290,77 @@ Region take(size_t* cursor, size_t bytes) {
   return r;
 }
 
+int gcd_int(int64_t a, int64_t b) {
+  while (b != 0) {
+    const int64_t t = a % b;
+    a = b;
+    b = t;
+  }
+  return static_cast<int>(a);
+}
+
+// Splits the input gradient of a strided problem into phase sub-convolutions. Residue
+// class r (per axis, 0 <= r < s) holds dx positions s * j + r; the taps that reach it are
+// those with (r + p - t * d) divisible by s, an arithmetic progression of step s / gcd(d, s)
+// whose dy offsets (r + p - t * d) / s step by d / gcd(d, s). In dy coordinates the class is
+// a stride-1 convolution with that many taps, dilation d / g and padding -(smallest offset),
+// taps ordered by ascending offset (descending t), written to the strided sub-grid
+// (the reference's fold, convnd_cuda.cu:147-169 / input_column_offset convnd.h:79-104,
+// as dense sub-convolutions). False when there are too many classes or a class does not
+// fit the tcgen05 pass.
+bool plan_phases(const Axes& ax, const ConvPass& templ, Plan* plan) {
+  int64_t classes = 1;
+  for (int a = 0; a < ax.rank; ++a) classes *= ax.s[a];
+  if (classes > Plan::kMaxPhases || ax.rank > kMaxFastRank) return false;
+  plan->nphase = 0;
+  plan->phase_empty = false;
+  for (int64_t c = 0; c < classes; ++c) {
+    int64_t rest = c;
+    ConvPass ph = templ;
+    PackWeightArgs taps{};
+    ph.rank = ax.rank;
+    ph.out_strided = 1;
+    taps.phase_rank = ax.rank;
+    bool empty = false;
+    for (int a = ax.rank - 1; a >= 0; --a) {
+      const int64_t s = ax.s[a], r = rest % s;
+      rest /= s;
+      int64_t count = 0, t_last = -1;
+      for (int64_t t = 0; t < ax.k[a]; ++t) {
+        if ((r + ax.p[a] - t * ax.d[a]) % s == 0) {
+          ++count;
+          t_last = t;
+        }
+      }
+      const int64_t g = gcd_int(ax.d[a], s);
+      ph.in[a] = ax.out[a];
+      ph.out[a] = (ax.in[a] - r + s - 1) / s;
+      ph.k[a] = count > 0 ? count : 1;
+      ph.s[a] = 1;
+      ph.d[a] = ax.d[a] / g;
+      ph.p[a] = count > 0 ? -((r + ax.p[a] - t_last * ax.d[a]) / s) : 0;
+      ph.out_mul[a] = s;
+      ph.out_add[a] = r;
+      ph.out_full[a] = ax.in[a];
+      taps.k_sub[a] = static_cast<int>(ph.k[a]);
+      taps.k_full[a] = static_cast<int>(ax.k[a]);
+      taps.tap_first[a] = static_cast<int>(t_last);
+      taps.tap_step[a] = -static_cast<int>(s / g);
+      if (count == 0 || ph.out[a] <= 0) empty = true;
+    }
+    if (empty) {
+      plan->phase_empty = true;
+      continue;
+    }
+    const int i = plan->nphase;
+    if (!plan_fprop(ph, &plan->phase_plan[i])) return false;
+    plan->phase[i] = ph;
+    plan->phase_taps[i] = taps;
+    ++plan->nphase;
+  }
+  return plan->nphase > 0;
+}
+
 // Decides the kernel family of every pass and the workspace layout.
 // `forward` selects the forward plan; otherwise `mask` selects the backward passes.
 void make_plan(const cnd_problem& p, bool forward, const int32_t* mask, Plan* plan) {
@@ -369,6 +450,25 @@ void make_plan(const cnd_problem& p, bool forward, const int32_t* mask, Plan* pl
     dg.out_dtype = p.dtype;
     dg.out_cl = plan->x_cl ? 1 : 0;
     const bool dgrad_ok = !strided && !wide_pad && plan->cin_g <= 256;
+    if (strided && plan->cin_g <= 256) {
+      // Strided: phase sub-convolutions over the packed dy (float32 problems on the
+      // bf16 hi/lo parts when that halves the K steps, as below).
+      ConvPass templ = dg;
+      const int64_t bf16_pad = pad_channels(kOpBF16, plan->cout_g, 16);
+      if (plan->split3 && bf16_pad / 16 < plan->dy_pad / 8) {
+        templ.op = kOpBF16;
+        templ.c_pad = static_cast<int>(bf16_pad);
+        templ.split3 = 0;
+        plan->dgrad_bf16 = true;
+      }
+      if (plan_phases(reduced, templ, plan)) {
+        dg = templ;
+        plan->fast_dgrad = true;
+      } else {
+        plan->dgrad_bf16 = false;
+        plan->nphase = 0;
+      }
+    }
     // One bf16 K step covers 16 dy channels, one TF32 step 8: the bf16 parts win when
     // they need fewer K steps (dy channels >= 16); below that they would only lose
     // precision.
@@ -383,7 +483,7 @@ void make_plan(const cnd_problem& p, bool forward, const int32_t* mask, Plan* pl
         plan->fast_dgrad = true;
       }
     }
-    if (!plan->dgrad_bf16) {
+    if (!plan->dgrad_bf16 && plan->nphase == 0) {
       plan->fast_dgrad = dgrad_ok && plan_best(&dg, &plan->dgrad_plan, variants, nvariants, true);
     }
   }
@@ -425,7 +525,17 @@ void make_plan(const cnd_problem& p, bool forward, const int32_t* mask, Plan* pl
     plan->bias_partial = take(&cursor, static_cast<size_t>(p.batch * plan->groups) * blocks *
                                            plan->cout_g * sizeof(float));
   }
-  if (plan->fast_dgrad) {
+  if (plan->fast_dgrad && plan->nphase > 0) {
+    const size_t wes = plan->dgrad_bf16 ? 2 : es;
+    for (int i = 0; i < plan->nphase; ++i) {
+      int64_t sub = 1;
+      for (int a = 0; a < plan->phase[i].rank; ++a) sub *= plan->phase[i].k[a];
+      const size_t bytes = static_cast<size_t>(plan->groups * sub * plan->phase[i].n_pad *
+                                               plan->phase[i].c_pad) * wes;
+      plan->w_phase[i] = take(&cursor, bytes);
+      if (plan->split3 || plan->dgrad_bf16) plan->w_phase_small[i] = take(&cursor, bytes);
+    }
+  } else if (plan->fast_dgrad) {
     const size_t bytes =
         static_cast<size_t>(plan->groups * taps * plan->dgrad.n_pad * plan->dgrad.c_pad) * es;
     plan->w_dg = take(&cursor, bytes);
@@ -522,7 +632,18 @@ int cnd_plan_summary(const cnd_problem* problem, char* buffer, size_t size) {
                           "groups: %d run dense (block-diagonal weights)\n", bwd.bd);
   }
   describe("forward", fwd.fast_fwd, fwd.fwd_plan, fwd.fwd);
-  describe("dgrad", bwd.fast_dgrad, bwd.dgrad_plan, bwd.dgrad);
+  if (bwd.fast_dgrad && bwd.nphase > 0) {
+    used += std::snprintf(text + used, sizeof(text) - used,
+                          "dgrad: %d phase sub-convolutions of the strided input gradient%s\n",
+                          bwd.nphase, bwd.phase_empty ? " (dx zeroed first)" : "");
+    for (int i = 0; i < bwd.nphase && used < 3000; ++i) {
+      char name[32];
+      std::snprintf(name, sizeof(name), "dgrad phase %d", i);
+      describe(name, true, bwd.phase_plan[i], bwd.phase[i]);
+    }
+  } else {
+    describe("dgrad", bwd.fast_dgrad, bwd.dgrad_plan, bwd.dgrad);
+  }
   if (bwd.fast_wgrad) {
     char detail[256];
     cnd::describe_wgrad_pass(bwd.wgrad, detail, sizeof(detail));
@@ -792,7 +913,54 @@ int cnd_backward(const cnd_problem* problem, const void* dy, const void* x, cons
     }
   }
   // ---- input gradient ----
-  if (output_mask[0]) {
+  if (output_mask[0] && plan.fast_dgrad && plan.nphase > 0) {
+    // strided: one sub-convolution per residue class of dx positions
+    if (plan.phase_empty) {
+      const size_t bytes =
+          static_cast<size_t>(p.batch * p.channels * p.input_volume) * element_bytes(p.dtype);
+      cudaMemsetAsync(dx, 0, bytes, stream);
+    }
+    for (int i = 0; i < plan.nphase; ++i) {
+      const FpropPlan& fp = plan.phase_plan[i];
+      PackWeightArgs pw = plan.phase_taps[i];
+      int64_t sub = 1;
+      for (int a = 0; a < plan.phase[i].rank; ++a) sub *= plan.phase[i].k[a];
+      pw.w = w;
+      pw.dst = at(workspace, plan.w_phase[i]);
+      pw.dst_small = at(workspace, plan.w_phase_small[i]);
+      pw.groups = static_cast<int>(plan.groups);
+      pw.bd = plan.bd;
+      pw.cout_g = static_cast<int>(plan.cout_g);
+      pw.cin_g = static_cast<int>(plan.cin_g);
+      pw.taps = static_cast<int>(sub);
+      pw.taps_w = static_cast<int>(p.kernel_volume);
+      pw.n_pad = plan.phase[i].n_pad;
+      pw.c_pad = plan.phase[i].c_pad;
+      pw.dtype = p.dtype;
+      pw.mode = plan.dgrad_bf16 ? 4 : plan.pack_mode;
+      pw.dgrad = 1;
+      pw.shift0 = fp.shift0;
+      pw.shift1 = fp.shift1;
+      pw.fold = fp.fold;
+      pw.fold2 = fp.fold2;
+      for (int a = 0; a < 3; ++a) pw.k_box[a] = fp.k_box[a];
+      {
+        TimedPass timed(5, stream);
+        rc = pack_weights(pw, stream);
+      }
+      if (rc != CND_OK) return rc;
+      ConvPass pass = plan.phase[i];
+      pass.act = plan.dgrad_bf16 ? at(workspace, plan.wg_dy[0]) : dy_operand;
+      pass.act_small = at(workspace, plan.dgrad_bf16 ? plan.wg_dy[1] : plan.dy_pack_small);
+      pass.wt = pw.dst;
+      pass.wt_small = pw.dst_small;
+      pass.dst = dx;
+      pass.bias = nullptr;
+      TimedPass timed(2, stream);
+      rc = launch_fprop(pass, fp, stream, wait_timeout_ns(), 0);
+      if (rc != CND_OK) return rc;
+    }
+  } else if (output_mask[0]) {
     if (plan.fast_dgrad) {
       PackWeightArgs pw{};
       pw.w = w;

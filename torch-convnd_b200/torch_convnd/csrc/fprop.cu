@@ -572,6 +572,22 @@ __global__ void __launch_bounds__(kThreads, 1)
     const bool line_ok = i2 < P.b2o;
     const int prow = (i0 * P.b1 + i1) * P.b2o + i2;
     const int tile_rows = P.e0 * P.b1 * P.b2o;
+    // Spatial element offset of output (outer position of S, o0, o1, o2) in the output
+    // tensor, and that tensor's positions per image (a phase of a strided input gradient
+    // lands on a strided sub-grid of a larger tensor).
+    auto out_offset = [&](const Super& S, int o0, int o1, int o2) -> int64_t {
+      if (!P.out_strided) {
+        return S.outer_lin * P.out_box_vol + (static_cast<int64_t>(o0) * P.out[1] + o1) * P.out[2] + o2;
+      }
+      int64_t off = P.phase_base + o0 * P.ostride_box[0] + o1 * P.ostride_box[1] +
+                    o2 * P.ostride_box[2];
+#pragma unroll
+      for (int a = 0; a < kMaxOuter; ++a) {
+        if (a < P.n_outer) off += S.o[a] * P.ostride_o[a];
+      }
+      return off;
+    };
+    const int64_t out_vol = P.out_strided ? P.out_volume_full : P.out_volume;
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
     const int used = work_per_super < P.nacc ? work_per_super : P.nacc;
     const OutT* bias = static_cast<const OutT*>(P.bias);
@@ -612,7 +628,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int o1 = S.q1 * P.b1 + i1;
       const int o2 = S.q2 * P.b2o + i2;
       const int64_t channel_base =
-          (S.n * P.out_channels_total + static_cast<int64_t>(S.g) * P.n_real) * P.out_volume;
+          (S.n * P.out_channels_total + static_cast<int64_t>(S.g) * P.n_real) * out_vol;
       const OutT* group_bias = bias != nullptr ? bias + static_cast<int64_t>(S.g) * P.n_real : nullptr;
       if (P.tma_store && P.out_cl) {
         // Channels-last rows: stage the tile as [position][channel] (swizzled 16-byte
@@ -698,9 +714,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int m = 0; m < kMT; ++m) {
           const int o0 = (S.q0 * kMT + m) * P.e0 + i0;
           const bool valid = line_ok && o0 < P.out[0] && o1 < P.out[1] && o2 < P.out[2];
-          const int64_t sp = S.outer_lin * P.out_box_vol +
-                             (static_cast<int64_t>(o0) * P.out[1] + o1) * P.out[2] + o2;
-          OutT* dst = out + (S.n * P.out_volume + sp) * P.out_channels_total +
+          const int64_t sp = out_offset(S, o0, o1, o2);
+          OutT* dst = out + (S.n * out_vol + sp) * P.out_channels_total +
                       static_cast<int64_t>(S.g) * P.n_real;
           for (int c = 0; c < P.n_pad / 16; ++c) {
             float value[16];
@@ -716,8 +731,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int m = 0; m < kMT; ++m) {
         const int o0 = (S.q0 * kMT + m) * P.e0 + i0;
         const bool valid = line_ok && o0 < P.out[0] && o1 < P.out[1] && o2 < P.out[2];
-        const int64_t sp = S.outer_lin * P.out_box_vol +
-                           (static_cast<int64_t>(o0) * P.out[1] + o1) * P.out[2] + o2;
+        const int64_t sp = out_offset(S, o0, o1, o2);
         OutT* dst = out + channel_base + sp;
         for (int c = 0; c < P.n_pad / 16; ++c) {
           float value[16];
@@ -726,7 +740,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
               const int co = c * 16 + i;
-              if (co < P.n_real) dst[static_cast<int64_t>(co) * P.out_volume] = Traits::cast(value[i]);
+              if (co < P.n_real) dst[static_cast<int64_t>(co) * out_vol] = Traits::cast(value[i]);
             }
           }
         }
@@ -1079,6 +1093,28 @@ bool plan_fprop(const ConvPass& pass, FpropPlan* plan) {
   P.tma_store = 0;
   P.out_tile_bytes = round_up(static_cast<uint32_t>(pass.n_real * 128 * out_es), 1024);
   P.out_cl = pass.out_cl;
+  P.out_strided = pass.out_strided;
+  if (pass.out_strided) {
+    // element strides of the full tensor's axes (row-major), times the phase multipliers
+    int64_t stride_full[kMaxFastRank];
+    int64_t vol = 1;
+    for (int a = pass.rank - 1; a >= 0; --a) {
+      stride_full[a] = vol;
+      vol *= pass.out_full[a];
+    }
+    P.out_volume_full = vol;
+    P.phase_base = 0;
+    for (int a = 0; a < pass.rank; ++a) P.phase_base += pass.out_add[a] * stride_full[a];
+    const int n_outer = P.n_outer;
+    const int lead = 3 - (pass.rank - n_outer);
+    for (int a = 0; a < kMaxOuter; ++a) {
+      P.ostride_o[a] = a < n_outer ? pass.out_mul[a] * stride_full[a] : 0;
+    }
+    for (int a = 0; a < 3; ++a) {
+      const int src = a - lead + n_outer;
+      P.ostride_box[a] = a < lead ? 0 : pass.out_mul[src] * stride_full[src];
+    }
+  }
   // Channels-last rows go through TMA stores when one position's channels form 16 bytes
   // or a swizzle width (32 / 64 / 128 bytes), or whole 128-byte chunks.
   const int cl_row = pass.n_real * out_es;
@@ -1090,7 +1126,7 @@ bool plan_fprop(const ConvPass& pass, FpropPlan* plan) {
       P.out_span = 128;
     }
   }
-  const bool store_shape =
+  const bool store_shape = pass.out_strided ? false :
       pass.out_cl
           ? (P.out_span > 0 && pass.n_real <= 256 &&
              pass.batch * P.out_outer_vol <= kInt32Max &&

@@ -58,6 +58,12 @@ struct FpropParams {
   // store per chunk; otherwise each thread stores its position's channels directly.
   int out_cl;
   uint32_t out_span;
+  // Strided output (ConvPass::out_strided): element offset of output position (outer o,
+  // box o0..o2) is phase_base + sum o * ostride, over a tensor of out_volume_full positions
+  // per image; direct stores only.
+  int out_strided;
+  int64_t phase_base, out_volume_full;
+  int64_t ostride_box[3], ostride_o[kMaxOuter];
   uint32_t out_stage_off, out_tile_bytes;
   void* dst;
   const void* bias;

@@ -320,11 +320,25 @@ __global__ void pack_weight_kernel(const T* __restrict__ w, Tout* __restrict__ d
         v = to_float(w[((static_cast<int64_t>(g) * a.cout_g + nn) * cin_b + cw) * a.taps + t]);
       }
     } else {
-      // dgrad operand: B[n = input channel][k = output channel] of the flipped tap
+      // dgrad operand: B[n = input channel][k = output channel] of the flipped tap, or of
+      // the phase sub-kernel's mapped tap
       if (nn < a.cin_g && c < a.cout_g && nn / cin_b == c / cout_b) {
         const int nw = nn - (c / cout_b) * cin_b;
-        v = to_float(w[((static_cast<int64_t>(g) * a.cout_g + c) * cin_b + nw) * a.taps +
-                       (a.taps - 1 - t)]);
+        int tw = a.taps - 1 - t;
+        int taps_w = a.taps;
+        if (a.phase_rank > 0) {
+          int rest = t, u[kMaxFastRank];
+          for (int ax = a.phase_rank - 1; ax >= 0; --ax) {
+            u[ax] = rest % a.k_sub[ax];
+            rest /= a.k_sub[ax];
+          }
+          tw = 0;
+          for (int ax = 0; ax < a.phase_rank; ++ax) {
+            tw = tw * a.k_full[ax] + a.tap_first[ax] + u[ax] * a.tap_step[ax];
+          }
+          taps_w = a.taps_w;
+        }
+        v = to_float(w[((static_cast<int64_t>(g) * a.cout_g + c) * cin_b + nw) * taps_w + tw]);
       }
     }
     split_value<Tout, kMode>(v, dst, dst_small, nullptr, i);

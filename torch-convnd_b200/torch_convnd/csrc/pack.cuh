@@ -5,6 +5,8 @@
 
 #include <cstdint>
 
+#include "internal.h"
+
 namespace cnd {
 
 // mode: 0 = copy, 1 = TF32 big + small (3xTF32), 2 = round to TF32, 3 = fp32 -> bf16
@@ -40,6 +42,14 @@ struct PackWeightArgs {
   // > 1: the weights of a problem with bd groups packed as one dense block-diagonal
   // matrix (groups == 1, cout_g / cin_g = all channels; off-diagonal blocks are zero)
   int bd;
+  // > 0 (dgrad only): the packed taps are the sub-kernel of one phase of a strided input
+  // gradient. Packed tap u (row-major over k_sub[0..phase_rank)) is the weight's tap
+  // t_a = tap_first[a] + u_a * tap_step[a] (row-major over k_full), taken as is (the
+  // phase's tap order already is the flipped one); the weight has taps_w taps per (co, ci).
+  int phase_rank;
+  int taps_w;
+  int k_sub[kMaxFastRank], k_full[kMaxFastRank], tap_first[kMaxFastRank],
+      tap_step[kMaxFastRank];
 };
 
 int pack_activations(const PackActArgs& args, cudaStream_t stream);

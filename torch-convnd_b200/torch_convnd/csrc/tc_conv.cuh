@@ -34,6 +34,11 @@ struct ConvPass {
   const void* bias; // [G*n_real] of out_dtype, or null
   int out_dtype;    // cnd_dtype
   int out_cl;
+  // Strided output (one phase of a strided input gradient): output position j of axis a
+  // goes to position out_mul[a] * j + out_add[a] of a tensor whose axes have extents
+  // out_full[a]; out_strided = 0 means the output is exactly out[].
+  int out_strided;
+  int64_t out_mul[kMaxFastRank], out_add[kMaxFastRank], out_full[kMaxFastRank];
 };
 
 // Weight-gradient pass: dW[g][tap][ci][co] partials of
