@@ -62,6 +62,8 @@ def parse_args(argv=None):
     parser.add_argument("--c5-layout", default="channels-last",
                         choices=("channels-last", "channels-first"),
                         help="activation layout of the c5 training step")
+    parser.add_argument("--c5-gelu", default="fused", choices=("fused", "separate"),
+                        help="GELU of the c5 step inside the convolutions or as its own pass")
     parser.add_argument("--no-e2e", action="store_true")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--cpu-sample-images", type=int, default=1)
@@ -571,7 +573,10 @@ class C5Step:
         self.layers = [layer.with_batch(shard) for layer in configs.C5_LAYERS]
         self.job_flops = configs.C5_STEP_FLOPS
         self.dtype = "bf16"
-        self.net = configs.c5_network(torch_convnd.ConvNd, self.data.parameters, device)
+        # GELU fused into L1's and L2's epilogues (and its backward into their dy packs)
+        self.gelu = args.c5_gelu
+        self.net = configs.c5_network(torch_convnd.ConvNd, self.data.parameters, device,
+                                      fused_gelu=self.gelu == "fused")
         # one bucket per layer, so L3's and L2's all-reduces run under L1's weight gradient
         self.bucketer = GradientBucketer(layer_groups(self.net),
                                          batch_fraction=shard_fraction(configs.C5_BATCH, rank,
@@ -595,6 +600,7 @@ class C5Step:
         return {"workload": C5_WORKLOAD, "global_batch": configs.C5_BATCH,
                 "per_gpu_batch": self.layers[0].batch, "parallelism": f"dp{self.world}",
                 "activation_layout": self.layout,
+                "gelu": self.gelu,
                 "step_gflop_per_gpu": sum(l.step_flops for l in self.layers) / 1e9,
                 "gradient_buckets": len(self.bucketer.buckets),
                 "l2": "inputs larger than L2 (x alone is 537 MB at batch 64)"}

@@ -89,6 +89,13 @@ typedef enum cnd_fp32_mode {
 #define CND_LAYOUT_X_CL 1
 #define CND_LAYOUT_Y_CL 2
 
+/* Activation fused into the epilogue (also carried in cnd_problem.layout, bits 8-15, so
+ * that the workspace size functions see it). CND_ACT_GELU is PyTorch's exact GELU,
+ * 0.5 * v * (1 + erf(v / sqrt(2))). Used by cnd_forward_act / cnd_backward_act only. */
+#define CND_ACT_NONE 0
+#define CND_ACT_GELU 1
+#define CND_LAYOUT_ACT_SHIFT 8
+
 /* Convolution problem. Mirrors the reference's `Geometry` record (csrc/convnd.h:13-27)
  * plus batch size, dtype and activation layouts. Filled and validated by
  * cnd_problem_init (which sets layout to 0, channels-first). */
@@ -173,6 +180,24 @@ CND_API int cnd_forward_noalloc(const cnd_problem* problem, const void* x, const
 CND_API int cnd_backward(const cnd_problem* problem, const void* dy, const void* x, const void* w,
                  void* dx, void* dw, void* db, const int32_t output_mask[3],
                  void* workspace, size_t workspace_bytes, void* stream);
+
+/* Convolution with a fused activation (no counterpart in the reference, whose callers
+ * run the activation as a separate pass: the c5 training step's GELU between layers).
+ * cnd_forward_act writes y = act(conv(x, w) + b) and, when `pre` is not NULL, the
+ * pre-activation conv(x, w) + b to `pre` (same shape and layout as y), both from the fp32
+ * accumulators of one epilogue. cnd_backward_act takes the gradient of y, multiplies it
+ * by act'(pre) while packing it (the activation's backward, in fp32, rounded once to the
+ * problem's dtype as an eager activation backward would), and runs the convolution's
+ * backward on that product: dx, dw and db of conv + activation. `activation` is a
+ * CND_ACT_* value; set it in problem->layout (activation << CND_LAYOUT_ACT_SHIFT) too
+ * before asking for workspace sizes. */
+CND_API int cnd_forward_act(const cnd_problem* problem, const void* x, const void* w,
+                            const void* b, void* y, void* pre, int32_t activation,
+                            void* workspace, size_t workspace_bytes, void* stream);
+CND_API int cnd_backward_act(const cnd_problem* problem, const void* dy, const void* pre,
+                             int32_t activation, const void* x, const void* w, void* dx,
+                             void* dw, void* db, const int32_t output_mask[3],
+                             void* workspace, size_t workspace_bytes, void* stream);
 
 /* Which kernel family cnd_forward / cnd_backward would use for `problem`:
  * bit 0 = forward on tcgen05, bit 1 = dgrad on tcgen05, bit 2 = wgrad on tcgen05.

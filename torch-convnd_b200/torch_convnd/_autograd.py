@@ -137,6 +137,48 @@ def _vmap_conv_nd(info, in_dims, input, weight, bias, stride, padding, dilation,
     return output.unflatten(1, (size, cout)).movedim(1, 0), 0
 
 
+def _fake_forward_act(input, weight, bias, stride, padding, dilation, groups, workspace_bytes,
+                      activation):
+    output = _fake_forward(input, weight, bias, stride, padding, dilation, groups,
+                           workspace_bytes)
+    return output, torch.empty_like(output)
+
+
+def _fake_backward_act(grad_output, pre_activation, input, weight, stride, padding, dilation,
+                       groups, workspace_bytes, activation, output_mask):
+    return _fake_backward(grad_output, input, weight, stride, padding, dilation, groups,
+                          workspace_bytes, output_mask)
+
+
+def _setup_context_act(ctx, inputs, output):
+    input, weight, bias, *geometry = inputs
+    ctx.save_for_backward(input, weight, output[1])
+    ctx.geometry = geometry[:-1]  # stride, padding, dilation, groups, workspace_bytes
+    ctx.activation = geometry[-1]
+    ctx.has_bias = bias is not None
+
+
+def _backward_act(ctx, grad_output, grad_pre):
+    """Gradients of (activation(y), y), y = conv(x, W) + b: the activation's backward is
+    fused into the native backward's dy pack. A gradient reaching the pre-activation output
+    directly (rare) is added to the activation's backward in eager ops first."""
+    input, weight, pre = ctx.saved_tensors
+    needs = ctx.needs_input_grad
+    mask = [needs[0], needs[1], ctx.has_bias and needs[2]]
+    if grad_output is None and grad_pre is None:
+        return (None,) * 9
+    if grad_pre is None:
+        grads = torch.ops.torch_convnd.conv_nd_act_backward.default(
+            grad_output, pre, input, weight, *ctx.geometry, ctx.activation, mask)
+    else:
+        grad = grad_pre
+        if grad_output is not None:
+            grad = grad + torch.ops.aten.gelu_backward(grad_output, pre)
+        grads = torch.ops.torch_convnd.conv_nd_backward.default(
+            grad, input, weight, *ctx.geometry, mask)
+    return (*grads, None, None, None, None, None, None)
+
+
 def register_training() -> None:
     torch.library.register_fake("torch_convnd::conv_nd")(_fake_forward)
     torch.library.register_fake("torch_convnd::conv_nd_backward")(_fake_backward)
@@ -149,3 +191,8 @@ def register_training() -> None:
         setup_context=_setup_backward_context,
     )
     torch.library.register_vmap("torch_convnd::conv_nd", _vmap_conv_nd)
+    torch.library.register_fake("torch_convnd::conv_nd_act")(_fake_forward_act)
+    torch.library.register_fake("torch_convnd::conv_nd_act_backward")(_fake_backward_act)
+    torch.library.register_autograd(
+        "torch_convnd::conv_nd_act", _backward_act, setup_context=_setup_context_act
+    )

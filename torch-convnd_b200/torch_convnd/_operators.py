@@ -34,6 +34,29 @@ COMPATIBLE_CONV_ND_SCHEMA = (
 )
 
 
+# Convolution with a fused activation (no reference counterpart): (activation(y), y) for
+# y = conv + bias, and its backward from the gradient of activation(y) and y.
+CONV_ND_ACT_SCHEMA = (
+    "conv_nd_act(Tensor input, Tensor weight, Tensor? bias, int[] stride, int[] padding, "
+    "int[] dilation, int groups, int workspace_bytes, str activation) -> (Tensor, Tensor)"
+)
+CONV_ND_ACT_BACKWARD_SCHEMA = (
+    "conv_nd_act_backward(Tensor grad_output, Tensor pre_activation, Tensor input, "
+    "Tensor weight, int[] stride, int[] padding, int[] dilation, int groups, "
+    "int workspace_bytes, str activation, bool[3] output_mask) -> (Tensor?, Tensor?, Tensor?)"
+)
+
+
+def _first_call(name):
+    def run(*args):
+        from ._native import load_native
+
+        load_native()
+        return getattr(torch.ops.torch_convnd, name).default(*args)
+
+    return run
+
+
 def _compatible_conv_nd(input, weight, bias, stride, padding, dilation, groups, workspace_bytes,
                         backend):
     """The entry point of scripted graphs (reference _dispatch.py:160-181): a composite
@@ -83,6 +106,11 @@ def ensure_native_definitions() -> None:
         library.impl("conv_nd_backward", _first_call_backward, "CompositeExplicitAutograd")
         library.define(COMPATIBLE_CONV_ND_SCHEMA)
         library.impl("compatible_conv_nd", _compatible_conv_nd, "CompositeImplicitAutograd")
+        library.define(CONV_ND_ACT_SCHEMA)
+        library.define(CONV_ND_ACT_BACKWARD_SCHEMA)
+        library.impl("conv_nd_act", _first_call("conv_nd_act"), "CompositeExplicitAutograd")
+        library.impl("conv_nd_act_backward", _first_call("conv_nd_act_backward"),
+                     "CompositeExplicitAutograd")
         from ._autograd import register_training
 
         register_training()

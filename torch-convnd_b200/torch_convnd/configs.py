@@ -165,18 +165,21 @@ def make_c5_inputs(device="cpu", rank: int = 0, world: int = 1) -> C5Inputs:
                     target[start:stop].to(first.dtype).to(device), parameters)
 
 
-def c5_network(conv_class, parameters, device=None):
+def c5_network(conv_class, parameters, device=None, fused_gelu=False):
     """conv L1 -> GELU -> conv L2 -> GELU -> conv L3, built from `conv_class` (a ConvNd
-    with the reference's constructor) and loaded with `parameters`."""
+    with the reference's constructor) and loaded with `parameters`. With `fused_gelu` the
+    GELUs run inside L1's and L2's convolutions (ConvNd(..., activation='gelu'))."""
     layers = []
     for index, (layer, (weight, bias)) in enumerate(zip(C5_LAYERS, parameters, strict=True)):
+        last = index + 1 == len(C5_LAYERS)
+        extra = {"activation": "gelu"} if fused_gelu and not last else {}
         conv = conv_class(layer.in_channels, layer.out_channels, layer.kernel, layer.stride,
                           layer.padding, layer.dilation, layer.groups, bias=True,
-                          device=device, dtype=layer.dtype, dimensions=layer.rank)
+                          device=device, dtype=layer.dtype, dimensions=layer.rank, **extra)
         with torch.no_grad():
             conv.weight.copy_(weight)
             conv.bias.copy_(bias)
         layers.append(conv)
-        if index + 1 < len(C5_LAYERS):
+        if not last and not fused_gelu:
             layers.append(torch.nn.GELU())
     return torch.nn.Sequential(*layers)

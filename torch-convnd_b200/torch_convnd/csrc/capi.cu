@@ -158,6 +158,11 @@ struct Plan {
   // operand rows (16-bit, one pass group, channel count equal to the padded width) are
   // read in place: no layout pass and no workspace copy.
   bool x_cl = false, y_cl = false, x_direct = false, dy_direct = false;
+  // Fused activation (cnd_problem.layout bits 8-15): the forward epilogue applies it, the
+  // backward's dy pack multiplies by its derivative (so dy is always packed); dz_raw holds
+  // dy * act'(pre) in dy's layout when a generic pass needs the unpacked product.
+  int act = 0;
+  Region dz_raw;
   bool fast_fwd = false, fast_dgrad = false, fast_wgrad = false;
   // float32 dgrad on bfloat16 hi + lo operand parts (three kind::f16 products) instead
   // of 3xTF32, when that halves the K steps (dy channels a multiple of 16). Its packed dy
@@ -375,7 +380,18 @@ void make_plan(const cnd_problem& p, bool forward, const int32_t* mask, Plan* pl
   const bool low = p.dtype == CND_BF16 || p.dtype == CND_F16;
   const bool f32_tensor = p.dtype == CND_F32 && p.fp32_mode != CND_FP32_SIMT;
   plan->tensor_cores = (low || f32_tensor) && merged.rank <= kMaxFastRank && p.batch > 0;
-  if (!plan->tensor_cores) return;
+  if (!plan->tensor_cores) {
+    // generic kernels only: the activation backward needs its product materialised
+    plan->act = (p.layout >> CND_LAYOUT_ACT_SHIFT) & 0xff;
+    if (!forward && plan->act != 0 && p.batch > 0) {
+      size_t cursor = 0;
+      plan->dz_raw = take(&cursor, static_cast<size_t>(p.batch * p.output_channels *
+                                                       p.output_volume) *
+                                       element_bytes(p.dtype));
+      plan->total = cursor;
+    }
+    return;
+  }
   plan->op = operand_type(p.dtype);
   plan->split3 = (p.dtype == CND_F32 && p.fp32_mode == CND_FP32_3XTF32) ? 1 : 0;
   plan->pack_mode = p.dtype == CND_F32 ? (plan->split3 ? 1 : 2) : 0;
@@ -401,8 +417,9 @@ void make_plan(const cnd_problem& p, bool forward, const int32_t* mask, Plan* pl
   plan->x_cl = (p.layout & CND_LAYOUT_X_CL) != 0;
   plan->y_cl = (p.layout & CND_LAYOUT_Y_CL) != 0;
   plan->x_direct = plan->x_cl && low && plan->groups == 1 && p.channels == plan->x_pad;
-  plan->dy_direct =
-      plan->y_cl && low && plan->groups == 1 && p.output_channels == plan->dy_pad;
+  plan->act = (p.layout >> CND_LAYOUT_ACT_SHIFT) & 0xff;
+  plan->dy_direct = plan->act == 0 && plan->y_cl && low && plan->groups == 1 &&
+                    p.output_channels == plan->dy_pad;
   const int64_t taps = p.kernel_volume;
   size_t cursor = 0;
 
@@ -456,9 +473,9 @@ void make_plan(const cnd_problem& p, bool forward, const int32_t* mask, Plan* pl
       ConvPass templ = dg;
       const int64_t bf16_pad = pad_channels(kOpBF16, plan->cout_g, 16);
       if (plan->split3 && bf16_pad / 16 < plan->dy_pad / 8) {
+        // split3 stays set: two operand parts, three products (the 2xBF16 kernel)
         templ.op = kOpBF16;
         templ.c_pad = static_cast<int>(bf16_pad);
-        templ.split3 = 0;
         plan->dgrad_bf16 = true;
       }
       if (plan_phases(reduced, templ, plan)) {
@@ -556,6 +573,11 @@ void make_plan(const cnd_problem& p, bool forward, const int32_t* mask, Plan* pl
     const size_t grad =
         static_cast<size_t>(p.batch * plan->groups * p.output_volume) * plan->wg_dy_pad * 2;
     for (int part = 0; part < 2; ++part) plan->wg_dy[part] = take(&cursor, grad);
+  }
+  if (plan->act != 0 && ((mask[0] && !plan->fast_dgrad) || (mask[1] && !plan->fast_wgrad) ||
+                         (mask[2] && !plan->fast_dgrad && !plan->fast_wgrad))) {
+    plan->dz_raw = take(&cursor, static_cast<size_t>(p.batch * p.output_channels *
+                                                     p.output_volume) * es);
   }
   plan->total = cursor;
 }
@@ -661,23 +683,38 @@ int cnd_plan_summary(const cnd_problem* problem, char* buffer, size_t size) {
   return used;
 }
 
-int cnd_forward(const cnd_problem* problem, const void* x, const void* w, const void* b,
-                void* y, void* workspace, size_t workspace_bytes, void* stream_handle) {
-  using namespace cnd;
+}  // extern "C"
+
+namespace cnd {
+namespace {
+
+// Forward with an optional fused activation (act = 0: plain cnd_forward).
+int forward_impl(const cnd_problem* problem, const void* x, const void* w, const void* b,
+                 void* y, void* pre, int act, void* workspace, size_t workspace_bytes,
+                 void* stream_handle) {
   clear_error();
   if (problem == nullptr || w == nullptr ||
       (problem->batch > 0 && (x == nullptr || y == nullptr))) {
     return fail(CND_ERR_INVALID, "cnd_forward: null argument");
   }
-  const cnd_problem& p = *problem;
+  if (act != CND_ACT_NONE && act != CND_ACT_GELU) {
+    return fail(CND_ERR_UNSUPPORTED, "cnd_forward_act: unknown activation %d", act);
+  }
+  cnd_problem p = *problem;
+  p.layout = (p.layout & 0xff) | (act << CND_LAYOUT_ACT_SHIFT);
   cudaStream_t stream = static_cast<cudaStream_t>(stream_handle);
   if (p.batch == 0) return CND_OK;
   Plan plan;
   make_plan(p, true, nullptr, &plan);
   if (!plan.fast_fwd) {
-    GenericCall call{GenericCall::kForward, problem, x, w, b, y};
+    // generic convolution, then the activation as its own pass (pre keeps conv + b)
+    void* target = (act != CND_ACT_NONE && pre != nullptr) ? pre : y;
+    GenericCall call{GenericCall::kForward, &p, x, w, b, target};
     TimedPass timed(7, stream);
-    return run_generic(call, stream);
+    int rc = run_generic(call, stream);
+    if (rc != CND_OK || act == CND_ACT_NONE) return rc;
+    return activation_forward(target, y, p.batch * p.output_channels * p.output_volume,
+                              p.dtype, act, stream);
   }
   if (workspace_bytes < plan.total || (plan.total > 0 && workspace == nullptr)) {
     return fail(CND_ERR_WORKSPACE, "cnd_forward: workspace of %zu bytes is smaller than %zu",
@@ -735,8 +772,28 @@ int cnd_forward(const cnd_problem* problem, const void* x, const void* w, const 
   pass.wt_small = pw.dst_small;
   pass.dst = y;
   pass.bias = b;
+  pass.activation = act;
+  pass.pre = act != CND_ACT_NONE ? pre : nullptr;
   TimedPass timed(1, stream);
   return launch_fprop(pass, plan.fwd_plan, stream, wait_timeout_ns(), 0);
+}
+
+}  // namespace
+}  // namespace cnd
+
+extern "C" {
+
+int cnd_forward(const cnd_problem* problem, const void* x, const void* w, const void* b,
+                void* y, void* workspace, size_t workspace_bytes, void* stream_handle) {
+  return cnd::forward_impl(problem, x, w, b, y, nullptr, CND_ACT_NONE, workspace,
+                           workspace_bytes, stream_handle);
+}
+
+int cnd_forward_act(const cnd_problem* problem, const void* x, const void* w, const void* b,
+                    void* y, void* pre, int32_t activation, void* workspace,
+                    size_t workspace_bytes, void* stream_handle) {
+  return cnd::forward_impl(problem, x, w, b, y, pre, activation, workspace, workspace_bytes,
+                           stream_handle);
 }
 
 int cnd_forward_noalloc(const cnd_problem* problem, const void* x, const void* w,
@@ -778,11 +835,21 @@ int cnd_forward_noalloc(const cnd_problem* problem, const void* x, const void* w
   return rc;
 }
 
-int cnd_backward(const cnd_problem* problem, const void* dy, const void* x, const void* w,
-                 void* dx, void* dw, void* db, const int32_t output_mask[3], void* workspace,
-                 size_t workspace_bytes, void* stream_handle) {
-  using namespace cnd;
+}  // extern "C"
+
+namespace cnd {
+namespace {
+
+// Backward with an optional fused activation backward (act = 0: plain cnd_backward).
+int backward_impl(const cnd_problem* problem, const void* dy, const void* pre, int act,
+                  const void* x, const void* w, void* dx, void* dw, void* db,
+                  const int32_t output_mask[3], void* workspace, size_t workspace_bytes,
+                  void* stream_handle) {
   clear_error();
+  if (act != CND_ACT_NONE && (act != CND_ACT_GELU || (problem != nullptr &&
+                                                       problem->batch > 0 && pre == nullptr))) {
+    return fail(CND_ERR_INVALID, "cnd_backward_act: unknown activation or missing pre-activation");
+  }
   if (problem == nullptr || output_mask == nullptr || w == nullptr) {
     return fail(CND_ERR_INVALID, "cnd_backward: null argument");
   }
@@ -793,7 +860,8 @@ int cnd_backward(const cnd_problem* problem, const void* dy, const void* x, cons
       (output_mask[1] && dw == nullptr) || (output_mask[2] && db == nullptr)) {
     return fail(CND_ERR_INVALID, "cnd_backward: missing gradient buffer");
   }
-  const cnd_problem& p = *problem;
+  cnd_problem p = *problem;
+  p.layout = (p.layout & 0xff) | (act << CND_LAYOUT_ACT_SHIFT);
   cudaStream_t stream = static_cast<cudaStream_t>(stream_handle);
   const size_t es = element_bytes(p.dtype);
   if (p.batch == 0) {
@@ -819,12 +887,28 @@ int cnd_backward(const cnd_problem* problem, const void* dy, const void* x, cons
   int blocks = 0;  // bias-gradient partials per (n, g), set by the pack that makes them
   float* bias_partial = static_cast<float*>(at(workspace, plan.bias_partial));
   bool bias_from_pack = false;
+  // The gradient the convolution's backward sees: dy, or dy * act'(pre). It is formed by
+  // the packs (pack_act / pack_pre) or, when a generic pass reads it unpacked, once in dz_raw.
+  const void* grad = dy;
+  int pack_act = act;
+  const void* pack_pre = pre;
+  if (act != CND_ACT_NONE && plan.dz_raw.bytes > 0) {
+    void* dz = at(workspace, plan.dz_raw);
+    rc = activation_backward(dy, pre, dz, p.batch * p.output_channels * p.output_volume,
+                             p.dtype, act, stream);
+    if (rc != CND_OK) return rc;
+    grad = dz;
+    pack_act = CND_ACT_NONE;
+    pack_pre = nullptr;
+  }
   const void* dy_operand = plan.dy_direct ? dy : at(workspace, plan.dy_pack);
   if (plan.dy_pack.bytes > 0 || (plan.dy_direct && output_mask[2] && bias_partial != nullptr)) {
     // dy to the packed layout, with the bias-gradient partials of the same read; when dy
     // is read in place this pass only sums its channels.
     PackActArgs pa{};
-    pa.src = dy;
+    pa.src = grad;
+    pa.act = pack_act;
+    pa.pre = pack_pre;
     pa.dst = at(workspace, plan.dy_pack);
     pa.dst_small = at(workspace, plan.dy_pack_small);
     pa.batch = p.batch;
@@ -845,7 +929,9 @@ int cnd_backward(const cnd_problem* problem, const void* dy, const void* x, cons
   if (plan.wg_dy[0].bytes > 0) {
     // float32 dy as bfloat16 hi + lo parts (weight gradient, bf16-part dgrad)
     PackActArgs pa{};
-    pa.src = dy;
+    pa.src = grad;
+    pa.act = pack_act;
+    pa.pre = pack_pre;
     pa.dst = at(workspace, plan.wg_dy[0]);
     pa.dst_small = at(workspace, plan.wg_dy[1]);
     pa.batch = p.batch;
@@ -906,7 +992,7 @@ int cnd_backward(const cnd_problem* problem, const void* dy, const void* x, cons
                         static_cast<int>(plan.cout_g), dw, p.dtype, stream);
       if (rc != CND_OK) return rc;
     } else {
-      GenericCall call{GenericCall::kWgrad, problem, dy, x, nullptr, dw};
+      GenericCall call{GenericCall::kWgrad, &p, grad, x, nullptr, dw};
       TimedPass timed(7, stream);
       rc = run_generic(call, stream);
       if (rc != CND_OK) return rc;
@@ -997,7 +1083,7 @@ int cnd_backward(const cnd_problem* problem, const void* dy, const void* x, cons
       rc = launch_fprop(pass, plan.dgrad_plan, stream, wait_timeout_ns(), 0);
       if (rc != CND_OK) return rc;
     } else {
-      GenericCall call{GenericCall::kDgrad, problem, dy, w, nullptr, dx};
+      GenericCall call{GenericCall::kDgrad, &p, grad, w, nullptr, dx};
       TimedPass timed(7, stream);
       rc = run_generic(call, stream);
       if (rc != CND_OK) return rc;
@@ -1011,12 +1097,32 @@ int cnd_backward(const cnd_problem* problem, const void* dy, const void* x, cons
                        static_cast<int>(plan.groups), blocks, static_cast<int>(plan.cout_g), db,
                        p.dtype, stream);
     } else {
-      GenericCall call{GenericCall::kBias, problem, dy, nullptr, nullptr, db};
+      GenericCall call{GenericCall::kBias, &p, grad, nullptr, nullptr, db};
       rc = run_generic(call, stream);
     }
     if (rc != CND_OK) return rc;
   }
   return CND_OK;
+}
+
+}  // namespace
+}  // namespace cnd
+
+extern "C" {
+
+int cnd_backward(const cnd_problem* problem, const void* dy, const void* x, const void* w,
+                 void* dx, void* dw, void* db, const int32_t output_mask[3], void* workspace,
+                 size_t workspace_bytes, void* stream_handle) {
+  return cnd::backward_impl(problem, dy, nullptr, CND_ACT_NONE, x, w, dx, dw, db, output_mask,
+                            workspace, workspace_bytes, stream_handle);
+}
+
+int cnd_backward_act(const cnd_problem* problem, const void* dy, const void* pre,
+                     int32_t activation, const void* x, const void* w, void* dx, void* dw,
+                     void* db, const int32_t output_mask[3], void* workspace,
+                     size_t workspace_bytes, void* stream_handle) {
+  return cnd::backward_impl(problem, dy, pre, activation, x, w, dx, dw, db, output_mask,
+                            workspace, workspace_bytes, stream_handle);
 }
 
 int cnd_device_status(void* stream_handle) {

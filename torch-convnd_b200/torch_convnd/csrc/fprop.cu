@@ -144,6 +144,11 @@ struct OpTraits<kKind2xBF16> {
   static __device__ __forceinline__ float load(const Out* p) { return __ldg(p); }
 };
 
+// PyTorch's exact GELU (approximate='none'): 0.5 v (1 + erf(v / sqrt(2))).
+__device__ __forceinline__ float gelu_exact(float v) {
+  return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f));
+}
+
 // Rounding of an fp32 epilogue value to the output type.
 template <typename T>
 struct OpCast;
@@ -588,6 +593,31 @@ __global__ void __launch_bounds__(kThreads, 1)
       return off;
     };
     const int64_t out_vol = P.out_strided ? P.out_volume_full : P.out_volume;
+    // Fused activation: store the pre-activation values of this thread's row (M tile m,
+    // channels c * 16 ..), then apply the activation in place.
+    auto activate = [&](const Super& S, int m, int o1, int o2, int c, float (&value)[16]) {
+      if (!P.act) return;
+      const int o0 = (S.q0 * kMT + m) * P.e0 + i0;
+      if (P.pre != nullptr && line_ok && o0 < P.out[0] && o1 < P.out[1] && o2 < P.out[2]) {
+        OutT* pre = static_cast<OutT*>(P.pre);
+        const int64_t sp = out_offset(S, o0, o1, o2);
+        if (P.out_cl) {
+          store_run16<OutT>(pre + (S.n * out_vol + sp) * P.out_channels_total +
+                                static_cast<int64_t>(S.g) * P.n_real + c * 16,
+                            value, P.n_real - c * 16);
+        } else {
+          OutT* dst = pre + (S.n * P.out_channels_total + static_cast<int64_t>(S.g) * P.n_real) *
+                                out_vol + sp;
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int co = c * 16 + i;
+            if (co < P.n_real) dst[static_cast<int64_t>(co) * out_vol] = Traits::cast(value[i]);
+          }
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 16; ++i) value[i] = gelu_exact(value[i]);
+    };
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
     const int used = work_per_super < P.nacc ? work_per_super : P.nacc;
     const OutT* bias = static_cast<const OutT*>(P.bias);
@@ -645,6 +675,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int c = 0; c < P.n_pad / 16; ++c) {
             float value[16];
             chunk(dbase, m, c, group_bias, value);
+            activate(S, m, o1, o2, c, value);
             alignas(16) OutT packed[16];
 #pragma unroll
             for (int i = 0; i < 16; ++i) packed[i] = Traits::cast(value[i]);
@@ -690,6 +721,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int c = 0; c < P.n_pad / 16; ++c) {
             float value[16];
             chunk(dbase, m, c, group_bias, value);
+            activate(S, m, o1, o2, c, value);
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
               const int co = c * 16 + i;
@@ -720,6 +752,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int c = 0; c < P.n_pad / 16; ++c) {
             float value[16];
             chunk(dbase, m, c, group_bias, value);
+            activate(S, m, o1, o2, c, value);
             if (valid) store_run16<OutT>(dst + c * 16, value, P.n_real - c * 16);
           }
         }
@@ -736,6 +769,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int c = 0; c < P.n_pad / 16; ++c) {
           float value[16];
           chunk(dbase, m, c, group_bias, value);
+          activate(S, m, o1, o2, c, value);
           if (valid) {
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
@@ -1093,6 +1127,7 @@ bool plan_fprop(const ConvPass& pass, FpropPlan* plan) {
   P.tma_store = 0;
   P.out_tile_bytes = round_up(static_cast<uint32_t>(pass.n_real * 128 * out_es), 1024);
   P.out_cl = pass.out_cl;
+  P.act = pass.activation;
   P.out_strided = pass.out_strided;
   if (pass.out_strided) {
     // element strides of the full tensor's axes (row-major), times the phase multipliers
@@ -1173,6 +1208,7 @@ int launch_fprop(const ConvPass& pass, const FpropPlan& plan_in, cudaStream_t st
   FpropParams& P = plan.params;
   P.dst = pass.dst;
   P.bias = pass.bias;
+  P.pre = pass.pre;
   P.err = device_error_word();
   P.timeout_ns = timeout_ns;
   P.debug_stall = debug_stall;

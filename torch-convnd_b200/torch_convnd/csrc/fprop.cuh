@@ -61,6 +61,8 @@ struct FpropParams {
   // Strided output (ConvPass::out_strided): element offset of output position (outer o,
   // box o0..o2) is phase_base + sum o * ostride, over a tensor of out_volume_full positions
   // per image; direct stores only.
+  int act;    // CND_ACT_*: the epilogue applies it after the bias
+  void* pre;  // pre-activation output (same layout as dst), or null
   int out_strided;
   int64_t phase_base, out_volume_full;
   int64_t ostride_box[3], ostride_o[kMaxOuter];

@@ -57,6 +57,13 @@ __device__ __forceinline__ __half from_float<__half>(float v) {
 
 constexpr int kPackPositions = 64;
 
+// Derivative of PyTorch's exact GELU: Phi(v) + v * phi(v).
+__device__ __forceinline__ float gelu_grad(float v) {
+  const float cdf = 0.5f * (1.0f + erff(v * 0.70710678118654752f));
+  const float pdf = 0.39894228040143268f * expf(-0.5f * v * v);
+  return cdf + v * pdf;
+}
+
 // Splits v into `parts` terms of type T whose sum reproduces v: TF32 big/small (kMode 1),
 // a TF32 rounding (kMode 2), or bf16 hi/mid/lo (kMode 3) and hi/lo (kMode 4), the
 // error-compensated operands of the split-product MMAs.
@@ -89,7 +96,8 @@ __global__ void __launch_bounds__(256) pack_act_kernel(const Tin* __restrict__ s
                                                        Tout* __restrict__ dst1,
                                                        Tout* __restrict__ dst2, int64_t S,
                                                        int Cg, int c_pad, int G,
-                                                       float* __restrict__ chan_partial) {
+                                                       float* __restrict__ chan_partial,
+                                                       const Tin* __restrict__ pre) {
   extern __shared__ float tile[];  // [c_pad][kPackPositions + 1]
   const int64_t s0 = static_cast<int64_t>(blockIdx.x) * kPackPositions;
   const int g = blockIdx.y;
@@ -102,7 +110,11 @@ __global__ void __launch_bounds__(256) pack_act_kernel(const Tin* __restrict__ s
       const int s = i / c_pad;
       const int c = i - s * c_pad;
       float v = 0.0f;
-      if (c < Cg && s0 + s < S) v = to_float(in[s * row + c]);
+      if (c < Cg && s0 + s < S) {
+        const int64_t at = (n * S + s0) * row + static_cast<int64_t>(g) * Cg + s * row + c;
+        v = to_float(in[s * row + c]);
+        if (pre != nullptr) v = to_float(from_float<Tin>(v * gelu_grad(to_float(pre[at]))));
+      }
       tile[c * width + s] = v;
     }
   } else {
@@ -111,7 +123,11 @@ __global__ void __launch_bounds__(256) pack_act_kernel(const Tin* __restrict__ s
       const int c = i / kPackPositions;
       const int s = i - c * kPackPositions;
       float v = 0.0f;
-      if (c < Cg && s0 + s < S) v = to_float(in[static_cast<int64_t>(c) * S + s0 + s]);
+      if (c < Cg && s0 + s < S) {
+        const int64_t at = (n * G + g) * static_cast<int64_t>(Cg) * S + c * S + s0 + s;
+        v = to_float(in[static_cast<int64_t>(c) * S + s0 + s]);
+        if (pre != nullptr) v = to_float(from_float<Tin>(v * gelu_grad(to_float(pre[at]))));
+      }
       tile[c * width + s] = v;
     }
   }
@@ -263,7 +279,9 @@ constexpr int kSumRows = 512;
 template <typename T>
 __global__ void __launch_bounds__(256) channel_sum_cl16_kernel(const T* __restrict__ src,
                                                                int64_t S, int C,
-                                                               float* __restrict__ partial) {
+                                                               float* __restrict__ partial,
+                                                               T* __restrict__ dst,
+                                                               const T* __restrict__ pre) {
   __shared__ float part[256][8];
   const int vpr = C >> 3;  // 16-byte vectors per row
   const int per_pass = 256 / vpr;
@@ -277,8 +295,17 @@ __global__ void __launch_bounds__(256) channel_sum_cl16_kernel(const T* __restri
     for (int r = r0; r < kSumRows; r += per_pass) {
       const int64_t pos = row_base + r;
       if (pos >= S) break;
-      const uint4 word = __ldg(reinterpret_cast<const uint4*>(src + (image * S + pos) * C) + v);
-      const T* x = reinterpret_cast<const T*>(&word);
+      const int64_t at = (image * S + pos) * C;
+      uint4 word = __ldg(reinterpret_cast<const uint4*>(src + at) + v);
+      T* x = reinterpret_cast<T*>(&word);
+      if (pre != nullptr) {
+        // activation backward: dy * act'(pre), rounded once to T
+        const uint4 pw = __ldg(reinterpret_cast<const uint4*>(pre + at) + v);
+        const T* z = reinterpret_cast<const T*>(&pw);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) x[i] = from_float<T>(to_float(x[i]) * gelu_grad(to_float(z[i])));
+      }
+      if (dst != nullptr) *(reinterpret_cast<uint4*>(dst + at) + v) = word;
 #pragma unroll
       for (int i = 0; i < 8; ++i) sum[i] += to_float(x[i]);
     }
@@ -286,6 +313,7 @@ __global__ void __launch_bounds__(256) channel_sum_cl16_kernel(const T* __restri
 #pragma unroll
   for (int i = 0; i < 8; ++i) part[t][i] = sum[i];
   __syncthreads();
+  if (partial == nullptr) return;
   for (int c = t; c < C; c += blockDim.x) {
     const int group = c >> 3;
     float total = 0.0f;
@@ -443,7 +471,8 @@ int launch_pack_act_impl(const PackActArgs& a, cudaStream_t stream) {
   kernel<<<grid, 256, smem, stream>>>(static_cast<const Tin*>(a.src), static_cast<Tout*>(a.dst),
                                       static_cast<Tout*>(a.dst_small),
                                       static_cast<Tout*>(a.dst_third), a.spatial, a.cg, a.c_pad,
-                                      static_cast<int>(a.groups), a.chan_partial);
+                                      static_cast<int>(a.groups), a.chan_partial,
+                                      a.act ? static_cast<const Tin*>(a.pre) : nullptr);
   count_launch();
   return CND_OK;
 }
@@ -493,11 +522,94 @@ int launch_pack_act16(const PackActArgs& a, cudaStream_t stream) {
 }
 
 bool pack16_fast_ok(const PackActArgs& a) {
-  return a.mode == 0 && !a.src_cl && a.dst != nullptr && (a.c_pad == 8 || a.c_pad == 16 || a.c_pad == 32 || a.c_pad == 64) &&
+  return a.mode == 0 && !a.src_cl && a.dst != nullptr && a.act == 0 && (a.c_pad == 8 || a.c_pad == 16 || a.c_pad == 32 || a.c_pad == 64) &&
          a.cg <= a.c_pad && a.spatial % 8 == 0 &&
          (a.spatial + 63) / 64 <= 0x7FFFFFFF && a.groups <= 65535 &&
          a.batch <= 65535 && reinterpret_cast<uintptr_t>(a.src) % 16 == 0 &&
          reinterpret_cast<uintptr_t>(a.dst) % 16 == 0;
+}
+
+template <typename T>
+struct Wide {
+  using type = float;
+};
+template <>
+struct Wide<double> {
+  using type = double;
+};
+
+template <typename T>
+__device__ __forceinline__ typename Wide<T>::type widen(T v) {
+  return static_cast<typename Wide<T>::type>(v);
+}
+template <>
+__device__ __forceinline__ float widen<__nv_bfloat16>(__nv_bfloat16 v) {
+  return __bfloat162float(v);
+}
+template <>
+__device__ __forceinline__ float widen<__half>(__half v) {
+  return __half2float(v);
+}
+
+__device__ __forceinline__ double gelu_of(double v) {
+  return 0.5 * v * (1.0 + erf(v * 0.70710678118654752440));
+}
+__device__ __forceinline__ float gelu_of(float v) {
+  return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f));
+}
+__device__ __forceinline__ double gelu_grad_of(double v) {
+  return 0.5 * (1.0 + erf(v * 0.70710678118654752440)) +
+         v * 0.39894228040143267794 * exp(-0.5 * v * v);
+}
+__device__ __forceinline__ float gelu_grad_of(float v) { return gelu_grad(v); }
+
+template <typename T>
+__global__ void activation_forward_kernel(const T* __restrict__ src, T* dst, int64_t n) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    dst[i] = static_cast<T>(gelu_of(widen(src[i])));
+  }
+}
+
+template <typename T>
+__global__ void activation_backward_kernel(const T* __restrict__ dy, const T* __restrict__ pre,
+                                           T* __restrict__ dz, int64_t n) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    dz[i] = static_cast<T>(widen(dy[i]) * gelu_grad_of(widen(pre[i])));
+  }
+}
+
+template <typename T>
+int activation_typed(const void* a, const void* b, void* out, int64_t n, bool backward,
+                     cudaStream_t stream) {
+  if (n == 0) return CND_OK;
+  const int blocks = grid_for(n, 256);
+  if (backward) {
+    activation_backward_kernel<T><<<blocks, 256, 0, stream>>>(
+        static_cast<const T*>(a), static_cast<const T*>(b), static_cast<T*>(out), n);
+  } else {
+    activation_forward_kernel<T><<<blocks, 256, 0, stream>>>(static_cast<const T*>(a),
+                                                             static_cast<T*>(out), n);
+  }
+  count_launch();
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(CND_ERR_CUDA, "activation launch: %s", cudaGetErrorString(e));
+  return CND_OK;
+}
+
+int activation_dispatch(const void* a, const void* b, void* out, int64_t n, int dtype,
+                        bool backward, cudaStream_t stream) {
+  switch (dtype) {
+    case CND_BF16:
+      return activation_typed<__nv_bfloat16>(a, b, out, n, backward, stream);
+    case CND_F16:
+      return activation_typed<__half>(a, b, out, n, backward, stream);
+    case CND_F32:
+      return activation_typed<float>(a, b, out, n, backward, stream);
+    default:
+      return activation_typed<double>(a, b, out, n, backward, stream);
+  }
 }
 
 bool channel_sums_fast_ok(const PackActArgs& a);
@@ -623,7 +735,13 @@ int reduce_bias(const float* partial, int64_t batch, int groups, int blocks, int
 
 bool channel_sums_fast_ok(const PackActArgs& a) {
   const int64_t channels = a.groups * a.cg;
-  return a.src_cl && a.dst == nullptr && (a.dtype == CND_BF16 || a.dtype == CND_F16) &&
+  // channels-last 16-bit rows that already are the packed rows: channel sums only, or a
+  // row copy (with the activation backward) into the packed layout
+  const bool rows_match = a.groups == 1 && a.cg == a.c_pad && a.mode == 0 &&
+                          (a.dst == nullptr || reinterpret_cast<uintptr_t>(a.dst) % 16 == 0);
+  return a.src_cl && (a.dst == nullptr || rows_match) &&
+         (a.dtype == CND_BF16 || a.dtype == CND_F16) &&
+         (a.act == 0 || reinterpret_cast<uintptr_t>(a.pre) % 16 == 0) &&
          channels % 8 == 0 && channels <= 256 && 256 % (channels / 8) == 0 &&
          a.batch <= 65535 && reinterpret_cast<uintptr_t>(a.src) % 16 == 0;
 }
@@ -634,15 +752,30 @@ int channel_sums(const PackActArgs& a, cudaStream_t stream) {
   const dim3 grid(static_cast<unsigned>(blocks), 1, static_cast<unsigned>(a.batch));
   if (a.dtype == CND_BF16) {
     channel_sum_cl16_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(
-        static_cast<const __nv_bfloat16*>(a.src), a.spatial, channels, a.chan_partial);
+        static_cast<const __nv_bfloat16*>(a.src), a.spatial, channels, a.chan_partial,
+        static_cast<__nv_bfloat16*>(a.dst),
+        a.act ? static_cast<const __nv_bfloat16*>(a.pre) : nullptr);
   } else {
     channel_sum_cl16_kernel<__half><<<grid, 256, 0, stream>>>(
-        static_cast<const __half*>(a.src), a.spatial, channels, a.chan_partial);
+        static_cast<const __half*>(a.src), a.spatial, channels, a.chan_partial,
+        static_cast<__half*>(a.dst), a.act ? static_cast<const __half*>(a.pre) : nullptr);
   }
   count_launch();
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(CND_ERR_CUDA, "channel_sum launch: %s", cudaGetErrorString(e));
   return CND_OK;
+}
+
+int activation_forward(const void* src, void* dst, int64_t n, int dtype, int act,
+                       cudaStream_t stream) {
+  if (act != CND_ACT_GELU) return fail(CND_ERR_UNSUPPORTED, "unknown activation %d", act);
+  return activation_dispatch(src, nullptr, dst, n, dtype, false, stream);
+}
+
+int activation_backward(const void* dy, const void* pre, void* dz, int64_t n, int dtype,
+                        int act, cudaStream_t stream) {
+  if (act != CND_ACT_GELU) return fail(CND_ERR_UNSUPPORTED, "unknown activation %d", act);
+  return activation_dispatch(dy, pre, dz, n, dtype, true, stream);
 }
 
 int64_t pack_blocks(const PackActArgs& args) {

@@ -22,6 +22,10 @@ struct PackActArgs {
   int cg, c_pad, dtype, mode;
   float* chan_partial;  // optional [batch][groups][pack_blocks(spatial)][cg]
   int src_cl;           // 1: the source is channels-last
+  // Fused activation backward: each value is multiplied by act'(pre) (pre has the
+  // source's shape and layout; CND_ACT_*) in fp32 before it is stored, rounded once.
+  int act;
+  const void* pre;
 };
 
 // Weights [groups*cout_g][cin_g][taps] -> [groups][taps][n_pad][c_pad] (mode as for
@@ -60,6 +64,12 @@ int reduce_wgrad(const float* partial, int splits, int groups, int bd, int taps,
                  int cout_g, void* dw, int dtype, cudaStream_t stream);
 int reduce_bias(const float* partial, int64_t batch, int groups, int blocks, int cg, void* db,
                 int dtype, cudaStream_t stream);
+// Elementwise activation passes for problems the tcgen05 epilogue / pack do not serve:
+// dst = act(src) (dst may alias src), and dz = dy * act'(pre); n elements of `dtype`.
+int activation_forward(const void* src, void* dst, int64_t n, int dtype, int act,
+                       cudaStream_t stream);
+int activation_backward(const void* dy, const void* pre, void* dz, int64_t n, int dtype,
+                        int act, cudaStream_t stream);
 // Number of position blocks (and so of bias-gradient partials per (n, g)) the activation
 // pack of `args` produces.
 int64_t pack_blocks(const PackActArgs& args);

@@ -14,6 +14,7 @@
 #include <torch/library.h>
 
 #include <array>
+#include <string>
 #include <optional>
 #include <tuple>
 #include <vector>
@@ -202,6 +203,87 @@ conv_nd_backward_cuda(const at::Tensor& grad_output, const at::Tensor& input,
   return {grad_input, grad_weight, grad_bias};
 }
 
+int32_t activation_code(c10::string_view activation) {
+  if (activation == "gelu") return CND_ACT_GELU;
+  TORCH_CHECK(false, "conv_nd_act supports activation='gelu', got '", std::string(activation),
+              "'");
+}
+
+// conv + bias + activation in one epilogue: (activation(y), y) with y = conv(x, w) + b, both
+// in the input's layout. The pre-activation output is what the backward needs.
+std::tuple<at::Tensor, at::Tensor> conv_nd_act_cuda(
+    const at::Tensor& input, const at::Tensor& weight, const std::optional<at::Tensor>& bias,
+    at::IntArrayRef stride, at::IntArrayRef padding, at::IntArrayRef dilation, int64_t groups,
+    int64_t workspace_bytes, c10::string_view activation) {
+  const int32_t act = activation_code(activation);
+  cnd_problem problem = make_problem(input, weight, stride, padding, dilation, groups);
+  check_bias(bias, input, problem);
+  check_status(cnd_check_workspace_budget(&problem, input.element_size(), workspace_bytes));
+  const c10::cuda::CUDAGuard guard(input.device());
+  const bool cl = is_channels_last(input);
+  const at::Tensor x = cl ? input : input.contiguous();
+  problem.layout = (cl ? CND_LAYOUT_X_CL | CND_LAYOUT_Y_CL : 0) | (act << CND_LAYOUT_ACT_SHIFT);
+  const at::Tensor w = weight.contiguous();
+  at::Tensor b;
+  if (bias.has_value()) b = bias->contiguous();
+  at::Tensor output = empty_activation(output_shape(input, problem), cl, input.options());
+  at::Tensor pre = empty_activation(output_shape(input, problem), cl, input.options());
+  if (input.size(0) == 0) return {output, pre};
+  const size_t bytes = cnd_forward_workspace_size(&problem);
+  at::Tensor workspace = workspace_tensor(bytes, input);
+  const auto stream = c10::cuda::getCurrentCUDAStream(input.device().index());
+  check_status(cnd_forward_act(&problem, x.const_data_ptr(), w.const_data_ptr(),
+                               b.defined() ? b.const_data_ptr() : nullptr,
+                               output.mutable_data_ptr(), pre.mutable_data_ptr(), act,
+                               workspace.mutable_data_ptr(), bytes, stream.stream()));
+  return {output, pre};
+}
+
+std::tuple<std::optional<at::Tensor>, std::optional<at::Tensor>, std::optional<at::Tensor>>
+conv_nd_act_backward_cuda(const at::Tensor& grad_output, const at::Tensor& pre_activation,
+                          const at::Tensor& input, const at::Tensor& weight,
+                          at::IntArrayRef stride, at::IntArrayRef padding,
+                          at::IntArrayRef dilation, int64_t groups, int64_t workspace_bytes,
+                          c10::string_view activation, std::array<bool, 3> output_mask) {
+  const int32_t act = activation_code(activation);
+  cnd_problem problem = make_problem(input, weight, stride, padding, dilation, groups);
+  check_grad_output(grad_output, input, problem);
+  check_grad_output(pre_activation, input, problem);
+  check_backward_budget(input, problem, workspace_bytes, output_mask);
+  const c10::cuda::CUDAGuard guard(input.device());
+  std::optional<at::Tensor> grad_input, grad_weight, grad_bias;
+  const bool x_cl = is_channels_last(input);
+  const bool dy_cl = is_channels_last(grad_output);
+  problem.layout = (x_cl ? CND_LAYOUT_X_CL : 0) | (dy_cl ? CND_LAYOUT_Y_CL : 0) |
+                   (act << CND_LAYOUT_ACT_SHIFT);
+  if (output_mask[0]) grad_input = empty_activation(input.sizes().vec(), x_cl, input.options());
+  if (output_mask[1]) grad_weight = at::empty(weight.sizes(), weight.options());
+  if (output_mask[2]) grad_bias = at::empty({problem.output_channels}, input.options());
+  if (!output_mask[0] && !output_mask[1] && !output_mask[2]) {
+    return {grad_input, grad_weight, grad_bias};
+  }
+  const at::Tensor dy = dy_cl ? grad_output : grad_output.contiguous();
+  // the pre-activation is read with dy's indexing: same layout as dy
+  at::Tensor pre = pre_activation;
+  if (dy_cl != is_channels_last(pre) || (!dy_cl && !pre.is_contiguous())) {
+    pre = empty_activation(pre_activation.sizes().vec(), dy_cl, pre_activation.options());
+    pre.copy_(pre_activation);
+  }
+  const at::Tensor x = x_cl ? input : input.contiguous();
+  const at::Tensor w = weight.contiguous();
+  const int32_t mask[3] = {output_mask[0], output_mask[1], output_mask[2]};
+  const size_t bytes = cnd_backward_workspace_size(&problem, mask);
+  at::Tensor workspace = workspace_tensor(bytes, input);
+  const auto stream = c10::cuda::getCurrentCUDAStream(input.device().index());
+  check_status(cnd_backward_act(
+      &problem, dy.const_data_ptr(), pre.const_data_ptr(), act, x.const_data_ptr(),
+      w.const_data_ptr(), grad_input ? grad_input->mutable_data_ptr() : nullptr,
+      grad_weight ? grad_weight->mutable_data_ptr() : nullptr,
+      grad_bias ? grad_bias->mutable_data_ptr() : nullptr, mask, workspace.mutable_data_ptr(),
+      bytes, stream.stream()));
+  return {grad_input, grad_weight, grad_bias};
+}
+
 [[noreturn]] void refuse_cpu() {
   TORCH_CHECK(false,
               "torch_convnd B200 build: the native convolution runs on CUDA devices only; "
@@ -234,6 +316,32 @@ conv_nd_backward_cpu(const at::Tensor& grad_output, const at::Tensor& input,
   refuse_cpu();
 }
 
+std::tuple<at::Tensor, at::Tensor> conv_nd_act_cpu(
+    const at::Tensor& input, const at::Tensor& weight, const std::optional<at::Tensor>& bias,
+    at::IntArrayRef stride, at::IntArrayRef padding, at::IntArrayRef dilation, int64_t groups,
+    int64_t workspace_bytes, c10::string_view activation) {
+  activation_code(activation);
+  cnd_problem problem = make_problem(input, weight, stride, padding, dilation, groups);
+  check_bias(bias, input, problem);
+  check_status(cnd_check_workspace_budget(&problem, input.element_size(), workspace_bytes));
+  refuse_cpu();
+}
+
+std::tuple<std::optional<at::Tensor>, std::optional<at::Tensor>, std::optional<at::Tensor>>
+conv_nd_act_backward_cpu(const at::Tensor& grad_output, const at::Tensor& pre_activation,
+                         const at::Tensor& input, const at::Tensor& weight,
+                         at::IntArrayRef stride, at::IntArrayRef padding,
+                         at::IntArrayRef dilation, int64_t groups, int64_t workspace_bytes,
+                         c10::string_view activation, std::array<bool, 3> output_mask) {
+  activation_code(activation);
+  cnd_problem problem = make_problem(input, weight, stride, padding, dilation, groups);
+  check_grad_output(grad_output, input, problem);
+  check_grad_output(pre_activation, input, problem);
+  (void)workspace_bytes;
+  (void)output_mask;
+  refuse_cpu();
+}
+
 // Autocast: cast floating operands to the autocast dtype, then redispatch below the
 // autocast key (the standard PyTorch pattern the reference also uses, convnd.cpp:417-431).
 template <c10::DeviceType Device>
@@ -253,23 +361,46 @@ at::Tensor conv_nd_autocast(const at::Tensor& input, const at::Tensor& weight,
                  groups, workspace_bytes);
 }
 
+template <c10::DeviceType Device>
+std::tuple<at::Tensor, at::Tensor> conv_nd_act_autocast(
+    const at::Tensor& input, const at::Tensor& weight, const std::optional<at::Tensor>& bias,
+    at::IntArrayRef stride, at::IntArrayRef padding, at::IntArrayRef dilation, int64_t groups,
+    int64_t workspace_bytes, c10::string_view activation) {
+  const c10::impl::ExcludeDispatchKeyGuard no_autocast(
+      at::autocast::get_autocast_dispatch_key_from_device_type(Device));
+  const at::ScalarType target = at::autocast::get_autocast_dtype(Device);
+  static const auto op = c10::Dispatcher::singleton()
+                             .findSchemaOrThrow("torch_convnd::conv_nd_act", "")
+                             .typed<decltype(conv_nd_act_cuda)>();
+  return op.call(at::autocast::cached_cast(target, input, Device),
+                 at::autocast::cached_cast(target, weight, Device),
+                 at::autocast::cached_cast(target, bias, Device), stride, padding, dilation,
+                 groups, workspace_bytes, activation);
+}
+
 }  // namespace
 }  // namespace convnd_b200
 
 TORCH_LIBRARY_IMPL(torch_convnd, CUDA, library) {
   library.impl("conv_nd", &convnd_b200::conv_nd_cuda);
   library.impl("conv_nd_backward", &convnd_b200::conv_nd_backward_cuda);
+  library.impl("conv_nd_act", &convnd_b200::conv_nd_act_cuda);
+  library.impl("conv_nd_act_backward", &convnd_b200::conv_nd_act_backward_cuda);
 }
 
 TORCH_LIBRARY_IMPL(torch_convnd, AutocastCUDA, library) {
   library.impl("conv_nd", &convnd_b200::conv_nd_autocast<c10::DeviceType::CUDA>);
+  library.impl("conv_nd_act", &convnd_b200::conv_nd_act_autocast<c10::DeviceType::CUDA>);
 }
 
 TORCH_LIBRARY_IMPL(torch_convnd, CPU, library) {
   library.impl("conv_nd", &convnd_b200::conv_nd_cpu);
   library.impl("conv_nd_backward", &convnd_b200::conv_nd_backward_cpu);
+  library.impl("conv_nd_act", &convnd_b200::conv_nd_act_cpu);
+  library.impl("conv_nd_act_backward", &convnd_b200::conv_nd_act_backward_cpu);
 }
 
 TORCH_LIBRARY_IMPL(torch_convnd, AutocastCPU, library) {
   library.impl("conv_nd", &convnd_b200::conv_nd_autocast<c10::DeviceType::CPU>);
+  library.impl("conv_nd_act", &convnd_b200::conv_nd_act_autocast<c10::DeviceType::CPU>);
 }

@@ -39,6 +39,10 @@ struct ConvPass {
   // out_full[a]; out_strided = 0 means the output is exactly out[].
   int out_strided;
   int64_t out_mul[kMaxFastRank], out_add[kMaxFastRank], out_full[kMaxFastRank];
+  // Fused activation (CND_ACT_*): dst receives activation(conv + bias) and `pre` (if not
+  // null) conv + bias, in the same layout.
+  int activation;
+  void* pre;
 };
 
 // Weight-gradient pass: dW[g][tap][ci][co] partials of

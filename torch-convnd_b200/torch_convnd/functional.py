@@ -95,6 +95,7 @@ def conv_nd(
     padding_mode: str = "zeros",
     workspace_bytes: int = DEFAULT_WORKSPACE_BYTES,
     backend: str = "auto",
+    activation: str | None = None,
 ) -> Tensor:
     """Dense N-dimensional convolution with Conv2d/Conv3d-style semantics.
 
@@ -102,7 +103,9 @@ def conv_nd(
     ``input`` is ``[N, in_channels, d_0, ..., d_{r-1}]`` (or unbatched without N).
     ``backend`` accepts ``'auto'`` and ``'native'`` (both run the B200 kernels).
     ``workspace_bytes`` is validated with the reference's rule; the kernels need no
-    patch buffer.
+    patch buffer. ``activation='gelu'`` (an extension of the reference's API) returns
+    ``gelu(conv + bias)`` from the convolution's own epilogue, and its backward multiplies
+    by the GELU derivative while packing the gradient: no separate activation passes.
     """
     rank = weight.ndim - 2
     if not 1 <= rank <= 62:
@@ -128,7 +131,14 @@ def conv_nd(
 
     if not is_loaded():
         load_native()
-    output = torch.ops.torch_convnd.conv_nd.default(
-        input, weight, bias, list(stride), list(implicit), list(dilation), groups, workspace_bytes
-    )
+    if activation is None:
+        output = torch.ops.torch_convnd.conv_nd.default(
+            input, weight, bias, list(stride), list(implicit), list(dilation), groups,
+            workspace_bytes)
+    elif activation == "gelu":
+        output, _ = torch.ops.torch_convnd.conv_nd_act.default(
+            input, weight, bias, list(stride), list(implicit), list(dilation), groups,
+            workspace_bytes, activation)
+    else:
+        raise ValueError(f"Invalid activation {activation!r}; expected None or 'gelu'")
     return output.squeeze(0) if unbatched else output

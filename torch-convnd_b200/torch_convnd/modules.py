@@ -38,6 +38,7 @@ class ConvNd(nn.Module):
         dimensions: int,
         workspace_bytes: int = DEFAULT_WORKSPACE_BYTES,
         backend: str = "auto",
+        activation: str | None = None,
     ):
         super().__init__()
         if not isinstance(dimensions, int) or isinstance(dimensions, bool) or not 1 <= dimensions <= 62:
@@ -54,6 +55,9 @@ class ConvNd(nn.Module):
         self.transposed = False
         self.output_padding = (0,) * dimensions
         self.workspace_bytes = workspace_bytes
+        if activation not in (None, "gelu"):
+            raise ValueError(f"Invalid activation {activation!r}; expected None or 'gelu'")
+        self.activation = activation
         if backend not in ("auto", "native", "torch"):
             raise ValueError(f"Invalid backend {backend!r}")
         self.backend = backend
@@ -107,11 +111,14 @@ class ConvNd(nn.Module):
             padding_mode=self.padding_mode,
             workspace_bytes=self.workspace_bytes,
             backend=self.backend,
+            activation=self.activation,
         )
 
     def __prepare_scriptable__(self):
         """torch.jit.script hook: script the TorchScript form, which calls the native
         operator through torch_convnd::compatible_conv_nd (reference modules.py:137-155)."""
+        if self.activation is not None:
+            raise NotImplementedError("a fused activation does not support TorchScript")
         from ._script import ScriptableConvNd
 
         return ScriptableConvNd(self)
@@ -122,6 +129,7 @@ class ConvNd(nn.Module):
             f"dimensions={self.dimensions}, stride={self.stride}, padding={self.padding}, "
             f"dilation={self.dilation}, groups={self.groups}, bias={self.bias is not None}, "
             f"padding_mode={self.padding_mode!r}, backend={self.backend!r}"
+            + (f", activation={self.activation!r}" if self.activation else "")
         )
 
 
