@@ -163,5 +163,6 @@ def test_full_size_config_matches_oracle_whole(name):
         print(f"{name} {key}: rel-L2 {relative_l2(value, expected[key]):.3e}, "
               f"max |expected| {float(expected[key].abs().max()):.4g}, literal-bar "
               f"violations {literal[0]} of {value.numel()} (worst {literal[1]:.3g}x allowed)")
-        magnitude, terms = magnitudes.get(key, (None, None))
-        assert_matches(value, expected[key], cfg.dtype, f"{name} {key}", magnitude, terms)
+        magnitude, terms, split = magnitudes.get(key, (None, None, False))
+        assert_matches(value, expected[key], cfg.dtype, f"{name} {key}", magnitude, terms,
+                       split)

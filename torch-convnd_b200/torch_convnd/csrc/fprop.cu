@@ -1208,6 +1208,7 @@ int launch_fprop(const ConvPass& pass, const FpropPlan& plan_in, cudaStream_t st
   FpropParams& P = plan.params;
   P.dst = pass.dst;
   P.bias = pass.bias;
+  P.act = pass.activation;  // set per call: plans are made before the activation is known
   P.pre = pass.pre;
   P.err = device_error_word();
   P.timeout_ns = timeout_ns;
