@@ -269,7 +269,11 @@ __device__ __forceinline__ void store_run16(OutT* dst, const float (&value)[16],
       }
     }
   }
-  for (int i = done; i < 16 && i < count; ++i) dst[i] = OpCast<OutT>::cast(value[i]);
+  // constant indices only: a runtime index would move `value` to local memory
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    if (i >= done && i < count) dst[i] = OpCast<OutT>::cast(value[i]);
+  }
 }
 
 template <int kOp, int kKSteps, int kMT, int kFold>
