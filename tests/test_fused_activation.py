@@ -43,6 +43,38 @@ def test_fused_activation_schemas_and_fake_shapes():
         torch.jit.script(ConvNd(2, 2, 1, dimensions=4, activation="gelu"))
 
 
+def test_backward_runs_the_fused_operator_when_the_pre_activation_is_unused():
+    """Autograd must not hand the unused pre-activation output a materialised zero
+    gradient: that would route every backward through eager GELU-backward and add ops."""
+    from torch.utils._python_dispatch import TorchDispatchMode
+
+    class OpLog(TorchDispatchMode):
+        def __init__(self):
+            super().__init__()
+            self.ops = []
+
+        def __torch_dispatch__(self, func, types, args=(), kwargs=None):
+            self.ops.append(str(func))
+            return func(*args, **(kwargs or {}))
+
+    x = channels_last(torch.empty(2, 16, 4, 5, 6, 7)).to("meta").requires_grad_()
+    w = torch.empty(8, 16, 3, 3, 3, 3, device="meta", requires_grad=True)
+    b = torch.empty(8, device="meta", requires_grad=True)
+    geometry = ([1] * 4, [1] * 4, [1] * 4, 1, 1 << 20)
+    y, _ = torch.ops.torch_convnd.conv_nd_act(x, w, b, *geometry, "gelu")
+    with OpLog() as log:
+        y.sum().backward()
+    convs = [op for op in log.ops if "torch_convnd" in op or "gelu" in op]
+    assert convs == ["torch_convnd.conv_nd_act_backward.default"]
+    assert not any("zeros" in op or "fill" in op for op in log.ops)
+    # a gradient that does reach the pre-activation takes the eager sum instead
+    y, pre = torch.ops.torch_convnd.conv_nd_act(x, w, b, *geometry, "gelu")
+    with OpLog() as log:
+        (y.sum() + pre.sum()).backward()
+    assert "torch_convnd.conv_nd_backward.default" in log.ops
+    assert "aten.gelu_backward.default" in log.ops
+
+
 CASES = [
     # dtype, layout, batch, cin, cout, spatial, kernel, stride, padding, dilation, groups
     (torch.bfloat16, "first", 2, 32, 32, (6, 5, 7, 8), (3,) * 4, (1,) * 4, (1,) * 4, (1,) * 4, 1),

@@ -153,6 +153,9 @@ def _fake_backward_act(grad_output, pre_activation, input, weight, stride, paddi
 def _setup_context_act(ctx, inputs, output):
     input, weight, bias, *geometry = inputs
     ctx.save_for_backward(input, weight, output[1])
+    # An unused pre-activation output must arrive as None, not as a materialised zero
+    # gradient (which would turn every backward into the eager fallback below).
+    ctx.set_materialize_grads(False)
     ctx.geometry = geometry[:-1]  # stride, padding, dilation, groups, workspace_bytes
     ctx.activation = geometry[-1]
     ctx.has_bias = bias is not None

@@ -434,6 +434,7 @@ void make_plan(const cnd_problem& p, bool forward, const int32_t* mask, Plan* pl
     f.split3 = plan->split3;
     f.out_dtype = p.dtype;
     f.out_cl = plan->y_cl ? 1 : 0;
+    f.activation = plan->act;  // the planner reserves staging for the pre-activation
     plan->fast_fwd =
         plan->cout_g <= 256 && plan_best(&f, &plan->fwd_plan, variants, nvariants, false);
     if (plan->fast_fwd) {

@@ -43,6 +43,7 @@ struct FpropMaps {
   CUtensorMap act[2];
   CUtensorMap wt[2];
   CUtensorMap out;  // channels-first output, dims (o2, o1, o0, outer, n*C): TMA stores
+  CUtensorMap pre;  // the pre-activation output, same layout as `out` (pre_staged only)
 };
 
 __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
@@ -599,10 +600,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int64_t out_vol = P.out_strided ? P.out_volume_full : P.out_volume;
     // Fused activation: store the pre-activation values of this thread's row (M tile m,
     // channels c * 16 ..), then apply the activation in place.
+    // With pre_staged the staged branches write the pre-activation tile themselves.
     auto activate = [&](const Super& S, int m, int o1, int o2, int c, float (&value)[16]) {
       if (!P.act) return;
       const int o0 = (S.q0 * kMT + m) * P.e0 + i0;
-      if (P.pre != nullptr && line_ok && o0 < P.out[0] && o1 < P.out[1] && o2 < P.out[2]) {
+      if (P.pre != nullptr && !P.pre_staged && line_ok && o0 < P.out[0] && o1 < P.out[1] &&
+          o2 < P.out[2]) {
         OutT* pre = static_cast<OutT*>(P.pre);
         const int64_t sp = out_offset(S, o0, o1, o2);
         if (P.out_cl) {
@@ -672,37 +675,49 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t mask = span == 128 ? 7u : (span == 64 ? 3u : (span == 32 ? 1u : 0u));
         const int row_bytes = P.n_real * static_cast<int>(sizeof(OutT));
         const int32_t merged = static_cast<int32_t>(S.n * P.out_outer_vol + S.outer_lin);
+        // One 16-channel chunk of this thread's row into a staging buffer.
+        auto stage_row = [&](uint8_t* stage, int c, const float (&value)[16]) {
+          alignas(16) OutT packed[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) packed[i] = Traits::cast(value[i]);
+#pragma unroll
+          for (int v = 0; v < static_cast<int>(sizeof(OutT)); ++v) {  // 16-byte vectors
+            const int off = c * 16 * static_cast<int>(sizeof(OutT)) + v * 16;
+            if (off < row_bytes && line_ok) {
+              const uint32_t part = static_cast<uint32_t>(off) / span;
+              uint32_t addr = part * 128u * span + static_cast<uint32_t>(prow) * span +
+                              static_cast<uint32_t>(off) % span;
+              addr ^= ((addr >> 7) & mask) << 4;
+              *reinterpret_cast<uint4*>(stage + addr) = reinterpret_cast<const uint4*>(packed)[v];
+            }
+          }
+        };
         for (int m = 0; m < kMT; ++m, ++out_tiles) {
-          uint8_t* stage = smem + P.out_stage_off + (out_tiles & 1) * P.out_tile_bytes;
+          // tile t: buffer t % 2, and with pre_staged its pre-activation buffer beside it
+          uint8_t* stage = smem + P.out_stage_off +
+                           (out_tiles & 1) * (P.pre_staged ? 2 : 1) * P.out_tile_bytes;
+          uint8_t* pre_stage = stage + P.out_tile_bytes;
           if (store_issuer) dev::bulk_wait_group_read<1>();
           dev::named_barrier(1, 128);
           for (int c = 0; c < P.n_pad / 16; ++c) {
             float value[16];
             chunk(dbase, m, c, group_bias, value);
+            if (P.pre_staged) stage_row(pre_stage, c, value);
             activate(S, m, o1, o2, c, value);
-            alignas(16) OutT packed[16];
-#pragma unroll
-            for (int i = 0; i < 16; ++i) packed[i] = Traits::cast(value[i]);
-#pragma unroll
-            for (int v = 0; v < static_cast<int>(sizeof(OutT)); ++v) {  // 16-byte vectors
-              const int off = c * 16 * static_cast<int>(sizeof(OutT)) + v * 16;
-              if (off < row_bytes && line_ok) {
-                const uint32_t part = static_cast<uint32_t>(off) / span;
-                uint32_t addr = part * 128u * span + static_cast<uint32_t>(prow) * span +
-                                static_cast<uint32_t>(off) % span;
-                addr ^= ((addr >> 7) & mask) << 4;
-                *reinterpret_cast<uint4*>(stage + addr) =
-                    reinterpret_cast<const uint4*>(packed)[v];
-              }
-            }
+            stage_row(stage, c, value);
           }
           dev::fence_proxy_async();
           dev::named_barrier(1, 128);
           if (store_issuer) {
+            const int32_t o0 = (S.q0 * kMT + m) * P.e0;
             for (int k = 0; k * static_cast<int>(span) < row_bytes; ++k) {
-              dev::tma_store_5d(&maps.out, stage + k * 128 * span,
-                                S.g * P.n_real + k * static_cast<int>(span / sizeof(OutT)),
-                                S.q2 * P.b2o, S.q1 * P.b1, (S.q0 * kMT + m) * P.e0, merged);
+              const int32_t ch = S.g * P.n_real + k * static_cast<int>(span / sizeof(OutT));
+              dev::tma_store_5d(&maps.out, stage + k * 128 * span, ch, S.q2 * P.b2o,
+                                S.q1 * P.b1, o0, merged);
+              if (P.pre_staged) {
+                dev::tma_store_5d(&maps.pre, pre_stage + k * 128 * span, ch, S.q2 * P.b2o,
+                                  S.q1 * P.b1, o0, merged);
+              }
             }
             dev::bulk_commit_group();
           }
@@ -717,26 +732,38 @@ __global__ void __launch_bounds__(kThreads, 1)
         // buffer of tile t is reused by tile t + 2 once that store has read it.
         const int32_t nc0 = static_cast<int32_t>(S.n * P.out_channels_total +
                                                  static_cast<int64_t>(S.g) * P.n_real);
+        auto stage_cols = [&](OutT* buf, int c, const float (&value)[16]) {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int co = c * 16 + i;
+            if (co < P.n_real && line_ok) buf[co * tile_rows + prow] = Traits::cast(value[i]);
+          }
+        };
         for (int m = 0; m < kMT; ++m, ++out_tiles) {
-          OutT* stage_buf = reinterpret_cast<OutT*>(smem + P.out_stage_off +
-                                                    (out_tiles & 1) * P.out_tile_bytes);
+          OutT* stage_buf = reinterpret_cast<OutT*>(
+              smem + P.out_stage_off +
+              (out_tiles & 1) * (P.pre_staged ? 2 : 1) * P.out_tile_bytes);
+          OutT* pre_buf = reinterpret_cast<OutT*>(reinterpret_cast<uint8_t*>(stage_buf) +
+                                                  P.out_tile_bytes);
           if (store_issuer) dev::bulk_wait_group_read<1>();
           dev::named_barrier(1, 128);
           for (int c = 0; c < P.n_pad / 16; ++c) {
             float value[16];
             chunk(dbase, m, c, group_bias, value);
+            if (P.pre_staged) stage_cols(pre_buf, c, value);
             activate(S, m, o1, o2, c, value);
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              const int co = c * 16 + i;
-              if (co < P.n_real && line_ok) stage_buf[co * tile_rows + prow] = Traits::cast(value[i]);
-            }
+            stage_cols(stage_buf, c, value);
           }
           dev::fence_proxy_async();
           dev::named_barrier(1, 128);
           if (store_issuer) {
-            dev::tma_store_5d(&maps.out, stage_buf, S.q2 * P.b2o, S.q1 * P.b1,
-                              (S.q0 * kMT + m) * P.e0, static_cast<int32_t>(S.outer_lin), nc0);
+            const int32_t o0 = (S.q0 * kMT + m) * P.e0;
+            dev::tma_store_5d(&maps.out, stage_buf, S.q2 * P.b2o, S.q1 * P.b1, o0,
+                              static_cast<int32_t>(S.outer_lin), nc0);
+            if (P.pre_staged) {
+              dev::tma_store_5d(&maps.pre, pre_buf, S.q2 * P.b2o, S.q1 * P.b1, o0,
+                                static_cast<int32_t>(S.outer_lin), nc0);
+            }
             dev::bulk_commit_group();
           }
         }
@@ -1129,6 +1156,7 @@ bool plan_fprop(const ConvPass& pass, FpropPlan* plan) {
   // staging buffers fit beside at least two stages, without giving up two CTAs per SM.
   const size_t extra = 1024 + (2 * 8 + 4) * 8 + 64;
   P.tma_store = 0;
+  P.pre_staged = 0;
   P.out_tile_bytes = round_up(static_cast<uint32_t>(pass.n_real * 128 * out_es), 1024);
   P.out_cl = pass.out_cl;
   P.act = pass.activation;
@@ -1177,18 +1205,21 @@ bool plan_fprop(const ConvPass& pass, FpropPlan* plan) {
     const bool two = static_cast<size_t>(P.stages) * P.stage_bytes + extra <= 110 * 1024 &&
                      pow2_columns(2 * P.nacc * P.mt * P.n_blk) <= 256;
     const size_t cap = two ? 110 * 1024 - extra : 216 * 1024;
-    const size_t staging = 2 * static_cast<size_t>(P.out_tile_bytes);
+    // a fused activation also stages its pre-activation tile: two buffers per tile
+    const int buffers = pass.activation != 0 ? 4 : 2;
+    const size_t staging = buffers * static_cast<size_t>(P.out_tile_bytes);
     if (cap > staging) {
       int st = static_cast<int>((cap - staging) / P.stage_bytes);
       if (st > 8) st = 8;
       if (st >= 2) {
         P.stages = st;
         P.tma_store = 1;
+        P.pre_staged = pass.activation != 0 ? 1 : 0;
       }
     }
   }
   P.out_stage_off = static_cast<uint32_t>(P.stages) * P.stage_bytes;
-  P.bar_off = P.out_stage_off + (P.tma_store ? 2 * P.out_tile_bytes : 0);
+  P.bar_off = P.out_stage_off + (P.tma_store ? (P.pre_staged ? 4 : 2) * P.out_tile_bytes : 0);
   P.idesc = make_idesc(pass.op, 128, pass.n_pad);
   P.idesc_base = P.idesc & ~(0x3Fu << 17);
   P.out_dtype = pass.out_dtype;
@@ -1214,6 +1245,8 @@ int launch_fprop(const ConvPass& pass, const FpropPlan& plan_in, cudaStream_t st
   P.bias = pass.bias;
   P.act = pass.activation;  // set per call: plans are made before the activation is known
   P.pre = pass.pre;
+  // staged pre-activation tiles need a fused activation and a pre-activation tensor
+  P.pre_staged = P.pre_staged && P.act != 0 && pass.pre != nullptr ? 1 : 0;
   P.err = device_error_word();
   P.timeout_ns = timeout_ns;
   P.debug_stall = debug_stall;
@@ -1295,12 +1328,16 @@ int launch_fprop(const ConvPass& pass, const FpropPlan& plan_in, cudaStream_t st
         : P.out_span == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
         : P.out_span == 32 ? CU_TENSOR_MAP_SWIZZLE_32B
                            : CU_TENSOR_MAP_SWIZZLE_NONE;
-    const CUresult r = encode(&maps.out, out_type, 5, pass.dst, odims, ostrides, obox, oestr,
-                              CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
-                              CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) {
-      return fail(CND_ERR_CUDA, "cuTensorMapEncodeTiled (channels-last output) failed with code %d",
-                  static_cast<int>(r));
+    for (int which = 0; which < (P.pre_staged ? 2 : 1); ++which) {
+      const CUresult r = encode(which == 0 ? &maps.out : &maps.pre, out_type, 5,
+                                which == 0 ? pass.dst : pass.pre, odims, ostrides, obox, oestr,
+                                CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+                                CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+      if (r != CUDA_SUCCESS) {
+        return fail(CND_ERR_CUDA,
+                    "cuTensorMapEncodeTiled (channels-last output) failed with code %d",
+                    static_cast<int>(r));
+      }
     }
   } else if (P.tma_store) {
     // the output's own element type (float32 problems may run bf16-part operands)
@@ -1327,12 +1364,15 @@ int launch_fprop(const ConvPass& pass, const FpropPlan& plan_in, cudaStream_t st
     cuuint32_t obox[5] = {static_cast<cuuint32_t>(P.b2o), static_cast<cuuint32_t>(P.b1),
                           static_cast<cuuint32_t>(P.e0), 1, static_cast<cuuint32_t>(pass.n_real)};
     cuuint32_t oestr[5] = {1, 1, 1, 1, 1};
-    const CUresult r = encode(&maps.out, out_type, 5, pass.dst, odims, ostrides, obox,
-                              oestr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                              CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) {
-      return fail(CND_ERR_CUDA, "cuTensorMapEncodeTiled (output) failed with code %d",
-                  static_cast<int>(r));
+    for (int which = 0; which < (P.pre_staged ? 2 : 1); ++which) {
+      const CUresult r = encode(which == 0 ? &maps.out : &maps.pre, out_type, 5,
+                                which == 0 ? pass.dst : pass.pre, odims, ostrides, obox, oestr,
+                                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                                CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+      if (r != CUDA_SUCCESS) {
+        return fail(CND_ERR_CUDA, "cuTensorMapEncodeTiled (output) failed with code %d",
+                    static_cast<int>(r));
+      }
     }
   }
   // Persistent grid: two CTAs per SM when both fit (shared memory and TMEM), else one,

@@ -63,6 +63,9 @@ struct FpropParams {
   // per image; direct stores only.
   int act;    // CND_ACT_*: the epilogue applies it after the bias
   void* pre;  // pre-activation output (same layout as dst), or null
+  // pre_staged = 1: with tma_store, each tile's pre-activation is staged beside its
+  // output (two buffers per tile) and written by its own TMA store through maps.pre
+  int pre_staged;
   int out_strided;
   int64_t phase_base, out_volume_full;
   int64_t ostride_box[3], ostride_o[kMaxOuter];

@@ -60,7 +60,9 @@ constexpr int kPackPositions = 64;
 // Derivative of PyTorch's exact GELU: Phi(v) + v * phi(v).
 __device__ __forceinline__ float gelu_grad(float v) {
   const float cdf = 0.5f * (1.0f + erff(v * 0.70710678118654752f));
-  const float pdf = 0.39894228040143268f * expf(-0.5f * v * v);
+  // fast exponential: the product is rounded to the operand type (or checked against the
+  // float32 tolerance), far above its relative error of a few 1e-7
+  const float pdf = 0.39894228040143268f * __expf(-0.5f * v * v);
   return cdf + v * pdf;
 }
 
@@ -292,9 +294,11 @@ __global__ void __launch_bounds__(256) channel_sum_cl16_kernel(const T* __restri
   const int64_t row_base = static_cast<int64_t>(blockIdx.x) * kSumRows;
   const int64_t image = blockIdx.z;
   if (r0 < per_pass) {
+    // no early exit: the unrolled rows' loads are all in flight together
+#pragma unroll 4
     for (int r = r0; r < kSumRows; r += per_pass) {
       const int64_t pos = row_base + r;
-      if (pos >= S) break;
+      if (pos >= S) continue;
       const int64_t at = (image * S + pos) * C;
       uint4 word = __ldg(reinterpret_cast<const uint4*>(src + at) + v);
       T* x = reinterpret_cast<T*>(&word);
@@ -373,52 +377,76 @@ __global__ void pack_weight_kernel(const T* __restrict__ w, Tout* __restrict__ d
   }
 }
 
-// dw[(g*cout_g + co)*cin_g*taps + ci*taps + t] = sum over splits of
-// partial[s][g][t][ci][co], summed in split order. Threads walk the partial layout so the
-// split-strided reads are coalesced.
-template <typename T>
-__global__ void wgrad_reduce_kernel(const float* __restrict__ partial, int splits, int G,
-                                    int taps, int cin_g, int cout_g, T* __restrict__ dw) {
-  const int64_t total = static_cast<int64_t>(G) * taps * cin_g * cout_g;
-  for (int64_t p = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; p < total;
-       p += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    int64_t r = p;
-    const int co = static_cast<int>(r % cout_g);
-    r /= cout_g;
-    const int ci = static_cast<int>(r % cin_g);
-    r /= cin_g;
-    const int t = static_cast<int>(r % taps);
-    const int g = static_cast<int>(r / taps);
-    float sum = 0.0f;
-    // unrolled so the loads of several splits are in flight at once; the sum keeps
-    // split order
-#pragma unroll 8
-    for (int s = 0; s < splits; ++s) sum += partial[s * total + p];
-    dw[((static_cast<int64_t>(g) * cout_g + co) * cin_g + ci) * taps + t] = from_float<T>(sum);
-  }
-}
+// Split-K weight-gradient reduce. Element p of one split's partial block (`stride`
+// floats per split) is summed over the splits and written to dw:
+//  - dense groups: partial[s][g][t][ci][co] -> dw[(g*cout_g + co)*cin_g*taps + ci*taps + t]
+//  - block-diagonal (bd groups run as one): p walks (t, cb, co) with co fastest and reads
+//    partial[s][t][gb*cin_b + cb][co], gb = co / cout_b -> dw[co][cb][t].
+// A CTA takes 32 consecutive elements (one per lane, coalesced) and its 8 warps take 8
+// contiguous split ranges, each summed in split order with several loads in flight; the 8
+// range sums are then added in range order. The association is fixed, so every run gives
+// the same bits, and the CTAs keep enough loads in flight for HBM bandwidth even when a
+// layer has few weights and many splits.
+struct WgradReduceMap {
+  int bd;  // 1: dense groups; > 1: block-diagonal
+  int G, taps, cin, cout;  // cin / cout: per group (dense) or all channels (bd)
+};
 
-// Block-diagonal variant: the partials [s][t][ci][co] cover all channel pairs of a
-// problem with bd groups; dw[co][cb][t] = sum over splits of partial[s][t][gb*cin_b+cb][co]
-// with gb = co / cout_b. Threads walk (t, cb, co) with co fastest.
-template <typename T>
-__global__ void wgrad_reduce_bd_kernel(const float* __restrict__ partial, int splits, int bd,
-                                       int taps, int cin, int cout, T* __restrict__ dw) {
-  const int cin_b = cin / bd, cout_b = cout / bd;
-  const int64_t stride = static_cast<int64_t>(taps) * cin * cout;
-  const int64_t total = static_cast<int64_t>(taps) * cin_b * cout;
-  for (int64_t p = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; p < total;
-       p += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+__device__ __forceinline__ void wgrad_reduce_index(const WgradReduceMap& m, int64_t p,
+                                                   int64_t* src, int64_t* dst) {
+  if (m.bd == 1) {
     int64_t r = p;
-    const int co = static_cast<int>(r % cout);
-    r /= cout;
+    const int co = static_cast<int>(r % m.cout);
+    r /= m.cout;
+    const int ci = static_cast<int>(r % m.cin);
+    r /= m.cin;
+    const int t = static_cast<int>(r % m.taps);
+    const int g = static_cast<int>(r / m.taps);
+    *src = p;
+    *dst = ((static_cast<int64_t>(g) * m.cout + co) * m.cin + ci) * m.taps + t;
+  } else {
+    const int cin_b = m.cin / m.bd, cout_b = m.cout / m.bd;
+    int64_t r = p;
+    const int co = static_cast<int>(r % m.cout);
+    r /= m.cout;
     const int cb = static_cast<int>(r % cin_b);
     const int t = static_cast<int>(r / cin_b);
     const int ci = (co / cout_b) * cin_b + cb;
-    const int64_t src = (static_cast<int64_t>(t) * cin + ci) * cout + co;
+    *src = (static_cast<int64_t>(t) * m.cin + ci) * m.cout + co;
+    *dst = (static_cast<int64_t>(co) * cin_b + cb) * m.taps + t;
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) wgrad_reduce_kernel(const float* __restrict__ partial,
+                                                           int splits, int64_t stride,
+                                                           int64_t total, WgradReduceMap m,
+                                                           T* __restrict__ dw) {
+  __shared__ float range_sum[8][32];
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int s_begin = (warp * splits) / 8;
+  const int s_end = ((warp + 1) * splits) / 8;
+  for (int64_t base = static_cast<int64_t>(blockIdx.x) * 32; base < total;
+       base += static_cast<int64_t>(gridDim.x) * 32) {
+    const int64_t p = base + lane;
+    int64_t src = 0, dst = 0;
+    if (p < total) wgrad_reduce_index(m, p, &src, &dst);
     float sum = 0.0f;
-    for (int s = 0; s < splits; ++s) sum += partial[s * stride + src];
-    dw[(static_cast<int64_t>(co) * cin_b + cb) * taps + t] = from_float<T>(sum);
+    if (p < total) {
+      const float* at = partial + src;
+#pragma unroll 8
+      for (int s = s_begin; s < s_end; ++s) sum += at[static_cast<int64_t>(s) * stride];
+    }
+    range_sum[warp][lane] = sum;
+    __syncthreads();
+    if (warp == 0 && p < total) {
+      float v = range_sum[0][lane];
+#pragma unroll
+      for (int j = 1; j < 8; ++j) v += range_sum[j][lane];
+      dw[dst] = from_float<T>(v);
+    }
+    __syncthreads();
   }
 }
 
@@ -679,33 +707,19 @@ int pack_weights(const PackWeightArgs& in, cudaStream_t stream) {
 
 int reduce_wgrad(const float* partial, int splits, int groups, int bd, int taps, int cin_g,
                  int cout_g, void* dw, int dtype, cudaStream_t stream) {
-  if (bd > 1) {
-    const int blocks = grid_for(static_cast<int64_t>(taps) * (cin_g / bd) * cout_g, 256);
-    if (dtype == CND_BF16) {
-      wgrad_reduce_bd_kernel<<<blocks, 256, 0, stream>>>(partial, splits, bd, taps, cin_g,
-                                                         cout_g, static_cast<__nv_bfloat16*>(dw));
-    } else if (dtype == CND_F16) {
-      wgrad_reduce_bd_kernel<<<blocks, 256, 0, stream>>>(partial, splits, bd, taps, cin_g,
-                                                         cout_g, static_cast<__half*>(dw));
-    } else {
-      wgrad_reduce_bd_kernel<<<blocks, 256, 0, stream>>>(partial, splits, bd, taps, cin_g,
-                                                         cout_g, static_cast<float*>(dw));
-    }
-    count_launch();
-    const cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return fail(CND_ERR_CUDA, "wgrad_reduce: %s", cudaGetErrorString(e));
-    return CND_OK;
-  }
-  const int64_t total = static_cast<int64_t>(groups) * cout_g * cin_g * taps;
-  const int blocks = grid_for(total, 256);
+  WgradReduceMap m{bd, groups, taps, cin_g, cout_g};
+  // elements of one split's partial block, and the dW elements the reduce writes
+  const int64_t stride = static_cast<int64_t>(groups) * taps * cin_g * cout_g;
+  const int64_t total = bd > 1 ? static_cast<int64_t>(taps) * (cin_g / bd) * cout_g : stride;
+  const int blocks = grid_for((total + 31) / 32, 1);
   if (dtype == CND_BF16) {
-    wgrad_reduce_kernel<<<blocks, 256, 0, stream>>>(partial, splits, groups, taps, cin_g, cout_g,
+    wgrad_reduce_kernel<<<blocks, 256, 0, stream>>>(partial, splits, stride, total, m,
                                                     static_cast<__nv_bfloat16*>(dw));
   } else if (dtype == CND_F16) {
-    wgrad_reduce_kernel<<<blocks, 256, 0, stream>>>(partial, splits, groups, taps, cin_g, cout_g,
+    wgrad_reduce_kernel<<<blocks, 256, 0, stream>>>(partial, splits, stride, total, m,
                                                     static_cast<__half*>(dw));
   } else {
-    wgrad_reduce_kernel<<<blocks, 256, 0, stream>>>(partial, splits, groups, taps, cin_g, cout_g,
+    wgrad_reduce_kernel<<<blocks, 256, 0, stream>>>(partial, splits, stride, total, m,
                                                     static_cast<float*>(dw));
   }
   count_launch();
