@@ -35,7 +35,10 @@ namespace cnd {
 
 namespace {
 
-constexpr int kThreads = 192;
+// Warp 0: TMA producer, warp 1: MMA issuer, then epi_groups groups of four epilogue
+// warps (one per TMEM lane quarter); group g drains M tiles g, g + epi_groups, ...
+constexpr int kMaxEpiGroups = 2;
+constexpr int kMaxThreads = 64 + 128 * kMaxEpiGroups;
 constexpr uint32_t kSiteProducer = 0x301, kSiteMma = 0x302, kSiteEpilogue = 0x303,
                    kSiteMmaAcc = 0x304, kSiteDrain = 0x305;
 
@@ -278,7 +281,8 @@ __device__ __forceinline__ void store_run16(OutT* dst, const float (&value)[16],
 }
 
 template <int kOp, int kKSteps, int kMT, int kFold>
-__global__ void __launch_bounds__(kThreads, 1)
+// Ten warps put three on one scheduler, whose 16 K registers then allow 168 per thread.
+__global__ void __launch_bounds__(kMaxThreads, 1)
     fprop_kernel(const __grid_constant__ FpropMaps maps, const __grid_constant__ FpropParams P) {
   using Traits = OpTraits<kOp>;
   using OutT = typename Traits::Out;
@@ -304,7 +308,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       dev::mbar_init(&acc_full[b], 1);
-      dev::mbar_init(&acc_empty[b], 128);
+      dev::mbar_init(&acc_empty[b], 128 * P.epi_groups);
     }
     *progress = 0;
     dev::fence_barrier_init();
@@ -572,7 +576,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp >= 2) {
     // ------------------------------ epilogue ------------------------------
-    const int quarter = warp & 3;
+    const int group = (warp - 2) >> 2;
+    const int groups = P.epi_groups;
+    const int quarter = warp & 3;  // TMEM lanes 32 * (warp % 4) ..
     const int row = quarter * 32 + lane;
     const int i2 = row % P.b2;
     const int i1 = (row / P.b2) % P.b1;
@@ -629,7 +635,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int used = work_per_super < P.nacc ? work_per_super : P.nacc;
     const OutT* bias = static_cast<const OutT*>(P.bias);
     OutT* out = static_cast<OutT*>(P.dst);
-    const bool store_issuer = threadIdx.x == 64;  // warp 2, lane 0
+    const bool store_issuer = threadIdx.x == 64 + 128 * group;  // lane 0 of the group
+    // Staging: one group alternates two buffers (a store may still read the older one);
+    // with two groups each has one, reused once its previous store has read it.
+    const int stage_slots = groups == 1 ? 2 : 1;
+    const uint32_t stage_slot_bytes = (P.pre_staged ? 2 : 1) * P.out_tile_bytes;
+    uint8_t* const group_stage = smem + P.out_stage_off + group * stage_slot_bytes;
+    const int barrier_id = 1 + group;
     // TMEM column of M tile m's accumulator (descending when the a0 taps are folded).
     auto tile_col = [&](int m) { return (kFold > 0 ? kMT - 1 - m : m) * P.n_blk; };
     // One 16-channel chunk of this thread's output row of M tile m.
@@ -643,7 +655,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
     if constexpr (kFold > 0) {
       // Folded MMAs all accumulate: start both accumulator buffers at zero.
-      for (int c = 0; c < 2 * P.acc_stride; c += 16) {
+      for (int c = 16 * group; c < 2 * P.acc_stride; c += 16 * groups) {
         __syncwarp();
         dev::tmem_zero16(lane_addr + static_cast<uint32_t>(c));
       }
@@ -692,13 +704,20 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         };
-        for (int m = 0; m < kMT; ++m, ++out_tiles) {
-          // tile t: buffer t % 2, and with pre_staged its pre-activation buffer beside it
-          uint8_t* stage = smem + P.out_stage_off +
-                           (out_tiles & 1) * (P.pre_staged ? 2 : 1) * P.out_tile_bytes;
+        for (int m = group; m < kMT; m += groups, ++out_tiles) {
+          // this group's buffer of the tile, and with pre_staged its pre-activation
+          // buffer beside it
+          uint8_t* stage = group_stage + (out_tiles & (stage_slots - 1)) * groups *
+                                             stage_slot_bytes;
           uint8_t* pre_stage = stage + P.out_tile_bytes;
-          if (store_issuer) dev::bulk_wait_group_read<1>();
-          dev::named_barrier(1, 128);
+          if (store_issuer) {
+            if (stage_slots == 2) {
+              dev::bulk_wait_group_read<1>();
+            } else {
+              dev::bulk_wait_group_read<0>();
+            }
+          }
+          dev::named_barrier(barrier_id, 128);
           for (int c = 0; c < P.n_pad / 16; ++c) {
             float value[16];
             chunk(dbase, m, c, group_bias, value);
@@ -707,7 +726,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             stage_row(stage, c, value);
           }
           dev::fence_proxy_async();
-          dev::named_barrier(1, 128);
+          dev::named_barrier(barrier_id, 128);
           if (store_issuer) {
             const int32_t o0 = (S.q0 * kMT + m) * P.e0;
             for (int k = 0; k * static_cast<int>(span) < row_bytes; ++k) {
@@ -739,14 +758,19 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (co < P.n_real && line_ok) buf[co * tile_rows + prow] = Traits::cast(value[i]);
           }
         };
-        for (int m = 0; m < kMT; ++m, ++out_tiles) {
+        for (int m = group; m < kMT; m += groups, ++out_tiles) {
           OutT* stage_buf = reinterpret_cast<OutT*>(
-              smem + P.out_stage_off +
-              (out_tiles & 1) * (P.pre_staged ? 2 : 1) * P.out_tile_bytes);
+              group_stage + (out_tiles & (stage_slots - 1)) * groups * stage_slot_bytes);
           OutT* pre_buf = reinterpret_cast<OutT*>(reinterpret_cast<uint8_t*>(stage_buf) +
                                                   P.out_tile_bytes);
-          if (store_issuer) dev::bulk_wait_group_read<1>();
-          dev::named_barrier(1, 128);
+          if (store_issuer) {
+            if (stage_slots == 2) {
+              dev::bulk_wait_group_read<1>();
+            } else {
+              dev::bulk_wait_group_read<0>();
+            }
+          }
+          dev::named_barrier(barrier_id, 128);
           for (int c = 0; c < P.n_pad / 16; ++c) {
             float value[16];
             chunk(dbase, m, c, group_bias, value);
@@ -755,7 +779,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             stage_cols(stage_buf, c, value);
           }
           dev::fence_proxy_async();
-          dev::named_barrier(1, 128);
+          dev::named_barrier(barrier_id, 128);
           if (store_issuer) {
             const int32_t o0 = (S.q0 * kMT + m) * P.e0;
             dev::tma_store_5d(&maps.out, stage_buf, S.q2 * P.b2o, S.q1 * P.b1, o0,
@@ -774,7 +798,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (P.out_cl) {
         // Channels-last rows: this thread's position holds n_real consecutive channels.
-        for (int m = 0; m < kMT; ++m) {
+        for (int m = group; m < kMT; m += groups) {
           const int o0 = (S.q0 * kMT + m) * P.e0 + i0;
           const bool valid = line_ok && o0 < P.out[0] && o1 < P.out[1] && o2 < P.out[2];
           const int64_t sp = out_offset(S, o0, o1, o2);
@@ -792,7 +816,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         dev::mbar_arrive(&acc_empty[buf]);
         continue;
       }
-      for (int m = 0; m < kMT; ++m) {
+      for (int m = group; m < kMT; m += groups) {
         const int o0 = (S.q0 * kMT + m) * P.e0 + i0;
         const bool valid = line_ok && o0 < P.out[0] && o1 < P.out[1] && o2 < P.out[2];
         const int64_t sp = out_offset(S, o0, o1, o2);
@@ -1201,8 +1225,13 @@ bool plan_fprop(const ConvPass& pass, FpropPlan* plan) {
           : ((static_cast<int64_t>(P.out[2]) * out_es) % 16 == 0 && (P.b2o * out_es) % 16 == 0 &&
              pass.n_real <= 256 && pass.batch * pass.groups * pass.n_real <= kInt32Max &&
              P.out_outer_vol <= kInt32Max);
+  // Two epilogue groups whenever a super tile has two M tiles to share: the epilogue's
+  // TMEM loads, activation math and stores are latency-bound with one warp per
+  // scheduler. A CTA of ten warps holds its SM alone, so it gets the full shared memory.
+  P.epi_groups = P.mt >= 2 ? 2 : 1;
   if (store_shape) {
-    const bool two = static_cast<size_t>(P.stages) * P.stage_bytes + extra <= 110 * 1024 &&
+    const bool two = P.epi_groups == 1 &&
+                     static_cast<size_t>(P.stages) * P.stage_bytes + extra <= 110 * 1024 &&
                      pow2_columns(2 * P.nacc * P.mt * P.n_blk) <= 256;
     const size_t cap = two ? 110 * 1024 - extra : 216 * 1024;
     // a fused activation also stages its pre-activation tile: two buffers per tile
@@ -1377,7 +1406,7 @@ int launch_fprop(const ConvPass& pass, const FpropPlan& plan_in, cudaStream_t st
   }
   // Persistent grid: two CTAs per SM when both fit (shared memory and TMEM), else one,
   // enforced through the shared-memory request.
-  const bool two_per_sm = plan.smem <= 110 * 1024 && P.tmem_cols <= 256;
+  const bool two_per_sm = P.epi_groups == 1 && plan.smem <= 110 * 1024 && P.tmem_cols <= 256;
   size_t smem = plan.smem;
   if (!two_per_sm && smem < 120 * 1024) smem = 120 * 1024;
   int64_t grid = P.supers_total;
@@ -1420,7 +1449,7 @@ int launch_fprop(const ConvPass& pass, const FpropPlan& plan_in, cudaStream_t st
   if (kernel == nullptr) return fail(CND_ERR_UNSUPPORTED, "no fprop kernel for this operand");
   cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        static_cast<int>(smem));
-  kernel<<<static_cast<unsigned>(grid), kThreads, smem, stream>>>(maps, P);
+  kernel<<<static_cast<unsigned>(grid), 64 + 128 * P.epi_groups, smem, stream>>>(maps, P);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     return fail(CND_ERR_CUDA, "fprop_kernel launch failed: %s", cudaGetErrorString(e));

@@ -47,6 +47,8 @@ struct FpropParams {
   uint32_t a_part_bytes, b_part_bytes, b_off, stage_bytes, tx_bytes, idesc, tmem_cols;
   uint32_t idesc_base;  // idesc without its N field (folded MMAs set N per slice)
   int stages;
+  // epilogue groups of four warps (1 or 2); group g drains M tiles g, g + groups, ...
+  int epi_groups;
   uint32_t bar_off;  // barriers after the stages (and the output staging buffers)
   // output (channels-first); tma_store = 1 stages each M tile in shared memory as
   // [channel][position] (two buffers of out_tile_bytes at out_stage_off) and writes it
