@@ -185,6 +185,13 @@ struct Plan {
   // x and dy again as 3 (3xtf32 mode) or 2 (tf32 mode) bfloat16 terms.
   int wg_op = 0, wg_parts = 1, wg_mode = 0;
   int64_t wg_x_pad = 0, wg_dy_pad = 0;
+  // wg_fold > 1: the weight gradient reads x with the last axis's wg_fold taps folded
+  // into its channels (k1 taps per channel group instead of whole padded rows fill the
+  // M tiles of thin-channel layers); the pass sees that axis as a one-tap axis of
+  // wg_fold_last_dst positions, and wg_x holds wg_x_spatial positions per image.
+  int wg_fold = 1;
+  int64_t wg_fold_last_src = 0, wg_fold_last_dst = 0, wg_fold_d = 1, wg_fold_p = 0;
+  int64_t wg_x_spatial = 0;
   // workspace
   Region x_pack, x_pack_small, w_fwd, w_fwd_small, dy_pack, dy_pack_small, w_dg, w_dg_small,
       partial, bias_partial;
@@ -514,14 +521,59 @@ void make_plan(const cnd_problem& p, bool forward, const int32_t* mask, Plan* pl
   plan->wg_mode = f32 ? 4 : 0;
   plan->wg_x_pad = f32 ? pad_channels(kOpBF16, plan->cin_g, 1) : plan->x_pad;
   plan->wg_dy_pad = f32 ? pad_channels(kOpBF16, plan->cout_g, 16) : plan->dy_pad;
+  plan->wg_x_spatial = p.input_volume;
+  if (mask[1] && plan->bd == 1 && reduced.rank >= 1) {
+    // Fold the last axis's taps into the channels when that fills the weight-gradient
+    // M tiles markedly better. The kernel's M tile is 128 rows of tap atoms, one padded
+    // channel row each; halo plans take the a1 taps as atoms (k1 of every ceil(k1 / atoms)
+    // * atoms used), the others consecutive taps. c4 (8 channels as 16-wide bf16 parts,
+    // k1 = 3): 3/8 * 8/16 of the rows used, folded (24 channels in 32) 3/4 * 24/32.
+    const int L = reduced.rank - 1;
+    const int64_t k_last = reduced.k[L];
+    const int64_t c_fold = k_last * plan->cin_g;
+    const int fold_op = f32 ? kOpBF16 : plan->op;
+    if (k_last >= 2 && c_fold <= 64 && reduced.out[L] >= 1) {
+      const int64_t k1 = reduced.rank >= 2 ? reduced.k[L - 1] : 1;
+      const bool halo = reduced.rank >= 2 && k1 >= 2 && reduced.s[L - 1] == 1;
+      auto m_use = [&](int64_t c_real, int64_t c_pad, int64_t taps_now) {
+        const int64_t atoms = 128 / c_pad;
+        double used;
+        if (halo) {
+          used = double(k1) / double((k1 + atoms - 1) / atoms * atoms);
+        } else {
+          used = double(taps_now) / double((taps_now + atoms - 1) / atoms * atoms);
+        }
+        return used * double(c_real) / double(c_pad);
+      };
+      const int64_t pad_fold = pad_channels(fold_op, c_fold, 1);
+      if (m_use(c_fold, pad_fold, taps / k_last) >
+          1.25 * m_use(plan->cin_g, plan->wg_x_pad, taps)) {
+        plan->wg_fold = static_cast<int>(k_last);
+        plan->wg_x_pad = pad_fold;
+        plan->wg_fold_last_src = reduced.in[L];
+        plan->wg_fold_last_dst = (reduced.out[L] - 1) * reduced.s[L] + 1;
+        plan->wg_fold_d = reduced.d[L];
+        plan->wg_fold_p = reduced.p[L];
+        plan->wg_x_spatial = p.input_volume / reduced.in[L] * plan->wg_fold_last_dst;
+      }
+    }
+  }
   if (mask[1]) {
     WgradPass& wg = plan->wgrad;
     wg.rank = reduced.rank;
     wg.batch = p.batch;
     wg.groups = plan->groups;
     fill_spatial(reduced, wg.in, wg.out, wg.k, wg.s, wg.d, wg.p);
+    if (plan->wg_fold > 1) {
+      // the folded axis: one tap at offset 0 over the shifted copies' positions
+      const int L = reduced.rank - 1;
+      wg.in[L] = plan->wg_fold_last_dst;
+      wg.k[L] = 1;
+      wg.d[L] = 1;
+      wg.p[L] = 0;
+    }
     wg.c_pad = static_cast<int>(plan->wg_x_pad);
-    wg.cin_real = static_cast<int>(plan->cin_g);
+    wg.cin_real = static_cast<int>(plan->cin_g * plan->wg_fold);
     wg.n_pad = static_cast<int>(plan->wg_dy_pad);
     wg.n_real = static_cast<int>(plan->cout_g);
     wg.op = plan->wg_op;
@@ -562,8 +614,8 @@ void make_plan(const cnd_problem& p, bool forward, const int32_t* mask, Plan* pl
   if (plan->fast_wgrad) {
     const size_t wes = f32 ? 2 : es;
     const size_t act =
-        static_cast<size_t>(p.batch * plan->groups * p.input_volume) * plan->wg_x_pad * wes;
-    if (f32 || !plan->x_direct) {
+        static_cast<size_t>(p.batch * plan->groups * plan->wg_x_spatial) * plan->wg_x_pad * wes;
+    if (f32 || !plan->x_direct || plan->wg_fold > 1) {
       for (int part = 0; part < plan->wg_parts; ++part) plan->wg_x[part] = take(&cursor, act);
     }
     plan->partial = take(&cursor, static_cast<size_t>(plan->wgrad.splits) * plan->groups * taps *
@@ -671,8 +723,9 @@ int cnd_plan_summary(const cnd_problem* problem, char* buffer, size_t size) {
     char detail[256];
     cnd::describe_wgrad_pass(bwd.wgrad, detail, sizeof(detail));
     used += std::snprintf(text + used, sizeof(text) - used,
-                          "wgrad: tcgen05 splits=%d parts=%d x_pad=%lld dy_pad=%lld %s\n",
-                          bwd.wgrad.splits, bwd.wgrad.parts,
+                          "wgrad: tcgen05 splits=%d parts=%d taps_in_channels=%d x_pad=%lld "
+                          "dy_pad=%lld %s\n",
+                          bwd.wgrad.splits, bwd.wgrad.parts, bwd.wg_fold,
                           static_cast<long long>(bwd.wg_x_pad),
                           static_cast<long long>(bwd.wg_dy_pad), detail);
   } else {
@@ -970,6 +1023,11 @@ int backward_impl(const cnd_problem* problem, const void* dy, const void* pre, i
         pa.dtype = p.dtype;
         pa.mode = plan.wg_mode;
         pa.src_cl = plan.x_cl ? 1 : 0;
+        pa.fold_taps = plan.wg_fold;
+        pa.fold_dilation = static_cast<int>(plan.wg_fold_d);
+        pa.fold_padding = static_cast<int>(plan.wg_fold_p);
+        pa.fold_last_src = plan.wg_fold_last_src;
+        pa.fold_last_dst = plan.wg_fold_last_dst;
         TimedPass timed(4, stream);
         rc = pack_activations(pa, stream);
         if (rc != CND_OK) return rc;
@@ -990,7 +1048,7 @@ int backward_impl(const cnd_problem* problem, const void* dy, const void* pre, i
       TimedPass timed(6, stream);
       rc = reduce_wgrad(wg.partial, wg.splits, static_cast<int>(plan.groups), plan.bd,
                         static_cast<int>(p.kernel_volume), static_cast<int>(plan.cin_g),
-                        static_cast<int>(plan.cout_g), dw, p.dtype, stream);
+                        static_cast<int>(plan.cout_g), dw, p.dtype, stream, plan.wg_fold);
       if (rc != CND_OK) return rc;
     } else {
       GenericCall call{GenericCall::kWgrad, &p, grad, x, nullptr, dw};

@@ -377,6 +377,84 @@ __global__ void pack_weight_kernel(const T* __restrict__ w, Tout* __restrict__ d
   }
 }
 
+// Weight-gradient operand with the last axis's taps folded into the channels
+// (PackActArgs::fold_taps): destination [n][g][q][c_pad], channel c = j * Cg + ci taken
+// from source channel ci at q's position shifted along the last axis by j * dil - pad
+// (zero outside the input). One block: 64 destination positions x all channels of one
+// (n, g), staged through shared memory; loads coalesced along positions (channels-first
+// source) or channels (channels-last), stores coalesced along channels.
+template <typename Tin, typename Tout, int kMode, bool kSrcCL>
+__global__ void __launch_bounds__(256) pack_fold_kernel(
+    const Tin* __restrict__ src, Tout* __restrict__ dst0, Tout* __restrict__ dst1,
+    int64_t S_src, int64_t S_dst, int64_t last_src, int64_t last_dst, int Cg, int c_pad, int G,
+    int taps, int dil, int pad) {
+  static_assert(sizeof(Tout) == 2, "16-bit operands");
+  extern __shared__ float tile[];  // [c_pad][kPackPositions + 1]
+  // The block's positions decoded once: source position of the unshifted row (-1 past
+  // the end) and the last-axis coordinate before the tap shift.
+  __shared__ int64_t row_base[kPackPositions];
+  __shared__ int row_last[kPackPositions];
+  const int64_t s0 = static_cast<int64_t>(blockIdx.x) * kPackPositions;
+  const int g = blockIdx.y;
+  const int64_t n = blockIdx.z;
+  const int width = kPackPositions + 1;
+  const int folded = taps * Cg;
+  if (threadIdx.x < kPackPositions) {
+    const int64_t q = s0 + threadIdx.x;
+    const int64_t outer = q / last_dst;
+    row_base[threadIdx.x] = q < S_dst ? outer * last_src : -1;
+    row_last[threadIdx.x] = static_cast<int>(q - outer * last_dst) - pad;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < c_pad * kPackPositions; i += blockDim.x) {
+    int c, s;
+    if constexpr (kSrcCL) {
+      s = i / c_pad;
+      c = i - s * c_pad;
+    } else {
+      c = i / kPackPositions;
+      s = i - c * kPackPositions;
+    }
+    float v = 0.0f;
+    const int64_t rb = row_base[s];
+    if (c < folded && rb >= 0) {
+      const int j = c / Cg;
+      const int ci = c - j * Cg;
+      const int at = row_last[s] + j * dil;
+      if (at >= 0 && at < last_src) {
+        const int64_t pos = rb + at;
+        if constexpr (kSrcCL) {
+          v = to_float(src[(n * S_src + pos) * G * Cg + static_cast<int64_t>(g) * Cg + ci]);
+        } else {
+          v = to_float(src[((n * G + g) * Cg + ci) * S_src + pos]);
+        }
+      }
+    }
+    tile[c * width + s] = v;
+  }
+  __syncthreads();
+  // 16-byte stores of 8 channels (c_pad is a multiple of 8); mode 4 writes bf16 hi + lo.
+  const int64_t base = ((n * G + g) * S_dst + s0) * c_pad;
+  const int count = static_cast<int>(S_dst - s0 < kPackPositions ? S_dst - s0 : kPackPositions);
+  for (int i = threadIdx.x; i < count * c_pad / 8; i += blockDim.x) {
+    const int e = i * 8;
+    const int s = e / c_pad;
+    const int c = e - s * c_pad;
+    alignas(16) Tout hi[8];
+    alignas(16) Tout lo[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const float v = tile[(c + k) * width + s];
+      hi[k] = from_float<Tout>(v);
+      if constexpr (kMode == 4) lo[k] = from_float<Tout>(v - to_float(hi[k]));
+    }
+    *reinterpret_cast<uint4*>(dst0 + base + e) = *reinterpret_cast<const uint4*>(hi);
+    if constexpr (kMode == 4) {
+      *reinterpret_cast<uint4*>(dst1 + base + e) = *reinterpret_cast<const uint4*>(lo);
+    }
+  }
+}
+
 // Split-K weight-gradient reduce. Element p of one split's partial block (`stride`
 // floats per split) is summed over the splits and written to dw:
 //  - dense groups: partial[s][g][t][ci][co] -> dw[(g*cout_g + co)*cin_g*taps + ci*taps + t]
@@ -390,18 +468,25 @@ __global__ void pack_weight_kernel(const T* __restrict__ w, Tout* __restrict__ d
 struct WgradReduceMap {
   int bd;  // 1: dense groups; > 1: block-diagonal
   int G, taps, cin, cout;  // cin / cout: per group (dense) or all channels (bd)
+  int fold;  // > 1 (dense only): last-axis taps folded into the partials' channels
 };
 
 __device__ __forceinline__ void wgrad_reduce_index(const WgradReduceMap& m, int64_t p,
                                                    int64_t* src, int64_t* dst) {
   if (m.bd == 1) {
+    // partial [g][t'][j * cin + ci][co] with t' over taps / fold: dw tap t' * fold + j
+    const int taps_f = m.taps / m.fold;
+    const int cin_f = m.cin * m.fold;
     int64_t r = p;
     const int co = static_cast<int>(r % m.cout);
     r /= m.cout;
-    const int ci = static_cast<int>(r % m.cin);
-    r /= m.cin;
-    const int t = static_cast<int>(r % m.taps);
-    const int g = static_cast<int>(r / m.taps);
+    const int cf = static_cast<int>(r % cin_f);
+    r /= cin_f;
+    const int tf = static_cast<int>(r % taps_f);
+    const int g = static_cast<int>(r / taps_f);
+    const int j = cf / m.cin;
+    const int ci = cf - j * m.cin;
+    const int t = tf * m.fold + j;
     *src = p;
     *dst = ((static_cast<int64_t>(g) * m.cout + co) * m.cin + ci) * m.taps + t;
   } else {
@@ -509,6 +594,34 @@ template <typename Tin, typename Tout, int kMode>
 int launch_pack_act(const PackActArgs& a, cudaStream_t stream) {
   if (a.src_cl) return launch_pack_act_impl<Tin, Tout, kMode, true>(a, stream);
   return launch_pack_act_impl<Tin, Tout, kMode, false>(a, stream);
+}
+
+template <typename Tin, typename Tout, int kMode, bool kSrcCL>
+int launch_pack_fold_impl(const PackActArgs& a, cudaStream_t stream) {
+  const int64_t s_dst = a.spatial / a.fold_last_src * a.fold_last_dst;
+  const int64_t blocks = (s_dst + kPackPositions - 1) / kPackPositions;
+  if (blocks > 0x7FFFFFFF || a.groups > 65535 || a.batch > 65535) {
+    return fail(CND_ERR_UNSUPPORTED, "pack_fold: grid too large");
+  }
+  const dim3 grid(static_cast<unsigned>(blocks), static_cast<unsigned>(a.groups),
+                  static_cast<unsigned>(a.batch));
+  const size_t smem = static_cast<size_t>(a.c_pad) * (kPackPositions + 1) * sizeof(float);
+  if (smem > 200 * 1024) return fail(CND_ERR_UNSUPPORTED, "pack_fold: too many channels");
+  auto kernel = pack_fold_kernel<Tin, Tout, kMode, kSrcCL>;
+  cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       static_cast<int>(smem));
+  kernel<<<grid, 256, smem, stream>>>(
+      static_cast<const Tin*>(a.src), static_cast<Tout*>(a.dst), static_cast<Tout*>(a.dst_small),
+      a.spatial, s_dst, a.fold_last_src, a.fold_last_dst, a.cg, a.c_pad,
+      static_cast<int>(a.groups), a.fold_taps, a.fold_dilation, a.fold_padding);
+  count_launch();
+  return CND_OK;
+}
+
+template <typename Tin, typename Tout, int kMode>
+int launch_pack_fold(const PackActArgs& a, cudaStream_t stream) {
+  if (a.src_cl) return launch_pack_fold_impl<Tin, Tout, kMode, true>(a, stream);
+  return launch_pack_fold_impl<Tin, Tout, kMode, false>(a, stream);
 }
 
 template <typename T>
@@ -645,7 +758,26 @@ int channel_sums(const PackActArgs& a, cudaStream_t stream);
 
 int pack_activations(const PackActArgs& args, cudaStream_t stream) {
   int rc;
-  if (channel_sums_fast_ok(args)) {
+  if (args.fold_taps > 1) {
+    if (args.dst == nullptr || args.act != 0 || args.chan_partial != nullptr ||
+        args.fold_last_src < 1 || args.fold_last_dst < 1 ||
+        args.spatial % args.fold_last_src != 0 || args.fold_taps * args.cg > args.c_pad) {
+      return fail(CND_ERR_INVALID, "pack_activations: invalid folded-tap pack");
+    }
+    if (args.c_pad % 8 != 0 || reinterpret_cast<uintptr_t>(args.dst) % 16 != 0 ||
+        (args.mode == 4 && reinterpret_cast<uintptr_t>(args.dst_small) % 16 != 0)) {
+      return fail(CND_ERR_INVALID, "pack_activations: folded-tap pack needs 16-byte rows");
+    }
+    if (args.dtype == CND_BF16) {
+      rc = launch_pack_fold<__nv_bfloat16, __nv_bfloat16, 0>(args, stream);
+    } else if (args.dtype == CND_F16) {
+      rc = launch_pack_fold<__half, __half, 0>(args, stream);
+    } else if (args.dtype == CND_F32 && args.mode == 4) {
+      rc = launch_pack_fold<float, __nv_bfloat16, 4>(args, stream);
+    } else {
+      return fail(CND_ERR_UNSUPPORTED, "pack_activations: folded taps need 16-bit operands");
+    }
+  } else if (channel_sums_fast_ok(args)) {
     return channel_sums(args, stream);
   } else if ((args.dtype == CND_BF16 || args.dtype == CND_F16) && pack16_fast_ok(args)) {
     rc = args.dtype == CND_BF16 ? launch_pack_act16<__nv_bfloat16>(args, stream)
@@ -706,8 +838,12 @@ int pack_weights(const PackWeightArgs& in, cudaStream_t stream) {
 }
 
 int reduce_wgrad(const float* partial, int splits, int groups, int bd, int taps, int cin_g,
-                 int cout_g, void* dw, int dtype, cudaStream_t stream) {
-  WgradReduceMap m{bd, groups, taps, cin_g, cout_g};
+                 int cout_g, void* dw, int dtype, cudaStream_t stream, int fold) {
+  if (fold < 1 || taps % fold != 0 || (fold > 1 && bd > 1)) {
+    return fail(CND_ERR_INVALID, "wgrad_reduce: %d folded taps of %d (block-diagonal %d)",
+                fold, taps, bd);
+  }
+  WgradReduceMap m{bd, groups, taps, cin_g, cout_g, fold};
   // elements of one split's partial block, and the dW elements the reduce writes
   const int64_t stride = static_cast<int64_t>(groups) * taps * cin_g * cout_g;
   const int64_t total = bd > 1 ? static_cast<int64_t>(taps) * (cin_g / bd) * cout_g : stride;

@@ -26,6 +26,15 @@ struct PackActArgs {
   // source's shape and layout; CND_ACT_*) in fp32 before it is stored, rounded once.
   int act;
   const void* pre;
+  // fold_taps > 1 (weight-gradient operand): the taps of the last spatial axis folded
+  // into the channels. Destination channel j * cg + ci (j < fold_taps) holds source
+  // channel ci at the position shifted along the last axis by j * fold_dilation -
+  // fold_padding (zero outside the input); the destination's last axis has
+  // fold_last_dst positions (the source's fold_last_src), so it has
+  // spatial / fold_last_src * fold_last_dst positions. No activation or channel sums.
+  int fold_taps;
+  int fold_dilation, fold_padding;
+  int64_t fold_last_src, fold_last_dst;
 };
 
 // Weights [groups*cout_g][cin_g][taps] -> [groups][taps][n_pad][c_pad] (mode as for
@@ -60,8 +69,11 @@ int pack_activations(const PackActArgs& args, cudaStream_t stream);
 int pack_weights(const PackWeightArgs& args, cudaStream_t stream);
 // bd > 1: the partials are of the dense block-diagonal problem (groups == 1, cin_g /
 // cout_g = all channels); only the bd diagonal blocks are written to dw.
+// fold > 1: the partials are of the problem whose last axis's `fold` taps were folded
+// into the channels (PackActArgs::fold_taps): partial channel j * cin_g + ci of folded
+// tap t' is dw's channel ci at tap t' * fold + j (taps counts dw's taps).
 int reduce_wgrad(const float* partial, int splits, int groups, int bd, int taps, int cin_g,
-                 int cout_g, void* dw, int dtype, cudaStream_t stream);
+                 int cout_g, void* dw, int dtype, cudaStream_t stream, int fold = 1);
 int reduce_bias(const float* partial, int64_t batch, int groups, int blocks, int cg, void* db,
                 int dtype, cudaStream_t stream);
 // Elementwise activation passes for problems the tcgen05 epilogue / pack do not serve:
