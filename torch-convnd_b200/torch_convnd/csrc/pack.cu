@@ -406,31 +406,39 @@ __global__ void __launch_bounds__(256) pack_fold_kernel(
     row_last[threadIdx.x] = static_cast<int>(q - outer * last_dst) - pad;
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < c_pad * kPackPositions; i += blockDim.x) {
-    int c, s;
+  // Each (source channel, position) item loads its `taps` shifted copies (independent
+  // loads); the padding channels past taps * Cg are zero.
+  for (int i = threadIdx.x; i < (c_pad - folded) * kPackPositions; i += blockDim.x) {
+    tile[(folded + i / kPackPositions) * width + i % kPackPositions] = 0.0f;
+  }
+  // unrolled: a thread's items issue all their loads before the shared-memory stores
+#pragma unroll 4
+  for (int i = threadIdx.x; i < Cg * kPackPositions; i += blockDim.x) {
+    int ci, s;
     if constexpr (kSrcCL) {
-      s = i / c_pad;
-      c = i - s * c_pad;
+      s = i / Cg;
+      ci = i - s * Cg;
     } else {
-      c = i / kPackPositions;
-      s = i - c * kPackPositions;
+      ci = i / kPackPositions;
+      s = i - ci * kPackPositions;
     }
-    float v = 0.0f;
     const int64_t rb = row_base[s];
-    if (c < folded && rb >= 0) {
-      const int j = c / Cg;
-      const int ci = c - j * Cg;
-      const int at = row_last[s] + j * dil;
-      if (at >= 0 && at < last_src) {
-        const int64_t pos = rb + at;
-        if constexpr (kSrcCL) {
-          v = to_float(src[(n * S_src + pos) * G * Cg + static_cast<int64_t>(g) * Cg + ci]);
-        } else {
-          v = to_float(src[((n * G + g) * Cg + ci) * S_src + pos]);
-        }
-      }
+    const Tin* row;
+    int64_t step;  // elements between neighbouring positions of the source row
+    if constexpr (kSrcCL) {
+      row = src + (n * S_src + (rb < 0 ? 0 : rb)) * G * Cg + static_cast<int64_t>(g) * Cg + ci;
+      step = static_cast<int64_t>(G) * Cg;
+    } else {
+      row = src + ((n * G + g) * Cg + ci) * S_src + (rb < 0 ? 0 : rb);
+      step = 1;
     }
-    tile[c * width + s] = v;
+#pragma unroll 4
+    for (int j = 0; j < taps; ++j) {
+      const int at = row_last[s] + j * dil;
+      float v = 0.0f;
+      if (rb >= 0 && at >= 0 && at < last_src) v = to_float(row[at * step]);
+      tile[(j * Cg + ci) * width + s] = v;
+    }
   }
   __syncthreads();
   // 16-byte stores of 8 channels (c_pad is a multiple of 8); mode 4 writes bf16 hi + lo.
