@@ -532,7 +532,8 @@ void make_plan(const cnd_problem& p, bool forward, const int32_t* mask, Plan* pl
     const int64_t k_last = reduced.k[L];
     const int64_t c_fold = k_last * plan->cin_g;
     const int fold_op = f32 ? kOpBF16 : plan->op;
-    if (k_last >= 2 && c_fold <= 64 && reduced.out[L] >= 1) {
+    const bool whole_chunks = plan->cin_g == 8 || plan->cin_g == 16 || plan->cin_g == 32;
+    if (k_last >= 2 && c_fold <= 64 && whole_chunks && reduced.out[L] >= 1) {
       const int64_t k1 = reduced.rank >= 2 ? reduced.k[L - 1] : 1;
       const bool halo = reduced.rank >= 2 && k1 >= 2 && reduced.s[L - 1] == 1;
       auto m_use = [&](int64_t c_real, int64_t c_pad, int64_t taps_now) {

@@ -380,85 +380,110 @@ __global__ void pack_weight_kernel(const T* __restrict__ w, Tout* __restrict__ d
 // Weight-gradient operand with the last axis's taps folded into the channels
 // (PackActArgs::fold_taps): destination [n][g][q][c_pad], channel c = j * Cg + ci taken
 // from source channel ci at q's position shifted along the last axis by j * dil - pad
-// (zero outside the input). One block: 64 destination positions x all channels of one
-// (n, g), staged through shared memory; loads coalesced along positions (channels-first
-// source) or channels (channels-last), stores coalesced along channels.
-template <typename Tin, typename Tout, int kMode, bool kSrcCL>
+// (zero outside the input). One thread per destination position gathers its channels (a
+// warp's loads of one channel cover consecutive positions: coalesced for a channels-first
+// source, cache-line reuse along a channels-last source's rows); the warp then writes its
+// 32 positions' rows, which are contiguous in the destination, through a padded
+// shared-memory stage as 512-byte runs (mode 4: bf16 hi, then lo). The pack is bound by
+// instructions and store wavefronts, not bytes, so nothing here divides by a runtime value.
+constexpr int kFoldMaxPad = 64;  // channels per destination row (16, 32 or 64)
+
+template <typename Tin, typename Tout, int kMode, bool kSrcCL, int kCg>
 __global__ void __launch_bounds__(256) pack_fold_kernel(
     const Tin* __restrict__ src, Tout* __restrict__ dst0, Tout* __restrict__ dst1,
-    int64_t S_src, int64_t S_dst, int64_t last_src, int64_t last_dst, int Cg, int c_pad, int G,
-    int taps, int dil, int pad) {
+    int64_t S_src, int64_t S_dst, int64_t last_src, int64_t last_dst, int Cg_rt, int c_pad,
+    int G, int taps, int dil, int pad) {
   static_assert(sizeof(Tout) == 2, "16-bit operands");
-  extern __shared__ float tile[];  // [c_pad][kPackPositions + 1]
-  // The block's positions decoded once: source position of the unshifted row (-1 past
-  // the end) and the last-axis coordinate before the tap shift.
-  __shared__ int64_t row_base[kPackPositions];
-  __shared__ int row_last[kPackPositions];
-  const int64_t s0 = static_cast<int64_t>(blockIdx.x) * kPackPositions;
+  static_assert(kCg % 8 == 0, "whole 8-channel chunks per tap");
+  constexpr int kPitch = kFoldMaxPad * 2 + 16;  // bytes per staged row (bank spread)
+  constexpr bool kRaw = kMode == 0 && sizeof(Tin) == sizeof(Tout);  // copy the bits as is
+  (void)Cg_rt;
+  __shared__ __align__(16) uint8_t stage[8][32 * kPitch];
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
   const int g = blockIdx.y;
   const int64_t n = blockIdx.z;
-  const int width = kPackPositions + 1;
-  const int folded = taps * Cg;
-  if (threadIdx.x < kPackPositions) {
-    const int64_t q = s0 + threadIdx.x;
-    const int64_t outer = q / last_dst;
-    row_base[threadIdx.x] = q < S_dst ? outer * last_src : -1;
-    row_last[threadIdx.x] = static_cast<int>(q - outer * last_dst) - pad;
-  }
-  __syncthreads();
-  // Each (source channel, position) item loads its `taps` shifted copies (independent
-  // loads); the padding channels past taps * Cg are zero.
-  for (int i = threadIdx.x; i < (c_pad - folded) * kPackPositions; i += blockDim.x) {
-    tile[(folded + i / kPackPositions) * width + i % kPackPositions] = 0.0f;
-  }
-  // unrolled: a thread's items issue all their loads before the shared-memory stores
-#pragma unroll 4
-  for (int i = threadIdx.x; i < Cg * kPackPositions; i += blockDim.x) {
-    int ci, s;
+  const int64_t q0 = static_cast<int64_t>(blockIdx.x) * blockDim.x + warp * 32;  // warp's first
+  const int64_t q = q0 + lane;
+  const bool valid = q < S_dst;
+  uint8_t* row_stage = stage[warp] + lane * kPitch;
+  uint4 lo_vec[kFoldMaxPad / 8];
+  {
+    const int64_t qc = valid ? q : 0;
+    const int64_t outer = qc / last_dst;
+    const int i_last = static_cast<int>(qc - outer * last_dst) - pad;
+    const int64_t row0 = outer * last_src;  // source position of (outer, last-axis 0)
+    const Tin* plane;   // channel 0 of this (n, g) at source position row0
+    int64_t ch_step;    // elements between channels
+    int64_t pos_step;   // elements between positions
     if constexpr (kSrcCL) {
-      s = i / Cg;
-      ci = i - s * Cg;
+      pos_step = static_cast<int64_t>(G) * kCg;
+      ch_step = 1;
+      plane = src + (n * S_src + row0) * pos_step + static_cast<int64_t>(g) * kCg;
     } else {
-      ci = i / kPackPositions;
-      s = i - ci * kPackPositions;
+      pos_step = 1;
+      ch_step = S_src;
+      plane = src + (n * G + g) * kCg * S_src + row0;
     }
-    const int64_t rb = row_base[s];
-    const Tin* row;
-    int64_t step;  // elements between neighbouring positions of the source row
-    if constexpr (kSrcCL) {
-      row = src + (n * S_src + (rb < 0 ? 0 : rb)) * G * Cg + static_cast<int64_t>(g) * Cg + ci;
-      step = static_cast<int64_t>(G) * Cg;
-    } else {
-      row = src + ((n * G + g) * Cg + ci) * S_src + (rb < 0 ? 0 : rb);
-      step = 1;
-    }
-#pragma unroll 4
     for (int j = 0; j < taps; ++j) {
-      const int at = row_last[s] + j * dil;
-      float v = 0.0f;
-      if (rb >= 0 && at >= 0 && at < last_src) v = to_float(row[at * step]);
-      tile[(j * Cg + ci) * width + s] = v;
+      const int at = i_last + j * dil;
+      const bool in = valid && at >= 0 && at < last_src;
+      const Tin* p = plane + (in ? at : 0) * pos_step;
+#pragma unroll
+      for (int c8 = 0; c8 < kCg; c8 += 8) {
+        alignas(16) Tout hi[8];
+        alignas(16) Tout lo[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          if constexpr (kRaw) {
+            hi[k] = in ? p[(c8 + k) * ch_step] : Tout{};
+          } else {
+            const float v = in ? to_float(p[(c8 + k) * ch_step]) : 0.0f;
+            hi[k] = from_float<Tout>(v);
+            if constexpr (kMode == 4) lo[k] = from_float<Tout>(v - to_float(hi[k]));
+          }
+        }
+        const int m = j * kCg + c8;  // first channel of the chunk
+        *reinterpret_cast<uint4*>(row_stage + m * 2) = *reinterpret_cast<const uint4*>(hi);
+        if constexpr (kMode == 4) {
+#pragma unroll
+          for (int u = 0; u < kFoldMaxPad / 8; ++u) {
+            if (u == m / 8) lo_vec[u] = *reinterpret_cast<const uint4*>(lo);
+          }
+        }
+      }
+    }
+    for (int m = taps * kCg; m < c_pad; m += 8) {  // padding channels
+      *reinterpret_cast<uint4*>(row_stage + m * 2) = make_uint4(0, 0, 0, 0);
+      if constexpr (kMode == 4) {
+#pragma unroll
+        for (int u = 0; u < kFoldMaxPad / 8; ++u) {
+          if (u == m / 8) lo_vec[u] = make_uint4(0, 0, 0, 0);
+        }
+      }
     }
   }
-  __syncthreads();
-  // 16-byte stores of 8 channels (c_pad is a multiple of 8); mode 4 writes bf16 hi + lo.
-  const int64_t base = ((n * G + g) * S_dst + s0) * c_pad;
-  const int count = static_cast<int>(S_dst - s0 < kPackPositions ? S_dst - s0 : kPackPositions);
-  for (int i = threadIdx.x; i < count * c_pad / 8; i += blockDim.x) {
-    const int e = i * 8;
-    const int s = e / c_pad;
-    const int c = e - s * c_pad;
-    alignas(16) Tout hi[8];
-    alignas(16) Tout lo[8];
+  // copy-out: the warp's rows are contiguous in the destination (row_bytes each)
+  uint8_t* ws = stage[warp];
+  const int row_shift = __ffs(c_pad * 2) - 1;  // log2 of the row bytes (32, 64 or 128)
+  const int64_t out_base = ((n * G + g) * S_dst + q0) * c_pad;  // elements
+  const int64_t rows_here = S_dst - q0 < 32 ? S_dst - q0 : 32;
+  const int run_bytes = static_cast<int>(rows_here) << row_shift;
+  for (int part = 0; part < (kMode == 4 ? 2 : 1); ++part) {
+    if (part == 1) {
+      __syncwarp();
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const float v = tile[(c + k) * width + s];
-      hi[k] = from_float<Tout>(v);
-      if constexpr (kMode == 4) lo[k] = from_float<Tout>(v - to_float(hi[k]));
+      for (int u = 0; u < kFoldMaxPad / 8; ++u) {
+        if (u * 8 < c_pad) *reinterpret_cast<uint4*>(row_stage + u * 16) = lo_vec[u];
+      }
     }
-    *reinterpret_cast<uint4*>(dst0 + base + e) = *reinterpret_cast<const uint4*>(hi);
-    if constexpr (kMode == 4) {
-      *reinterpret_cast<uint4*>(dst1 + base + e) = *reinterpret_cast<const uint4*>(lo);
+    __syncwarp();
+    uint8_t* out = reinterpret_cast<uint8_t*>((part == 0 ? dst0 : dst1) + out_base);
+    for (int o = lane * 16; o < run_bytes; o += 512) {
+      const int row = o >> row_shift;
+      const int within = o & ((1 << row_shift) - 1);
+      *reinterpret_cast<uint4*>(out + o) =
+          *reinterpret_cast<const uint4*>(ws + row * kPitch + within);
     }
   }
 }
@@ -607,21 +632,28 @@ int launch_pack_act(const PackActArgs& a, cudaStream_t stream) {
 template <typename Tin, typename Tout, int kMode, bool kSrcCL>
 int launch_pack_fold_impl(const PackActArgs& a, cudaStream_t stream) {
   const int64_t s_dst = a.spatial / a.fold_last_src * a.fold_last_dst;
-  const int64_t blocks = (s_dst + kPackPositions - 1) / kPackPositions;
+  const int64_t blocks = (s_dst + 255) / 256;
   if (blocks > 0x7FFFFFFF || a.groups > 65535 || a.batch > 65535) {
     return fail(CND_ERR_UNSUPPORTED, "pack_fold: grid too large");
   }
   const dim3 grid(static_cast<unsigned>(blocks), static_cast<unsigned>(a.groups),
                   static_cast<unsigned>(a.batch));
-  const size_t smem = static_cast<size_t>(a.c_pad) * (kPackPositions + 1) * sizeof(float);
-  if (smem > 200 * 1024) return fail(CND_ERR_UNSUPPORTED, "pack_fold: too many channels");
-  auto kernel = pack_fold_kernel<Tin, Tout, kMode, kSrcCL>;
-  cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                       static_cast<int>(smem));
-  kernel<<<grid, 256, smem, stream>>>(
-      static_cast<const Tin*>(a.src), static_cast<Tout*>(a.dst), static_cast<Tout*>(a.dst_small),
-      a.spatial, s_dst, a.fold_last_src, a.fold_last_dst, a.cg, a.c_pad,
-      static_cast<int>(a.groups), a.fold_taps, a.fold_dilation, a.fold_padding);
+  auto args = [&](auto kernel) {
+    kernel<<<grid, 256, 0, stream>>>(
+        static_cast<const Tin*>(a.src), static_cast<Tout*>(a.dst),
+        static_cast<Tout*>(a.dst_small), a.spatial, s_dst, a.fold_last_src, a.fold_last_dst,
+        a.cg, a.c_pad, static_cast<int>(a.groups), a.fold_taps, a.fold_dilation,
+        a.fold_padding);
+  };
+  if (a.cg == 8) {
+    args(pack_fold_kernel<Tin, Tout, kMode, kSrcCL, 8>);
+  } else if (a.cg == 16) {
+    args(pack_fold_kernel<Tin, Tout, kMode, kSrcCL, 16>);
+  } else if (a.cg == 32) {
+    args(pack_fold_kernel<Tin, Tout, kMode, kSrcCL, 32>);
+  } else {
+    return fail(CND_ERR_UNSUPPORTED, "pack_fold: %d channels per group", a.cg);
+  }
   count_launch();
   return CND_OK;
 }
@@ -772,7 +804,8 @@ int pack_activations(const PackActArgs& args, cudaStream_t stream) {
         args.spatial % args.fold_last_src != 0 || args.fold_taps * args.cg > args.c_pad) {
       return fail(CND_ERR_INVALID, "pack_activations: invalid folded-tap pack");
     }
-    if (args.c_pad % 8 != 0 || reinterpret_cast<uintptr_t>(args.dst) % 16 != 0 ||
+    if ((args.c_pad != 16 && args.c_pad != 32 && args.c_pad != kFoldMaxPad) ||
+        reinterpret_cast<uintptr_t>(args.dst) % 16 != 0 ||
         (args.mode == 4 && reinterpret_cast<uintptr_t>(args.dst_small) % 16 != 0)) {
       return fail(CND_ERR_INVALID, "pack_activations: folded-tap pack needs 16-byte rows");
     }
