@@ -14,6 +14,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <memory>
 #include <mutex>
 #include <vector>
 
@@ -647,22 +648,65 @@ int check_cuda(const char* what) {
 }
 
 }  // namespace
+// Plans depend only on the problem (all of its bytes, which include the layout and
+// activation bits and the fp32 mode), the pass kind and the gradient mask, so the host
+// cost-model search runs once per distinct problem and is kept (the newest
+// kPlanCacheSize problems; a shared pointer keeps a dropped plan alive for a caller still
+// using it). A training step then spends no host time planning.
+constexpr size_t kPlanCacheSize = 64;
+struct PlanCacheEntry {
+  uint64_t hash;
+  int kind;
+  cnd_problem problem;
+  std::shared_ptr<const Plan> plan;
+};
+std::mutex g_plan_cache_mutex;
+std::vector<PlanCacheEntry> g_plan_cache;
+
+uint64_t problem_hash(const cnd_problem& p, int kind) {
+  const unsigned char* bytes = reinterpret_cast<const unsigned char*>(&p);
+  uint64_t h = 1469598103934665603ull ^ static_cast<uint64_t>(kind);
+  for (size_t i = 0; i < sizeof(p); i += 8) {
+    uint64_t word = 0;
+    std::memcpy(&word, bytes + i, sizeof(p) - i < 8 ? sizeof(p) - i : 8);
+    h = (h ^ word) * 1099511628211ull;
+  }
+  return h;
+}
+
+std::shared_ptr<const Plan> cached_plan(const cnd_problem& p, bool forward, const int32_t* mask) {
+  const int kind =
+      forward ? 8 : ((mask[0] != 0 ? 1 : 0) | (mask[1] != 0 ? 2 : 0) | (mask[2] != 0 ? 4 : 0));
+  const uint64_t hash = problem_hash(p, kind);
+  {
+    std::lock_guard<std::mutex> lock(g_plan_cache_mutex);
+    for (auto it = g_plan_cache.rbegin(); it != g_plan_cache.rend(); ++it) {
+      if (it->hash == hash && it->kind == kind &&
+          std::memcmp(&it->problem, &p, sizeof(p)) == 0) {
+        return it->plan;
+      }
+    }
+  }
+  auto plan = std::make_shared<Plan>();
+  make_plan(p, forward, mask, plan.get());
+  std::lock_guard<std::mutex> lock(g_plan_cache_mutex);
+  if (g_plan_cache.size() >= kPlanCacheSize) g_plan_cache.erase(g_plan_cache.begin());
+  g_plan_cache.push_back(PlanCacheEntry{hash, kind, p, plan});
+  return plan;
+}
+
 }  // namespace cnd
 
 extern "C" {
 
 size_t cnd_forward_workspace_size(const cnd_problem* problem) {
   if (problem == nullptr) return 0;
-  cnd::Plan plan;
-  cnd::make_plan(*problem, true, nullptr, &plan);
-  return plan.total;
+  return cnd::cached_plan(*problem, true, nullptr)->total;
 }
 
 size_t cnd_backward_workspace_size(const cnd_problem* problem, const int32_t output_mask[3]) {
   if (problem == nullptr || output_mask == nullptr) return 0;
-  cnd::Plan plan;
-  cnd::make_plan(*problem, false, output_mask, &plan);
-  return plan.total;
+  return cnd::cached_plan(*problem, false, output_mask)->total;
 }
 
 int cnd_fast_path_mask(const cnd_problem* problem) {
@@ -759,8 +803,8 @@ int forward_impl(const cnd_problem* problem, const void* x, const void* w, const
   p.layout = (p.layout & 0xff) | (act << CND_LAYOUT_ACT_SHIFT);
   cudaStream_t stream = static_cast<cudaStream_t>(stream_handle);
   if (p.batch == 0) return CND_OK;
-  Plan plan;
-  make_plan(p, true, nullptr, &plan);
+  const std::shared_ptr<const Plan> planned = cached_plan(p, true, nullptr);
+  const Plan& plan = *planned;
   if (!plan.fast_fwd) {
     // generic convolution, then the activation as its own pass (pre keeps conv + b)
     void* target = (act != CND_ACT_NONE && pre != nullptr) ? pre : y;
@@ -931,8 +975,8 @@ int backward_impl(const cnd_problem* problem, const void* dy, const void* pre, i
     if (output_mask[2]) cudaMemsetAsync(db, 0, static_cast<size_t>(p.output_channels) * es, stream);
     return check_cuda("cnd_backward (empty batch)");
   }
-  Plan plan;
-  make_plan(p, false, output_mask, &plan);
+  const std::shared_ptr<const Plan> planned = cached_plan(p, false, output_mask);
+  const Plan& plan = *planned;
   if (workspace_bytes < plan.total || (plan.total > 0 && workspace == nullptr)) {
     return fail(CND_ERR_WORKSPACE, "cnd_backward: workspace of %zu bytes is smaller than %zu",
                 workspace_bytes, plan.total);
