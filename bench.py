@@ -64,6 +64,8 @@ def parse_args(argv=None):
                         help="activation layout of the c5 training step")
     parser.add_argument("--c5-gelu", default="fused", choices=("fused", "separate"),
                         help="GELU of the c5 step inside the convolutions or as its own pass")
+    parser.add_argument("--c5-graph", default="on", choices=("on", "off"),
+                        help="replay the warmed-up c5 training step as one CUDA graph")
     parser.add_argument("--no-e2e", action="store_true")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--cpu-sample-images", type=int, default=1)
@@ -583,6 +585,16 @@ class C5Step:
                                                                        world))
         self.optimizer = torch.optim.SGD(self.net.parameters(), lr=1e-4)
         self.mse = torch.nn.functional.mse_loss
+        self.dist = dist
+        # With --c5-graph on, the warmed-up step (forward, MSE, backward with its
+        # hook-started all-reduces, SGD) is captured once and replayed: at small per-GPU
+        # batches the eager step is bound by host work (autograd, hooks, launches).
+        self.use_graph = args.c5_graph == "on"
+        self.graph = None
+        self.graph_loss = None
+        self.graph_launches = 0
+        self.replayed_launches = 0
+        self.graph_note = "off"
 
     def _train(self, x, target):
         loss = self.mse(self.net(x), target)
@@ -592,8 +604,62 @@ class C5Step:
         self.optimizer.zero_grad(set_to_none=True)
         return loss
 
+    def prepare(self):
+        """Captures one training step as a CUDA graph (after the eager warm-up steps).
+        Every rank captures the same step; the ranks agree on success before any replay
+        (one eager all-reduce), so a capture failure anywhere leaves all of them eager."""
+        import torch
+
+        import torch_convnd
+
+        if not self.use_graph or self.graph is not None:
+            return
+        ok = 1
+        graph = None
+        try:
+            torch.cuda.synchronize()
+            self.optimizer.zero_grad(set_to_none=True)
+            graph = torch.cuda.CUDAGraph()
+            before = torch_convnd.launch_count()
+            with torch.cuda.graph(graph, capture_error_mode="thread_local"):
+                loss = self.mse(self.net(self.data.x), self.data.target)
+                loss.backward()
+                self.bucketer.finish()
+                self.optimizer.step()
+            self.graph_launches = torch_convnd.launch_count() - before
+            self.graph_loss = loss.detach()
+        except RuntimeError as error:  # capture refused: keep the eager step
+            ok = 0
+            self.graph_note = f"capture failed: {str(error).splitlines()[0][:120]}"
+        if self.world > 1:
+            flag = torch.tensor([ok], device=self.device, dtype=torch.int32)
+            self.dist.all_reduce(flag, op=self.dist.ReduceOp.MIN)
+            ok = int(flag.item())
+        self.optimizer.zero_grad(set_to_none=True)
+        if ok:
+            self.graph = graph
+            self.graph_note = "on"
+        else:
+            if graph is not None:
+                graph.reset()
+            if self.graph_note == "on" or self.graph_note == "off":
+                self.graph_note = "capture failed on another rank"
+            self.use_graph = False
+
     def step(self):
+        if self.graph is None:
+            return self._train(self.data.x, self.data.target)
+        self.graph.replay()
+        self.replayed_launches += self.graph_launches
+        return self.graph_loss
+
+    def eager_step(self):
         return self._train(self.data.x, self.data.target)
+
+    def close(self):
+        if self.graph is not None:
+            self.graph.reset()
+            self.graph = None
 
     def config(self):
         configs = load_configs()
@@ -601,6 +667,8 @@ class C5Step:
                 "per_gpu_batch": self.layers[0].batch, "parallelism": f"dp{self.world}",
                 "activation_layout": self.layout,
                 "gelu": self.gelu,
+                "cuda_graph": self.graph_note,
+                "launches_per_step": self.graph_launches or None,
                 "step_gflop_per_gpu": sum(l.step_flops for l in self.layers) / 1e9,
                 "gradient_buckets": len(self.bucketer.buckets),
                 "l2": "inputs larger than L2 (x alone is 537 MB at batch 64)"}
@@ -716,25 +784,33 @@ def measure(workload, args, world, dist, device, peaks):
         workload.step()
     torch.cuda.synchronize()
     torch_convnd.device_status()
+    # A workload may turn its warmed-up step into a CUDA graph here (c5); its replays
+    # launch the library's kernels without the host seeing them, so it counts them.
+    if hasattr(workload, "prepare"):
+        workload.prepare()
+        torch.cuda.synchronize()
     props = torch.cuda.get_device_properties(device)
     uuid = getattr(props, "uuid", None)
     sampler = ClockSampler(f"GPU-{uuid}" if uuid is not None else str(device.index))
     sampler.start()
     time.sleep(0.3)
     torch_convnd.launch_count(reset=True)
+    if hasattr(workload, "replayed_launches"):
+        workload.replayed_launches = 0
     begin = time.time()
     ms = timed_ms(workload.step, args.steps, world, dist, device)
     sampler.window(begin, time.time())
     clocks = sampler.stop()
-    launches = torch_convnd.launch_count()
+    launches = torch_convnd.launch_count() + getattr(workload, "replayed_launches", 0)
     value = workload.job_flops / (ms / 1e3) / 1e12
     torch_convnd.device_status()
 
     # Per-pass durations with CUDA events on the launching stream (a separate loop).
     torch_convnd._native.set_kernel_timing(True)
     timing_steps = min(args.steps, 5)
+    eager_step = getattr(workload, "eager_step", workload.step)  # events need eager launches
     for _ in range(timing_steps):
-        workload.step()
+        eager_step()
     torch.cuda.synchronize()
     timings = torch_convnd._native.collect_kernel_timings()
     torch_convnd._native.set_kernel_timing(False)
@@ -836,6 +912,8 @@ def run_b200(args):
     if workload.dtype == "fp32":
         config["fp32_precision"] = args.fp32_precision
     headline_dtype, headline_scaling = workload.dtype, workload.scaling
+    if hasattr(workload, "close"):
+        workload.close()  # a graph holding NCCL calls goes before the process group
     del workload
     torch.cuda.empty_cache()
 
@@ -855,6 +933,8 @@ def run_b200(args):
         if other.dtype == "fp32":
             result["config"]["fp32_precision"] = args.fp32_precision
         extra[name] = result
+        if hasattr(other, "close"):
+            other.close()
         del other
         torch.cuda.empty_cache()
 
