@@ -493,14 +493,13 @@ class SingleOp:
             self.op.conv_nd_backward.default(i.grad, i.x, i.weight, *self.geo,
                                              [True, True, has_bias])
             return y
-        # Weight and bias gradients first; their all-reduce runs under the dgrad pass.
+        # One backward call (dy is packed once for both gradients), then the all-reduce
+        # of the weight and bias gradients. Splitting the call to run the all-reduce under
+        # the input gradient cost a second dy pack, and NCCL's kernel finds no free SM
+        # beside the persistent convolution kernel, so it did not overlap.
         _, dw, db = self.op.conv_nd_backward.default(i.grad, i.x, i.weight, *self.geo,
-                                                     [False, True, has_bias])
-        grads = [g for g in (dw, db) if g is not None]
-        pending = self._allreduce_start(grads)
-        self.op.conv_nd_backward.default(i.grad, i.x, i.weight, *self.geo,
-                                         [True, False, False])
-        self._allreduce_finish(grads, *pending)
+                                                     [True, True, has_bias])
+        self._allreduce([g for g in (dw, db) if g is not None])
         return y
 
     def config(self):
