@@ -195,7 +195,7 @@ struct Plan {
   int64_t wg_x_spatial = 0;
   // workspace
   Region x_pack, x_pack_small, w_fwd, w_fwd_small, dy_pack, dy_pack_small, w_dg, w_dg_small,
-      partial, bias_partial;
+      partial, bias_partial, bias_chunks;
   Region wg_x[3], wg_dy[3];
   size_t total = 0;
 };
@@ -596,6 +596,8 @@ void make_plan(const cnd_problem& p, bool forward, const int32_t* mask, Plan* pl
     const size_t blocks = static_cast<size_t>((p.output_volume + 63) / 64);
     plan->bias_partial = take(&cursor, static_cast<size_t>(p.batch * plan->groups) * blocks *
                                            plan->cout_g * sizeof(float));
+    plan->bias_chunks = take(&cursor, bias_chunk_bytes(static_cast<int>(plan->groups),
+                                                       static_cast<int>(plan->cout_g)));
   }
   if (plan->fast_dgrad && plan->nphase > 0) {
     const size_t wes = plan->dgrad_bf16 ? 2 : es;
@@ -1199,7 +1201,7 @@ int backward_impl(const cnd_problem* problem, const void* dy, const void* pre, i
     if (bias_from_pack) {
       rc = reduce_bias(static_cast<const float*>(at(workspace, plan.bias_partial)), p.batch,
                        static_cast<int>(plan.groups), blocks, static_cast<int>(plan.cout_g), db,
-                       p.dtype, stream);
+                       p.dtype, static_cast<float*>(at(workspace, plan.bias_chunks)), stream);
     } else {
       GenericCall call{GenericCall::kBias, &p, grad, nullptr, nullptr, db};
       rc = run_generic(call, stream);

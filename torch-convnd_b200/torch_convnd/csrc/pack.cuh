@@ -74,8 +74,10 @@ int pack_weights(const PackWeightArgs& args, cudaStream_t stream);
 // tap t' is dw's channel ci at tap t' * fold + j (taps counts dw's taps).
 int reduce_wgrad(const float* partial, int splits, int groups, int bd, int taps, int cin_g,
                  int cout_g, void* dw, int dtype, cudaStream_t stream, int fold = 1);
+// chunk_sums: bias_chunk_bytes(groups, cg) bytes of scratch for the first pass.
+size_t bias_chunk_bytes(int groups, int cg);
 int reduce_bias(const float* partial, int64_t batch, int groups, int blocks, int cg, void* db,
-                int dtype, cudaStream_t stream);
+                int dtype, float* chunk_sums, cudaStream_t stream);
 // Elementwise activation passes for problems the tcgen05 epilogue / pack do not serve:
 // dst = act(src) (dst may alias src), and dz = dy * act'(pre); n elements of `dtype`.
 int activation_forward(const void* src, void* dst, int64_t n, int dtype, int act,
