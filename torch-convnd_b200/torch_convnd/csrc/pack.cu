@@ -388,17 +388,41 @@ __global__ void pack_weight_kernel(const T* __restrict__ w, Tout* __restrict__ d
 // instructions and store wavefronts, not bytes, so nothing here divides by a runtime value.
 constexpr int kFoldMaxPad = 64;  // channels per destination row (16, 32 or 64)
 
+// Split of one value into the destination's parts (split_value's modes): hi only (mode 0,
+// or a TF32 rounding in mode 2), TF32 big + small (mode 1), bf16 hi + lo (mode 4).
+template <typename Tout, int kMode>
+__device__ __forceinline__ void split_two(float v, Tout& hi, Tout& lo) {
+  if constexpr (kMode == 1) {
+    const float big = tf32_round(v);
+    hi = from_float<Tout>(big);
+    lo = from_float<Tout>(tf32_round(v - big));
+  } else if constexpr (kMode == 2) {
+    hi = from_float<Tout>(tf32_round(v));
+  } else if constexpr (kMode == 4) {
+    hi = from_float<Tout>(v);
+    lo = from_float<Tout>(v - to_float(hi));
+  } else {
+    hi = from_float<Tout>(v);
+  }
+}
+
+// With chan_partial the kernel also writes the channel sums of every 64 destination
+// positions (two warps): chan_partial[((n * G + g) * ceil(S_dst / 64) + block) * Cg + c],
+// the layout of pack_act_kernel's partials, summed in a fixed order.
 template <typename Tin, typename Tout, int kMode, bool kSrcCL, int kCg>
 __global__ void __launch_bounds__(256) pack_fold_kernel(
     const Tin* __restrict__ src, Tout* __restrict__ dst0, Tout* __restrict__ dst1,
     int64_t S_src, int64_t S_dst, int64_t last_src, int64_t last_dst, int Cg_rt, int c_pad,
-    int G, int taps, int dil, int pad) {
-  static_assert(sizeof(Tout) == 2, "16-bit operands");
+    int G, int taps, int dil, int pad, float* __restrict__ chan_partial) {
+  static_assert(sizeof(Tout) == 2 || sizeof(Tout) == 4, "16- or 32-bit operands");
   static_assert(kCg % 8 == 0, "whole 8-channel chunks per tap");
   constexpr int kPitch = kFoldMaxPad * 2 + 16;  // bytes per staged row (bank spread)
-  constexpr bool kRaw = kMode == 0 && sizeof(Tin) == sizeof(Tout);  // copy the bits as is
+  constexpr int kChunkVecs = 8 * static_cast<int>(sizeof(Tout)) / 16;  // uint4 per 8 channels
+  constexpr bool kTwo = kMode == 1 || kMode == 4;                       // second part
+  constexpr bool kRaw = kMode == 0 && sizeof(Tin) == sizeof(Tout);     // copy the bits
   (void)Cg_rt;
   __shared__ __align__(16) uint8_t stage[8][32 * kPitch];
+  __shared__ float sums[8][kCg];
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int g = blockIdx.y;
@@ -407,82 +431,88 @@ __global__ void __launch_bounds__(256) pack_fold_kernel(
   const int64_t q = q0 + lane;
   const bool valid = q < S_dst;
   uint8_t* row_stage = stage[warp] + lane * kPitch;
-  uint4 lo_vec[kFoldMaxPad / 8];
-  {
-    const int64_t qc = valid ? q : 0;
-    const int64_t outer = qc / last_dst;
-    const int i_last = static_cast<int>(qc - outer * last_dst) - pad;
-    const int64_t row0 = outer * last_src;  // source position of (outer, last-axis 0)
-    const Tin* plane;   // channel 0 of this (n, g) at source position row0
-    int64_t ch_step;    // elements between channels
-    int64_t pos_step;   // elements between positions
-    if constexpr (kSrcCL) {
-      pos_step = static_cast<int64_t>(G) * kCg;
-      ch_step = 1;
-      plane = src + (n * S_src + row0) * pos_step + static_cast<int64_t>(g) * kCg;
-    } else {
-      pos_step = 1;
-      ch_step = S_src;
-      plane = src + (n * G + g) * kCg * S_src + row0;
-    }
+  const int64_t qc = valid ? q : 0;
+  const int64_t outer = qc / last_dst;
+  const int i_last = static_cast<int>(qc - outer * last_dst) - pad;
+  const int64_t row0 = outer * last_src;  // source position of (outer, last-axis 0)
+  const Tin* plane;   // channel 0 of this (n, g) at source position row0
+  int64_t ch_step;    // elements between channels
+  int64_t pos_step;   // elements between positions
+  if constexpr (kSrcCL) {
+    pos_step = static_cast<int64_t>(G) * kCg;
+    ch_step = 1;
+    plane = src + (n * S_src + row0) * pos_step + static_cast<int64_t>(g) * kCg;
+  } else {
+    pos_step = 1;
+    ch_step = S_src;
+    plane = src + (n * G + g) * kCg * S_src + row0;
+  }
+  uint8_t* ws = stage[warp];
+  const int row_bytes = c_pad * static_cast<int>(sizeof(Tout));
+  const int row_shift = __ffs(row_bytes) - 1;  // log2 of the row bytes (32, 64 or 128)
+  const int64_t out_base = ((n * G + g) * S_dst + q0) * c_pad;  // elements
+  const int64_t rows_here = S_dst - q0 < 32 ? S_dst - q0 : 32;
+  const int run_bytes = static_cast<int>(rows_here) << row_shift;
+  // One gather per destination part (the second one re-reads the source from cache): the
+  // part's row goes to this lane's staged row, then the warp writes its rows.
+  for (int part = 0; part < (kTwo ? 2 : 1); ++part) {
+    if (part == 1) __syncwarp();  // the first part's copy-out has read the stage
     for (int j = 0; j < taps; ++j) {
       const int at = i_last + j * dil;
       const bool in = valid && at >= 0 && at < last_src;
       const Tin* p = plane + (in ? at : 0) * pos_step;
 #pragma unroll
       for (int c8 = 0; c8 < kCg; c8 += 8) {
-        alignas(16) Tout hi[8];
-        alignas(16) Tout lo[8];
+        alignas(16) Tout out[8];
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
           if constexpr (kRaw) {
-            hi[k] = in ? p[(c8 + k) * ch_step] : Tout{};
+            out[k] = in ? p[(c8 + k) * ch_step] : Tout{};
           } else {
             const float v = in ? to_float(p[(c8 + k) * ch_step]) : 0.0f;
-            hi[k] = from_float<Tout>(v);
-            if constexpr (kMode == 4) lo[k] = from_float<Tout>(v - to_float(hi[k]));
+            Tout hi, lo;
+            split_two<Tout, kMode>(v, hi, lo);
+            out[k] = part == 0 ? hi : lo;
+            if (chan_partial != nullptr && part == 0) {  // one tap: the bias partials
+              float sum = v;
+#pragma unroll
+              for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+              if (lane == 0) sums[warp][c8 + k] = sum;
+            }
           }
         }
         const int m = j * kCg + c8;  // first channel of the chunk
-        *reinterpret_cast<uint4*>(row_stage + m * 2) = *reinterpret_cast<const uint4*>(hi);
-        if constexpr (kMode == 4) {
 #pragma unroll
-          for (int u = 0; u < kFoldMaxPad / 8; ++u) {
-            if (u == m / 8) lo_vec[u] = *reinterpret_cast<const uint4*>(lo);
-          }
+        for (int u = 0; u < kChunkVecs; ++u) {
+          *reinterpret_cast<uint4*>(row_stage + m * sizeof(Tout) + u * 16) =
+              reinterpret_cast<const uint4*>(out)[u];
         }
       }
     }
     for (int m = taps * kCg; m < c_pad; m += 8) {  // padding channels
-      *reinterpret_cast<uint4*>(row_stage + m * 2) = make_uint4(0, 0, 0, 0);
-      if constexpr (kMode == 4) {
 #pragma unroll
-        for (int u = 0; u < kFoldMaxPad / 8; ++u) {
-          if (u == m / 8) lo_vec[u] = make_uint4(0, 0, 0, 0);
-        }
+      for (int u = 0; u < kChunkVecs; ++u) {
+        *reinterpret_cast<uint4*>(row_stage + m * sizeof(Tout) + u * 16) = make_uint4(0, 0, 0, 0);
       }
     }
-  }
-  // copy-out: the warp's rows are contiguous in the destination (row_bytes each)
-  uint8_t* ws = stage[warp];
-  const int row_shift = __ffs(c_pad * 2) - 1;  // log2 of the row bytes (32, 64 or 128)
-  const int64_t out_base = ((n * G + g) * S_dst + q0) * c_pad;  // elements
-  const int64_t rows_here = S_dst - q0 < 32 ? S_dst - q0 : 32;
-  const int run_bytes = static_cast<int>(rows_here) << row_shift;
-  for (int part = 0; part < (kMode == 4 ? 2 : 1); ++part) {
-    if (part == 1) {
-      __syncwarp();
-#pragma unroll
-      for (int u = 0; u < kFoldMaxPad / 8; ++u) {
-        if (u * 8 < c_pad) *reinterpret_cast<uint4*>(row_stage + u * 16) = lo_vec[u];
+    if (chan_partial != nullptr && part == 0) {
+      // channel sums of each 64-position block: warps 2b and 2b + 1, added in warp order
+      __syncthreads();
+      const int64_t blocks_total = (S_dst + 63) / 64;
+      const int local = threadIdx.x / kCg;  // block within the CTA
+      const int c = threadIdx.x % kCg;
+      const int64_t block = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 64) + local;
+      if (local < static_cast<int>(blockDim.x / 64) && block < blocks_total) {
+        chan_partial[((n * G + g) * blocks_total + block) * kCg + c] =
+            sums[2 * local][c] + sums[2 * local + 1][c];
       }
     }
     __syncwarp();
-    uint8_t* out = reinterpret_cast<uint8_t*>((part == 0 ? dst0 : dst1) + out_base);
+    uint8_t* dst = reinterpret_cast<uint8_t*>((part == 0 ? dst0 : dst1) + out_base);
     for (int o = lane * 16; o < run_bytes; o += 512) {
       const int row = o >> row_shift;
       const int within = o & ((1 << row_shift) - 1);
-      *reinterpret_cast<uint4*>(out + o) =
+      *reinterpret_cast<uint4*>(dst + o) =
           *reinterpret_cast<const uint4*>(ws + row * kPitch + within);
     }
   }
@@ -673,7 +703,7 @@ int launch_pack_fold_impl(const PackActArgs& a, cudaStream_t stream) {
         static_cast<const Tin*>(a.src), static_cast<Tout*>(a.dst),
         static_cast<Tout*>(a.dst_small), a.spatial, s_dst, a.fold_last_src, a.fold_last_dst,
         a.cg, a.c_pad, static_cast<int>(a.groups), a.fold_taps, a.fold_dilation,
-        a.fold_padding);
+        a.fold_padding, a.chan_partial);
   };
   if (a.cg == 8) {
     args(pack_fold_kernel<Tin, Tout, kMode, kSrcCL, 8>);
@@ -826,9 +856,39 @@ int activation_dispatch(const void* a, const void* b, void* out, int64_t n, int 
 bool channel_sums_fast_ok(const PackActArgs& a);
 int channel_sums(const PackActArgs& a, cudaStream_t stream);
 
+// Plain channels-first float32 packs into operand parts (TF32 big + small, a TF32
+// rounding, or bf16 hi + lo), with or without the bias partials, run as a one-tap
+// pack_fold_kernel: the shared-memory transpose of pack_act_kernel is bound by its
+// instruction count (c4: dy 67 us, x 41 us).
+bool plain_fold_ok(const PackActArgs& a) {
+  const int out_es = a.mode == 4 ? 2 : 4;
+  const int row = a.c_pad * out_es;
+  const bool two = a.mode == 1 || a.mode == 4;
+  return a.fold_taps <= 1 && !a.src_cl && a.act == 0 && a.dst != nullptr &&
+         a.dtype == CND_F32 && (a.mode == 1 || a.mode == 2 || a.mode == 4) &&
+         (a.cg == 8 || a.cg == 16 || a.cg == 32) && a.cg <= a.c_pad &&
+         (row == 32 || row == 64 || row == 128) && a.groups <= 65535 && a.batch <= 65535 &&
+         reinterpret_cast<uintptr_t>(a.dst) % 16 == 0 &&
+         (!two || reinterpret_cast<uintptr_t>(a.dst_small) % 16 == 0);
+}
+
 int pack_activations(const PackActArgs& args, cudaStream_t stream) {
   int rc;
-  if (args.fold_taps > 1) {
+  if (plain_fold_ok(args)) {
+    PackActArgs one = args;
+    one.fold_taps = 1;
+    one.fold_dilation = 0;
+    one.fold_padding = 0;
+    one.fold_last_src = one.fold_last_dst = args.spatial > 0 ? args.spatial : 1;
+    if (args.spatial == 0) return CND_OK;
+    if (args.mode == 4) {
+      rc = launch_pack_fold<float, __nv_bfloat16, 4>(one, stream);
+    } else if (args.mode == 1) {
+      rc = launch_pack_fold<float, float, 1>(one, stream);
+    } else {
+      rc = launch_pack_fold<float, float, 2>(one, stream);
+    }
+  } else if (args.fold_taps > 1) {
     if (args.dst == nullptr || args.act != 0 || args.chan_partial != nullptr ||
         args.fold_last_src < 1 || args.fold_last_dst < 1 ||
         args.spatial % args.fold_last_src != 0 || args.fold_taps * args.cg > args.c_pad) {
