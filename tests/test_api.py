@@ -186,6 +186,19 @@ def test_c_abi_problem_init_and_budget():
     # c2: x packed channels-last bf16 (16*65536*32*2) + packed weights (81*64*32*2), 1 KiB aligned
     assert library.cnd_forward_workspace_size(ctypes.byref(problem)) == 67108864 + 331776
     assert library.cnd_fast_path_mask(ctypes.byref(problem)) == 7
+    # Plans are cached per problem, pass kind and gradient mask: sizes queried in any
+    # order agree, and a changed layout field is a different problem.
+    library.cnd_backward_workspace_size.restype = ctypes.c_size_t
+    masks = [(1, 0, 0), (0, 1, 0), (1, 1, 1), (0, 0, 1)]
+    size = lambda m: library.cnd_backward_workspace_size(ctypes.byref(problem),
+                                                         (ctypes.c_int32 * 3)(*m))
+    first = [size(m) for m in masks]
+    assert [size(m) for m in reversed(masks)] == list(reversed(first))
+    assert first[2] >= max(first[0], first[1]) and len(set(first)) > 1
+    problem.reserved = 1  # channels-last input with 32 channels: read in place, no pack
+    assert library.cnd_forward_workspace_size(ctypes.byref(problem)) == 331776
+    problem.reserved = 0
+    assert library.cnd_forward_workspace_size(ctypes.byref(problem)) == 67108864 + 331776
     status = library.cnd_problem_init(ctypes.byref(problem), 4, arr(1, 2, 3, 3, 3, 3),
                                       arr(4, 2, 4, 2, 2, 2), arr(1, 1, 1, 1), arr(0, 0, 0, 0),
                                       arr(1, 1, 1, 1), ctypes.c_int64(1), 2)
