@@ -653,6 +653,43 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
                                                  group_bias, P.n_real, value);
       }
     };
+    // The 16-channel chunks of tile m, each handed to body(c, value) with the bias added.
+    // With one accumulator set and no a2 fold, chunk c + 1's TMEM load is issued before
+    // chunk c is processed, so its latency hides behind the activation and the stores.
+    auto tile_chunks = [&](uint32_t dbase, int m, const OutT* group_bias, auto&& body) {
+      const int nchunks = P.n_pad / 16;
+      if (P.k2f > 1 || used > 1) {
+        for (int c = 0; c < nchunks; ++c) {
+          float value[16];
+          chunk(dbase, m, c, group_bias, value);
+          body(c, value);
+        }
+        return;
+      }
+      const uint32_t col0 = dbase + static_cast<uint32_t>(tile_col(m));
+      uint32_t raw[16];
+      __syncwarp();
+      dev::tmem_load16(col0, raw);
+      for (int c = 0; c < nchunks; ++c) {
+        dev::tmem_load_wait();
+        float value[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) value[i] = __uint_as_float(raw[i]);
+        if constexpr (kFold > 0) dev::tmem_zero16(col0 + 16u * static_cast<uint32_t>(c));
+        if (c + 1 < nchunks) {
+          __syncwarp();
+          dev::tmem_load16(col0 + 16u * static_cast<uint32_t>(c + 1), raw);
+        }
+        if (group_bias != nullptr) {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int co = c * 16 + i;
+            if (co < P.n_real) value[i] += Traits::load(group_bias + co);
+          }
+        }
+        body(c, value);
+      }
+    };
     if constexpr (kFold > 0) {
       // Folded MMAs all accumulate: start both accumulator buffers at zero.
       for (int c = 16 * group; c < 2 * P.acc_stride; c += 16 * groups) {
@@ -718,13 +755,11 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
             }
           }
           dev::named_barrier(barrier_id, 128);
-          for (int c = 0; c < P.n_pad / 16; ++c) {
-            float value[16];
-            chunk(dbase, m, c, group_bias, value);
+          tile_chunks(dbase, m, group_bias, [&](int c, float (&value)[16]) {
             if (P.pre_staged) stage_row(pre_stage, c, value);
             activate(S, m, o1, o2, c, value);
             stage_row(stage, c, value);
-          }
+          });
           dev::fence_proxy_async();
           dev::named_barrier(barrier_id, 128);
           if (store_issuer) {
@@ -771,13 +806,11 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
             }
           }
           dev::named_barrier(barrier_id, 128);
-          for (int c = 0; c < P.n_pad / 16; ++c) {
-            float value[16];
-            chunk(dbase, m, c, group_bias, value);
+          tile_chunks(dbase, m, group_bias, [&](int c, float (&value)[16]) {
             if (P.pre_staged) stage_cols(pre_buf, c, value);
             activate(S, m, o1, o2, c, value);
             stage_cols(stage_buf, c, value);
-          }
+          });
           dev::fence_proxy_async();
           dev::named_barrier(barrier_id, 128);
           if (store_issuer) {
@@ -804,12 +837,10 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
           const int64_t sp = out_offset(S, o0, o1, o2);
           OutT* dst = out + (S.n * out_vol + sp) * P.out_channels_total +
                       static_cast<int64_t>(S.g) * P.n_real;
-          for (int c = 0; c < P.n_pad / 16; ++c) {
-            float value[16];
-            chunk(dbase, m, c, group_bias, value);
+          tile_chunks(dbase, m, group_bias, [&](int c, float (&value)[16]) {
             activate(S, m, o1, o2, c, value);
             if (valid) store_run16<OutT>(dst + c * 16, value, P.n_real - c * 16);
-          }
+          });
         }
         if constexpr (kFold > 0) dev::tmem_store_wait();
         dev::tc_fence_before();
@@ -821,9 +852,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
         const bool valid = line_ok && o0 < P.out[0] && o1 < P.out[1] && o2 < P.out[2];
         const int64_t sp = out_offset(S, o0, o1, o2);
         OutT* dst = out + channel_base + sp;
-        for (int c = 0; c < P.n_pad / 16; ++c) {
-          float value[16];
-          chunk(dbase, m, c, group_bias, value);
+        tile_chunks(dbase, m, group_bias, [&](int c, float (&value)[16]) {
           activate(S, m, o1, o2, c, value);
           if (valid) {
 #pragma unroll
@@ -832,7 +861,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
               if (co < P.n_real) dst[static_cast<int64_t>(co) * out_vol] = Traits::cast(value[i]);
             }
           }
-        }
+        });
       }
       if constexpr (kFold > 0) dev::tmem_store_wait();
       dev::tc_fence_before();
