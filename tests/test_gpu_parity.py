@@ -126,6 +126,8 @@ def _sweep():
     cases.append((4, 2, 32, 32, (9, 10, 4, 6), (3, 3, 1, 1), (1,) * 4, (2, 2, 0, 0),
                   (2, 2, 1, 1), 4))
     cases.append((6, 1, 16, 16, (1, 1, 1, 1, 1, 1), (1,) * 6, (1,) * 6, (0,) * 6, (1,) * 6, 1))
+    # a0 taps at dilation 2 folded over output planes of one parity (odd a0 extent)
+    cases.append((4, 2, 16, 32, (9, 6, 5, 7), (3,) * 4, (1,) * 4, (2, 1, 1, 1), (2, 1, 1, 1), 1))
     # strided input gradients as phase sub-convolutions: mixed strides and paddings,
     # dilation sharing a factor with the stride, and a kernel-1 stride-2 axis whose odd
     # positions receive no tap (zeroed residue classes)

@@ -62,6 +62,7 @@ struct Super {
   int64_t outer_lin;  // row-major index over the outer output axes
   int o[kMaxOuter];
   int q0, q1, q2;
+  int a0_first;  // output a0 coordinate of the super tile's first M tile
 };
 
 __device__ __forceinline__ void decode_super(const FpropParams& P, int64_t st, Super& s) {
@@ -72,6 +73,9 @@ __device__ __forceinline__ void decode_super(const FpropParams& P, int64_t st, S
   rest /= P.nsup[1];
   s.q0 = static_cast<int>(rest % P.nsup[0]);
   rest /= P.nsup[0];
+  // With a parity split (par0 = 2) super tiles alternate between even and odd a0 planes.
+  const int blk = s.q0 / P.par0;
+  s.a0_first = (blk * P.mt * P.e0) * P.par0 + (s.q0 - blk * P.par0);
   s.outer_lin = rest % P.out_outer_vol;
   rest /= P.out_outer_vol;
   s.n = rest % P.batch;
@@ -345,7 +349,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
       for (int a = 0; a < kMaxOuter; ++a) {
         ibo[a] = a < P.n_outer ? S.o[a] * P.s_o[a] - P.p_o[a] : 0;
       }
-      const int x0 = S.q0 * kMT * P.e0 * P.s[0] - P.p[0];
+      const int x0 = S.a0_first * P.s[0] - P.p[0];
       const int x1 = S.q1 * P.b1 * P.s[1] - P.p[1];
       const int x2 = S.q2 * P.b2o * P.s[2] - P.p[2];
       int to[kMaxOuter];
@@ -444,7 +448,9 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
         dev::make_smem_desc(0, 16, 8u * static_cast<uint32_t>(P.row_bytes), P.layout);
     const uint32_t row_units = static_cast<uint32_t>(P.row_bytes) >> 4;
     const uint32_t tile_units = static_cast<uint32_t>(P.e0 * P.h1 * P.b2) * row_units;
-    const uint32_t j0_units = static_cast<uint32_t>(P.d[0] * P.h1 * P.b2) * row_units;
+    // a0 taps are d0 / par0 box slices apart (one slice with a parity split)
+    const uint32_t j0_units =
+        static_cast<uint32_t>((P.d[0] / P.par0) * P.h1 * P.b2) * row_units;
     const uint32_t j1_units = static_cast<uint32_t>(P.d[1] * P.b2) * row_units;
     // B rows and TMEM columns of one tap block: n_pad, or k2f * n_pad with the a2 fold.
     const uint32_t btap_units = static_cast<uint32_t>(P.n_blk) * row_units;
@@ -609,7 +615,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
     // With pre_staged the staged branches write the pre-activation tile themselves.
     auto activate = [&](const Super& S, int m, int o1, int o2, int c, float (&value)[16]) {
       if (!P.act) return;
-      const int o0 = (S.q0 * kMT + m) * P.e0 + i0;
+      const int o0 = S.a0_first + m * P.a0_tile_step + i0;
       if (P.pre != nullptr && !P.pre_staged && line_ok && o0 < P.out[0] && o1 < P.out[1] &&
           o2 < P.out[2]) {
         OutT* pre = static_cast<OutT*>(P.pre);
@@ -763,7 +769,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
           dev::fence_proxy_async();
           dev::named_barrier(barrier_id, 128);
           if (store_issuer) {
-            const int32_t o0 = (S.q0 * kMT + m) * P.e0;
+            const int32_t o0 = S.a0_first + m * P.a0_tile_step;
             for (int k = 0; k * static_cast<int>(span) < row_bytes; ++k) {
               const int32_t ch = S.g * P.n_real + k * static_cast<int>(span / sizeof(OutT));
               dev::tma_store_5d(&maps.out, stage + k * 128 * span, ch, S.q2 * P.b2o,
@@ -814,7 +820,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
           dev::fence_proxy_async();
           dev::named_barrier(barrier_id, 128);
           if (store_issuer) {
-            const int32_t o0 = (S.q0 * kMT + m) * P.e0;
+            const int32_t o0 = S.a0_first + m * P.a0_tile_step;
             dev::tma_store_5d(&maps.out, stage_buf, S.q2 * P.b2o, S.q1 * P.b1, o0,
                               static_cast<int32_t>(S.outer_lin), nc0);
             if (P.pre_staged) {
@@ -832,7 +838,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
       if (P.out_cl) {
         // Channels-last rows: this thread's position holds n_real consecutive channels.
         for (int m = group; m < kMT; m += groups) {
-          const int o0 = (S.q0 * kMT + m) * P.e0 + i0;
+          const int o0 = S.a0_first + m * P.a0_tile_step + i0;
           const bool valid = line_ok && o0 < P.out[0] && o1 < P.out[1] && o2 < P.out[2];
           const int64_t sp = out_offset(S, o0, o1, o2);
           OutT* dst = out + (S.n * out_vol + sp) * P.out_channels_total +
@@ -848,7 +854,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
         continue;
       }
       for (int m = group; m < kMT; m += groups) {
-        const int o0 = (S.q0 * kMT + m) * P.e0 + i0;
+        const int o0 = S.a0_first + m * P.a0_tile_step + i0;
         const bool valid = line_ok && o0 < P.out[0] && o1 < P.out[1] && o2 < P.out[2];
         const int64_t sp = out_offset(S, o0, o1, o2);
         OutT* dst = out + channel_base + sp;
@@ -1055,10 +1061,12 @@ bool layout_candidate(const ConvPass& pass, FpropParams* P, const Candidate& c, 
   P->n_blk = c.k2f * pass.n_pad;
   P->nshift0 = c.shift0 ? k0 : 1;
   P->nshift1 = c.shift1 ? k1 : 1;
-  P->h0 = c.mt * c.e0 + (c.shift0 ? (k0 - 1) * P->d[0] : 0);
+  P->par0 = (c.fold && P->d[0] == 2) ? 2 : 1;
+  P->a0_tile_step = c.e0 * P->par0;
+  P->h0 = c.mt * c.e0 + (c.shift0 ? (k0 - 1) * (P->d[0] / P->par0) : 0);
   P->h1 = c.b1 + (c.shift1 ? (k1 - 1) * P->d[1] : 0);
   // TMA box extents (elements of the packed tensor, before element striding).
-  const int box0 = c.shift0 ? P->h0 : c.mt * c.e0 * P->s[0];
+  const int box0 = c.shift0 ? P->h0 * P->par0 : c.mt * c.e0 * P->s[0];
   const int box1 = c.shift1 ? P->h1 : c.b1 * P->s[1];
   const int box2 = c.b2 * P->s[2];
   if (box0 > 256 || box1 > 256 || box2 > 256) return false;
@@ -1107,7 +1115,9 @@ bool plan_fprop(const ConvPass& pass, FpropPlan* plan) {
     // Folding the a0 taps into N needs unit-stride a0 tiles of one slice, three a0 taps
     // and 3 * n_pad <= 256. fold = 2 folds the a2 taps as well (k2f = k2): unit-stride a2,
     // 3 * k2 * n_pad <= 256, lines of 16 or 32 rows.
-    if (fold && (P.k[0] != 3 || P.d[0] != 1 || P.s[0] != 1 || 3 * pass.n_pad > 256)) {
+    // Dilation 2 folds too, over output planes of one parity (FpropParams::par0).
+    if (fold && (P.k[0] != 3 || (P.d[0] != 1 && P.d[0] != 2) || P.s[0] != 1 ||
+                 3 * pass.n_pad > 256)) {
       continue;
     }
     const int k2f = fold == 2 ? P.k[2] : 1;
@@ -1144,7 +1154,10 @@ bool plan_fprop(const ConvPass& pass, FpropPlan* plan) {
             if (2 * nacc * mt * n_blk > 512) continue;
             // Estimated cycles per useful output position.
             const int b2o = trial.b2o;
-            const double tiles0 = (P.out[0] + mt * e0 - 1) / (mt * e0);
+            // super tiles along a0 (per parity with a parity split) times their tiles
+            const int par0 = trial.par0;
+            const int per_parity = (P.out[0] + par0 - 1) / par0;
+            const double tiles0 = par0 * ((per_parity + mt * e0 - 1) / (mt * e0));
             const double waste = (tiles0 * mt * e0 / P.out[0]) *
                                  (double((P.out[1] + b1 - 1) / b1) * b1 / P.out[1]) *
                                  (double((P.out[2] + b2o - 1) / b2o) * b2 / P.out[2]);
@@ -1195,7 +1208,7 @@ bool plan_fprop(const ConvPass& pass, FpropPlan* plan) {
   plan->score = best;
   P = chosen;
   P.units = P.taps / (P.nshift0 * P.nshift1 * P.k2f);
-  P.nsup[0] = (P.out[0] + P.mt * P.e0 - 1) / (P.mt * P.e0);
+  P.nsup[0] = P.par0 * (((P.out[0] + P.par0 - 1) / P.par0 + P.mt * P.e0 - 1) / (P.mt * P.e0));
   P.nsup[1] = (P.out[1] + P.b1 - 1) / P.b1;
   P.nsup[2] = (P.out[2] + P.b2o - 1) / P.b2o;
   P.supers_total = outer_count * P.nsup[0] * P.nsup[1] * P.nsup[2];
@@ -1322,14 +1335,14 @@ int launch_fprop(const ConvPass& pass, const FpropPlan& plan_in, cudaStream_t st
                           static_cast<cuuint64_t>(pass.batch * pass.groups * P.in_merged_per_gn)};
     const cuuint64_t c = static_cast<cuuint64_t>(pass.c_pad) * es;
     cuuint64_t strides[4] = {c, c * P.in[2], c * P.in[2] * P.in[1], c * P.in[2] * P.in[1] * P.in[0]};
-    const int box0 = P.nshift0 > 1 ? P.h0 : P.mt * P.e0 * P.s[0];
+    const int box0 = P.nshift0 > 1 ? P.h0 * P.par0 : P.mt * P.e0 * P.s[0];
     const int box1 = P.nshift1 > 1 ? P.h1 : P.b1 * P.s[1];
     cuuint32_t boxd[5] = {static_cast<cuuint32_t>(P.cblk_elems),
                           static_cast<cuuint32_t>(P.b2 * P.s[2]), static_cast<cuuint32_t>(box1),
                           static_cast<cuuint32_t>(box0), 1};
     cuuint32_t estr[5] = {1, static_cast<cuuint32_t>(P.s[2]),
                           static_cast<cuuint32_t>(P.nshift1 > 1 ? 1 : P.s[1]),
-                          static_cast<cuuint32_t>(P.nshift0 > 1 ? 1 : P.s[0]), 1};
+                          static_cast<cuuint32_t>(P.nshift0 > 1 ? P.par0 : P.s[0]), 1};
     CUresult r = encode(&maps.act[part], map_dtype(pass.op), 5, const_cast<void*>(act[part]),
                         dims, strides, boxd, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                         swizzle_for(P.row_bytes), CU_TENSOR_MAP_L2_PROMOTION_L2_256B,

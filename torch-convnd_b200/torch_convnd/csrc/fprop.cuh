@@ -38,6 +38,11 @@ struct FpropParams {
   // (b2o = b2). n_blk = k2f * n_pad TMEM columns per M tile.
   int k2f, b2o, n_blk;
   int h0, h1;            // halo box extents (rows) along a0 / a1
+  // par0 = 2 (folded a0 taps at dilation 2): a super tile covers output planes of one
+  // parity, whose a0 taps read input planes of that parity only; the TMA box steps a0 by
+  // 2 (element stride), so the taps are consecutive box slices as at dilation 1.
+  // a0_tile_step = e0 * par0 output planes between consecutive M tiles.
+  int par0, a0_tile_step;
   int nsup[3];
   int64_t supers_total;
   int units;             // load units per super tile (taps / shifted taps)
