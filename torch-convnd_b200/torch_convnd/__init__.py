@@ -17,8 +17,9 @@ from ._native import (
     set_fp32_precision,
 )
 from ._operators import ensure_native_definitions
+from ._partial import PartialConvOutput, partial_conv_nd
 from .functional import conv_nd
-from .modules import Conv1d, Conv2d, Conv3d, Conv4d, ConvNd
+from .modules import Conv1d, Conv2d, Conv3d, Conv4d, ConvNd, PartialConvNd
 from .onnx import export_onnx
 
 __version__ = "0.5.0+b200.1"
@@ -34,6 +35,8 @@ __all__ = [
     "Conv3d",
     "Conv4d",
     "ConvNd",
+    "PartialConvNd",
+    "PartialConvOutput",
     "channels_last",
     "conv_nd",
     "device_status",
@@ -43,6 +46,7 @@ __all__ = [
     "launch_count",
     "load_native",
     "native_unavailable_reason",
+    "partial_conv_nd",
     "set_fp32_precision",
     "__version__",
 ]

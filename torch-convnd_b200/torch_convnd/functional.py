@@ -19,7 +19,7 @@ from ._geometry import DEFAULT_WORKSPACE_BYTES, _tuple, has_rank
 from ._padding import apply_padding, padding_pairs
 
 BACKENDS = ("auto", "native", "torch")
-_PADDING_MODES = ("zeros", "reflect", "replicate", "circular")
+_PADDING_MODES = ("zeros", "reflect", "replicate", "circular", "partial")
 _CASTABLE = (torch.float16, torch.bfloat16, torch.float32)
 
 
@@ -37,8 +37,6 @@ def _check_options(padding_mode: str, workspace_bytes: int, backend: str) -> Non
         )
     if workspace_bytes <= 0:
         raise ValueError("workspace_bytes must be positive")
-    if padding_mode == "partial":
-        raise NotImplementedError("padding_mode='partial' is not part of the B200 build")
     if padding_mode not in _PADDING_MODES:
         raise ValueError(f"Invalid padding_mode {padding_mode!r}")
 
@@ -119,6 +117,18 @@ def conv_nd(
     dilation = _tuple(dilation, rank, "dilation")
     padding = padding if isinstance(padding, str) else _tuple(padding, rank, "padding")
     _check_options(padding_mode, workspace_bytes, backend)
+    if padding_mode == "partial":
+        # zero padding rescaled as a mask-free partial convolution (the reference's
+        # functional.py:107-122)
+        if activation is not None:
+            raise ValueError("a fused activation does not combine with padding_mode='partial'")
+        from ._partial import partial_conv
+
+        output, _ = partial_conv(
+            input, weight, bias, stride, padding, dilation, groups, mask=None,
+            multi_channel=False, padding_mode="zeros", workspace_bytes=workspace_bytes,
+            backend=backend, need_update=False)
+        return output.squeeze(0) if unbatched else output
     amp = _check_arguments(input, weight, stride, padding, dilation, groups)
     _check_bias(input, weight, bias, amp)
     pairs = padding_pairs(padding, weight.shape[2:], stride, dilation)

@@ -15,6 +15,7 @@ from torch import Tensor, nn
 
 from ._geometry import DEFAULT_WORKSPACE_BYTES, _tuple, has_rank
 from ._padding import padding_pairs
+from ._partial import PartialConvOutput, partial_conv
 from .functional import _PADDING_MODES, conv_nd
 
 
@@ -119,6 +120,9 @@ class ConvNd(nn.Module):
         operator through torch_convnd::compatible_conv_nd (reference modules.py:137-155)."""
         if self.activation is not None:
             raise NotImplementedError("a fused activation does not support TorchScript")
+        if self.padding_mode == "partial":
+            raise NotImplementedError(
+                "padding_mode='partial' does not support TorchScript; use eager execution")
         from ._script import ScriptableConvNd
 
         return ScriptableConvNd(self)
@@ -193,3 +197,81 @@ class Conv4d(_FixedConvNd):
     """Dense 4-D convolution (for example x, y, z and time)."""
 
     _spatial_dimensions = 4
+
+
+class PartialConvNd(ConvNd):
+    """NVIDIA's partial convolution at any spatial rank, with ConvNd's parameters (the
+    reference's PartialConvNd, modules.py:218-320).
+
+    ``forward(input, mask=None)`` convolves only valid samples and rescales each window by
+    its valid fraction (``torch_convnd.partial_conv_nd`` states the formula and the mask
+    contract). ``multi_channel`` (fixed per layer) takes one mask channel per input
+    channel; ``return_mask`` sets whether calls also return the update mask as
+    ``PartialConvOutput(output, mask)``, and each call can override it. State dicts match
+    ConvNd's.
+    """
+
+    def __init__(
+        self,
+        in_channels: int,
+        out_channels: int,
+        kernel_size: int | Sequence[int],
+        stride: int | Sequence[int] = 1,
+        padding: str | int | Sequence[int] = 0,
+        dilation: int | Sequence[int] = 1,
+        groups: int = 1,
+        bias: bool = True,
+        padding_mode: str = "zeros",
+        device=None,
+        dtype=None,
+        *,
+        dimensions: int,
+        workspace_bytes: int = DEFAULT_WORKSPACE_BYTES,
+        backend: str = "auto",
+        multi_channel: bool = False,
+        return_mask: bool = False,
+    ):
+        super().__init__(in_channels, out_channels, kernel_size, stride, padding, dilation,
+                         groups, bias, padding_mode, device, dtype, dimensions=dimensions,
+                         workspace_bytes=workspace_bytes, backend=backend)
+        if not isinstance(multi_channel, bool) or not isinstance(return_mask, bool):
+            raise TypeError("multi_channel and return_mask must be bools")
+        if padding_mode == "partial":
+            raise ValueError(
+                "PartialConvNd already rescales zero padding; use padding_mode='zeros'")
+        self.multi_channel = multi_channel
+        self.return_mask = return_mask
+
+    def forward(  # type: ignore[override]
+        self,
+        input: Tensor,
+        mask: Tensor | None = None,
+        mask_in: Tensor | None = None,
+        return_mask: bool | None = None,
+    ) -> Tensor | PartialConvOutput:
+        """Convolve the valid samples; with ``return_mask`` also return the update mask.
+        ``mask_in`` is NVIDIA's keyword for ``mask``."""
+        if mask_in is not None:
+            if mask is not None:
+                raise TypeError("pass mask or mask_in, not both")
+            mask = mask_in
+        if return_mask is None:
+            return_mask = self.return_mask
+        elif not isinstance(return_mask, bool):
+            raise TypeError("return_mask must be a bool or None")
+        if not has_rank(input.ndim, self.dimensions):
+            raise ValueError(
+                f"expected {self.dimensions + 1} unbatched or {self.dimensions + 2} batched "
+                f"dimensions, got {input.ndim}"
+            )
+        output, update = partial_conv(
+            input, self.weight, self.bias, self.stride, self.padding, self.dilation,
+            self.groups, mask=mask, multi_channel=self.multi_channel,
+            padding_mode=self.padding_mode, workspace_bytes=self.workspace_bytes,
+            backend=self.backend, need_update=return_mask)
+        if not return_mask:
+            return output
+        return PartialConvOutput(output, update)
+
+    def __prepare_scriptable__(self):
+        raise NotImplementedError("PartialConvNd does not support TorchScript; use eager execution")
